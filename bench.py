@@ -1,0 +1,461 @@
+"""Benchmark of the Conv3d hot path on B200.
+
+Workload ("trunk"): the UNet3D trunk sweep at batch 4 per GPU, bf16, NDHWC —
+k3 pad1 convs 1->24 and 24->24 at 64x128x128, 48->48 at 32x64x64, 96->96 at
+16x32x32, 192->192 at 8x16x16, and k1 convs 48->24, 96->48, 192->96 at the
+matching levels. One step = forward, dW (+db) and dX of every layer, seeded
+synthetic N(0,1) inputs / grad_out and default-init weights.
+
+Metric: conv TFLOP/s over fwd+dW+dX (algorithmic FLOPs 2*V*Cin*Cout*k^3 per
+leg; padding MACs not counted), whole job. With N GPUs each rank runs its own
+batch-4 sweep (weak scaling, batch-sharded data parallel) and the fp32 dW/db
+of every layer are all-reduced over NCCL on a side stream while dX runs.
+
+Usage:  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+Prints ONE JSON line on rank 0.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "rdna4-conv3d-wmma_b200"))
+
+import torch  # noqa: E402
+
+# name, cin, cout, (D, H, W), k
+TRUNK = [
+    ("k3 1->24", 1, 24, (64, 128, 128), 3),
+    ("k3 24->24", 24, 24, (64, 128, 128), 3),
+    ("k3 48->48", 48, 48, (32, 64, 64), 3),
+    ("k3 96->96", 96, 96, (16, 32, 32), 3),
+    ("k3 192->192", 192, 192, (8, 16, 16), 3),
+    ("k1 48->24", 48, 24, (64, 128, 128), 1),
+    ("k1 96->48", 96, 48, (32, 64, 64), 1),
+    ("k1 192->96", 192, 96, (16, 32, 32), 1),
+]
+BATCH = 4
+METRIC = "conv TFLOP/s (fwd/dW/dX) vs bf16 peak; UNet3D ms/sample at 1/2/4/8 B200"
+
+
+def layer_flops(cin, cout, spatial, k, batch=BATCH):
+    d, h, w = spatial
+    return 2.0 * batch * d * h * w * cin * cout * k ** 3   # pad=(k-1)/2 keeps the output size
+
+
+def layer_bytes(cin, cout, spatial, k, batch=BATCH, leg="fwd"):
+    """Minimum HBM bytes of one leg (bf16 activations, fp32 dW)."""
+    d, h, w = spatial
+    v = batch * d * h * w
+    wbytes = cin * cout * k ** 3
+    if leg == "dw":
+        return 2 * v * (cin + cout) + 4 * wbytes
+    return 2 * v * (cin + cout) + 2 * wbytes
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            j = json.load(f)
+        return {"hbm_gbs": j["hbm_gbs"], "bf16_tflops": j["bf16_tflops"],
+                "bf16_tflops_sustained": j.get("bf16_tflops_sustained", j["bf16_tflops"]), "src": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "src": "fallback"}
+
+
+def load_traffic():
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f)
+    return {}
+
+
+# ---------------------------------------------------------------------------
+# clocks sampler (nvidia-smi during the timed region)
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.lines = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.idx)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for nm, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(nm)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# distributed set-up
+# ---------------------------------------------------------------------------
+def init_dist(n_gpus):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the reference's CPU path (stock PyTorch fp32 conv3d)
+# ---------------------------------------------------------------------------
+def cpu_sample_pass(layers, frac_d):
+    """fwd + dW + dX of every layer on CPU fp32, batch 1, depth cut to frac_d."""
+    import torch.nn.functional as F
+    flops = 0.0
+    t0 = time.perf_counter()
+    for name, cin, cout, (d, h, w), k in layers:
+        dd = max(2, int(round(d * frac_d)))
+        g = torch.Generator().manual_seed(0)
+        x = torch.randn(1, cin, dd, h, w, generator=g)
+        wt = torch.randn(cout, cin, k, k, k, generator=g) / (cin * k ** 3) ** 0.5
+        pad = (k - 1) // 2
+        y = F.conv3d(x, wt, None, 1, pad)
+        go = torch.randn_like(y)
+        torch.nn.grad.conv3d_weight(x, wt.shape, go, 1, pad)
+        torch.nn.grad.conv3d_input(x.shape, wt, go, 1, pad)
+        flops += 3 * layer_flops(cin, cout, (dd, h, w), k, batch=1)
+    return flops, time.perf_counter() - t0
+
+
+def cpu_baseline(layers, budget_s=15.0, frac_d=1 / 16):
+    cores = torch.get_num_threads()
+    cpu_sample_pass(layers, frac_d)  # warm-up
+    rates, t_start = [], time.perf_counter()
+    while len(rates) < 5 or (time.perf_counter() - t_start < budget_s and len(rates) < 50):
+        fl, dt = cpu_sample_pass(layers, frac_d)
+        rates.append(fl / dt / 1e12)
+        if time.perf_counter() - t_start > 2 * budget_s:
+            break
+    return {"value": round(statistics.median(rates), 5), "unit": "TFLOP/s", "cores": cores, "kind": "port",
+            "sample": (f"stock torch fp32 F.conv3d + conv3d_weight + conv3d_input on CPU (the reference's "
+                       f"CPU path, conv3d_wmma.py:1437-1438,1299-1314) over every trunk layer at batch 1 and "
+                       f"{frac_d:.4g} of the depth; median of {len(rates)} passes; os.cpu_count()="
+                       f"{os.cpu_count()}")}
+
+
+def run_reference_arm(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    frac = 1 / 32
+    for _ in range(args.warmup):
+        cpu_sample_pass(TRUNK, frac)
+    fl_tot, t_tot = 0.0, 0.0
+    for _ in range(args.steps):
+        fl, dt = cpu_sample_pass(TRUNK, frac)
+        fl_tot += fl
+        t_tot += dt
+    val = fl_tot / t_tot / 1e12
+    cores = torch.get_num_threads()
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(val, 5), "unit": "TFLOP/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(t_tot / args.steps * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "trunk sweep (BASELINE configs[1]) fwd+dW+dX, CPU sample",
+                   "batch": 1, "depth_fraction": frac, "layers": [t[0] for t in TRUNK]},
+        "cpu_baseline": {"value": round(val, 5), "unit": "TFLOP/s", "cores": cores, "kind": "port",
+                         "sample": (f"each step: stock torch fp32 conv3d fwd+dW+dX on CPU (the reference's CPU "
+                                    f"path) over every trunk layer at batch 1 and {frac:.4g} of the depth")},
+        "e2e": {"value": round(val, 5), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+class Layer:
+    def __init__(self, spec, device, seed):
+        import torch.nn as nn
+        self.name, self.cin, self.cout, self.spatial, self.k = spec
+        self.pad = (self.k - 1) // 2
+        d, h, w = self.spatial
+        g = torch.Generator(device=device).manual_seed(seed)
+        cl = torch.channels_last_3d
+        self.x = torch.randn(BATCH, self.cin, d, h, w, device=device, generator=g).to(
+            torch.bfloat16).contiguous(memory_format=cl)
+        self.go = torch.randn(BATCH, self.cout, d, h, w, device=device, generator=g).to(
+            torch.bfloat16).contiguous(memory_format=cl)
+        conv = nn.Conv3d(self.cin, self.cout, self.k, padding=self.pad)
+        self.w = conv.weight.detach().to(device=device, dtype=torch.bfloat16)
+        self.b = conv.bias.detach().to(device=device, dtype=torch.bfloat16)
+        self.flops = layer_flops(self.cin, self.cout, self.spatial, self.k)
+
+
+def run_step(layers, reducer, ev=None):
+    """fwd, dW(+db) and dX of every layer through the package's launch path."""
+    cw = sys.modules["rdna4_conv3d.conv3d_wmma"]
+    p3 = lambda p: (p, p, p)  # noqa: E731
+    outs = []
+    for i, L in enumerate(layers):
+        if ev is not None:
+            ev[i][0].record()
+        y = cw._launch_fwd(L.x, L.w, L.b, p3(L.pad))
+        if ev is not None:
+            ev[i][1].record()
+        dw, db = cw._launch_wgrad(L.x, L.go, L.w.shape, p3(L.pad), True)
+        handle = reducer.reduce_async([dw, db]) if reducer is not None else None
+        if ev is not None:
+            ev[i][2].record()
+        dx = cw._launch_dgrad(L.go, L.w, L.x.shape, p3(L.pad))
+        if ev is not None:
+            ev[i][3].record()
+        if handle is not None:
+            handle.wait()
+        outs.append((y, dw, db, dx))
+    return outs
+
+
+def run_e2e(layers, host, steps, warmup, world):
+    """Public-API legs with inputs copied from pinned host memory and results
+    read back every step (wmma_fwd / wmma_dw / wmma_dx)."""
+    from rdna4_conv3d import wmma_dw, wmma_dx, wmma_fwd
+    h2d = sum(hx.numel() * 2 + hg.numel() * 2 for hx, hg, _ in host)
+    d2h = 0
+    for L in layers:
+        d2h += L.x.numel() * 2 // L.cin * L.cout + L.x.numel() * 2 + L.w.numel() * 2
+    out_bufs = []
+    for L in layers:
+        yb = torch.empty((BATCH, L.cout) + L.spatial, dtype=torch.bfloat16, pin_memory=True)
+        dxb = torch.empty(L.x.shape, dtype=torch.bfloat16, pin_memory=True)
+        dwb = torch.empty(L.w.shape, dtype=torch.bfloat16, pin_memory=True)
+        out_bufs.append((yb, dxb, dwb))
+    cl = torch.channels_last_3d
+
+    def step():
+        for L, (hx, hg, hw), (yb, dxb, dwb) in zip(layers, host, out_bufs):
+            x = hx.to("cuda", non_blocking=True).contiguous(memory_format=cl)
+            go = hg.to("cuda", non_blocking=True).contiguous(memory_format=cl)
+            y = wmma_fwd(x, L.w, L.b, 1, L.pad)
+            dw = wmma_dw(x, L.w, go, 1, L.pad)
+            dx = wmma_dx(x, L.w, go, 1, L.pad)
+            yb.copy_(y, non_blocking=True)
+            dxb.copy_(dx, non_blocking=True)
+            dwb.copy_(dw, non_blocking=True)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1), world)
+    barrier(world)
+    return ms, h2d, d2h
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    if args.impl == "reference":
+        return run_reference_arm(args)
+
+    world, rank, local = init_dist(args.gpus)
+    dev = torch.device("cuda", local)
+    from rdna4_conv3d import _native
+    from rdna4_conv3d.conv3d_wmma import conv3d_kernels
+    _native.lib()
+
+    layers = [Layer(spec, dev, seed=1000 * rank + i) for i, spec in enumerate(TRUNK)]
+    reducer = None
+    if world > 1:
+        from rdna4_conv3d.distributed import GradAllReducer
+        reducer = GradAllReducer()
+
+    step_flops = sum(3 * L.flops for L in layers)
+    for _ in range(args.warmup):
+        run_step(layers, reducer)
+    torch.cuda.synchronize()
+
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in layers]
+    leg_ms = [[0.0, 0.0, 0.0] for _ in layers]
+    sampler = ClockSampler(local)
+    barrier(world)
+    torch.cuda.synchronize()
+    sampler.start()
+    time.sleep(0.3)
+    n_launch0 = _native.launch_count()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(args.steps):
+        run_step(layers, reducer, ev)
+        torch.cuda.synchronize()
+        for i in range(len(layers)):
+            for j in range(3):
+                leg_ms[i][j] += ev[i][j].elapsed_time(ev[i][j + 1])
+    t1.record()
+    torch.cuda.synchronize()
+    launches = _native.launch_count() - n_launch0
+    clocks = sampler.stop()
+    ms_total = max_over_ranks(t0.elapsed_time(t1), world)
+    barrier(world)
+
+    ms_step = ms_total / args.steps
+    value = step_flops * world * args.steps / (ms_total / 1e3) / 1e12
+    peaks = load_peaks()
+
+    # per-layer breakdown (this rank) and the dominant kernel
+    breakdown = []
+    dom = None
+    for L, lm in zip(layers, leg_ms):
+        fam = conv3d_kernels((BATCH, L.cin) + L.spatial, L.cout, L.k, L.pad)
+        row = {"layer": L.name, "gflop_per_leg": round(L.flops / 1e9, 3)}
+        for j, leg in enumerate(("fwd", "dw", "dx")):
+            ms = lm[j] / args.steps
+            row[leg + "_us"] = round(ms * 1e3, 2)
+            row[leg + "_tflops"] = round(L.flops / (ms / 1e3) / 1e12, 2) if ms > 0 else None
+            row[leg + "_kernel"] = fam[leg]
+            if dom is None or ms > dom[0]:
+                dom = (ms, L, leg)
+        breakdown.append(row)
+    ms_dom, Ld, leg_d = dom
+    ai = Ld.flops / layer_bytes(Ld.cin, Ld.cout, Ld.spatial, Ld.k, leg=leg_d)
+    ridge = peaks["bf16_tflops_sustained"] * 1e12 / (peaks["hbm_gbs"] * 1e9)
+    traffic_tab = load_traffic()
+    tkey = f"{Ld.name} {leg_d}"
+    if ai >= ridge:
+        achieved = Ld.flops / (ms_dom / 1e3) / 1e12
+        roof = {"bound": "tensor", "achieved": round(achieved, 2), "peak": peaks["bf16_tflops_sustained"],
+                "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_tflops_sustained"], 4)}
+    else:
+        achieved = layer_bytes(Ld.cin, Ld.cout, Ld.spatial, Ld.k, leg=leg_d) / (ms_dom / 1e3) / 1e9
+        roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": round(achieved / peaks["hbm_gbs"], 4)}
+    roof["traffic"] = traffic_tab.get(tkey)
+    roof["kernel"] = f"{tkey} ({breakdown[layers.index(Ld)][leg_d + '_kernel']})"
+    roof["peak_src"] = f"{peaks['src']} (sustained bf16 / copy bandwidth)"
+
+    e2e = None
+    if not args.no_e2e:
+        host = []
+        for L in layers:
+            host.append((L.x.cpu().contiguous().pin_memory(), L.go.cpu().contiguous().pin_memory(), None))
+        e2e_steps = max(1, min(args.steps, 3))
+        ms_e2e, h2d, d2h = run_e2e(layers, host, e2e_steps, 1, world)
+        e2e = {"value": round(step_flops * world * e2e_steps / (ms_e2e / 1e3) / 1e12, 3), "unit": "TFLOP/s",
+               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+               "ms_per_step": round(ms_e2e / e2e_steps, 3),
+               "path": "public API wmma_fwd/wmma_dw/wmma_dx, pinned host inputs copied in and results copied "
+                       "back inside the timed region"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(TRUNK)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 3), "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic",
+            "config": {"workload": "trunk sweep (BASELINE configs[1]): k3 1->24, 24->24, 48->48, 96->96, "
+                                   "192->192 and k1 48->24, 96->48, 192->96, fwd+dW+dX",
+                       "batch_per_gpu": BATCH, "global_batch": BATCH * world, "dtype": "bf16",
+                       "parallelism": f"dp{world}" if world > 1 else "single",
+                       "l2": "no flush: each step streams ~1.7 GB of activations, far above the 126 MB L2"},
+            "gflop_per_step_per_gpu": round(step_flops / 1e9, 2),
+            "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": int(launches),
+            "clocks": clocks, "layers": breakdown,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        barrier(world)
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,186 @@
+/*
+ * r4c_conv3d.h — C ABI of the B200 (sm_100a) Conv3d / ConvTranspose3d hot path.
+ *
+ * This library replaces the device half of the rdna4_conv3d package: the Triton
+ * launchers in src/rdna4_conv3d/conv3d_wmma.py and the optional HIP fprop
+ * (src/rdna4_conv3d/conv3d_wmma_hip.hip:148-195). Each entry point below names
+ * the reference function it stands in for.
+ *
+ * Conventions
+ *   - Activations are NDHWC (channels_last_3d), bf16 or fp16, densely packed:
+ *     element (n, d, h, w, c) lives at ((((n*D + d)*H + h)*W + w)*C + c).
+ *   - Weights are handed over pre-packed by r4c_pack_weight(); the packed
+ *     layout is private to the kernel that the descriptor selects, so a packed
+ *     buffer must come from r4c_pack_weight() with the same descriptor and leg.
+ *   - Weight and bias gradients are written in fp32, in PyTorch's own layout
+ *     (OIDHW for Conv3d, (Cin, Cout, 2, 2, 2) for ConvTranspose3d).
+ *   - Every buffer, including the workspace, is owned by the caller. Nothing is
+ *     allocated inside the library and no state is kept between calls apart
+ *     from a per-device cache of kernel attributes.
+ *   - Work is enqueued on the given stream and ordered only by it; calls may
+ *     come from any host thread.
+ *   - Errors are returned as negative status codes; nothing is thrown across
+ *     the ABI. r4c_strerror() turns a code into text.
+ */
+#ifndef R4C_CONV3D_H_
+#define R4C_CONV3D_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* cudaStream_t without pulling in the CUDA headers. */
+typedef struct CUstream_st* r4c_stream_t;
+
+/* Status codes. */
+enum {
+  R4C_OK = 0,
+  R4C_ERR_INVALID = -1,      /* bad pointer, size or descriptor field            */
+  R4C_ERR_UNSUPPORTED = -2,  /* geometry outside k in {1,3} / tconv k2s2 scope   */
+  R4C_ERR_WORKSPACE = -3,    /* workspace smaller than r4c_workspace_size()      */
+  R4C_ERR_CUDA = -4,         /* a CUDA runtime/driver call failed                */
+  R4C_ERR_ALIGN = -5,        /* pointer not aligned as the kernel requires       */
+  R4C_ERR_NO_DEVICE = -6,    /* no sm_100 device current                         */
+  R4C_ERR_TOO_LARGE = -7     /* size above a fixed maximum of the entry point    */
+};
+
+/* Element types of activations / packed weights. */
+enum { R4C_BF16 = 0, R4C_F16 = 1, R4C_F32 = 2 };
+
+/* Legs, for r4c_pack_weight / r4c_workspace_size. */
+enum {
+  R4C_LEG_FWD = 0,   /* Conv3d forward                          */
+  R4C_LEG_DX = 1,    /* Conv3d input gradient                   */
+  R4C_LEG_DW = 2,    /* Conv3d weight (+bias) gradient          */
+  R4C_LEG_TFWD = 3,  /* ConvTranspose3d k2s2 forward            */
+  R4C_LEG_TDX = 4,   /* ConvTranspose3d k2s2 input gradient     */
+  R4C_LEG_TDW = 5    /* ConvTranspose3d k2s2 weight gradient    */
+};
+
+/* Kernel families the dispatcher can pick (r4c_plan_kernel). */
+enum {
+  R4C_KERNEL_NONE = 0,
+  R4C_KERNEL_GENERIC = 1,   /* SIMT implicit GEMM, any channel count         */
+  R4C_KERNEL_TC = 2         /* tcgen05 + TMA implicit GEMM (sm_100a)          */
+};
+
+/*
+ * Problem descriptor. For Conv3d (k = 1 or 3, stride 1, dilation 1, groups 1)
+ * n/d/h/w are the INPUT sizes; the output is
+ *   o = i + 2*pad - (k - 1)    per spatial axis.
+ * For ConvTranspose3d (k = 2, stride 2, pad 0) n/d/h/w are the input sizes and
+ * the output is 2x in every spatial axis; pad_* must be 0.
+ */
+typedef struct r4c_conv_desc {
+  int32_t n, d, h, w;
+  int32_t cin, cout;
+  int32_t k;                 /* 1 or 3 (Conv3d), 2 (ConvTranspose3d) */
+  int32_t pad_d, pad_h, pad_w;
+  int32_t dtype;             /* R4C_BF16 or R4C_F16 */
+  int32_t force_kernel;      /* 0 = automatic, else an R4C_KERNEL_* value */
+} r4c_conv_desc;
+
+/* Library / error text. */
+const char* r4c_strerror(int status);
+int r4c_version(void);
+
+/*
+ * Device-side error flag of the current device. Every wait inside a kernel is
+ * bounded (about one second); a wait that runs out makes the kernel record a
+ * non-zero code here and return early instead of hanging the GPU. The call
+ * synchronizes `stream`, returns the flag (0 = none) and clears it when
+ * `clear` is non-zero. No reference counterpart (the Triton kernels have no
+ * device-side waits).
+ */
+int r4c_device_error(r4c_stream_t stream, int clear);
+
+/* Total number of CUDA kernels this library has launched in this process
+ * (all devices, all threads). Lets a caller count the kernels behind a timed
+ * region. No reference counterpart. */
+uint64_t r4c_launch_count(void);
+
+/* Which kernel family runs `leg` for `desc` (an R4C_KERNEL_* value, or a
+ * negative status when the geometry is out of scope). Pure host logic. */
+int r4c_plan_kernel(const r4c_conv_desc* desc, int leg);
+
+/* Human-readable description of the kernel plan for `leg` (family, tiles,
+ * stages, shared memory) written into buf (NUL-terminated, truncated to
+ * len). Returns the same value as r4c_plan_kernel. Pure host logic. */
+int r4c_describe_plan(const r4c_conv_desc* desc, int leg, char* buf, size_t len);
+
+/* Bytes of the packed weight buffer for `leg` (FWD, DX, TFWD or TDX). */
+size_t r4c_packed_weight_bytes(const r4c_conv_desc* desc, int leg);
+
+/* Bytes of caller-owned workspace that `leg` needs (0 when none). */
+size_t r4c_workspace_size(const r4c_conv_desc* desc, int leg);
+
+/*
+ * Pack a PyTorch-layout weight for one leg.
+ *   Conv3d:          w_src is OIDHW (Cout, Cin, k, k, k).
+ *   ConvTranspose3d: w_src is (Cin, Cout, 2, 2, 2).
+ * src_dtype is R4C_F32, R4C_BF16 or R4C_F16; the packed buffer is desc->dtype.
+ * Replaces _pack_weight / _tr_pack_w and the flip/transpose/repack that k3 dX
+ * does per call (src/rdna4_conv3d/conv3d_wmma.py:1023-1026,1154-1162,1453-1459).
+ */
+int r4c_pack_weight(const r4c_conv_desc* desc, int leg, const void* w_src,
+                    int src_dtype, void* w_packed, r4c_stream_t stream);
+
+/*
+ * Conv3d forward: y = conv3d(x, w) + bias.
+ * x NDHWC [n,d,h,w,cin]; y NDHWC [n,od,oh,ow,cout]; bias (cout) in desc->dtype
+ * or NULL. Replaces _launch_fwd (conv3d_wmma.py:1048-1105) and the HIP
+ * fwd_k3 (conv3d_wmma_hip.hip:148-195).
+ */
+int r4c_conv3d_fwd(const r4c_conv_desc* desc, const void* x, const void* w_packed,
+                   const void* bias, void* y, void* workspace, size_t ws_bytes,
+                   r4c_stream_t stream);
+
+/*
+ * Conv3d input gradient: dx = conv3d_input(go, w).
+ * go NDHWC [n,od,oh,ow,cout]; dx NDHWC [n,d,h,w,cin]; w_packed from
+ * r4c_pack_weight(..., R4C_LEG_DX, ...). Replaces _launch_dgrad
+ * (conv3d_wmma.py:1108-1179); the k3 case uses pad' = 2 - pad, so every pad in
+ * {0,1,2} is exact (the reference reuses pad, correct only for pad 1).
+ */
+int r4c_conv3d_dx(const r4c_conv_desc* desc, const void* go, const void* w_packed,
+                  void* dx, void* workspace, size_t ws_bytes, r4c_stream_t stream);
+
+/*
+ * Conv3d weight and bias gradient, fp32, deterministic.
+ * x NDHWC, go NDHWC; dw OIDHW fp32 [cout,cin,k,k,k]; db fp32 [cout] or NULL.
+ * Split-K partials over N*D*H*W go to the workspace and are summed in a fixed
+ * order. Replaces _launch_wgrad + partial.sum(0) (conv3d_wmma.py:1182-1214)
+ * and the separate db reduction (conv3d_wmma.py:1318).
+ */
+int r4c_conv3d_dw(const r4c_conv_desc* desc, const void* x, const void* go,
+                  float* dw, float* db, void* workspace, size_t ws_bytes,
+                  r4c_stream_t stream);
+
+/*
+ * ConvTranspose3d k2 s2 p0 forward. x NDHWC [n,d,h,w,cin]; y NDHWC
+ * [n,2d,2h,2w,cout]; bias (cout) or NULL. Replaces transpose_k2s2_fwd
+ * (conv3d_wmma.py:1462-1488).
+ */
+int r4c_tconv_fwd(const r4c_conv_desc* desc, const void* x, const void* w_packed,
+                  const void* bias, void* y, void* workspace, size_t ws_bytes,
+                  r4c_stream_t stream);
+
+/* ConvTranspose3d k2s2 input gradient. Replaces transpose_k2s2_dx
+ * (conv3d_wmma.py:1491-1514). */
+int r4c_tconv_dx(const r4c_conv_desc* desc, const void* go, const void* w_packed,
+                 void* dx, void* workspace, size_t ws_bytes, r4c_stream_t stream);
+
+/* ConvTranspose3d k2s2 weight/bias gradient, fp32 (Cin,Cout,2,2,2) and
+ * (Cout). Replaces transpose_k2s2_dw (conv3d_wmma.py:1517-1542). */
+int r4c_tconv_dw(const r4c_conv_desc* desc, const void* x, const void* go,
+                 float* dw, float* db, void* workspace, size_t ws_bytes,
+                 r4c_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* R4C_CONV3D_H_ */

@@ -1,0 +1,89 @@
+// r4c_internal.h — declarations shared by the library's translation units.
+#pragma once
+
+#include "r4c_common.cuh"
+
+namespace r4c {
+
+enum { MODE_CONV = 0, MODE_TFWD = 1, MODE_TDX = 2, MODE_TDW = 3 };
+
+namespace generic {
+
+// Forward-shaped implicit GEMM: out[M, N] = A[M, K] * B[K, N] (+ bias).
+struct FwdParams {
+  const void* a;      // activation source, NDHWC
+  const void* b;      // packed weight, row-major [K][N]
+  const void* bias;   // [N] (MODE_CONV) or [oc] (MODE_TFWD), may be null
+  void* out;          // NDHWC
+  int64_t M;
+  int N, K;
+  int sd, sh, sw, sc; // source tensor spatial dims and channels
+  int md, mh, mw;     // grid the GEMM row index m walks (n is the outer index)
+  int ks, pd, ph, pw; // conv kernel size and zero padding (MODE_CONV)
+  int oc;             // channels of y (MODE_TFWD)
+};
+
+// Weight-gradient GEMM: partial[s][P][N] = sum over m in split s.
+struct WgradParams {
+  const void* x;
+  const void* go;
+  float* partial;
+  int P, N;
+  int64_t M;
+  int chunk;
+  int d, h, w, cin;   // x dims
+  int md, mh, mw;     // reduction grid (go dims for conv, x dims for tconv)
+  int cout;
+  int ks, pd, ph, pw;
+};
+
+cudaError_t launch_fwd(const FwdParams& p, int mode, int dtype, cudaStream_t st);
+void wgrad_split(int64_t M, int P, int N, int* S, int* chunk);
+void db_split(int64_t V, int* S, int64_t* chunk);
+cudaError_t launch_wgrad(const WgradParams& p, int mode, int dtype, int S, float* dw, int taps,
+                         cudaStream_t st);
+cudaError_t launch_db(const void* go, int64_t V, int C, int dtype, float* part, float* db,
+                      cudaStream_t st);
+
+}  // namespace generic
+
+namespace tc {
+
+// Host-side plan of the tcgen05 conv kernel (k in {1,3}; fwd, or dX run as a
+// conv of dY with the flipped weight and padding k-1-p).
+struct ConvPlan {
+  bool ok;
+  int n, d, h, w;        // source (input) dims of the conv actually run
+  int od, oh, ow;        // its output dims
+  int cin, cout;         // its channels (dX: cin = Cout of the layer)
+  int ks, pd, ph, pw;
+  int c8;                // 8-channel chunks of cin
+  int npad;              // cout rounded up to the MMA N granule (16)
+  int G, ngroups;        // chunks per pipeline stage, stages per kd plane
+  int nsteps;            // 16-wide K steps per stage
+  int wt, ht;            // output tile (cols, rows) of one plane
+  int pitch_w, pitch_h;  // brick pitches: wt + ks - 1, ht + ks - 1
+  int cpb;               // bytes of one chunk plane (128-aligned)
+  int mtiles, nsets;     // 128-row M tiles per unit; TMEM accumulator sets
+  int a_bytes, b_bytes, stage_bytes, stages, smem_bytes;
+  int wres;              // 1: the whole packed weight stays resident in smem
+  int wres_bytes;        // its size (ks * ngroups * b_bytes) when resident
+  int tmem_cols;
+  double est_cycles;     // planner's cost-model estimate for the whole launch
+  int64_t work_units;    // n * od * tiles_h * tiles_w
+  int grid;
+};
+
+bool plan_conv(int n, int d, int h, int w, int cin, int cout, int ks, int pd, int ph, int pw,
+               ConvPlan* pl);
+size_t packed_bytes(const ConvPlan& pl);
+// Packs a logical weight W[co][tap][ci] (fp32 view given by a functor on host is
+// not used; the device pack kernel reads the PyTorch layout directly).
+cudaError_t pack_weight(const ConvPlan& pl, bool flip_for_dx, const void* w_src, int src_dtype,
+                        void* w_packed, int dtype, cudaStream_t st);
+int launch_conv(const ConvPlan& pl, const void* x, const void* w_packed, const void* bias,
+                void* y, int dtype, cudaStream_t st);
+
+}  // namespace tc
+
+}  // namespace r4c

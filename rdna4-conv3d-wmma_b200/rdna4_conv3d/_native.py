@@ -1,0 +1,275 @@
+"""ctypes binding of the B200 C-ABI library (``libr4c_conv3d.so``).
+
+This module is the only place Python touches the native kernels. It is the
+reference-side binding of ``include/r4c_conv3d.h``: it turns torch tensors into
+plain pointers and sizes, passes torch's current CUDA stream, and turns status
+codes into exceptions. There is deliberately no host fallback: if the library
+is missing or the call fails, the caller gets an exception.
+
+Reference counterpart: the JIT loader of the HIP extension
+(src/rdna4_conv3d/hip_backend.py:1-37) and the Triton launchers it sat next to
+(src/rdna4_conv3d/conv3d_wmma.py:1015-1227, 1453-1542).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from typing import Optional, Tuple
+
+import torch
+
+_LIB_NAME = "libr4c_conv3d.so"
+_LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), _LIB_NAME)
+_lib = None
+_lock = threading.Lock()
+
+# Must match include/r4c_conv3d.h.
+R4C_OK = 0
+R4C_BF16, R4C_F16, R4C_F32 = 0, 1, 2
+LEG_FWD, LEG_DX, LEG_DW, LEG_TFWD, LEG_TDX, LEG_TDW = range(6)
+KERNEL_NONE, KERNEL_GENERIC, KERNEL_TC = 0, 1, 2
+
+
+class ConvDesc(ctypes.Structure):
+    _fields_ = [
+        ("n", ctypes.c_int32), ("d", ctypes.c_int32), ("h", ctypes.c_int32), ("w", ctypes.c_int32),
+        ("cin", ctypes.c_int32), ("cout", ctypes.c_int32), ("k", ctypes.c_int32),
+        ("pad_d", ctypes.c_int32), ("pad_h", ctypes.c_int32), ("pad_w", ctypes.c_int32),
+        ("dtype", ctypes.c_int32), ("force_kernel", ctypes.c_int32),
+    ]
+
+
+class NativeError(RuntimeError):
+    """A C-ABI entry point returned a non-zero status."""
+
+
+def library_path() -> str:
+    return _LIB_PATH
+
+
+def _bind(lib) -> None:
+    P = ctypes.c_void_p
+    D = ctypes.POINTER(ConvDesc)
+    sz = ctypes.c_size_t
+    i = ctypes.c_int
+    sig = {
+        "r4c_strerror": ([i], ctypes.c_char_p),
+        "r4c_version": ([], i),
+        "r4c_device_error": ([P, i], i),
+        "r4c_launch_count": ([], ctypes.c_uint64),
+        "r4c_plan_kernel": ([D, i], i),
+        "r4c_describe_plan": ([D, i, ctypes.c_char_p, sz], i),
+        "r4c_packed_weight_bytes": ([D, i], sz),
+        "r4c_workspace_size": ([D, i], sz),
+        "r4c_pack_weight": ([D, i, P, i, P, P], i),
+        "r4c_conv3d_fwd": ([D, P, P, P, P, P, sz, P], i),
+        "r4c_conv3d_dx": ([D, P, P, P, P, sz, P], i),
+        "r4c_conv3d_dw": ([D, P, P, P, P, P, sz, P], i),
+        "r4c_tconv_fwd": ([D, P, P, P, P, P, sz, P], i),
+        "r4c_tconv_dx": ([D, P, P, P, P, sz, P], i),
+        "r4c_tconv_dw": ([D, P, P, P, P, P, sz, P], i),
+    }
+    for name, (args, res) in sig.items():
+        fn = getattr(lib, name)
+        fn.argtypes = args
+        fn.restype = res
+
+
+def lib():
+    """Load (once) and return the native library; raise if it is missing."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(_LIB_PATH):
+                raise NativeError(
+                    f"rdna4_conv3d native library not built: {_LIB_PATH} is missing "
+                    "(run `python -m rdna4_conv3d.build` or __graft_entry__.build())")
+            handle = ctypes.CDLL(_LIB_PATH)
+            _bind(handle)
+            _lib = handle
+    return _lib
+
+
+def available() -> bool:
+    try:
+        lib()
+        return True
+    except (NativeError, OSError):
+        return False
+
+
+def strerror(status: int) -> str:
+    return lib().r4c_strerror(int(status)).decode()
+
+
+def _check(status: int, what: str) -> None:
+    if status != R4C_OK:
+        raise NativeError(f"{what} failed: {strerror(status)} (status {status})")
+
+
+def dtype_code(dt: torch.dtype) -> int:
+    if dt == torch.bfloat16:
+        return R4C_BF16
+    if dt == torch.float16:
+        return R4C_F16
+    if dt == torch.float32:
+        return R4C_F32
+    raise NativeError(f"unsupported dtype {dt}")
+
+
+def make_desc(n, d, h, w, cin, cout, k, pad, dtype: torch.dtype, force_kernel: int = 0) -> ConvDesc:
+    pd, ph, pw = pad
+    return ConvDesc(int(n), int(d), int(h), int(w), int(cin), int(cout), int(k),
+                    int(pd), int(ph), int(pw), dtype_code(dtype), int(force_kernel))
+
+
+def _stream(device: torch.device):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    return ctypes.c_void_p(0 if t is None else t.data_ptr())
+
+
+def _require_cuda(*ts: Optional[torch.Tensor]) -> torch.device:
+    dev = None
+    for t in ts:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise NativeError("rdna4_conv3d native kernels need CUDA tensors")
+        dev = t.device if dev is None else dev
+    return dev
+
+
+def plan_kernel(desc: ConvDesc, leg: int) -> int:
+    return int(lib().r4c_plan_kernel(ctypes.byref(desc), leg))
+
+
+def describe_plan(desc: ConvDesc, leg: int) -> str:
+    buf = ctypes.create_string_buffer(512)
+    lib().r4c_describe_plan(ctypes.byref(desc), leg, buf, 512)
+    return buf.value.decode()
+
+
+def workspace_bytes(desc: ConvDesc, leg: int) -> int:
+    return int(lib().r4c_workspace_size(ctypes.byref(desc), leg))
+
+
+def packed_weight_bytes(desc: ConvDesc, leg: int) -> int:
+    return int(lib().r4c_packed_weight_bytes(ctypes.byref(desc), leg))
+
+
+def _workspace(desc: ConvDesc, leg: int, device) -> Tuple[Optional[torch.Tensor], int]:
+    nb = workspace_bytes(desc, leg)
+    if nb == 0:
+        return None, 0
+    return torch.empty(nb, dtype=torch.uint8, device=device), nb
+
+
+def pack_weight(desc: ConvDesc, leg: int, weight: torch.Tensor) -> torch.Tensor:
+    """Pack a PyTorch-layout weight for one leg (r4c_pack_weight)."""
+    dev = _require_cuda(weight)
+    w = weight.contiguous()
+    nbytes = packed_weight_bytes(desc, leg)
+    if nbytes == 0:
+        raise NativeError("descriptor rejected by r4c_packed_weight_bytes")
+    out = torch.empty(nbytes // 2, dtype=torch.bfloat16 if desc.dtype == R4C_BF16 else torch.float16,
+                      device=dev)
+    with torch.cuda.device(dev):
+        st = lib().r4c_pack_weight(ctypes.byref(desc), leg, _ptr(w), dtype_code(w.dtype), _ptr(out),
+                                   _stream(dev))
+    _check(st, "r4c_pack_weight")
+    return out
+
+
+def _ndhwc_empty(n, c, d, h, w, device, dtype) -> torch.Tensor:
+    return torch.empty((n, c, d, h, w), device=device, dtype=dtype, memory_format=torch.channels_last_3d)
+
+
+def conv_fwd(desc: ConvDesc, x_cl: torch.Tensor, w_packed: torch.Tensor, bias: Optional[torch.Tensor],
+             out_shape) -> torch.Tensor:
+    dev = _require_cuda(x_cl, w_packed, bias)
+    od, oh, ow = out_shape
+    y = _ndhwc_empty(desc.n, desc.cout, od, oh, ow, dev, x_cl.dtype)
+    ws, nb = _workspace(desc, LEG_FWD, dev)
+    with torch.cuda.device(dev):
+        st = lib().r4c_conv3d_fwd(ctypes.byref(desc), _ptr(x_cl), _ptr(w_packed), _ptr(bias), _ptr(y),
+                                  _ptr(ws), nb, _stream(dev))
+    _check(st, "r4c_conv3d_fwd")
+    return y
+
+
+def conv_dx(desc: ConvDesc, go_cl: torch.Tensor, w_packed: torch.Tensor) -> torch.Tensor:
+    dev = _require_cuda(go_cl, w_packed)
+    dx = _ndhwc_empty(desc.n, desc.cin, desc.d, desc.h, desc.w, dev, go_cl.dtype)
+    ws, nb = _workspace(desc, LEG_DX, dev)
+    with torch.cuda.device(dev):
+        st = lib().r4c_conv3d_dx(ctypes.byref(desc), _ptr(go_cl), _ptr(w_packed), _ptr(dx), _ptr(ws), nb,
+                                 _stream(dev))
+    _check(st, "r4c_conv3d_dx")
+    return dx
+
+
+def conv_dw(desc: ConvDesc, x_cl: torch.Tensor, go_cl: torch.Tensor, want_db: bool):
+    """fp32 OIDHW weight gradient and (optionally) fp32 bias gradient."""
+    dev = _require_cuda(x_cl, go_cl)
+    k = desc.k
+    dw = torch.empty((desc.cout, desc.cin, k, k, k), dtype=torch.float32, device=dev)
+    db = torch.empty((desc.cout,), dtype=torch.float32, device=dev) if want_db else None
+    ws, nb = _workspace(desc, LEG_DW, dev)
+    with torch.cuda.device(dev):
+        st = lib().r4c_conv3d_dw(ctypes.byref(desc), _ptr(x_cl), _ptr(go_cl), _ptr(dw), _ptr(db), _ptr(ws), nb,
+                                 _stream(dev))
+    _check(st, "r4c_conv3d_dw")
+    return dw, db
+
+
+def tconv_fwd(desc: ConvDesc, x_cl: torch.Tensor, w_packed: torch.Tensor,
+              bias: Optional[torch.Tensor]) -> torch.Tensor:
+    dev = _require_cuda(x_cl, w_packed, bias)
+    y = _ndhwc_empty(desc.n, desc.cout, 2 * desc.d, 2 * desc.h, 2 * desc.w, dev, x_cl.dtype)
+    ws, nb = _workspace(desc, LEG_TFWD, dev)
+    with torch.cuda.device(dev):
+        st = lib().r4c_tconv_fwd(ctypes.byref(desc), _ptr(x_cl), _ptr(w_packed), _ptr(bias), _ptr(y),
+                                 _ptr(ws), nb, _stream(dev))
+    _check(st, "r4c_tconv_fwd")
+    return y
+
+
+def tconv_dx(desc: ConvDesc, go_cl: torch.Tensor, w_packed: torch.Tensor) -> torch.Tensor:
+    dev = _require_cuda(go_cl, w_packed)
+    dx = _ndhwc_empty(desc.n, desc.cin, desc.d, desc.h, desc.w, dev, go_cl.dtype)
+    ws, nb = _workspace(desc, LEG_TDX, dev)
+    with torch.cuda.device(dev):
+        st = lib().r4c_tconv_dx(ctypes.byref(desc), _ptr(go_cl), _ptr(w_packed), _ptr(dx), _ptr(ws), nb,
+                                _stream(dev))
+    _check(st, "r4c_tconv_dx")
+    return dx
+
+
+def tconv_dw(desc: ConvDesc, x_cl: torch.Tensor, go_cl: torch.Tensor, want_db: bool):
+    dev = _require_cuda(x_cl, go_cl)
+    dw = torch.empty((desc.cin, desc.cout, 2, 2, 2), dtype=torch.float32, device=dev)
+    db = torch.empty((desc.cout,), dtype=torch.float32, device=dev) if want_db else None
+    ws, nb = _workspace(desc, LEG_TDW, dev)
+    with torch.cuda.device(dev):
+        st = lib().r4c_tconv_dw(ctypes.byref(desc), _ptr(x_cl), _ptr(go_cl), _ptr(dw), _ptr(db), _ptr(ws), nb,
+                                _stream(dev))
+    _check(st, "r4c_tconv_dw")
+    return dw, db
+
+
+def launch_count() -> int:
+    """Kernels launched by the native library so far in this process."""
+    return int(lib().r4c_launch_count())
+
+
+def device_error(device=None, clear: bool = True) -> int:
+    """Read (and clear) the kernels' device-side timeout flag."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    with torch.cuda.device(dev):
+        return int(lib().r4c_device_error(_stream(dev), 1 if clear else 0))

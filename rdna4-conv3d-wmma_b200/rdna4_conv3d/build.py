@@ -1,0 +1,49 @@
+"""Build ``libr4c_conv3d.so`` in-tree for sm_100a (``python -m rdna4_conv3d.build``).
+
+The library is plain nvcc output (no torch extension): the kernels and the
+C-ABI in ``csrc/`` compile to one shared object next to this file, where
+``_native`` loads it. Cross-compiles on a machine without a GPU.
+"""
+from __future__ import annotations
+
+import os
+import shutil
+import subprocess
+import sys
+
+PKG_DIR = os.path.dirname(os.path.abspath(__file__))
+SRC_DIR = os.path.join(os.path.dirname(PKG_DIR), "csrc")
+INC_DIR = os.path.join(os.path.dirname(os.path.dirname(PKG_DIR)), "include")
+OUT = os.path.join(PKG_DIR, "libr4c_conv3d.so")
+SOURCES = ["r4c_api.cu", "r4c_generic.cu", "r4c_tc.cu"]
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+
+
+def nvcc() -> str:
+    for cand in (shutil.which("nvcc"), "/usr/local/cuda/bin/nvcc"):
+        if cand and os.path.exists(cand):
+            return cand
+    raise RuntimeError("nvcc not found")
+
+
+def _newest(paths):
+    return max(os.path.getmtime(p) for p in paths)
+
+
+def build(force: bool = False, verbose: bool = False) -> str:
+    srcs = [os.path.join(SRC_DIR, s) for s in SOURCES]
+    deps = srcs + [os.path.join(SRC_DIR, f) for f in os.listdir(SRC_DIR) if f.endswith((".h", ".cuh"))]
+    deps.append(os.path.join(INC_DIR, "r4c_conv3d.h"))
+    if not force and os.path.exists(OUT) and os.path.getmtime(OUT) >= _newest(deps):
+        return OUT
+    cmd = [nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-shared",
+           "-diag-suppress", "177", "-I", INC_DIR, "-o", OUT + ".tmp", *srcs]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    subprocess.run(cmd, check=True)
+    os.replace(OUT + ".tmp", OUT)
+    return OUT
+
+
+if __name__ == "__main__":
+    print(build(force="--force" in sys.argv, verbose=True))

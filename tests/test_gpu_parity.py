@@ -1,0 +1,201 @@
+"""Kernel parity on a B200: every leg against the oracle, through the product path.
+
+Oracle: the reference's CPU path (stock PyTorch fp32 on CPU; oracle/oracle.py)
+fed the same bf16/fp16-rounded inputs, plus the golden vectors the reference's
+own Triton kernels produced (tests/golden). Tolerances are the north-star
+ones, written here:
+  forward and dX : max|out - ref| / max|ref| <= 2e-2
+  dW, db         : ||out - ref|| / ||ref||   <= 3e-2
+"""
+import glob
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from conftest import GOLDEN_DIR
+
+pytestmark = pytest.mark.gpu
+
+FWD_TOL = 2e-2
+DW_TOL = 3e-2
+
+# n, cin, cout, d, h, w, k, pad
+CONV_CASES = [
+    (2, 24, 24, 16, 32, 32, 3, 1),
+    (2, 5, 7, 9, 11, 13, 3, 1),        # reference test shapes
+    (2, 24, 1, 8, 16, 16, 1, 0),
+    (1, 24, 24, 8, 16, 16, 3, 1),
+    (1, 1, 24, 8, 16, 16, 3, 1),
+    (1, 16, 8, 6, 7, 9, 3, 0),         # pad 0 / pad 2
+    (1, 8, 16, 4, 5, 6, 3, 2),
+    (1, 24, 24, 5, 9, 11, 3, 0),
+    (1, 24, 24, 5, 9, 11, 3, 2),
+    (1, 16, 8, 4, 5, 6, 1, 1),         # k1 with padding
+    (1, 48, 48, 8, 16, 16, 3, 1),      # trunk channel counts, reduced volume
+    (1, 96, 96, 4, 8, 8, 3, 1),
+    (1, 192, 192, 4, 8, 8, 3, 1),
+    (1, 48, 24, 8, 16, 16, 1, 0),
+    (1, 96, 48, 4, 8, 8, 1, 0),
+    (1, 192, 96, 4, 8, 8, 1, 0),
+    (1, 8, 8, 3, 3, 3, 3, 1),          # one 8-channel chunk
+    (1, 40, 16, 4, 6, 10, 3, 1),       # five chunks (odd pairing)
+    (2, 24, 48, 3, 5, 130, 3, 1),      # W above 128
+    (1, 8, 8, 2, 2, 300, 3, 1),        # W split into two tiles
+    (1, 16, 200, 3, 4, 5, 3, 1),       # Cout not a multiple of 16
+    (1, 32, 256, 2, 4, 8, 3, 1),       # Cout = 256
+    (0, 24, 24, 4, 4, 4, 3, 1),        # empty batch
+]
+TCONV_CASES = [
+    (2, 16, 8, 3, 4, 5),
+    (1, 48, 24, 2, 4, 6),
+    (1, 192, 96, 2, 4, 4),
+    (1, 96, 48, 4, 4, 4),
+    (1, 5, 3, 2, 3, 4),
+    (0, 16, 8, 2, 2, 2),
+]
+
+
+def _cw():
+    import sys
+    return sys.modules["rdna4_conv3d.conv3d_wmma"]
+
+
+def _ids(cases):
+    return ["x".join(str(v) for v in c) for c in cases]
+
+
+def _inputs(n, cin, cout, d, h, w, k, pad, dtype, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(n, cin, d, h, w, generator=g).to(dtype)
+    wt = (torch.randn(cout, cin, k, k, k, generator=g) / (cin * k ** 3) ** 0.5).to(dtype)
+    b = torch.randn(cout, generator=g).to(dtype)
+    od, oh, ow = d + 2 * pad - (k - 1), h + 2 * pad - (k - 1), w + 2 * pad - (k - 1)
+    go = torch.randn(n, cout, od, oh, ow, generator=g).to(dtype)
+    return x, wt, b, go
+
+
+def _run_conv(x, wt, b, go, pad):
+    cw = _cw()
+    dev = "cuda"
+    xg, wg, bg, gg = (t.to(dev) for t in (x, wt, b, go))
+    y = cw._launch_fwd(xg, wg, bg, (pad,) * 3)
+    dx = cw._launch_dgrad(gg, wg, xg.shape, (pad,) * 3)
+    dw, db = cw._launch_wgrad(xg, gg, wg.shape, (pad,) * 3, True)
+    torch.cuda.synchronize()
+    return y.cpu(), dx.cpu(), dw.cpu(), db.cpu()
+
+
+@pytest.mark.parametrize("force", [0, 1], ids=["auto", "simt"])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16], ids=["bf16", "fp16"])
+@pytest.mark.parametrize("case", CONV_CASES, ids=_ids(CONV_CASES))
+def test_conv_legs_match_oracle(cuda_ready, case, dtype, force, monkeypatch):
+    n, cin, cout, d, h, w, k, pad = case
+    if force == 1 and cin * cout * d * h * w * k ** 3 > 40_000_000:
+        pytest.skip("SIMT path covered on the smaller shapes")
+    monkeypatch.setattr(_cw(), "_FORCE_KERNEL", force)
+    x, wt, b, go = _inputs(*case, dtype)
+    y, dx, dw, db = _run_conv(x, wt, b, go, pad)
+    assert y.shape == (n, cout, d + 2 * pad - (k - 1), h + 2 * pad - (k - 1), w + 2 * pad - (k - 1))
+    assert dx.shape == x.shape and dw.shape == wt.shape and dw.dtype == torch.float32
+    if n == 0:
+        assert float(dw.abs().sum()) == 0.0 and float(db.abs().sum()) == 0.0
+        return
+    yr = O.torch_conv_fwd(x, wt, b, pad)
+    dxr = O.torch_conv_dx(x.shape, wt, go, pad)
+    dwr = O.torch_conv_dw(x, go, wt.shape, pad)
+    dbr = go.float().sum(dim=(0, 2, 3, 4))
+    assert O.max_rel(y, yr) <= FWD_TOL
+    assert O.max_rel(dx, dxr) <= FWD_TOL
+    assert O.norm_rel(dw, dwr) <= DW_TOL
+    assert O.norm_rel(db, dbr) <= DW_TOL
+    # fp32 accumulation of identical inputs: far inside the stated bounds
+    assert O.norm_rel(dw, dwr) <= 1e-4
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16], ids=["bf16", "fp16"])
+@pytest.mark.parametrize("case", TCONV_CASES, ids=_ids(TCONV_CASES))
+def test_tconv_legs_match_oracle(cuda_ready, case, dtype):
+    n, cin, cout, d, h, w = case
+    cw = _cw()
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(n, cin, d, h, w, generator=g).to(dtype)
+    wt = (torch.randn(cin, cout, 2, 2, 2, generator=g) / cin ** 0.5).to(dtype)
+    b = torch.randn(cout, generator=g).to(dtype)
+    go = torch.randn(n, cout, 2 * d, 2 * h, 2 * w, generator=g).to(dtype)
+    xg, wg, bg, gg = (t.cuda() for t in (x, wt, b, go))
+    y = cw.transpose_k2s2_fwd(xg, wg, bg).cpu()
+    dx = cw.transpose_k2s2_dx(xg.shape, wg, gg).cpu()
+    dw, db = cw.transpose_k2s2_dw(xg, wg.shape, gg, True)
+    dw, db = dw.cpu(), db.cpu()
+    assert y.shape == (n, cout, 2 * d, 2 * h, 2 * w) and dx.shape == x.shape and dw.shape == wt.shape
+    if n == 0:
+        return
+    dxr, dwr = O.torch_tconv_grads(x, wt, go)
+    assert O.max_rel(y, O.torch_tconv_fwd(x, wt, b)) <= FWD_TOL
+    assert O.max_rel(dx, dxr) <= FWD_TOL
+    assert O.norm_rel(dw, dwr) <= 1e-4
+    assert O.norm_rel(db, go.float().sum(dim=(0, 2, 3, 4))) <= 1e-4
+
+
+GOLDEN = sorted(glob.glob(os.path.join(GOLDEN_DIR, "*.npz")))
+
+
+@pytest.mark.parametrize("path", GOLDEN, ids=[os.path.basename(p)[:-4] for p in GOLDEN])
+def test_matches_reference_golden(cuda_ready, path):
+    """fp16 kernels vs the reference's fp16 Triton outputs on identical inputs."""
+    z = np.load(path)
+    n, cin, cout, d, h, w, k, pad = (int(v) for v in z["meta"])
+    cw = _cw()
+    x, wt, b, go = (torch.from_numpy(z[key]).cuda() for key in ("x", "w", "b", "go"))
+    if k == 2:
+        y = cw.transpose_k2s2_fwd(x, wt, b)
+        dx = cw.transpose_k2s2_dx(x.shape, wt, go)
+        dw, _ = cw.transpose_k2s2_dw(x, wt.shape, go)
+    else:
+        y = cw._launch_fwd(x, wt, b, (pad,) * 3)
+        dx = cw._launch_dgrad(go, wt, x.shape, (pad,) * 3)
+        dw, _ = cw._launch_wgrad(x, go, wt.shape, (pad,) * 3, False)
+    assert O.max_rel(y.cpu(), torch.from_numpy(z["y"])) < 4e-3
+    assert O.norm_rel(dw.cpu(), torch.from_numpy(z["dw"])) < 2e-3
+    if "dx" in z.files:
+        assert O.max_rel(dx.cpu(), torch.from_numpy(z["dx"])) < 4e-3
+
+
+def test_small_cases_match_c_oracle(cuda_ready):
+    """The C restatement of the reference algorithm agrees with the kernels too."""
+    for case in [(1, 24, 24, 4, 6, 8, 3, 1), (1, 5, 7, 3, 4, 5, 3, 0), (1, 16, 8, 3, 4, 5, 1, 0)]:
+        n, cin, cout, d, h, w, k, pad = case
+        x, wt, b, go = _inputs(*case, torch.bfloat16, seed=3)
+        y, dx, dw, db = _run_conv(x, wt, b, go, pad)
+        assert O.max_rel(y, O.c_conv_fwd(x, wt, b, pad)) <= FWD_TOL
+        assert O.max_rel(dx, O.c_conv_dx(x.shape, wt, go, pad)) <= FWD_TOL
+        assert O.norm_rel(dw, O.c_conv_dw(x, go, wt.shape, pad)) <= 1e-4
+        assert O.norm_rel(db, O.c_bias_grad(go)) <= 1e-4
+
+
+def test_deterministic_dw(cuda_ready):
+    """Split-K partials are summed in a fixed order: bitwise-identical reruns."""
+    cw = _cw()
+    x, wt, b, go = _inputs(2, 24, 24, 16, 32, 32, 3, 1, torch.bfloat16)
+    xg, gg = x.cuda(), go.cuda()
+    a, da = cw._launch_wgrad(xg, gg, wt.shape, (1, 1, 1), True)
+    c, dc = cw._launch_wgrad(xg, gg, wt.shape, (1, 1, 1), True)
+    assert torch.equal(a, c) and torch.equal(da, dc)
+
+
+def test_kernel_families_used(cuda_ready):
+    """The tcgen05 family serves the trunk shapes (no silent SIMT routing)."""
+    cw = _cw()
+    for shape, cout, k in [((4, 24, 64, 128, 128), 24, 3), ((4, 48, 32, 64, 64), 48, 3),
+                           ((4, 96, 16, 32, 32), 96, 3), ((4, 192, 8, 16, 16), 192, 3),
+                           ((4, 48, 64, 128, 128), 24, 1)]:
+        fam = cw.conv3d_kernels(shape, cout, k, 1 if k == 3 else 0)
+        assert fam["fwd"] == "tcgen05" and fam["dx"] == "tcgen05", (shape, fam)
+
+
+def test_no_device_error_flag(cuda_ready):
+    from rdna4_conv3d import _native
+    assert _native.device_error() == 0

@@ -1,0 +1,88 @@
+"""The C-ABI library loads and exports every symbol include/*.h declares.
+
+CPU only: host-side entry points (plan, sizes, strerror, descriptor checks)
+are called; nothing launches a kernel.
+"""
+import ctypes
+import glob
+import os
+import re
+
+import torch
+
+from conftest import ROOT
+from rdna4_conv3d import _native
+
+HEADERS = glob.glob(os.path.join(ROOT, "include", "*.h"))
+
+
+def _declared():
+    names = set()
+    for h in HEADERS:
+        src = open(h).read()
+        src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+        names |= set(re.findall(r"\b(r4c_[a-z0-9_]+)\s*\(", src))
+    return names
+
+
+def test_header_declares_entry_points():
+    names = _declared()
+    for n in ("r4c_conv3d_fwd", "r4c_conv3d_dx", "r4c_conv3d_dw", "r4c_tconv_fwd", "r4c_tconv_dx",
+              "r4c_tconv_dw", "r4c_pack_weight", "r4c_workspace_size", "r4c_strerror"):
+        assert n in names
+
+
+def test_every_declared_symbol_is_exported():
+    lib = ctypes.CDLL(_native.library_path())
+    missing = [n for n in sorted(_declared()) if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_strerror_and_version():
+    assert _native.strerror(0) == "ok"
+    assert "workspace" in _native.strerror(-3)
+    assert _native.lib().r4c_version() >= 1
+
+
+def _d(n=2, cin=24, cout=24, d=16, h=32, w=32, k=3, p=1, dt=torch.bfloat16, force=0):
+    return _native.make_desc(n, d, h, w, cin, cout, k, (p, p, p), dt, force)
+
+
+def test_plan_families():
+    assert _native.plan_kernel(_d(), _native.LEG_FWD) == _native.KERNEL_TC
+    assert _native.plan_kernel(_d(), _native.LEG_DX) == _native.KERNEL_TC
+    # odd channel counts go to the SIMT kernels
+    assert _native.plan_kernel(_d(cin=5, cout=7), _native.LEG_FWD) == _native.KERNEL_GENERIC
+    # the generic family can be forced
+    assert _native.plan_kernel(_d(force=1), _native.LEG_FWD) == _native.KERNEL_GENERIC
+    assert "tcgen05" in _native.describe_plan(_d(), _native.LEG_FWD)
+
+
+def test_descriptor_validation():
+    assert _native.plan_kernel(_d(k=5), _native.LEG_FWD) == -2       # unsupported
+    assert _native.plan_kernel(_d(k=3), _native.LEG_TFWD) == -2      # tconv needs k=2
+    assert _native.plan_kernel(_d(p=-1), _native.LEG_FWD) == -1      # negative pad
+    assert _native.plan_kernel(_d(cin=0), _native.LEG_FWD) == -1
+    assert _native.plan_kernel(_d(d=1, p=0), _native.LEG_FWD) == -1  # empty output
+    bad = _d()
+    bad.dtype = 7
+    assert _native.plan_kernel(bad, _native.LEG_FWD) == -1
+
+
+def test_workspace_sizes():
+    ws = _native.workspace_bytes(_d(), _native.LEG_DW)
+    assert ws > 0 and ws % 256 == 0
+    assert _native.workspace_bytes(_d(), _native.LEG_FWD) == 0
+    t = _native.make_desc(1, 4, 4, 4, 16, 8, 2, (0, 0, 0), torch.bfloat16)
+    assert _native.workspace_bytes(t, _native.LEG_TDW) > 0
+
+
+def test_packed_sizes():
+    assert _native.packed_weight_bytes(_d(cin=5, cout=7), _native.LEG_FWD) == 5 * 7 * 27 * 2
+    assert _native.packed_weight_bytes(_d(), _native.LEG_FWD) >= 24 * 24 * 27 * 2
+
+
+def test_null_descriptor_rejected():
+    lib = _native.lib()
+    assert lib.r4c_plan_kernel(None, 0) == -1
+    assert lib.r4c_conv3d_fwd(None, None, None, None, None, None, 0, None) == -1

@@ -261,22 +261,26 @@ class Layer:
         self.flops = layer_flops(self.cin, self.cout, self.spatial, self.k)
 
 
-def run_step(layers, reducer, ev=None):
+def run_step(layers, reducer, ev=None, legs=("fwd", "dw", "dx")):
     """fwd, dW(+db) and dX of every layer through the package's launch path."""
     cw = sys.modules["rdna4_conv3d.conv3d_wmma"]
     p3 = lambda p: (p, p, p)  # noqa: E731
     outs = []
     for i, L in enumerate(layers):
+        y = dw = db = dx = handle = None
         if ev is not None:
             ev[i][0].record()
-        y = cw._launch_fwd(L.x, L.w, L.b, p3(L.pad))
+        if "fwd" in legs:
+            y = cw._launch_fwd(L.x, L.w, L.b, p3(L.pad))
         if ev is not None:
             ev[i][1].record()
-        dw, db = cw._launch_wgrad(L.x, L.go, L.w.shape, p3(L.pad), True)
-        handle = reducer.reduce_async([dw, db]) if reducer is not None else None
+        if "dw" in legs:
+            dw, db = cw._launch_wgrad(L.x, L.go, L.w.shape, p3(L.pad), True)
+            handle = reducer.reduce_async([dw, db]) if reducer is not None else None
         if ev is not None:
             ev[i][2].record()
-        dx = cw._launch_dgrad(L.go, L.w, L.x.shape, p3(L.pad))
+        if "dx" in legs:
+            dx = cw._launch_dgrad(L.go, L.w, L.x.shape, p3(L.pad))
         if ev is not None:
             ev[i][3].record()
         if handle is not None:
@@ -336,6 +340,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--only", default=None, help="run one trunk layer, e.g. 'k3 24->24' (profiling)")
+    ap.add_argument("--legs", default="fwd,dw,dx", help="comma list of legs to run (profiling)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -348,15 +354,19 @@ def main():
     from rdna4_conv3d.conv3d_wmma import conv3d_kernels
     _native.lib()
 
-    layers = [Layer(spec, dev, seed=1000 * rank + i) for i, spec in enumerate(TRUNK)]
+    specs = [t for t in TRUNK if args.only is None or t[0] == args.only]
+    if not specs:
+        raise SystemExit(f"unknown layer {args.only!r}; choose from {[t[0] for t in TRUNK]}")
+    legs = tuple(args.legs.split(","))
+    layers = [Layer(spec, dev, seed=1000 * rank + i) for i, spec in enumerate(specs)]
     reducer = None
     if world > 1:
         from rdna4_conv3d.distributed import GradAllReducer
         reducer = GradAllReducer()
 
-    step_flops = sum(3 * L.flops for L in layers)
+    step_flops = sum(len(legs) * L.flops for L in layers)
     for _ in range(args.warmup):
-        run_step(layers, reducer)
+        run_step(layers, reducer, legs=legs)
     torch.cuda.synchronize()
 
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in layers]
@@ -370,7 +380,7 @@ def main():
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record()
     for _ in range(args.steps):
-        run_step(layers, reducer, ev)
+        run_step(layers, reducer, ev, legs=legs)
         torch.cuda.synchronize()
         for i in range(len(layers)):
             for j in range(3):
@@ -393,6 +403,8 @@ def main():
         fam = conv3d_kernels((BATCH, L.cin) + L.spatial, L.cout, L.k, L.pad)
         row = {"layer": L.name, "gflop_per_leg": round(L.flops / 1e9, 3)}
         for j, leg in enumerate(("fwd", "dw", "dx")):
+            if leg not in legs:
+                continue
             ms = lm[j] / args.steps
             row[leg + "_us"] = round(ms * 1e3, 2)
             row[leg + "_tflops"] = round(L.flops / (ms / 1e3) / 1e12, 2) if ms > 0 else None
@@ -418,7 +430,7 @@ def main():
     roof["peak_src"] = f"{peaks['src']} (sustained bf16 / copy bandwidth)"
 
     e2e = None
-    if not args.no_e2e:
+    if not args.no_e2e and args.only is None and len(legs) == 3:
         host = []
         for L in layers:
             host.append((L.x.cpu().contiguous().pin_memory(), L.go.cpu().contiguous().pin_memory(), None))
@@ -431,7 +443,7 @@ def main():
                        "back inside the timed region"}
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.only is None:
         cpu = cpu_baseline(TRUNK)
 
     if rank == 0:

@@ -110,8 +110,9 @@ def test_tconv_module(cuda_ready):
     assert O.max_rel(xg.grad.float().cpu(), xr.grad) <= 2e-2
     assert O.norm_rel(mod.weight.grad.cpu(), ref.weight.grad) <= 3e-2
     # output_size that disagrees with 2x falls back to the stock module
-    out = mod(xg.detach(), output_size=(7, 9, 11))
+    out = mod(x.cuda(), output_size=(7, 9, 11))
     assert out.shape[-3:] == (7, 9, 11)
+    torch.testing.assert_close(out, ref.cuda()(x.cuda(), output_size=(7, 9, 11)))
 
 
 def _block(cin, cout, conv):

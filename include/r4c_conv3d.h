@@ -179,6 +179,31 @@ int r4c_tconv_dw(const r4c_conv_desc* desc, const void* x, const void* go,
                  float* dw, float* db, void* workspace, size_t ws_bytes,
                  r4c_stream_t stream);
 
+/*
+ * Conv3d weight and bias gradient without any allocation. No counterpart in
+ * the reference: it exists for callers that cannot allocate device memory,
+ * e.g. a plugin or custom op running inside another framework that owns the
+ * whole device memory pool (its guests may not call cudaMalloc, which would
+ * bypass the pool and can synchronize the device), or code on a latency path
+ * that must make no allocation call at all.
+ *
+ * Same inputs, outputs and results as r4c_conv3d_dw(), but the split-K
+ * scratch lives in a fixed device array inside this library
+ * (R4C_NOALLOC_SCRATCH_BYTES, present on every GPU that loads the library
+ * until the process exits) instead of a caller workspace. Descriptors whose
+ * r4c_workspace_size(desc, R4C_LEG_DW) exceeds that size are rejected with
+ * R4C_ERR_TOO_LARGE. The first call on a device looks up the array's device
+ * address (cudaGetSymbolAddress) with that device current; make that first
+ * call before any stream capture. All calls share the one array: calls whose
+ * work overlaps on the GPU (different streams, or different host threads)
+ * race on it and must be serialized by the caller. The kernels write every
+ * scratch element they read, so stale contents from a previous call are
+ * never used.
+ */
+#define R4C_NOALLOC_SCRATCH_BYTES ((size_t)32 << 20)
+int r4c_conv3d_dw_noalloc(const r4c_conv_desc* desc, const void* x, const void* go,
+                          float* dw, float* db, r4c_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -106,14 +106,64 @@ WgradLayout wgrad_layout(const Geom& g, bool tconv) {
   return L;
 }
 
+// Channel padding: TMA needs the innermost stride (Cin * 2 bytes) to be a
+// multiple of 16, so forward and dW with Cin not a multiple of 8 first copy
+// the activation into caller workspace with Cin rounded up to 8 (zeros in the
+// extra channels; their weights are packed as zeros).
+int cin_eff(const Geom& g) { return g.cin % 8 ? (g.cin + 7) / 8 * 8 : g.cin; }
+bool needs_cpad(const Geom& g) { return g.cin % 8 != 0; }
+size_t cpad_bytes(const Geom& g) {
+  return needs_cpad(g) ? align_up((size_t)g.in_vox() * cin_eff(g) * 2, 256) : 0;
+}
+
+template <typename T>
+__global__ void cpad_kernel(const T* __restrict__ x, T* __restrict__ xp, int64_t vox, int cin, int cinp) {
+  const int chunks = cinp / 8;
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= vox * chunks) return;
+  const int64_t v = i / chunks;
+  const int c0 = (int)(i - v * chunks) * 8;
+  __align__(16) T tmp[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) tmp[j] = (c0 + j < cin) ? x[v * cin + c0 + j] : Elem<T>::from_f(0.f);
+  *reinterpret_cast<uint4*>(xp + v * cinp + c0) = *reinterpret_cast<const uint4*>(tmp);
+}
+
+cudaError_t launch_cpad(const void* x, void* xp, const Geom& g, int dtype, cudaStream_t st) {
+  const int cinp = cin_eff(g);
+  const int64_t n = g.in_vox() * (cinp / 8);
+  const unsigned blocks = (unsigned)((n + 255) / 256);
+  if (n == 0) return cudaSuccess;
+  if (dtype == R4C_BF16)
+    cpad_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x),
+                                                       static_cast<__nv_bfloat16*>(xp), g.in_vox(), g.cin, cinp);
+  else
+    cpad_kernel<__half><<<blocks, 256, 0, st>>>(static_cast<const __half*>(x), static_cast<__half*>(xp), g.in_vox(),
+                                                g.cin, cinp);
+  note_launches(1);
+  return cudaGetLastError();
+}
+
 bool use_tc(const r4c_conv_desc* ds, int leg, const Geom& g, tc::ConvPlan* pl) {
   if (ds->force_kernel == R4C_KERNEL_GENERIC) return false;
   if (leg == R4C_LEG_FWD)
-    return tc::plan_conv(g.n, g.d, g.h, g.w, g.cin, g.cout, g.k, g.pd, g.ph, g.pw, pl);
+    return tc::plan_conv(g.n, g.d, g.h, g.w, cin_eff(g), g.cout, g.k, g.pd, g.ph, g.pw, pl);
   if (leg == R4C_LEG_DX)
     return tc::plan_conv(g.n, g.od, g.oh, g.ow, g.cout, g.cin, g.k, g.k - 1 - g.pd,
                          g.k - 1 - g.ph, g.k - 1 - g.pw, pl);
+  if (leg == R4C_LEG_DW)
+    return tc::dw_supported(g.n, g.d, g.h, g.w, cin_eff(g), g.cout, g.k, g.pd, g.ph, g.pw);
   return false;
+}
+
+// Workspace of the tcgen05 dW: its split partials plus the generic db
+// partials (used when the kernel cannot fold db into its spare rows).
+size_t tc_dw_ws(const Geom& g, size_t* part_bytes) {
+  size_t a = align_up(tc::dw_workspace(g.n, g.d, g.h, g.w, cin_eff(g), g.cout, g.k, g.pd, g.ph, g.pw), 256);
+  int Sdb; int64_t ch;
+  generic::db_split(g.out_vox(), &Sdb, &ch);
+  if (part_bytes) *part_bytes = a;
+  return a + align_up((size_t)Sdb * g.cout * sizeof(float), 256);
 }
 
 }  // namespace
@@ -155,7 +205,11 @@ int r4c_describe_plan(const r4c_conv_desc* desc, int leg, char* buf, size_t len)
     snprintf(tmp, sizeof(tmp), "invalid: %s", r4c_strerror(st));
   } else {
     tc::ConvPlan pl;
-    if (use_tc(desc, leg, g, &pl)) {
+    if (leg == R4C_LEG_DW && use_tc(desc, leg, g, &pl)) {
+      tc::dw_describe(g.n, g.d, g.h, g.w, cin_eff(g), g.cout, g.k, g.pd, g.ph, g.pw, tmp, sizeof(tmp));
+      if (needs_cpad(g)) strncat(tmp, " (input channels padded to a multiple of 8)", sizeof(tmp) - strlen(tmp) - 1);
+      st = R4C_KERNEL_TC;
+    } else if (use_tc(desc, leg, g, &pl)) {
       snprintf(tmp, sizeof(tmp),
                "tcgen05 conv: cin=%d cout=%d(npad %d) k=%d tile=%dx%d pitch=%dx%d G=%d groups=%d "
                "steps=%d mtiles=%d sets=%d stages=%d stage=%dB wres=%d smem=%dB tmem=%d units=%lld grid=%d "
@@ -188,6 +242,14 @@ size_t r4c_packed_weight_bytes(const r4c_conv_desc* desc, int leg) {
 size_t r4c_workspace_size(const r4c_conv_desc* desc, int leg) {
   Geom g;
   if (check_desc(desc, leg, &g) != R4C_OK) return 0;
+  if (leg == R4C_LEG_DW) {
+    tc::ConvPlan pl;
+    if (use_tc(desc, leg, g, &pl)) return cpad_bytes(g) + tc_dw_ws(g, nullptr);
+  }
+  if (leg == R4C_LEG_FWD) {
+    tc::ConvPlan pl;
+    if (use_tc(desc, leg, g, &pl)) return cpad_bytes(g);
+  }
   if (leg == R4C_LEG_DW || leg == R4C_LEG_TDW) {
     WgradLayout L = wgrad_layout(g, leg == R4C_LEG_TDW);
     return L.part_bytes + L.db_bytes;
@@ -208,8 +270,8 @@ int r4c_pack_weight(const r4c_conv_desc* desc, int leg, const void* w_src, int s
   tc::ConvPlan pl;
   if (use_tc(desc, leg, g, &pl)) {
     if ((reinterpret_cast<uintptr_t>(w_packed) & 15) != 0) return R4C_ERR_ALIGN;
-    return cuda_status(tc::pack_weight(pl, leg == R4C_LEG_DX, w_src, src_dtype, w_packed,
-                                       desc->dtype, s));
+    return cuda_status(tc::pack_weight(pl, leg == R4C_LEG_DX, leg == R4C_LEG_DX ? pl.cin : g.cin, w_src,
+                                       src_dtype, w_packed, desc->dtype, s));
   }
   int taps = (leg == R4C_LEG_TFWD || leg == R4C_LEG_TDX) ? 8 : g.k * g.k * g.k;
   int64_t total = (int64_t)g.cin * g.cout * taps;
@@ -227,7 +289,6 @@ int r4c_pack_weight(const r4c_conv_desc* desc, int leg, const void* w_src, int s
 int r4c_conv3d_fwd(const r4c_conv_desc* desc, const void* x, const void* w_packed,
                    const void* bias, void* y, void* workspace, size_t ws_bytes,
                    r4c_stream_t stream) {
-  (void)workspace; (void)ws_bytes;
   Geom g;
   int st = check_desc(desc, R4C_LEG_FWD, &g);
   if (st != R4C_OK) return st;
@@ -235,8 +296,15 @@ int r4c_conv3d_fwd(const r4c_conv_desc* desc, const void* x, const void* w_packe
   if (!x || !w_packed || !y) return R4C_ERR_INVALID;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   tc::ConvPlan pl;
-  if (use_tc(desc, R4C_LEG_FWD, g, &pl))
-    return tc::launch_conv(pl, x, w_packed, bias, y, desc->dtype, s);
+  if (use_tc(desc, R4C_LEG_FWD, g, &pl)) {
+    const void* xin = x;
+    if (needs_cpad(g)) {
+      if (!workspace || ws_bytes < cpad_bytes(g)) return R4C_ERR_WORKSPACE;
+      if (launch_cpad(x, workspace, g, desc->dtype, s) != cudaSuccess) return R4C_ERR_CUDA;
+      xin = workspace;
+    }
+    return tc::launch_conv(pl, xin, w_packed, bias, y, desc->dtype, s);
+  }
   generic::FwdParams p{};
   p.a = x; p.b = w_packed; p.bias = bias; p.out = y;
   p.M = g.out_vox(); p.N = g.cout; p.K = g.k * g.k * g.k * g.cin;
@@ -276,10 +344,34 @@ int r4c_conv3d_dw(const r4c_conv_desc* desc, const void* x, const void* go, floa
   if (st != R4C_OK) return st;
   if (!dw) return R4C_ERR_INVALID;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int taps = g.k * g.k * g.k;
+  tc::ConvPlan tcp;
+  if (g.out_vox() > 0 && use_tc(desc, R4C_LEG_DW, g, &tcp)) {
+    size_t part_bytes = 0;
+    const size_t xpad = cpad_bytes(g);
+    const size_t need = xpad + tc_dw_ws(g, &part_bytes);
+    if (ws_bytes < need || !workspace) return R4C_ERR_WORKSPACE;
+    if (!x || !go) return R4C_ERR_INVALID;
+    const void* xin = x;
+    char* wsb = static_cast<char*>(workspace);
+    if (xpad) {
+      if (launch_cpad(x, workspace, g, desc->dtype, s) != cudaSuccess) return R4C_ERR_CUDA;
+      xin = workspace;
+      wsb += xpad;
+    }
+    bool db_done = false;
+    int rc = tc::launch_dw(g.n, g.d, g.h, g.w, cin_eff(g), g.cin, g.cout, g.k, g.pd, g.ph, g.pw, xin, go, dw, db,
+                           wsb, part_bytes, desc->dtype, s, &db_done);
+    if (rc != R4C_OK) return rc;
+    if (db && !db_done) {
+      float* part = reinterpret_cast<float*>(wsb + part_bytes);
+      return cuda_status(generic::launch_db(go, g.out_vox(), g.cout, desc->dtype, part, db, s));
+    }
+    return R4C_OK;
+  }
   WgradLayout L = wgrad_layout(g, false);
   if (ws_bytes < L.part_bytes + L.db_bytes || (!workspace && L.part_bytes + L.db_bytes))
     return R4C_ERR_WORKSPACE;
-  const int taps = g.k * g.k * g.k;
   if (g.out_vox() == 0) {
     cudaError_t e = cudaMemsetAsync(dw, 0, sizeof(float) * g.cout * g.cin * taps, s);
     if (e == cudaSuccess && db) e = cudaMemsetAsync(db, 0, sizeof(float) * g.cout, s);

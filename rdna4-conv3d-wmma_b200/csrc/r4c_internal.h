@@ -77,12 +77,25 @@ struct ConvPlan {
 bool plan_conv(int n, int d, int h, int w, int cin, int cout, int ks, int pd, int ph, int pw,
                ConvPlan* pl);
 size_t packed_bytes(const ConvPlan& pl);
-// Packs a logical weight W[co][tap][ci] (fp32 view given by a functor on host is
-// not used; the device pack kernel reads the PyTorch layout directly).
-cudaError_t pack_weight(const ConvPlan& pl, bool flip_for_dx, const void* w_src, int src_dtype,
-                        void* w_packed, int dtype, cudaStream_t st);
+// Packs the PyTorch-layout weight into the K-step blocks of the plan; input
+// channels at or above cin_real (channel padding) get zero weights.
+cudaError_t pack_weight(const ConvPlan& pl, bool flip_for_dx, int cin_real, const void* w_src,
+                        int src_dtype, void* w_packed, int dtype, cudaStream_t st);
 int launch_conv(const ConvPlan& pl, const void* x, const void* w_packed, const void* bias,
                 void* y, int dtype, cudaStream_t st);
+
+// Device address of the kernels' bounded-wait error flag (current device).
+int* device_error_flag();
+
+// tcgen05 weight gradient (r4c_tc_dw.cu). Geometry is the layer's: input
+// dims, Cin, Cout, k and pads. db is produced in-kernel when *db_done is set.
+bool dw_supported(int n, int d, int h, int w, int cin, int cout, int ks, int pd, int ph, int pw);
+size_t dw_workspace(int n, int d, int h, int w, int cin, int cout, int ks, int pd, int ph, int pw);
+int dw_describe(int n, int d, int h, int w, int cin, int cout, int ks, int pd, int ph, int pw, char* buf,
+                size_t len);
+int launch_dw(int n, int d, int h, int w, int cin, int cin_real, int cout, int ks, int pd, int ph, int pw,
+              const void* x, const void* go, float* dw, float* db, void* ws, size_t ws_bytes, int dtype,
+              cudaStream_t st, bool* db_done);
 
 }  // namespace tc
 

@@ -233,6 +233,7 @@ size_t packed_bytes(const ConvPlan& P) {
 // ---------------------------------------------------------------------------
 struct PackArgs {
   int ks, G, ngroups, nsteps, npad, cin, cout;  // cin/cout of the conv being run
+  int cin_real;                                  // input channels present in the source (<= cin)
   int flip;                                      // dX: W'[o][i][t] = W[i][o][T-1-t]
   int src_cin;                                   // channel count of the OIDHW source's dim 1
   signed char kh[kMaxSteps][2], kw[kMaxSteps][2], c[kMaxSteps][2], zero[kMaxSteps][2];
@@ -253,12 +254,12 @@ __global__ void pack_tc_kernel(const void* __restrict__ src, int sdt, TO* __rest
   float v = 0.f;
   if (!a.zero[j][half] && nrow < a.cout) {
     int ci = (g * a.G + a.c[j][half]) * 8 + e;
-    if (ci < a.cin) {
+    if (ci < a.cin_real) {
       int T = a.ks * a.ks * a.ks;
       int tap = (kd * a.ks + a.kh[j][half]) * a.ks + a.kw[j][half];
       long long s;
       if (!a.flip) {
-        s = ((long long)nrow * a.cin + ci) * T + tap;  // W[co=nrow][ci][tap]
+        s = ((long long)nrow * a.src_cin + ci) * T + tap;  // W[co=nrow][ci][tap]
       } else {
         s = ((long long)ci * a.src_cin + nrow) * T + (T - 1 - tap);  // W[co=ci][ci'=nrow][T-1-tap]
       }
@@ -270,14 +271,17 @@ __global__ void pack_tc_kernel(const void* __restrict__ src, int sdt, TO* __rest
   dst[i] = Elem<TO>::from_f(v);
 }
 
-cudaError_t pack_weight(const ConvPlan& P, bool flip, const void* w_src, int src_dtype, void* w_packed,
-                        int dtype, cudaStream_t st) {
+cudaError_t pack_weight(const ConvPlan& P, bool flip, int cin_real, const void* w_src, int src_dtype,
+                        void* w_packed, int dtype, cudaStream_t st) {
   std::vector<Step> steps;
   build_steps(P.ks, P.G, P.pitch_w, P.cpb, steps);
   PackArgs a{};
   a.ks = P.ks; a.G = P.G; a.ngroups = P.ngroups; a.nsteps = (int)steps.size();
   a.npad = P.npad; a.cin = P.cin; a.cout = P.cout; a.flip = flip ? 1 : 0;
-  a.src_cin = P.cout;  // for dX the OIDHW source has dim1 = Cin_layer = cout of this conv
+  a.cin_real = cin_real;
+  // OIDHW source dim 1: the real Cin for the forward weight; for dX (flipped)
+  // it is Cin of the layer, i.e. this conv's output channels.
+  a.src_cin = flip ? P.cout : cin_real;
   for (int j = 0; j < a.nsteps; ++j)
     for (int hf = 0; hf < 2; ++hf) {
       a.kh[j][hf] = (signed char)steps[j].h[hf].kh;
@@ -479,14 +483,20 @@ __global__ void __launch_bounds__(kThreads, 1) tc_conv_kernel(const __grid_const
                 a.wres ? smem_u32(wres_smem + (size_t)(kd * a.ngroups + g) * a.b_bytes)
                        : smem_u32(stage0 + (size_t)stage * a.stage_bytes + a.a_bytes);
             const bool first_stage = (kd == 0 && g == 0);
+            // Descriptors: one build per K step, 64-bit adds for the M tiles
+            // (2048 B = 128 descriptor units apart) and K steps of B.
+            const uint64_t bdesc0 = smem_desc(sB, (uint32_t)(a.npad * 16), 128);
+            const uint64_t bstep = (uint64_t)((2 * a.npad * 16) >> 4);
             for (int j = 0; j < a.nsteps; ++j) {
-              const uint64_t bdesc = smem_desc(sB + (uint32_t)(j * 2 * a.npad * 16), (uint32_t)(a.npad * 16), 128);
-              const uint32_t abase = (uint32_t)((int)sA + a.a_off[j]);
-              const uint32_t lbo = (uint32_t)a.lbo[j];
+              const uint64_t bdesc = bdesc0 + (uint64_t)j * bstep;
+              const uint64_t adesc = smem_desc((uint32_t)((int)sA + a.a_off[j]), (uint32_t)a.lbo[j], 128);
               const uint32_t accum = (first_stage && j == 0) ? 0u : 1u;
+              uint32_t d = dbase;
+              uint64_t ad = adesc;
               for (int t = 0; t < a.mtiles; ++t) {
-                const uint64_t adesc = smem_desc(abase + (uint32_t)(t * 2048), lbo, 128);
-                mma_f16_ss(dbase + (uint32_t)(t * a.npad), adesc, bdesc, a.idesc, accum);
+                mma_f16_ss(d, ad, bdesc, a.idesc, accum);
+                d += (uint32_t)a.npad;
+                ad += 128;
               }
             }
             mma_commit(&empty[stage]);
@@ -642,6 +652,27 @@ int launch_conv(const ConvPlan& P, const void* x, const void* w_packed, const vo
   return e == cudaSuccess ? R4C_OK : R4C_ERR_CUDA;
 }
 
+}  // namespace tc
+}  // namespace r4c
+
+namespace r4c {
+namespace tc {
+// Device address of the error flag for the current device, for kernels in
+// other translation units (device symbols are per translation unit without
+// relocatable device code).
+int* device_error_flag() {
+  static int* ptrs[64] = {nullptr};
+  static std::mutex mu;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lk(mu);
+  if (!ptrs[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_r4c_dev_error) != cudaSuccess) return nullptr;
+    ptrs[dev] = static_cast<int*>(p);
+  }
+  return ptrs[dev];
+}
 }  // namespace tc
 }  // namespace r4c
 

@@ -1,0 +1,576 @@
+// r4c_tc_dw.cu — tcgen05 + TMA weight (and bias) gradient of a stride-1
+// Conv3d (k = 1 or 3), split-K over output rows with a fixed-order reduce.
+//
+// Reference counterpart: _wgrad_kernel + _launch_wgrad + partial.sum(0) and
+// the separate db reduction (src/rdna4_conv3d/conv3d_wmma.py:543-634,
+// 1182-1214, 1318). The reference keeps taps in the GEMM's N dimension
+// (M = Cout, N = k^3*Cin, K = voxels) with masked gathers; here:
+//
+//  * GEMM per kw: D[(c, kd, kh, ci8), co] += X[v + (kd, kh, kw)][c*8+ci8] *
+//    dY[v][co] over the output positions v of one output row (K = 16
+//    positions per MMA). Both operands are MN-major in shared memory.
+//  * A (M rows): for one output row (n, z, y) and each 8-channel chunk c, ONE
+//    TMA box (8 ch x pitch_w x k x k) loads the k x k input rows
+//    (z+kd-pad, y+kh-pad) as a chunk plane [kd][kh][w]. The M groups
+//    (c, kd, kh) are then k*k*C8 consecutive row blocks at a single stride
+//    (pitch_w * 16 B): one descriptor covers 16 groups = one M tile. kw is a
+//    16-byte shift of the start address.
+//  * B (N columns): the dY row, one TMA box per 8-channel chunk.
+//  * db: the group right after the last real one holds bf16 ones, so its
+//    accumulator rows (junk rows otherwise) are sum_v dY[v][co].
+//  * Each CTA owns one task (a range of M tiles, of N, of kw) for one split of
+//    the output rows; fp32 partials go to the caller's workspace and a second
+//    kernel sums them in split order into OIDHW dW and db (deterministic).
+//
+// Warp roles (192 threads): warp 0 TMA producer, warp 1 MMA issuer + TMEM
+// owner, warps 2-5 epilogue (TMEM lane quarter = warp % 4). All waits are
+// bounded (1 s), like r4c_tc.cu.
+#include <cuda.h>
+
+#include <stdio.h>
+#include <string.h>
+
+#include <algorithm>
+#include <mutex>
+#include <vector>
+
+#include "r4c_internal.h"
+#include "r4c_sm100.cuh"
+
+namespace r4c {
+namespace tcdw {
+
+using namespace r4c::sm100;
+
+constexpr int kThreads = 192;
+constexpr int kSmemMax = 232448;
+constexpr int kHeader = 1024;
+constexpr int kMaxStages = 6;
+
+struct alignas(64) DwArgs {
+  CUtensorMap tx;   // x:  dims (cin, w, h, d, n), box (8, pitch_w, k, k, 1)
+  CUtensorMap tg;   // dy: dims (cout, ow, oh, od, n), box (8, kpad, 1, 1, 1)
+  float* part;      // [S][cout][cin][k^3] fp32
+  float* dbpart;    // [S][cout] fp32 (nullptr when db is not produced here)
+  int* err;         // device error flag (r4c_device_error)
+  int od, oh, ow, cin, cout, ks, pd, ph, pw;
+  int c8, pitch_w, kpad, nwt, wt;
+  int mt0, mtn, n0, nn, kw0, kwn;   // task ranges (M tiles, N columns, kw)
+  int c_lo, c_hi;                    // chunks loaded for the task
+  int ones_group;                    // absolute group index of the ones group (or -1)
+  int a_bytes, g_bytes, stage_bytes, stages;
+  int tmem_cols;
+  long long rows;                    // output rows * w-tiles
+  long long rows_per_split;
+  int ntasks;
+  uint32_t idesc;
+};
+
+struct Task {
+  int mt0, mtn, n0, nn, kw0, kwn;
+};
+
+struct DwPlan {
+  bool ok;
+  int n, d, h, w, od, oh, ow, cin, cout, ks, pd, ph, pw;
+  int c8, groups, mtiles, pitch_w, kpad, wt, nwt;
+  int mtn, nn, kwn;  // task shape
+  std::vector<Task> tasks;
+  int S;
+  long long rows, rows_per_split;
+  int stages, stage_bytes, smem_bytes, tmem_cols;
+  bool db_in_kernel;
+  double est;
+};
+
+static int round_up(int v, int a) { return (v + a - 1) / a * a; }
+
+static int num_sms() {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (!cached[dev]) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) v = 148;
+    cached[dev] = v;
+  }
+  return cached[dev];
+}
+
+// Chunks [c_lo, c_hi] that the groups of M tiles [mt0, mt0+mtn) touch.
+static void chunk_range(int mt0, int mtn, int k2, int c8, int* lo, int* hi) {
+  int g0 = 16 * mt0, g1 = 16 * (mt0 + mtn) - 1;
+  *lo = std::min(g0 / k2, c8 - 1);
+  *hi = std::min(g1 / k2, c8 - 1);
+}
+
+static bool plan_dw(int n, int d, int h, int w, int cin, int cout, int ks, int pd, int ph, int pw, DwPlan* out) {
+  DwPlan P{};
+  P.ok = false;
+  if (ks != 1 && ks != 3) return false;
+  if (cin % 8 || cout % 8 || cin <= 0 || cout <= 0) return false;
+  if (n <= 0 || d <= 0 || h <= 0 || w <= 0) return false;
+  if (pd < -8 || pd > 8 || ph < -8 || ph > 8 || pw < -8 || pw > 8) return false;
+  P.n = n; P.d = d; P.h = h; P.w = w; P.cin = cin; P.cout = cout; P.ks = ks;
+  P.pd = pd; P.ph = ph; P.pw = pw;
+  P.od = d + 2 * pd - (ks - 1); P.oh = h + 2 * ph - (ks - 1); P.ow = w + 2 * pw - (ks - 1);
+  if (P.od <= 0 || P.oh <= 0 || P.ow <= 0) return false;
+  const int k2 = ks * ks;
+  P.c8 = cin / 8;
+  P.groups = k2 * P.c8;
+  // ones group lives right after the real groups; it needs a spare row block
+  // in the last M tile.
+  P.db_in_kernel = (P.groups % 16) != 0;
+  P.mtiles = (P.groups + (P.db_in_kernel ? 1 : 0) + 15) / 16;
+  // W tiles: K positions per row must be a multiple of 16 except the last tile
+  // (whose tail reads dY out of bounds = zeros), and the x box <= 256 wide.
+  int wt = P.ow;
+  while (round_up(wt, 16) + 8 > 256) wt = round_up((wt + 1) / 2, 16);
+  P.wt = wt;
+  P.nwt = (P.ow + wt - 1) / wt;
+  P.kpad = round_up(wt, 16);
+  P.pitch_w = round_up(P.kpad + ks - 1, 8);
+  P.rows = (long long)n * P.od * P.oh * P.nwt;
+  const int sms = num_sms();
+
+  // Task shape: largest N split and M-tile group that fits TMEM (512 cols)
+  // with all kw in one task when possible.
+  double best = 1e300;
+  for (int kwn : {ks, 1}) {
+    if (ks % kwn) continue;
+    for (int nn = cout; nn >= 8; nn -= 8) {
+      if (cout % nn) continue;
+      int npad = round_up(nn, 16);
+      if (npad > 256) continue;
+      for (int mtn = P.mtiles; mtn >= 1; --mtn) {
+        int cols = kwn * mtn * npad;
+        if (cols > 512) continue;
+        int ntask_m = (P.mtiles + mtn - 1) / mtn;
+        int ntasks = ntask_m * (cout / nn) * (ks / kwn);
+        // stage bytes: chunks touched by an M group of mtn tiles
+        int lo, hi;
+        chunk_range(0, mtn, k2, P.c8, &lo, &hi);
+        int nch = hi - lo + 2;  // +1 slack for a straddling group range
+        if (nch > P.c8) nch = P.c8;
+        int a_bytes = (nch * k2 + 1) * P.pitch_w * 16;
+        a_bytes = round_up(a_bytes, 128);
+        int g_bytes = (nn / 8) * P.kpad * 16;
+        int stage = round_up(a_bytes + g_bytes, 128);
+        int tail = 16 * mtn * P.pitch_w * 16 + 256;
+        int stages = std::min(kMaxStages, (kSmemMax - kHeader - tail) / stage);
+        if (stages < 2) continue;
+        // cost per row per task
+        double t_mma = std::max({npad / 2.0, (4096.0 + 32.0 * npad) / 128.0, 44.6});
+        double mma = (double)(P.kpad / 16) * kwn * mtn * t_mma;
+        double load = (double)(nch * k2 * P.pitch_w * 16 + g_bytes) / 48.0;
+        double per_row = std::max(mma, load) + 60.0;
+        // split so that tasks * S ~ a few waves
+        int S = (int)std::max<long long>(1, std::min<long long>(P.rows, (2LL * sms + ntasks - 1) / ntasks));
+        long long rps = (P.rows + S - 1) / S;
+        S = (int)((P.rows + rps - 1) / rps);
+        long long ctas = (long long)ntasks * S;
+        long long waves = (ctas + sms - 1) / sms;
+        double est = waves * (rps * per_row + 3000.0);
+        if (est < best) {
+          best = est;
+          P.mtn = mtn; P.nn = nn; P.kwn = kwn;
+          P.S = S; P.rows_per_split = rps;
+          P.stages = stages; P.stage_bytes = stage;
+          P.smem_bytes = kHeader + stages * stage + tail;
+          int alloc = 32;
+          while (alloc < cols) alloc *= 2;
+          P.tmem_cols = alloc;
+          P.est = est;
+          P.ok = true;
+        }
+      }
+    }
+  }
+  if (!P.ok) return false;
+  P.tasks.clear();
+  for (int mt0 = 0; mt0 < P.mtiles; mt0 += P.mtn)
+    for (int n0 = 0; n0 < cout; n0 += P.nn)
+      for (int kw0 = 0; kw0 < ks; kw0 += P.kwn)
+        P.tasks.push_back(Task{mt0, std::min(P.mtn, P.mtiles - mt0), n0, P.nn, kw0, P.kwn});
+  if (out) *out = P;
+  return true;
+}
+
+// ---------------------------------------------------------------------------
+// Kernel
+// ---------------------------------------------------------------------------
+template <typename T> struct OneBits;
+template <> struct OneBits<__nv_bfloat16> { static constexpr uint32_t v = 0x3F803F80u; };  // bf16 1.0 x2
+template <> struct OneBits<__half> { static constexpr uint32_t v = 0x3C003C00u; };         // fp16 1.0 x2
+
+struct TaskTable {
+  int mt0[128], mtn[128], n0[128], kw0[128];
+};
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 1)
+    tc_dw_kernel(const __grid_constant__ DwArgs a, const __grid_constant__ TaskTable tt) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* empty = full + kMaxStages;
+  uint64_t* done = empty + kMaxStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint8_t* stage0 = smem + kHeader;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  if ((smem_u32(smem) & 127u) != 0u) {
+    if (threadIdx.x == 0) atomicExch(a.err, 2);
+    return;
+  }
+  const int task = blockIdx.x % a.ntasks;
+  const int split = blockIdx.x / a.ntasks;
+  const int mt0 = tt.mt0[task], mtn = tt.mtn[task], n0 = tt.n0[task], kw0 = tt.kw0[task];
+  const int k2 = a.ks * a.ks;
+  int c_lo = min((16 * mt0) / k2, a.c8 - 1);
+  int c_hi = min((16 * (mt0 + mtn) - 1) / k2, a.c8 - 1);
+  const int nch = c_hi - c_lo + 1;
+  const int sbo_a = a.pitch_w * 16;
+  // group g (absolute) lives at row block (g - c_lo*k2) of the stage's A region
+  const bool has_ones = a.ones_group >= 16 * mt0 && a.ones_group < 16 * (mt0 + mtn) && kw0 == 0 &&
+                        a.dbpart != nullptr;
+  const int npad = (a.nn + 15) / 16 * 16;
+  const uint32_t tx_bytes = (uint32_t)(nch * k2 * sbo_a + (a.nn / 8) * a.kpad * 16);
+
+  // zero the whole dynamic region (finite junk rows), then the ones rows
+  {
+    const int total = a.stages * a.stage_bytes + 16 * mtn * sbo_a + 256;
+    uint4 z = make_uint4(0, 0, 0, 0);
+    for (int i = threadIdx.x * 16; i < total; i += kThreads * 16) *reinterpret_cast<uint4*>(stage0 + i) = z;
+    __syncthreads();
+    if (a.ones_group >= 0) {
+      const int rel = a.ones_group - c_lo * k2;
+      if (rel >= 0 && (rel + 1) * sbo_a <= a.a_bytes) {
+        for (int s = 0; s < a.stages; ++s) {
+          uint32_t* o = reinterpret_cast<uint32_t*>(stage0 + (size_t)s * a.stage_bytes + (size_t)rel * sbo_a);
+          for (int i = threadIdx.x; i < sbo_a / 4; i += kThreads) o[i] = OneBits<T>::v;
+        }
+      }
+    }
+  }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < a.stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, (uint32_t)a.tmem_cols);
+    tmem_relinquish();
+  }
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  const long long r_beg = (long long)split * a.rows_per_split;
+  const long long r_end = min(r_beg + a.rows_per_split, a.rows);
+  const uint64_t kWaitNs = 1000000000ull;
+  auto wait = [&](uint64_t* bar, uint32_t par) -> bool {
+    uint64_t deadline = global_timer_ns() + kWaitNs;
+    uint32_t spins = 0;
+    while (!mbar_try_wait(bar, par)) {
+      if (((++spins) & 255u) == 0) {
+        if (*abort_flag) return false;
+        if (global_timer_ns() > deadline) {
+          *abort_flag = 1;
+          atomicExch(a.err, 1);
+          return false;
+        }
+      }
+    }
+    return true;
+  };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tmap(&a.tx);
+      prefetch_tmap(&a.tg);
+      int stage = 0;
+      uint32_t epar = 1;
+      bool pending[kMaxStages];
+      uint32_t last_par[kMaxStages];
+      for (int s = 0; s < kMaxStages; ++s) { pending[s] = false; last_par[s] = 0; }
+      for (long long r = r_beg; r < r_end; ++r) {
+        const int wi = (int)(r % a.nwt);
+        long long q = r / a.nwt;
+        const int y = (int)(q % a.oh); q /= a.oh;
+        const int z = (int)(q % a.od);
+        const int nb = (int)(q / a.od);
+        const int w0 = wi * a.wt;
+        if (!wait(&empty[stage], epar)) break;
+        uint8_t* sA = stage0 + (size_t)stage * a.stage_bytes;
+        mbar_arrive_expect_tx(&full[stage], tx_bytes);
+        for (int c = 0; c < nch; ++c)
+          tma_load_5d(sA + (size_t)c * k2 * sbo_a, &a.tx, &full[stage], (c_lo + c) * 8, w0 - a.pw, y - a.ph,
+                      z - a.pd, nb);
+        for (int c = 0; c < a.nn / 8; ++c)
+          tma_load_5d(sA + a.a_bytes + (size_t)c * a.kpad * 16, &a.tg, &full[stage], n0 + c * 8, w0, y, z, nb);
+        pending[stage] = true;
+        last_par[stage] = epar ^ 1;
+        if (++stage == a.stages) { stage = 0; epar ^= 1; }
+      }
+      for (int s = 0; s < a.stages; ++s) {
+        if (!pending[s]) continue;
+        uint64_t dl = global_timer_ns() + kWaitNs;
+        while (!mbar_try_wait(&full[s], last_par[s]) && global_timer_ns() < dl) {
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t fpar = 0;
+      bool first = true;
+      const uint32_t a_tile = (uint32_t)(16 * sbo_a) >> 4;       // descriptor units
+      const int rel0 = 16 * mt0 - c_lo * k2;                     // first group of the task
+      for (long long r = r_beg; r < r_end; ++r) {
+        if (!wait(&full[stage], fpar)) break;
+        tc_fence_after();
+        const uint32_t sA = smem_u32(stage0 + (size_t)stage * a.stage_bytes);
+        const uint64_t a0 = smem_desc(sA + (uint32_t)(rel0 * sbo_a) + (uint32_t)(kw0 * 16), 128, (uint32_t)sbo_a);
+        const uint64_t b0 = smem_desc(sA + (uint32_t)a.a_bytes, 128, (uint32_t)(a.kpad * 16));
+        const int ksteps = a.kpad / 16;
+        for (int ks = 0; ks < ksteps; ++ks) {
+          const uint32_t acc = (first && ks == 0) ? 0u : 1u;
+          const uint64_t b = b0 + (uint64_t)(ks * 16);  // 256 B per K step
+          for (int kw = 0; kw < a.kwn; ++kw) {
+            const uint64_t akw = a0 + (uint64_t)(ks * 16 + kw);
+            const uint32_t dk = tmem + (uint32_t)(kw * mtn * npad);
+            for (int t = 0; t < mtn; ++t)
+              mma_f16_ss(dk + (uint32_t)(t * npad), akw + (uint64_t)(t * a_tile), b, a.idesc, acc);
+          }
+        }
+        first = false;
+        mma_commit(&empty[stage]);
+        if (++stage == a.stages) { stage = 0; fpar ^= 1; }
+      }
+      mma_commit(done);
+    }
+  } else {
+    // epilogue: wait for every MMA, then write the fp32 partials of this task
+    if (wait(done, 0)) {
+      tc_fence_after();
+      const int q = warp & 3;
+      const int row = q * 32 + lane;
+      for (int kw = 0; kw < a.kwn; ++kw) {
+        for (int t = 0; t < mtn; ++t) {
+          const int g = 16 * (mt0 + t) + row / 8;  // absolute group
+          const int ci8 = row % 8;
+          const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)((kw * mtn + t) * npad);
+          for (int cc = 0; cc < npad; cc += 16) {
+            float v[16];
+            tmem_ld_16(tb + (uint32_t)cc, v);
+            if (g < k2 * a.c8) {
+              const int c = g / k2, rem = g % k2;
+              const int kd = rem / a.ks, kh = rem % a.ks;
+              const int ci = c * 8 + ci8;
+              const int tap = (kd * a.ks + kh) * a.ks + (kw0 + kw);
+              const int ntap = k2 * a.ks;
+              float* dst = a.part + (size_t)split * a.cout * a.cin * ntap;
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                const int co = n0 + cc + i;
+                if (cc + i < a.nn) dst[((size_t)co * a.cin + ci) * ntap + tap] = v[i];
+              }
+            } else if (has_ones && g == a.ones_group && ci8 == 0 && kw == 0) {
+#pragma unroll
+              for (int i = 0; i < 16; ++i)
+                if (cc + i < a.nn) a.dbpart[(size_t)split * a.cout + n0 + cc + i] = v[i];
+            }
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, (uint32_t)a.tmem_cols);
+  }
+}
+
+// dw[co][ci][tap] (ci < cin_real) = sum over splits, in split order, of the
+// partials laid out with cin_pad input channels.
+__global__ void dw_reduce_kernel(const float* __restrict__ part, int S, int cout, int cin_pad, int cin_real,
+                                 int ntap, float* __restrict__ dw, const float* __restrict__ dbpart,
+                                 float* __restrict__ db) {
+  const long long total_pad = (long long)cout * cin_pad * ntap;
+  const long long total = (long long)cout * cin_real * ntap;
+  long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < total) {
+    const int tap = (int)(i % ntap);
+    const long long r = i / ntap;
+    const int ci = (int)(r % cin_real);
+    const int co = (int)(r / cin_real);
+    const long long j = ((long long)co * cin_pad + ci) * ntap + tap;
+    float s = 0.f;
+    for (int k = 0; k < S; ++k) s += part[(size_t)k * total_pad + j];
+    dw[i] = s;
+  }
+  if (db != nullptr && dbpart != nullptr && i < cout) {
+    float s = 0.f;
+    for (int k = 0; k < S; ++k) s += dbpart[(size_t)k * cout + i];
+    db[i] = s;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, []() {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+static bool encode_ndhwc(CUtensorMap* m, const void* base, int dtype, int c, int w, int h, int d, int n,
+                         int bx, int by, int bz) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return false;
+  const cuuint64_t e = 2;
+  cuuint64_t dims[5] = {(cuuint64_t)c, (cuuint64_t)w, (cuuint64_t)h, (cuuint64_t)d, (cuuint64_t)n};
+  cuuint64_t str[4] = {c * e, (cuuint64_t)w * c * e, (cuuint64_t)h * w * c * e, (cuuint64_t)d * h * w * c * e};
+  cuuint32_t box[5] = {8, (cuuint32_t)bx, (cuuint32_t)by, (cuuint32_t)bz, 1};
+  cuuint32_t es[5] = {1, 1, 1, 1, 1};
+  return enc(m, dtype == R4C_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5,
+             const_cast<void*>(base), dims, str, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <typename T>
+static cudaError_t set_attr() {
+  static bool done[64] = {false};
+  static std::mutex mu;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lk(mu);
+  if (dev >= 0 && dev < 64 && done[dev]) return cudaSuccess;
+  e = cudaFuncSetAttribute(tc_dw_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
+  if (e == cudaSuccess && dev >= 0 && dev < 64) done[dev] = true;
+  return e;
+}
+
+}  // namespace tcdw
+
+namespace tc {
+
+bool dw_supported(int n, int d, int h, int w, int cin, int cout, int ks, int pd, int ph, int pw) {
+  tcdw::DwPlan P;
+  return tcdw::plan_dw(n, d, h, w, cin, cout, ks, pd, ph, pw, &P) && (int)P.tasks.size() <= 128;
+}
+
+size_t dw_workspace(int n, int d, int h, int w, int cin, int cout, int ks, int pd, int ph, int pw) {
+  tcdw::DwPlan P;
+  if (!tcdw::plan_dw(n, d, h, w, cin, cout, ks, pd, ph, pw, &P)) return 0;
+  size_t T = (size_t)ks * ks * ks;
+  size_t part = (size_t)P.S * cout * cin * T * sizeof(float);
+  part = (part + 255) / 256 * 256;
+  size_t dbp = (size_t)P.S * cout * sizeof(float);
+  return part + (dbp + 255) / 256 * 256;
+}
+
+int dw_describe(int n, int d, int h, int w, int cin, int cout, int ks, int pd, int ph, int pw, char* buf,
+                size_t len) {
+  tcdw::DwPlan P;
+  if (!tcdw::plan_dw(n, d, h, w, cin, cout, ks, pd, ph, pw, &P)) return 0;
+  snprintf(buf, len,
+           "tcgen05 dW: groups=%d mtiles=%d task(mt=%d n=%d kw=%d) tasks=%d splits=%d rows/split=%lld "
+           "wt=%d kpad=%d pitch=%d stages=%d stage=%dB smem=%dB tmem=%d db_in_kernel=%d est=%.0fus",
+           P.groups, P.mtiles, P.mtn, P.nn, P.kwn, (int)P.tasks.size(), P.S, P.rows_per_split, P.wt, P.kpad,
+           P.pitch_w, P.stages, P.stage_bytes, P.smem_bytes, P.tmem_cols, (int)P.db_in_kernel, P.est / 1.9e3);
+  return 1;
+}
+
+int launch_dw(int n, int d, int h, int w, int cin, int cin_real, int cout, int ks, int pd, int ph, int pw,
+              const void* x, const void* go, float* dw, float* db, void* ws, size_t ws_bytes, int dtype,
+              cudaStream_t st, bool* db_done) {
+  using namespace tcdw;
+  DwPlan P;
+  if (!plan_dw(n, d, h, w, cin, cout, ks, pd, ph, pw, &P)) return R4C_ERR_UNSUPPORTED;
+  if ((int)P.tasks.size() > 128) return R4C_ERR_UNSUPPORTED;
+  if (((uintptr_t)x & 15) || ((uintptr_t)go & 15)) return R4C_ERR_ALIGN;
+  const size_t T = (size_t)ks * ks * ks;
+  size_t part_bytes = ((size_t)P.S * cout * cin * T * sizeof(float) + 255) / 256 * 256;
+  size_t need = part_bytes + ((size_t)P.S * cout * sizeof(float) + 255) / 256 * 256;
+  if (ws_bytes < need || ws == nullptr) return R4C_ERR_WORKSPACE;
+  DwArgs a;
+  memset(&a, 0, sizeof(a));
+  if (!encode_ndhwc(&a.tx, x, dtype, cin, w, h, d, n, P.pitch_w, ks, ks)) return R4C_ERR_INVALID;
+  if (!encode_ndhwc(&a.tg, go, dtype, cout, P.ow, P.oh, P.od, n, P.kpad, 1, 1)) return R4C_ERR_INVALID;
+  a.part = static_cast<float*>(ws);
+  a.err = device_error_flag();
+  if (!a.err) return R4C_ERR_CUDA;
+  a.dbpart = (db != nullptr && P.db_in_kernel) ? reinterpret_cast<float*>(static_cast<char*>(ws) + part_bytes)
+                                               : nullptr;
+  a.od = P.od; a.oh = P.oh; a.ow = P.ow; a.cin = cin; a.cout = cout; a.ks = ks;
+  a.pd = pd; a.ph = ph; a.pw = pw;
+  a.c8 = P.c8; a.pitch_w = P.pitch_w; a.kpad = P.kpad; a.nwt = P.nwt; a.wt = P.wt;
+  a.mtn = P.mtn; a.nn = P.nn; a.kwn = P.kwn;
+  a.ones_group = P.db_in_kernel ? P.groups : -1;
+  a.stages = P.stages; a.stage_bytes = P.stage_bytes;
+  {
+    int lo, hi;
+    chunk_range(0, P.mtn, ks * ks, P.c8, &lo, &hi);
+    int nch = std::min(hi - lo + 2, P.c8);
+    a.a_bytes = round_up((nch * ks * ks + 1) * P.pitch_w * 16, 128);
+  }
+  a.g_bytes = (P.nn / 8) * P.kpad * 16;
+  a.tmem_cols = P.tmem_cols;
+  a.rows = P.rows;
+  a.rows_per_split = P.rows_per_split;
+  a.ntasks = (int)P.tasks.size();
+  a.idesc = sm100::instr_desc_f16(dtype == R4C_BF16, 128, round_up(P.nn, 16), 1, 1);
+  TaskTable tt;
+  memset(&tt, 0, sizeof(tt));
+  for (size_t i = 0; i < P.tasks.size(); ++i) {
+    tt.mt0[i] = P.tasks[i].mt0; tt.mtn[i] = P.tasks[i].mtn; tt.n0[i] = P.tasks[i].n0; tt.kw0[i] = P.tasks[i].kw0;
+  }
+  const unsigned grid = (unsigned)(P.tasks.size() * P.S);
+  cudaError_t e;
+  if (dtype == R4C_BF16) {
+    e = set_attr<__nv_bfloat16>();
+    if (e != cudaSuccess) return R4C_ERR_CUDA;
+    tc_dw_kernel<__nv_bfloat16><<<grid, kThreads, P.smem_bytes, st>>>(a, tt);
+  } else {
+    e = set_attr<__half>();
+    if (e != cudaSuccess) return R4C_ERR_CUDA;
+    tc_dw_kernel<__half><<<grid, kThreads, P.smem_bytes, st>>>(a, tt);
+  }
+  if (cudaGetLastError() != cudaSuccess) return R4C_ERR_CUDA;
+  const long long total = (long long)cout * cin_real * T;
+  const long long nthr = std::max<long long>(total, cout);
+  dw_reduce_kernel<<<(unsigned)((nthr + 255) / 256), 256, 0, st>>>(a.part, P.S, cout, cin, cin_real, (int)T, dw,
+                                                                    a.dbpart, a.dbpart ? db : nullptr);
+  note_launches(2);
+  if (cudaGetLastError() != cudaSuccess) return R4C_ERR_CUDA;
+  if (db_done) *db_done = (a.dbpart != nullptr);
+  return R4C_OK;
+}
+
+}  // namespace tc
+}  // namespace r4c

@@ -193,7 +193,7 @@ def test_kernel_families_used(cuda_ready):
                            ((4, 96, 16, 32, 32), 96, 3), ((4, 192, 8, 16, 16), 192, 3),
                            ((4, 48, 64, 128, 128), 24, 1)]:
         fam = cw.conv3d_kernels(shape, cout, k, 1 if k == 3 else 0)
-        assert fam["fwd"] == "tcgen05" and fam["dx"] == "tcgen05", (shape, fam)
+        assert fam["fwd"] == "tcgen05" and fam["dx"] == "tcgen05" and fam["dw"] == "tcgen05", (shape, fam)
 
 
 def test_no_device_error_flag(cuda_ready):

@@ -51,8 +51,11 @@ def _d(n=2, cin=24, cout=24, d=16, h=32, w=32, k=3, p=1, dt=torch.bfloat16, forc
 def test_plan_families():
     assert _native.plan_kernel(_d(), _native.LEG_FWD) == _native.KERNEL_TC
     assert _native.plan_kernel(_d(), _native.LEG_DX) == _native.KERNEL_TC
-    # odd channel counts go to the SIMT kernels
-    assert _native.plan_kernel(_d(cin=5, cout=7), _native.LEG_FWD) == _native.KERNEL_GENERIC
+    # odd input channels: the forward pads them to 8 in workspace and stays on
+    # tcgen05; dX of that layer (input channels = Cout = 7) uses the SIMT kernels
+    assert _native.plan_kernel(_d(cin=5, cout=7), _native.LEG_FWD) == _native.KERNEL_TC
+    assert _native.workspace_bytes(_d(cin=5, cout=7), _native.LEG_FWD) >= 2 * 16 * 32 * 32 * 8 * 2
+    assert _native.plan_kernel(_d(cin=5, cout=7), _native.LEG_DX) == _native.KERNEL_GENERIC
     # the generic family can be forced
     assert _native.plan_kernel(_d(force=1), _native.LEG_FWD) == _native.KERNEL_GENERIC
     assert "tcgen05" in _native.describe_plan(_d(), _native.LEG_FWD)
@@ -78,7 +81,7 @@ def test_workspace_sizes():
 
 
 def test_packed_sizes():
-    assert _native.packed_weight_bytes(_d(cin=5, cout=7), _native.LEG_FWD) == 5 * 7 * 27 * 2
+    assert _native.packed_weight_bytes(_d(cin=5, cout=7), _native.LEG_DX) == 5 * 7 * 27 * 2
     assert _native.packed_weight_bytes(_d(), _native.LEG_FWD) >= 24 * 24 * 27 * 2
 
 

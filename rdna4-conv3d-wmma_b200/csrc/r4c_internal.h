@@ -58,7 +58,10 @@ struct ConvPlan {
   int cin, cout;         // its channels (dX: cin = Cout of the layer)
   int ks, pd, ph, pw;
   int c8;                // 8-channel chunks of cin
-  int npad;              // cout rounded up to the MMA N granule (16)
+  int npad;              // cout rounded up to the MMA N granule (16): one TMEM "slot"
+  int P;                 // output planes per work unit (plane block)
+  int nin;               // input planes per unit: P + ks - 1
+  int fold;              // output-plane slots one MMA may cover (kd folded into N)
   int G, ngroups;        // chunks per pipeline stage, stages per kd plane
   int nsteps;            // 16-wide K steps per stage
   int wt, ht;            // output tile (cols, rows) of one plane
@@ -70,7 +73,7 @@ struct ConvPlan {
   int wres_bytes;        // its size (ks * ngroups * b_bytes) when resident
   int tmem_cols;
   double est_cycles;     // planner's cost-model estimate for the whole launch
-  int64_t work_units;    // n * od * tiles_h * tiles_w
+  int64_t work_units;    // n * ceil(od / P) * tiles_h * tiles_w
   int grid;
 };
 

@@ -1,33 +1,43 @@
-// r4c_tc.cu — tcgen05 + TMA implicit-GEMM Conv3d for sm_100a (k = 1 or 3,
-// stride 1, Cin a multiple of 8, Cout <= 256). Runs the forward conv and, with
-// the flipped/transposed weight and padding k-1-p, the input gradient.
+// r4c_tc.cu — tcgen05 implicit-GEMM Conv3d for sm_100a (k = 1 or 3, stride 1,
+// Cin a multiple of 8, Cout <= 256). Runs the forward conv and, with the
+// flipped/transposed weight and padding k-1-p, the input gradient.
 //
 // Reference counterpart: _fwd_k3_kernel / _fwd_k1_kernel and the k3 dX reuse
 // in _launch_dgrad (src/rdna4_conv3d/conv3d_wmma.py:327-444, 1154-1162). The
 // reference gathers a masked 27-tap im2col tile per K step; here the GEMM is
 // laid out for the B200 memory system instead:
 //
-//  * Work unit = one output plane tile (n, z, ht rows x wt cols), persistent
-//    CTAs (one per SM) walk the units.
-//  * For each kd in 0..k-1 and each group of G 8-channel chunks, ONE TMA box
-//    per chunk brings the (ht+k-1) x (wt+k-1) input halo of plane z+kd-pad into
-//    shared memory as a "chunk plane": rows are brick positions, 16 bytes (8
-//    channels) each. TMA's out-of-bounds zero fill is the conv padding.
+//  * Work unit = a block of P consecutive output planes of one (ht x wt)
+//    plane tile. Persistent CTAs (one per SM) walk the units.
+//  * Each input plane of the block (P + k - 1 of them) is loaded ONCE, as
+//    "chunk planes": for every 8-channel chunk, the (ht+k-1) x (wt+k-1) halo
+//    brick with 16 bytes per position. Four producer warps gather it with
+//    coalesced 16-byte cp.async copies (zero fill = the conv padding); TMA is
+//    not used for activations because its rate is about one box row per
+//    clock and the rows here are only 16 bytes wide.
 //  * GEMM rows are brick positions p = hh*(wt+k-1) + ww ("padded grid"): a tap
-//    (kh, kw) is then a constant shift of the A start address, so all k*k taps
-//    read the same brick without any im2col copy. Rows with ww >= wt or
-//    hh >= ht are junk and are simply not stored.
-//  * tcgen05.mma kind::f16, M = 128, N = Cout padded to 16, K = 16 (two
-//    8-channel core-matrix columns whose distance is the descriptor LBO). For
-//    an odd number of chunks (Cin = 24) two taps share one K step: (kw, kw+1)
-//    are 16 bytes apart, (kh, kh+1) one brick row apart.
-//  * fp32 accumulators live in TMEM (double-buffered when they fit), the
-//    epilogue warps read them with tcgen05.ld, add bias, round, and store.
+//    (kh, kw) is a constant shift of the A start address, so the k*k taps of
+//    a plane read the same brick. Rows with ww >= wt or hh >= ht are junk.
+//  * kd is folded into N: input plane j feeds output planes j-kd (kd = 0..k-1)
+//    of the block, so one tcgen05.mma (M = 128, N = slots * Cout_pad <= 256)
+//    updates up to three output-plane accumulators. This matters because an
+//    M=128 K=16 MMA costs ~45 SM clocks whatever N <= 48 is (shared-memory
+//    operand fetch), so N=32 alone would cap the tensor pipe near 35%.
+//  * K = 16 = two 8-channel core-matrix columns at distance LBO. Even chunk
+//    counts pair (c, c+1); odd chunk counts (Cin = 24) pair taps instead:
+//    (kw, kw+1) are 16 B apart, (kh, kh+1) one brick row apart; a final single
+//    chunk pairs with a zero-weight half.
+//  * fp32 accumulators live in TMEM ([set][tile][slot][Cout_pad] columns,
+//    double-buffered when they fit); four epilogue warps read them with
+//    tcgen05.ld, add bias, round and store NDHWC.
 //
-// Warp roles (192 threads): warp 0 TMA producer, warp 1 MMA issuer + TMEM
-// owner, warps 2-5 epilogue (TMEM lane quarter = warp % 4).
+// Warp roles (288 threads): warps 0-3 producers, warp 4 MMA issuer + TMEM
+// owner, warps 5-8 epilogue (TMEM lane quarter = warp % 4). Every wait is
+// bounded (1 s); a timeout sets the device error flag and the kernel winds
+// down (copies drained, TMEM released) instead of hanging.
 #include <cuda.h>
 
+#include <algorithm>
 #include <mutex>
 #include <vector>
 
@@ -41,28 +51,31 @@ __device__ int g_r4c_dev_error = 0;
 namespace tc {
 
 constexpr int kMaxSteps = 64;
-constexpr int kMaxStages = 6;
-constexpr int kThreads = 192;
+constexpr int kMaxStages = 8;
+constexpr int kMaxMt = 8;  // M tiles per unit (the issue loop is unrolled over them)
+constexpr int kThreads = 288;
+constexpr int kProducerThreads = 128;
 constexpr int kSmemMax = 232448;  // 227 KB opt-in dynamic shared memory
 constexpr int kHeader = 2048;     // barriers + bias
 
-struct alignas(64) TcConvArgs {
-  CUtensorMap tmap;
+struct TcConvArgs {
+  const void* x;
   const uint8_t* wpack;
   const void* bias;
   void* y;
-  int n, od, oh, ow, cout, npad;
+  int n, d, h, w, cin;
+  int od, oh, ow, cout;
   int pd, ph, pw, ks;
-  int ht, wt, nht, nwt;
-  int pitch_w;
+  int ht, wt, nht, nwt, nzb;
+  int pitch_w, pitch_h;
+  int slot_w, P, nin, fold;
   int G, ngroups, nsteps;
   int mtiles, nsets;
   int cpb, a_bytes, b_bytes, stage_bytes, stages;
   int wres, wres_bytes;
   int tmem_cols;
   long long units;
-  uint32_t idesc;
-  uint32_t tx_bytes;
+  uint32_t idesc[4];  // N = 1..3 slots
   int a_off[kMaxSteps];
   int lbo[kMaxSteps];
 };
@@ -81,6 +94,9 @@ static int steps_per_stage(int ks, int G) {
   return ks == 3 ? 4 * G + (G + 1) / 2 : (G + 1) / 2;
 }
 
+// K steps of one (input plane, chunk group) stage: which two 8-channel
+// halves each K=16 step reads, the A offset of its first half and the
+// distance (LBO) to its second half.
 static void build_steps(int ks, int G, int pitch_w, int cpb, std::vector<Step>& st) {
   st.clear();
   auto off = [&](int kh, int kw, int c) { return c * cpb + (kh * pitch_w + kw) * 16; };
@@ -94,17 +110,13 @@ static void build_steps(int ks, int G, int pitch_w, int cpb, std::vector<Step>& 
     return;
   }
   if (ks == 3) {
-    // (kw=0, kw=1) pairs: the second half is one brick position (16 B) later.
     for (int kh = 0; kh < 3; ++kh)
       for (int c = 0; c < G; ++c)
         st.push_back(Step{{ref(kh, 0, c), ref(kh, 1, c)}, off(kh, 0, c), 16});
-    // kw=2: (kh=0, kh=1) pairs, one brick row apart.
     for (int c = 0; c < G; ++c)
       st.push_back(Step{{ref(0, 2, c), ref(1, 2, c)}, off(0, 2, c), pitch_w * 16});
-    // (kh=2, kw=2): chunk pairs.
     for (int j = 0; j < (G - 1) / 2; ++j)
       st.push_back(Step{{ref(2, 2, 2 * j), ref(2, 2, 2 * j + 1)}, off(2, 2, 2 * j), cpb});
-    // Last chunk: paired with a zero-weight half that reads the preceding row.
     st.push_back(Step{{zero, ref(2, 2, G - 1)}, off(2, 2, G - 1) - 16, 16});
   } else {
     for (int j = 0; j < (G - 1) / 2; ++j)
@@ -130,8 +142,11 @@ static int num_sms() {
   return cached[dev];
 }
 
-bool plan_conv(int n, int d, int h, int w, int cin, int cout, int ks, int pd, int ph, int pw,
-               ConvPlan* pl) {
+// Clocks of one M=128 K=16 MMA with N columns when issued back to back
+// (measured on B200: 45 for N <= 32, 56 for 96, 64 for 128, 128 for 256).
+static double mma_clk(int n) { return std::max({n / 2.0, 40.0 + n / 6.0, 45.0}); }
+
+bool plan_conv(int n, int d, int h, int w, int cin, int cout, int ks, int pd, int ph, int pw, ConvPlan* pl) {
   ConvPlan P{};
   P.ok = false;
   if (ks != 1 && ks != 3) return false;
@@ -141,12 +156,12 @@ bool plan_conv(int n, int d, int h, int w, int cin, int cout, int ks, int pd, in
   P.oh = h + 2 * ph - (ks - 1);
   P.ow = w + 2 * pw - (ks - 1);
   if (P.od <= 0 || P.oh <= 0 || P.ow <= 0) return false;
-  // TMA coordinates are int32 and start at -pad: keep pads small.
   if (pd > 8 || ph > 8 || pw > 8 || pd < -8 || ph < -8 || pw < -8) return false;
   P.n = n; P.d = d; P.h = h; P.w = w;
   P.cin = cin; P.cout = cout; P.ks = ks; P.pd = pd; P.ph = ph; P.pw = pw;
   P.c8 = cin / 8;
   P.npad = round_up(cout, 16);
+  P.fold = std::max(1, std::min(ks, 256 / P.npad));
 
   std::vector<int> gs;
   if (P.c8 % 2 == 1) {
@@ -156,64 +171,82 @@ bool plan_conv(int n, int d, int h, int w, int cin, int cout, int ks, int pd, in
     for (int g = std::min(P.c8, 14); g >= 2; g -= 2)
       if (P.c8 % g == 0) gs.push_back(g);
   }
-  int wt_max = 256 - (ks - 1);
-  int nw = (P.ow + wt_max - 1) / wt_max;
-  int wt = (P.ow + nw - 1) / nw;
+  const int wt_max = 254 - (ks - 1);
+  const int nw = (P.ow + wt_max - 1) / wt_max;
+  const int wt = (P.ow + nw - 1) / nw;
   const int sms = num_sms();
 
-  // Cost model per work unit (SM clocks): tcgen05 issue (128xNx16 takes
-  // about N/2 clocks, at least ~10 to issue), L2 -> SMEM copy traffic at
-  // ~48 B/clk/SM, and the TMEM -> global epilogue (overlapped with the next
-  // unit's MMAs when two accumulator sets fit in TMEM). Launch estimate =
-  // waves * per-unit time; the plan with the smallest estimate wins.
   double best = 1e300;
   for (int G : gs) {
-    int nsteps = steps_per_stage(ks, G);
+    const int nsteps = steps_per_stage(ks, G);
     if (nsteps > kMaxSteps) continue;
     const int ngroups = P.c8 / G;
-    const int b_bytes = nsteps * 2 * P.npad * 16;
-    const int wbytes = ks * ngroups * b_bytes;
-    for (int wres = 0; wres <= 1; ++wres) {
+    const int b_bytes = nsteps * 2 * ks * P.npad * 16;
+    const int wbytes = ngroups * b_bytes;
+    for (int wres = 1; wres >= 0; --wres) {
       if (wres && wbytes > 96 * 1024) continue;
-      for (int ht = 1; ht <= P.oh && ht <= 256 - (ks - 1); ++ht) {
-        int pitch_w = wt + ks - 1, pitch_h = ht + ks - 1;
-        int span = (ht - 1) * pitch_w + wt;
-        int mtiles = (span + 127) / 128;
-        if (mtiles * P.npad > 512) break;
-        int nsets = (2 * mtiles * P.npad <= 512) ? 2 : 1;
-        int cpb = round_up(pitch_h * pitch_w * 16, 128);
-        int maxrow = 128 * mtiles - 1 + (ks - 1) * (pitch_w + 1);
-        int pad = round_up(std::max(0, (maxrow + 1) * 16 - cpb), 128);
-        int a_bytes = 128 + G * cpb + pad;
-        int stage = round_up(a_bytes + (wres ? 0 : b_bytes), 128);
-        int avail = kSmemMax - kHeader - (wres ? round_up(wbytes, 128) : 0);
-        int stages = std::min(kMaxStages, avail / stage);
-        if (stages < 2) continue;
-        int tiles_h = (P.oh + ht - 1) / ht;
-        long long units = (long long)n * P.od * tiles_h * nw;
-        double mma = (double)ks * ngroups * nsteps * mtiles * std::max(10.0, P.npad / 2.0);
-        double load = (double)ks * ngroups * (G * pitch_h * pitch_w * 16.0 + (wres ? 0.0 : b_bytes)) / 48.0;
-        double epi = (double)mtiles * (P.npad / 16.0) * 40.0;
-        double t_unit = std::max(mma, load) + 200.0;
-        t_unit = nsets == 2 ? std::max(t_unit, epi) : t_unit + epi;
-        long long waves = (units + sms - 1) / sms;
-        double est = (double)waves * t_unit + (wres ? wbytes / 48.0 : 0.0);
-        if (est < best) {
-          best = est;
-          P.G = G; P.ngroups = ngroups; P.nsteps = nsteps;
-          P.wt = wt; P.ht = ht; P.pitch_w = pitch_w; P.pitch_h = pitch_h;
-          P.cpb = cpb; P.mtiles = mtiles; P.nsets = nsets;
-          P.a_bytes = a_bytes; P.b_bytes = b_bytes; P.stage_bytes = stage; P.stages = stages;
-          P.wres = wres; P.wres_bytes = wres ? round_up(wbytes, 128) : 0;
-          P.smem_bytes = kHeader + P.wres_bytes + stages * stage;
-          int cols = nsets * mtiles * P.npad;
-          int alloc = 32;
-          while (alloc < cols) alloc *= 2;
-          P.tmem_cols = alloc;
-          P.work_units = units;
-          P.grid = (int)std::min<long long>(units, sms);
-          P.est_cycles = est;
-          P.ok = true;
+      for (int ht = 1; ht <= P.oh && ht <= 254 - (ks - 1); ++ht) {
+        const int pitch_w = wt + ks - 1, pitch_h = ht + ks - 1;
+        const int span = (ht - 1) * pitch_w + wt;
+        const int mtiles = (span + 127) / 128;
+        if (mtiles * P.npad > 512 || mtiles > kMaxMt) break;
+        const int cpb = round_up(pitch_h * pitch_w * 16, 128);
+        const int maxrow = 128 * mtiles - 1 + (ks - 1) * (pitch_w + 1);
+        const int pad = round_up(std::max(0, (maxrow + 1) * 16 - cpb), 128);
+        const int a_bytes = 128 + G * cpb + pad;
+        const int avail = kSmemMax - kHeader - (wres ? round_up(wbytes, 128) : 0);
+        const int tiles_h = (P.oh + ht - 1) / ht;
+        for (int Pb = 1; Pb <= std::min(P.od, 16); ++Pb) {
+          // a stage holds the A brick and, unless resident, the weight slots
+          // of the output planes its input plane feeds (at most min(ks, Pb))
+          const int sb = std::min(ks, Pb) * nsteps * 2 * P.npad * 16;
+          const int stage = round_up(a_bytes + (wres ? 0 : sb), 128);
+          const int stages = std::min(kMaxStages, avail / stage);
+          if (stages < 2) break;
+          int nsets = 2;
+          if (2 * Pb * P.npad * mtiles > 512) nsets = 1;
+          if (Pb * P.npad * mtiles > 512) break;
+          const int nin = Pb + ks - 1;
+          // MMA clocks per unit: every input plane, every K step, every tile
+          double mma = 0.0;
+          for (int j = 0; j < nin; ++j) {
+            const int lo = std::max(0, j - ks + 1), hi = std::min(Pb - 1, j);
+            int ns = hi - lo + 1;
+            double t = 0.0;
+            while (ns > 0) {
+              const int k = std::min(ns, P.fold);
+              t += mma_clk(k * P.npad);
+              ns -= k;
+            }
+            mma += t * nsteps * mtiles * ngroups;
+          }
+          const double load = (double)nin * ngroups * (G * pitch_h * pitch_w * 16.0 + (wres ? 0.0 : sb)) / 64.0;
+          const double epi = (double)Pb * mtiles * (P.npad / 16.0) * 40.0;
+          double t_unit = std::max(mma, load) + 150.0 * nin * ngroups;
+          t_unit = nsets == 2 ? std::max(t_unit, epi) : t_unit + epi;
+          const long long units = (long long)n * ((P.od + Pb - 1) / Pb) * tiles_h * nw;
+          const long long waves = (units + sms - 1) / sms;
+          // streaming the weights per stage competes with the tensor core for
+          // shared-memory bandwidth even when it hides under the MMAs
+          const double est = (double)waves * (t_unit + (wres ? 0.0 : 0.1 * load));
+          if (est < best) {
+            best = est;
+            P.G = G; P.ngroups = ngroups; P.nsteps = nsteps;
+            P.wt = wt; P.ht = ht; P.pitch_w = pitch_w; P.pitch_h = pitch_h;
+            P.cpb = cpb; P.mtiles = mtiles; P.nsets = nsets;
+            P.P = Pb; P.nin = nin;
+            P.a_bytes = a_bytes; P.b_bytes = b_bytes; P.stage_bytes = stage; P.stages = stages;
+            P.wres = wres; P.wres_bytes = wres ? round_up(wbytes, 128) : 0;
+            P.smem_bytes = kHeader + P.wres_bytes + stages * stage;
+            const int cols = nsets * Pb * P.npad * mtiles;
+            int alloc = 32;
+            while (alloc < cols) alloc *= 2;
+            P.tmem_cols = alloc;
+            P.work_units = units;
+            P.grid = (int)std::min<long long>(units, sms);
+            P.est_cycles = est;
+            P.ok = true;
+          }
         }
       }
     }
@@ -223,13 +256,11 @@ bool plan_conv(int n, int d, int h, int w, int cin, int cout, int ks, int pd, in
   return true;
 }
 
-
-size_t packed_bytes(const ConvPlan& P) {
-  return (size_t)P.ks * P.ngroups * P.b_bytes;
-}
+size_t packed_bytes(const ConvPlan& P) { return (size_t)P.ngroups * P.b_bytes; }
 
 // ---------------------------------------------------------------------------
-// Weight pack: PyTorch OIDHW -> per-stage K-step blocks [step][half][npad][8].
+// Weight pack: PyTorch OIDHW -> per chunk group, per K step:
+// [half][slot b (kd = ks-1-b)][npad rows][8 elements]
 // ---------------------------------------------------------------------------
 struct PackArgs {
   int ks, G, ngroups, nsteps, npad, cin, cout;  // cin/cout of the conv being run
@@ -241,28 +272,26 @@ struct PackArgs {
 
 template <typename TO>
 __global__ void pack_tc_kernel(const void* __restrict__ src, int sdt, TO* __restrict__ dst, PackArgs a) {
-  const long long total = (long long)a.ks * a.ngroups * a.nsteps * 2 * a.npad * 8;
+  const long long total = (long long)a.ngroups * a.nsteps * 2 * a.ks * a.npad * 8;
   long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= total) return;
-  int e = (int)(i % 8);
+  const int e = (int)(i % 8);
   long long r = i / 8;
-  int nrow = (int)(r % a.npad); r /= a.npad;
-  int half = (int)(r % 2); r /= 2;
-  int j = (int)(r % a.nsteps); r /= a.nsteps;
-  int g = (int)(r % a.ngroups);
-  int kd = (int)(r / a.ngroups);
+  const int nrow = (int)(r % a.npad); r /= a.npad;
+  const int b = (int)(r % a.ks); r /= a.ks;
+  const int half = (int)(r % 2); r /= 2;
+  const int j = (int)(r % a.nsteps);
+  const int g = (int)(r / a.nsteps);
+  const int kd = a.ks - 1 - b;
   float v = 0.f;
   if (!a.zero[j][half] && nrow < a.cout) {
-    int ci = (g * a.G + a.c[j][half]) * 8 + e;
+    const int ci = (g * a.G + a.c[j][half]) * 8 + e;
     if (ci < a.cin_real) {
-      int T = a.ks * a.ks * a.ks;
-      int tap = (kd * a.ks + a.kh[j][half]) * a.ks + a.kw[j][half];
+      const int T = a.ks * a.ks * a.ks;
+      const int tap = (kd * a.ks + a.kh[j][half]) * a.ks + a.kw[j][half];
       long long s;
-      if (!a.flip) {
-        s = ((long long)nrow * a.src_cin + ci) * T + tap;  // W[co=nrow][ci][tap]
-      } else {
-        s = ((long long)ci * a.src_cin + nrow) * T + (T - 1 - tap);  // W[co=ci][ci'=nrow][T-1-tap]
-      }
+      if (!a.flip) s = ((long long)nrow * a.src_cin + ci) * T + tap;           // W[co=nrow][ci][tap]
+      else s = ((long long)ci * a.src_cin + nrow) * T + (T - 1 - tap);         // W[co=ci][ci'=nrow][T-1-tap]
       if (sdt == R4C_F32) v = static_cast<const float*>(src)[s];
       else if (sdt == R4C_BF16) v = __bfloat162float(static_cast<const __nv_bfloat16*>(src)[s]);
       else v = __half2float(static_cast<const __half*>(src)[s]);
@@ -289,8 +318,8 @@ cudaError_t pack_weight(const ConvPlan& P, bool flip, int cin_real, const void* 
       a.c[j][hf] = (signed char)steps[j].h[hf].c;
       a.zero[j][hf] = (signed char)steps[j].h[hf].zero;
     }
-  long long total = (long long)a.ks * a.ngroups * a.nsteps * 2 * a.npad * 8;
-  unsigned blocks = (unsigned)((total + 255) / 256);
+  const long long total = (long long)a.ngroups * a.nsteps * 2 * a.ks * a.npad * 8;
+  const unsigned blocks = (unsigned)((total + 255) / 256);
   if (dtype == R4C_BF16)
     pack_tc_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(w_src, src_dtype,
                                                           static_cast<__nv_bfloat16*>(w_packed), a);
@@ -305,25 +334,102 @@ cudaError_t pack_weight(const ConvPlan& P, bool flip, int cin_real, const void* 
 // ---------------------------------------------------------------------------
 using namespace r4c::sm100;
 
-template <typename T>
-__device__ __forceinline__ void store_row16(T* dst, const float (&v)[16], const float* bias, int cc, int cout,
-                                            bool vec_ok) {
-  if (vec_ok && cc + 16 <= cout) {
-    uint32_t pk[8];
+// Store NV (16 or 32) accumulator columns starting at channel cc of one
+// output row: bias added, rounded to T; every complete 8-channel group inside
+// cout goes out as one 16-byte store when the row is 16-byte aligned.
+template <typename T, int NV>
+__device__ __forceinline__ void store_row(T* dst, const float (&v)[NV], const float* bias, int cc, int cout,
+                                          bool vec_ok) {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      T lo = Elem<T>::from_f(v[2 * i] + bias[cc + 2 * i]);
-      T hi = Elem<T>::from_f(v[2 * i + 1] + bias[cc + 2 * i + 1]);
-      pk[i] = (uint32_t)(*reinterpret_cast<uint16_t*>(&lo)) |
-              ((uint32_t)(*reinterpret_cast<uint16_t*>(&hi)) << 16);
+  for (int g = 0; g < NV / 8; ++g) {
+    const int c0 = cc + 8 * g;
+    if (c0 >= cout) break;
+    if (vec_ok && c0 + 8 <= cout) {
+      uint32_t pk[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        T lo = Elem<T>::from_f(v[8 * g + 2 * i] + bias[c0 + 2 * i]);
+        T hi = Elem<T>::from_f(v[8 * g + 2 * i + 1] + bias[c0 + 2 * i + 1]);
+        pk[i] = (uint32_t)(*reinterpret_cast<uint16_t*>(&lo)) |
+                ((uint32_t)(*reinterpret_cast<uint16_t*>(&hi)) << 16);
+      }
+      *reinterpret_cast<uint4*>(dst + c0) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if (c0 + i < cout) dst[c0 + i] = Elem<T>::from_f(v[8 * g + i] + bias[c0 + i]);
     }
-    uint4* d4 = reinterpret_cast<uint4*>(dst + cc);
-    d4[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-    d4[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
-  } else {
+  }
+}
+
+// MMA issue for K steps [s0, s1) of one stage. MT tiles x NS slot segments
+// per step, fully unrolled, and the step loop unrolled so that every loop
+// iteration carries at least four MMAs: the issuing thread's scalar work for
+// one MMA (descriptor arithmetic, the table load, the uniform-register moves)
+// is a dependent chain of ~100 clocks, so MMAs issued one per iteration run
+// at that rate instead of the tensor pipe's 45-64 clocks; an unrolled block
+// lets those chains overlap.
+//   adlo[s]  : low descriptor word of step s (A address field, biased by one
+//              16-byte unit, and LBO), relative to the stage base sA4
+//   bd0      : B descriptor of step 0; step s adds s * bstep
+//   d[k], bo[k], id[k], acc[k]: TMEM column, B offset (16-byte units),
+//              instruction descriptor and accumulate flag of segment k
+struct Segs {
+  uint32_t d[4];
+  uint32_t bo[4];
+  uint32_t id[4];
+  uint32_t acc[4];
+};
+
+template <int MT, int NS>
+__device__ __forceinline__ void issue_steps(const uint32_t* __restrict__ adlo, int s0, int s1, uint32_t sA4,
+                                            uint64_t bd0, uint64_t bstep, uint32_t dbase, uint32_t tile_cols,
+                                            const Segs& sg) {
+  constexpr uint64_t kAHi = (uint64_t)((128u >> 4) | (1u << 14)) << 32;  // SBO 128 B, version 1
+  constexpr int U = (MT * NS >= 4) ? 1 : ((MT * NS >= 2) ? 2 : 4);
+  uint32_t d[NS], bo[NS], id[NS], acc[NS];
 #pragma unroll
-    for (int i = 0; i < 16; ++i)
-      if (cc + i < cout) dst[cc + i] = Elem<T>::from_f(v[i] + bias[cc + i]);
+  for (int k = 0; k < NS; ++k) {
+    d[k] = dbase + sg.d[k];
+    bo[k] = sg.bo[k];
+    id[k] = sg.id[k];
+    acc[k] = sg.acc[k];
+  }
+#pragma unroll U
+  for (int s = s0; s < s1; ++s) {
+    const uint64_t ad = kAHi | (uint64_t)(adlo[s] + sA4);
+    const uint64_t bd = bd0 + (uint64_t)s * bstep;
+#pragma unroll
+    for (int t = 0; t < MT; ++t)
+#pragma unroll
+      for (int k = 0; k < NS; ++k)
+        mma_f16_ss(d[k] + (uint32_t)t * tile_cols, ad + (uint64_t)(t * 128), bd + bo[k], id[k], acc[k]);
+  }
+}
+
+template <int MT>
+__device__ __forceinline__ void issue_ns(int ns, const uint32_t* adlo, int s0, int s1, uint32_t sA4, uint64_t bd0,
+                                         uint64_t bstep, uint32_t dbase, uint32_t tile_cols, const Segs& sg) {
+  switch (ns) {
+    case 1: issue_steps<MT, 1>(adlo, s0, s1, sA4, bd0, bstep, dbase, tile_cols, sg); break;
+    case 2: issue_steps<MT, 2>(adlo, s0, s1, sA4, bd0, bstep, dbase, tile_cols, sg); break;
+    case 3: issue_steps<MT, 3>(adlo, s0, s1, sA4, bd0, bstep, dbase, tile_cols, sg); break;
+    default: issue_steps<MT, 4>(adlo, s0, s1, sA4, bd0, bstep, dbase, tile_cols, sg); break;
+  }
+}
+
+__device__ __forceinline__ void issue(int mt, int ns, const uint32_t* adlo, int s0, int s1, uint32_t sA4,
+                                      uint64_t bd0, uint64_t bstep, uint32_t dbase, uint32_t tile_cols,
+                                      const Segs& sg) {
+  switch (mt) {
+    case 1: issue_ns<1>(ns, adlo, s0, s1, sA4, bd0, bstep, dbase, tile_cols, sg); break;
+    case 2: issue_ns<2>(ns, adlo, s0, s1, sA4, bd0, bstep, dbase, tile_cols, sg); break;
+    case 3: issue_ns<3>(ns, adlo, s0, s1, sA4, bd0, bstep, dbase, tile_cols, sg); break;
+    case 4: issue_ns<4>(ns, adlo, s0, s1, sA4, bd0, bstep, dbase, tile_cols, sg); break;
+    case 5: issue_ns<5>(ns, adlo, s0, s1, sA4, bd0, bstep, dbase, tile_cols, sg); break;
+    case 6: issue_ns<6>(ns, adlo, s0, s1, sA4, bd0, bstep, dbase, tile_cols, sg); break;
+    case 7: issue_ns<7>(ns, adlo, s0, s1, sA4, bd0, bstep, dbase, tile_cols, sg); break;
+    default: issue_ns<8>(ns, adlo, s0, s1, sA4, bd0, bstep, dbase, tile_cols, sg); break;
   }
 }
 
@@ -339,14 +445,18 @@ __global__ void __launch_bounds__(kThreads, 1) tc_conv_kernel(const __grid_const
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(wbar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* sbias = reinterpret_cast<float*>(smem + 1024);
+  // low 32 bits of each K step's A descriptor relative to the stage base:
+  // ((a_off + 16) >> 4) in the address field (offsets start at -16 B, so they
+  // are biased by one 16-byte unit to stay non-negative) and the step's LBO
+  uint32_t* s_adlo = reinterpret_cast<uint32_t*>(smem + 512);
   uint8_t* wres_smem = smem + kHeader;
   uint8_t* stage0 = smem + kHeader + a.wres_bytes;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  // TMA writes need 128-byte aligned destinations; every stage offset is a
-  // multiple of 128 from the dynamic shared memory base, so check the base.
+  // Bulk copies need 16-byte aligned shared memory; keep the whole layout on
+  // 128-byte boundaries from the base.
   if ((smem_u32(smem) & 127u) != 0u || a.tmem_cols > 512) {
     if (threadIdx.x == 0) atomicExch(&g_r4c_dev_error, 2);
     return;
@@ -356,16 +466,19 @@ __global__ void __launch_bounds__(kThreads, 1) tc_conv_kernel(const __grid_const
   // the overrun pad are read by junk GEMM rows only, but keep them finite),
   // stage the bias as fp32, init barriers, allocate TMEM.
   {
-    uint4 z = make_uint4(0, 0, 0, 0);
+    const uint4 z = make_uint4(0, 0, 0, 0);
     const int total = a.stages * a.stage_bytes;
     for (int i = threadIdx.x * 16; i < total; i += kThreads * 16) *reinterpret_cast<uint4*>(stage0 + i) = z;
     const T* bias = static_cast<const T*>(a.bias);
-    for (int i = threadIdx.x; i < a.npad; i += kThreads)
+    for (int i = threadIdx.x; i < a.slot_w; i += kThreads)
       sbias[i] = (bias != nullptr && i < a.cout) ? Elem<T>::to_f(bias[i]) : 0.f;
+    for (int i = threadIdx.x; i < a.nsteps; i += kThreads)
+      s_adlo[i] = (uint32_t)(((a.a_off[i] + 16) >> 4) & 0x3FFF) | ((uint32_t)((a.lbo[i] >> 4) & 0x3FFF) << 16);
   }
   if (threadIdx.x == 0) {
     for (int s = 0; s < a.stages; ++s) {
-      mbar_init(&full[s], 1);
+      // one (asynchronous) arrival per producer thread, plus the weight copy
+      mbar_init(&full[s], kProducerThreads + (a.wres ? 0 : 1));
       mbar_init(&empty[s], 1);
     }
     for (int s = 0; s < 2; ++s) {
@@ -377,7 +490,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_conv_kernel(const __grid_const
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 1) {
+  if (warp == 4) {
     tmem_alloc(tmem_slot, (uint32_t)a.tmem_cols);
     tmem_relinquish();
   }
@@ -387,15 +500,17 @@ __global__ void __launch_bounds__(kThreads, 1) tc_conv_kernel(const __grid_const
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  const int tiles_per_plane = a.nht * a.nwt;
   const long long units = a.units;
   const uint64_t kWaitNs = 1000000000ull;  // 1 s per wait
-
-  auto wait = [&](uint64_t* bar, uint32_t par) -> bool {
-    uint64_t deadline = global_timer_ns() + kWaitNs;
+  // Bounded wait. `nap` > 0 makes the polling thread sleep between polls so
+  // that warps which only wait (producers, epilogue) leave issue slots to the
+  // MMA warp; the MMA issuer polls without sleeping.
+  auto wait = [&](uint64_t* bar, uint32_t par, uint32_t nap = 0) -> bool {
+    const uint64_t deadline = global_timer_ns() + kWaitNs;
     uint32_t spins = 0;
     while (!mbar_try_wait(bar, par)) {
-      if (((++spins) & 255u) == 0) {
+      if (nap) __nanosleep(nap);
+      if (((++spins) & 63u) == 0) {
         if (*abort_flag) return false;
         if (global_timer_ns() > deadline) {
           *abort_flag = 1;
@@ -406,152 +521,224 @@ __global__ void __launch_bounds__(kThreads, 1) tc_conv_kernel(const __grid_const
     }
     return true;
   };
+  const int set_cols = a.P * a.slot_w * a.mtiles;
 
-  if (warp == 0) {
-    // ---------------- TMA producer ----------------
-    if (lane == 0) {
-      prefetch_tmap(&a.tmap);
-      if (a.wres) {
-        mbar_arrive_expect_tx(wbar, (uint32_t)(a.ks * a.ngroups * a.b_bytes));
-        bulk_load(wres_smem, a.wpack, (uint32_t)(a.ks * a.ngroups * a.b_bytes), wbar);
-      }
-      int stage = 0;
-      uint32_t epar = 1;
-      bool pending[kMaxStages];
-      uint32_t last_par[kMaxStages];
-      for (int s = 0; s < kMaxStages; ++s) { pending[s] = false; last_par[s] = 0; }
-      bool ok = true;
-      for (long long u = blockIdx.x; u < units && ok; u += gridDim.x) {
-        int wi = (int)(u % a.nwt);
-        long long r = u / a.nwt;
-        int hi = (int)(r % a.nht); r /= a.nht;
-        int z = (int)(r % a.od);
-        int nb = (int)(r / a.od);
-        const int w0 = wi * a.wt - a.pw, h0 = hi * a.ht - a.ph;
-        for (int kd = 0; kd < a.ks && ok; ++kd) {
-          const int iz = z + kd - a.pd;
-          for (int g = 0; g < a.ngroups; ++g) {
-            if (!wait(&empty[stage], epar)) { ok = false; break; }
-            uint8_t* sA = stage0 + (size_t)stage * a.stage_bytes;
-            mbar_arrive_expect_tx(&full[stage], a.tx_bytes);
-            for (int cl = 0; cl < a.G; ++cl)
-              tma_load_5d(sA + 128 + cl * a.cpb, &a.tmap, &full[stage], (g * a.G + cl) * 8, w0, h0, iz, nb);
-            if (!a.wres)
-              bulk_load(sA + a.a_bytes, a.wpack + (size_t)(kd * a.ngroups + g) * a.b_bytes,
-                        (uint32_t)a.b_bytes, &full[stage]);
-            pending[stage] = true;
-            last_par[stage] = epar ^ 1;
-            if (++stage == a.stages) { stage = 0; epar ^= 1; }
+  if (warp < 4) {
+    // ---------------- producers: cp.async gather of the halo bricks ----------------
+    const int pt = threadIdx.x;
+    const T* __restrict__ x = static_cast<const T*>(a.x);
+    const int per_row = a.pitch_w * a.G;
+    const int q0w = pt / a.G, q0c = pt - (pt / a.G) * a.G;
+    const int dw128 = kProducerThreads / a.G, dc128 = kProducerThreads - dw128 * a.G;
+    if (pt == 0 && a.wres) {
+      const uint32_t wb = (uint32_t)(a.ngroups * a.b_bytes);
+      mbar_arrive_expect_tx(wbar, wb);
+      bulk_load(wres_smem, a.wpack, wb, wbar);
+    }
+    int stage = 0;
+    uint32_t epar = 1;
+    long long k = 0;
+    bool ok = true;
+    for (long long u = blockIdx.x; u < units && ok; u += gridDim.x) {
+      const int wi = (int)(u % a.nwt);
+      long long r = u / a.nwt;
+      const int hi = (int)(r % a.nht); r /= a.nht;
+      const int zb = (int)(r % a.nzb);
+      const int nb = (int)(r / a.nzb);
+      const int h0 = hi * a.ht - a.ph, w0 = wi * a.wt - a.pw;
+      for (int j = 0; j < a.nin && ok; ++j) {
+        const int iz = zb * a.P - a.pd + j;
+        const bool z_ok = iz >= 0 && iz < a.d;
+        for (int g = 0; g < a.ngroups; ++g) {
+          int got = 1;
+          if (lane == 0) got = wait(&empty[stage], epar, 64) ? 1 : 0;
+          got = __shfl_sync(0xffffffffu, got, 0);
+          if (!got) { ok = false; break; }
+          uint8_t* sbase = stage0 + (size_t)stage * a.stage_bytes;
+          const uint32_t sA = smem_u32(sbase) + 128u;
+          for (int hh = 0; hh < a.pitch_h; ++hh) {
+            const int ih = h0 + hh;
+            const bool r_ok = z_ok && ih >= 0 && ih < a.h;
+            const T* xrow = x + ((((long long)nb * a.d + (r_ok ? iz : 0)) * a.h + (r_ok ? ih : 0)) * a.w) * a.cin +
+                            g * a.G * 8;
+            const uint32_t drow = sA + (uint32_t)(hh * a.pitch_w * 16);
+            int ww = q0w, c = q0c;
+            for (int q = pt; q < per_row; q += kProducerThreads) {
+              const int iw = w0 + ww;
+              const bool ok2 = r_ok && iw >= 0 && iw < a.w;
+              const T* src = ok2 ? xrow + (long long)iw * a.cin + c * 8 : x;
+              cp_async_16(drow + (uint32_t)(c * a.cpb + ww * 16), src, ok2 ? 16u : 0u);
+              ww += dw128;
+              c += dc128;
+              if (c >= a.G) { c -= a.G; ++ww; }
+            }
           }
-        }
-      }
-      // Wait (bounded) until every copy this thread issued has landed, so no
-      // TMA write can outlive the CTA on the error path.
-      if (a.wres) {
-        uint64_t dl = global_timer_ns() + kWaitNs;
-        while (!mbar_try_wait(wbar, 0) && global_timer_ns() < dl) {
-        }
-      }
-      for (int s = 0; s < a.stages; ++s) {
-        if (!pending[s]) continue;
-        uint64_t dl = global_timer_ns() + kWaitNs;
-        while (!mbar_try_wait(&full[s], last_par[s]) && global_timer_ns() < dl) {
+          cp_async_commit();
+          if (pt == 0 && !a.wres) {
+            // weight rows of slots [lo, hi] for every K step and half:
+            // global [g][step][half][ks slots][rows] -> smem [step][half][nsl slots][rows]
+            const int lo = max(0, j - a.ks + 1), hi = min(a.P - 1, j);
+            const int nsl = hi - lo + 1, b0 = (a.ks - 1) - (j - lo);
+            const uint32_t slot_bytes = (uint32_t)(a.slot_w * 16);
+            mbar_arrive_expect_tx(&full[stage], (uint32_t)(a.nsteps * 2 * nsl) * slot_bytes);
+            const uint8_t* gsrc = a.wpack + (size_t)g * a.b_bytes + (size_t)b0 * slot_bytes;
+            uint8_t* sdst = sbase + a.a_bytes;
+            for (int sh = 0; sh < 2 * a.nsteps; ++sh)
+              bulk_load(sdst + (size_t)sh * nsl * slot_bytes, gsrc + (size_t)sh * a.ks * slot_bytes,
+                        (uint32_t)nsl * slot_bytes, &full[stage]);
+          }
+          // this thread's copies of the stage arrive on its full barrier when they land
+          cp_async_arrive_noinc(&full[stage]);
+          ++k;
+          if (++stage == a.stages) { stage = 0; epar ^= 1; }
         }
       }
     }
-  } else if (warp == 1) {
+    // no copy may outlive the CTA
+    cp_async_wait<0>();
+    if (pt == 0 && a.wres) {
+      // no bulk copy may outlive the CTA: wait (bounded) for the weight copy
+      const uint64_t dl = global_timer_ns() + kWaitNs;
+      while (!mbar_try_wait(wbar, 0) && global_timer_ns() < dl) {
+      }
+    }
+  } else if (warp == 4) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       int stage = 0;
       uint32_t fpar = 0;
       uint32_t tpar[2] = {1, 1};
-      int acc = 0;
-      const int nsets = a.nsets;
+      int set = 0;
       bool ok = true;
       if (a.wres && !wait(wbar, 0)) ok = false;
+      const uint32_t bslot = (uint32_t)(a.slot_w * 16);           // bytes of one slot's B rows
+      const int ks = a.ks, Pb = a.P, slot_w = a.slot_w, mtiles = a.mtiles, nsteps = a.nsteps;
+      const int fold = a.fold, ngroups = a.ngroups, nin = a.nin;
+      const uint32_t tile_cols = (uint32_t)(Pb * slot_w);
       for (long long u = blockIdx.x; u < units && ok; u += gridDim.x) {
-        if (!wait(&tempty[acc], tpar[acc])) { ok = false; break; }
-        tpar[acc] ^= 1;
+        if (!wait(&tempty[set], tpar[set])) { ok = false; break; }
+        tpar[set] ^= 1;
         tc_fence_after();
-        const uint32_t dbase = tmem + (uint32_t)(acc * a.mtiles * a.npad);
-        for (int kd = 0; kd < a.ks && ok; ++kd) {
-          for (int g = 0; g < a.ngroups; ++g) {
+        const uint32_t dset = tmem + (uint32_t)(set * set_cols);
+        for (int j = 0; j < nin && ok; ++j) {
+          const int lo = max(0, j - ks + 1), hi = min(Pb - 1, j);
+          const int b0 = (ks - 1) - (j - lo);
+          const int nsl = hi - lo + 1;
+          const bool has_new = j < Pb;  // slot j (== hi) gets its first product here
+          // Steady segments: slots lo..hi in runs of at most `fold` slots, one
+          // MMA each. The first K step of the stage that brings a new slot
+          // (g == 0) runs apart: slots lo..hi-1 accumulate, the new slot hi
+          // starts from zero (accumulate = 0) in an MMA of its own.
+          Segs steady, first;
+          int nst = 0, nfi = 0;
+          for (int o = lo; o <= hi && nst < 4; ++nst) {
+            const int n = min(fold, hi - o + 1);
+            steady.d[nst] = (uint32_t)(o * slot_w);
+            steady.bo[nst] = (uint32_t)(((o - lo) * bslot) >> 4);
+            steady.id[nst] = a.idesc[n];
+            steady.acc[nst] = 1u;
+            o += n;
+          }
+          if (has_new) {
+            for (int o = lo; o <= hi - 1 && nfi < 3; ++nfi) {
+              const int n = min(fold, hi - o);
+              first.d[nfi] = (uint32_t)(o * slot_w);
+              first.bo[nfi] = (uint32_t)(((o - lo) * bslot) >> 4);
+              first.id[nfi] = a.idesc[n];
+              first.acc[nfi] = 1u;
+              o += n;
+            }
+            first.d[nfi] = (uint32_t)(hi * slot_w);
+            first.bo[nfi] = (uint32_t)(((hi - lo) * bslot) >> 4);
+            first.id[nfi] = a.idesc[1];
+            first.acc[nfi] = 0u;
+            ++nfi;
+          }
+          // resident weights keep all ks slots per (step, half); staged ones
+          // only the nsl slots of this input plane
+          const int bslots = a.wres ? ks : nsl;
+          const uint64_t bstep = (uint64_t)((2 * bslots * bslot) >> 4);
+          const uint32_t blbo = (uint32_t)(bslots * bslot);
+          for (int g = 0; g < ngroups; ++g) {
             if (!wait(&full[stage], fpar)) { ok = false; break; }
             tc_fence_after();
-            const uint32_t sA = smem_u32(stage0 + (size_t)stage * a.stage_bytes) + 128;
-            const uint32_t sB =
-                a.wres ? smem_u32(wres_smem + (size_t)(kd * a.ngroups + g) * a.b_bytes)
-                       : smem_u32(stage0 + (size_t)stage * a.stage_bytes + a.a_bytes);
-            const bool first_stage = (kd == 0 && g == 0);
-            // Descriptors: one build per K step, 64-bit adds for the M tiles
-            // (2048 B = 128 descriptor units apart) and K steps of B.
-            const uint64_t bdesc0 = smem_desc(sB, (uint32_t)(a.npad * 16), 128);
-            const uint64_t bstep = (uint64_t)((2 * a.npad * 16) >> 4);
-            for (int j = 0; j < a.nsteps; ++j) {
-              const uint64_t bdesc = bdesc0 + (uint64_t)j * bstep;
-              const uint64_t adesc = smem_desc((uint32_t)((int)sA + a.a_off[j]), (uint32_t)a.lbo[j], 128);
-              const uint32_t accum = (first_stage && j == 0) ? 0u : 1u;
-              uint32_t d = dbase;
-              uint64_t ad = adesc;
-              for (int t = 0; t < a.mtiles; ++t) {
-                mma_f16_ss(d, ad, bdesc, a.idesc, accum);
-                d += (uint32_t)a.npad;
-                ad += 128;
-              }
+            // stage A base in 16-byte units, minus the one-unit bias of s_adlo
+            const uint32_t sA4 = ((smem_u32(stage0 + (size_t)stage * a.stage_bytes) + 128u) >> 4) - 1u;
+            const uint32_t sB = a.wres ? smem_u32(wres_smem + (size_t)g * a.b_bytes) + (uint32_t)b0 * bslot
+                                       : smem_u32(stage0 + (size_t)stage * a.stage_bytes + a.a_bytes);
+            const uint64_t bdesc = smem_desc(sB, blbo, 128);
+            int s0 = 0;
+            if (has_new && g == 0) {
+              issue(mtiles, nfi, s_adlo, 0, 1, sA4, bdesc, bstep, dset, tile_cols, first);
+              s0 = 1;
             }
+            issue(mtiles, nst, s_adlo, s0, nsteps, sA4, bdesc, bstep, dset, tile_cols, steady);
             mma_commit(&empty[stage]);
             if (++stage == a.stages) { stage = 0; fpar ^= 1; }
           }
         }
         if (!ok) break;
-        mma_commit(&tfull[acc]);
-        if (nsets == 2) acc ^= 1;
+        mma_commit(&tfull[set]);
+        if (a.nsets == 2) set ^= 1;
       }
-      // All MMAs issued by this thread complete before TMEM is released.
       mma_commit(mdone);
       wait(mdone, 0);
     }
   } else {
-    // ---------------- epilogue (warps 2..5) ----------------
+    // ---------------- epilogue (warps 5..8) ----------------
     const int q = warp & 3;
     const int row = q * 32 + lane;
     T* __restrict__ y = static_cast<T*>(a.y);
     const bool vec_ok = (a.cout % 8) == 0;
     uint32_t fpar[2] = {0, 0};
-    int acc = 0;
+    int set = 0;
     for (long long u = blockIdx.x; u < units; u += gridDim.x) {
-      int wi = (int)(u % a.nwt);
+      const int wi = (int)(u % a.nwt);
       long long r = u / a.nwt;
-      int hi = (int)(r % a.nht); r /= a.nht;
-      int z = (int)(r % a.od);
-      int nb = (int)(r / a.od);
-      const int h0 = hi * a.ht, w0 = wi * a.wt;
-      if (!wait(&tfull[acc], fpar[acc])) break;
-      fpar[acc] ^= 1;
+      const int hi = (int)(r % a.nht); r /= a.nht;
+      const int zb = (int)(r % a.nzb);
+      const int nb = (int)(r / a.nzb);
+      const int h0 = hi * a.ht, w0 = wi * a.wt, z0 = zb * a.P;
+      int got = 1;
+      if (lane == 0) got = wait(&tfull[set], fpar[set], 128) ? 1 : 0;
+      got = __shfl_sync(0xffffffffu, got, 0);
+      if (!got) break;
+      fpar[set] ^= 1;
       tc_fence_after();
       for (int t = 0; t < a.mtiles; ++t) {
         const int p = t * 128 + row;
         const int hh = p / a.pitch_w;
         const int ww = p - hh * a.pitch_w;
-        const bool valid = hh < a.ht && ww < a.wt && (h0 + hh) < a.oh && (w0 + ww) < a.ow;
-        T* dst = y + ((((long long)nb * a.od + z) * a.oh + (h0 + hh)) * a.ow + (w0 + ww)) * a.cout;
-        const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * a.mtiles * a.npad + t * a.npad);
-        for (int cc = 0; cc < a.npad; cc += 16) {
-          float v[16];
-          tmem_ld_16(tbase + (uint32_t)cc, v);
-          if (valid) store_row16<T>(dst, v, sbias, cc, a.cout, vec_ok);
+        const bool pos_ok = hh < a.ht && ww < a.wt && (h0 + hh) < a.oh && (w0 + ww) < a.ow;
+        for (int o = 0; o < a.P; ++o) {
+          const int z = z0 + o;
+          const bool valid = pos_ok && z < a.od;
+          T* dst = y + ((((long long)nb * a.od + z) * a.oh + (h0 + hh)) * a.ow + (w0 + ww)) * a.cout;
+          const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) +
+                              (uint32_t)(set * set_cols + t * a.P * a.slot_w + o * a.slot_w);
+          int cc = 0;
+          for (; cc + 32 <= a.slot_w; cc += 32) {
+            float v[32];
+            tmem_ld_32(tb + (uint32_t)cc, v);
+            if (valid) store_row<T, 32>(dst, v, sbias, cc, a.cout, vec_ok);
+          }
+          if (cc < a.slot_w) {
+            float v[16];
+            tmem_ld_16(tb + (uint32_t)cc, v);
+            if (valid) store_row<T, 16>(dst, v, sbias, cc, a.cout, vec_ok);
+          }
         }
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[acc]);
-      if (a.nsets == 2) acc ^= 1;
+      if (lane == 0) mbar_arrive(&tempty[set]);
+      if (a.nsets == 2) set ^= 1;
     }
   }
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == 4) {
     tc_fence_after();
     tmem_dealloc(tmem, (uint32_t)a.tmem_cols);
   }
@@ -560,24 +747,6 @@ __global__ void __launch_bounds__(kThreads, 1) tc_conv_kernel(const __grid_const
 // ---------------------------------------------------------------------------
 // Host launch.
 // ---------------------------------------------------------------------------
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static EncodeTiledFn get_encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, []() {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(p);
-  });
-  return fn;
-}
-
 template <typename T>
 static cudaError_t set_smem_attr() {
   static bool done[64] = {false};
@@ -595,44 +764,32 @@ static cudaError_t set_smem_attr() {
 int launch_conv(const ConvPlan& P, const void* x, const void* w_packed, const void* bias, void* y, int dtype,
                 cudaStream_t st) {
   if (((uintptr_t)x & 15) || ((uintptr_t)w_packed & 15)) return R4C_ERR_ALIGN;
-  EncodeTiledFn enc = get_encode_fn();
-  if (!enc) return R4C_ERR_CUDA;
   static_assert(sizeof(TcConvArgs) <= 4096, "kernel argument block too large");
   TcConvArgs a;
   memset(&a, 0, sizeof(a));
-  const cuuint64_t esz = 2;
-  cuuint64_t dims[5] = {(cuuint64_t)P.cin, (cuuint64_t)P.w, (cuuint64_t)P.h, (cuuint64_t)P.d, (cuuint64_t)P.n};
-  cuuint64_t strides[4] = {P.cin * esz, (cuuint64_t)P.w * P.cin * esz, (cuuint64_t)P.h * P.w * P.cin * esz,
-                           (cuuint64_t)P.d * P.h * P.w * P.cin * esz};
-  cuuint32_t box[5] = {8, (cuuint32_t)P.pitch_w, (cuuint32_t)P.pitch_h, 1, 1};
-  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
-  CUresult cr = enc(&a.tmap, dtype == R4C_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
-                    5, const_cast<void*>(x), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                    CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
-                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (cr != CUDA_SUCCESS) return R4C_ERR_INVALID;
-
   std::vector<Step> steps;
-  const int G = P.G;
-  const int cpb = P.cpb;
-  build_steps(P.ks, G, P.pitch_w, cpb, steps);
+  build_steps(P.ks, P.G, P.pitch_w, P.cpb, steps);
+  a.x = x;
   a.wpack = static_cast<const uint8_t*>(w_packed);
   a.bias = bias;
   a.y = y;
-  a.n = P.n; a.od = P.od; a.oh = P.oh; a.ow = P.ow; a.cout = P.cout; a.npad = P.npad;
+  a.n = P.n; a.d = P.d; a.h = P.h; a.w = P.w; a.cin = P.cin;
+  a.od = P.od; a.oh = P.oh; a.ow = P.ow; a.cout = P.cout;
   a.pd = P.pd; a.ph = P.ph; a.pw = P.pw; a.ks = P.ks;
   a.ht = P.ht; a.wt = P.wt;
   a.nht = (P.oh + P.ht - 1) / P.ht;
   a.nwt = (P.ow + P.wt - 1) / P.wt;
-  a.pitch_w = P.pitch_w;
-  a.G = G; a.ngroups = P.ngroups; a.nsteps = (int)steps.size();
+  a.nzb = (P.od + P.P - 1) / P.P;
+  a.pitch_w = P.pitch_w; a.pitch_h = P.pitch_h;
+  a.slot_w = P.npad; a.P = P.P; a.nin = P.nin; a.fold = P.fold;
+  a.G = P.G; a.ngroups = P.ngroups; a.nsteps = (int)steps.size();
   a.mtiles = P.mtiles; a.nsets = P.nsets;
-  a.cpb = cpb; a.a_bytes = P.a_bytes; a.b_bytes = P.b_bytes; a.stage_bytes = P.stage_bytes; a.stages = P.stages;
+  a.cpb = P.cpb; a.a_bytes = P.a_bytes; a.b_bytes = P.b_bytes; a.stage_bytes = P.stage_bytes; a.stages = P.stages;
   a.wres = P.wres; a.wres_bytes = P.wres_bytes;
   a.tmem_cols = P.tmem_cols;
   a.units = P.work_units;
-  a.idesc = sm100::instr_desc_f16(dtype == R4C_BF16, 128, P.npad, 0, 0);
-  a.tx_bytes = (uint32_t)(G * P.pitch_h * P.pitch_w * 16 + (P.wres ? 0 : P.b_bytes));
+  for (int k = 1; k <= 3; ++k)
+    a.idesc[k] = sm100::instr_desc_f16(dtype == R4C_BF16, 128, std::min(256, k * P.npad), 0, 0);
   for (int j = 0; j < a.nsteps; ++j) {
     a.a_off[j] = steps[j].a_off;
     a.lbo[j] = steps[j].lbo;
@@ -652,11 +809,6 @@ int launch_conv(const ConvPlan& P, const void* x, const void* w_packed, const vo
   return e == cudaSuccess ? R4C_OK : R4C_ERR_CUDA;
 }
 
-}  // namespace tc
-}  // namespace r4c
-
-namespace r4c {
-namespace tc {
 // Device address of the error flag for the current device, for kernels in
 // other translation units (device symbols are per translation unit without
 // relocatable device code).
@@ -673,6 +825,7 @@ int* device_error_flag() {
   }
   return ptrs[dev];
 }
+
 }  // namespace tc
 }  // namespace r4c
 
@@ -687,4 +840,3 @@ extern "C" int r4c_device_error(r4c_stream_t stream, int clear) {
   }
   return v;
 }
-

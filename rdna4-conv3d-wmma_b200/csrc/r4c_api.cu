@@ -303,7 +303,7 @@ int r4c_conv3d_fwd(const r4c_conv_desc* desc, const void* x, const void* w_packe
       if (launch_cpad(x, workspace, g, desc->dtype, s) != cudaSuccess) return R4C_ERR_CUDA;
       xin = workspace;
     }
-    return tc::launch_conv(pl, xin, w_packed, bias, y, desc->dtype, s);
+    return tc::launch_conv_tuned(pl, xin, w_packed, bias, y, desc->dtype, s);
   }
   generic::FwdParams p{};
   p.a = x; p.b = w_packed; p.bias = bias; p.out = y;
@@ -325,7 +325,7 @@ int r4c_conv3d_dx(const r4c_conv_desc* desc, const void* go, const void* w_packe
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   tc::ConvPlan pl;
   if (use_tc(desc, R4C_LEG_DX, g, &pl))
-    return tc::launch_conv(pl, go, w_packed, nullptr, dx, desc->dtype, s);
+    return tc::launch_conv_tuned(pl, go, w_packed, nullptr, dx, desc->dtype, s);
   // dX of a stride-1 conv is a conv of dY with the flipped, transposed kernel
   // and padding k-1-p (negative padding crops).
   generic::FwdParams p{};

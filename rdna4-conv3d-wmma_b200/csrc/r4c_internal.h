@@ -86,6 +86,10 @@ cudaError_t pack_weight(const ConvPlan& pl, bool flip_for_dx, int cin_real, cons
                         int src_dtype, void* w_packed, int dtype, cudaStream_t st);
 int launch_conv(const ConvPlan& pl, const void* x, const void* w_packed, const void* bias,
                 void* y, int dtype, cudaStream_t st);
+// launch_conv with the plan found fastest on this device for this shape
+// (timed on the first call, then cached); same packed weights as `pl`.
+int launch_conv_tuned(const ConvPlan& pl, const void* x, const void* w_packed, const void* bias,
+                      void* y, int dtype, cudaStream_t st);
 
 // Device address of the kernels' bounded-wait error flag (current device).
 int* device_error_flag();

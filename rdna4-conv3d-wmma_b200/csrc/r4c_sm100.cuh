@@ -102,15 +102,24 @@ __device__ __forceinline__ void cp_async_wait() {
 }
 
 // ---- tcgen05 --------------------------------------------------------------
+// The .sync.aligned tcgen05 instructions (alloc, dealloc, relinquish, ld)
+// must be executed by all 32 lanes of the warp together. A warp that arrives
+// from divergent code (a lane-0-only loop, a predicated store) is not
+// guaranteed to have reconverged, and a split warp executing them raises an
+// illegal-instruction fault; every wrapper below therefore starts with
+// __syncwarp(), which reconverges the full warp.
 __device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+  __syncwarp();
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
                "r"(ncols)
                : "memory");
 }
 __device__ __forceinline__ void tmem_relinquish() {
+  __syncwarp();
   asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
 }
 __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  __syncwarp();
   asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
 }
 __device__ __forceinline__ void tc_fence_before() {
@@ -131,6 +140,25 @@ __device__ __forceinline__ void mma_f16_ss(uint32_t d_tmem, uint64_t adesc, uint
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
 }
+// Warp-wide forms: the whole (converged) warp executes the instruction and
+// the elected lane (always lane 0 of a full warp) issues it. Keeping the
+// issuing code warp-uniform lets the compiler hold descriptors in uniform
+// registers; issuing from a lane-0-only branch costs ~25% more per MMA.
+__device__ __forceinline__ void mma_f16_ss_warp(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                                uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred e, p;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+__device__ __forceinline__ void mma_commit_warp(uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(smem_u32(bar))
+      : "memory");
+}
 // Arrive on `bar` once every tcgen05 op issued so far by this thread completes.
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
@@ -140,6 +168,7 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
 // 32 lanes x 16 columns of 32-bit from TMEM; thread i gets lane base+i.
 __device__ __forceinline__ void tmem_ld_16(uint32_t taddr, float (&v)[16]) {
   uint32_t r[16];
+  __syncwarp();
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, "
       "%13, %14, %15}, [%16];"
@@ -161,6 +190,7 @@ __device__ __forceinline__ void tmem_ld_16(uint32_t taddr, float (&v)[16]) {
 // as in/out operands so that no use of them can be scheduled before it.
 __device__ __forceinline__ void tmem_ld_32(uint32_t taddr, float (&v)[32]) {
   uint32_t r[32];
+  __syncwarp();
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, "
       "%13, %14, %15}, [%16];"
@@ -185,6 +215,22 @@ __device__ __forceinline__ void tmem_ld_32(uint32_t taddr, float (&v)[32]) {
                : "memory");
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Write zeros to 32 lanes x 16 columns of TMEM (thread i: lane base+i), and
+// wait for this thread's TMEM stores.
+__device__ __forceinline__ void tmem_zero_16(uint32_t taddr) {
+  const uint32_t z = 0u;
+  __syncwarp();
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, "
+      "%1, %1};" ::"r"(taddr),
+      "r"(z)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() {
+  __syncwarp();
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
 // No-swizzle smem matrix descriptor (addresses/offsets in bytes).

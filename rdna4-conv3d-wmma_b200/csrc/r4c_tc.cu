@@ -31,13 +31,17 @@
 //    double-buffered when they fit); four epilogue warps read them with
 //    tcgen05.ld, add bias, round and store NDHWC.
 //
-// Warp roles (288 threads): warps 0-3 producers, warp 4 MMA issuer + TMEM
-// owner, warps 5-8 epilogue (TMEM lane quarter = warp % 4). Every wait is
+// Warp roles (416 threads): warps 0-7 producers, warp 8 MMA issuer + TMEM
+// owner, warps 9-12 epilogue (TMEM lane quarter = warp % 4). Every wait is
 // bounded (1 s); a timeout sets the device error flag and the kernel winds
 // down (copies drained, TMEM released) instead of hanging.
 #include <cuda.h>
 
 #include <algorithm>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
 #include <mutex>
 #include <vector>
 
@@ -53,8 +57,11 @@ namespace tc {
 constexpr int kMaxSteps = 64;
 constexpr int kMaxStages = 8;
 constexpr int kMaxMt = 8;  // M tiles per unit (the issue loop is unrolled over them)
-constexpr int kThreads = 288;
-constexpr int kProducerThreads = 128;
+constexpr int kMaxEntries = 8;  // 16-byte copies per producer thread per brick row
+constexpr int kProducerWarps = 4;  // 8 warps copy faster alone (15.2 vs 11.4 B/clk/SM) but measured no faster in the kernel
+constexpr int kProducerThreads = 32 * kProducerWarps;
+constexpr int kMmaWarp = kProducerWarps;
+constexpr int kThreads = kProducerThreads + 32 + 128;
 constexpr int kSmemMax = 232448;  // 227 KB opt-in dynamic shared memory
 constexpr int kHeader = 2048;     // barriers + bias
 
@@ -146,17 +153,47 @@ static int num_sms() {
 // (measured on B200: 45 for N <= 32, 56 for 96, 64 for 128, 128 for 256).
 static double mma_clk(int n) { return std::max({n / 2.0, 40.0 + n / 6.0, 45.0}); }
 
-bool plan_conv(int n, int d, int h, int w, int cin, int cout, int ks, int pd, int ph, int pw, ConvPlan* pl) {
+// Tuning override: R4C_TC_PLAN="ht=4,nw=8,P=8,G=3,wres=1,stages=4" limits
+// the search to candidates with the given values (any subset of the keys;
+// stages caps the stage count). Unset keys are searched as usual.
+struct PlanForce {
+  int ht = 0, nw = 0, P = 0, G = 0, wres = -1, stages = 0;
+};
+static PlanForce plan_force() {
+  PlanForce f;
+  const char* e = getenv("R4C_TC_PLAN");
+  if (!e) return f;
+  char key[16];
+  int val = 0, used = 0;
+  while (*e && sscanf(e, " %15[a-zA-Z_] = %d%n", key, &val, &used) == 2) {
+    if (!strcmp(key, "ht")) f.ht = val;
+    else if (!strcmp(key, "nw")) f.nw = val;
+    else if (!strcmp(key, "P")) f.P = val;
+    else if (!strcmp(key, "G")) f.G = val;
+    else if (!strcmp(key, "wres")) f.wres = val;
+    else if (!strcmp(key, "stages")) f.stages = val;
+    e += used;
+    while (*e == ',' || *e == ' ') ++e;
+  }
+  return f;
+}
+
+// Every feasible plan of the conv, with its modelled cost in est_cycles, is
+// passed to visit(). G_only > 0 restricts the chunk group size (the packed
+// weight layout depends on G only).
+template <typename F>
+static void enumerate_plans(int n, int d, int h, int w, int cin, int cout, int ks, int pd, int ph, int pw, int G_only,
+                            const PlanForce& force, F&& visit) {
   ConvPlan P{};
   P.ok = false;
-  if (ks != 1 && ks != 3) return false;
-  if (cin % 8 != 0 || cin <= 0 || cout <= 0 || cout > 256) return false;
-  if (n <= 0 || d <= 0 || h <= 0 || w <= 0) return false;
+  if (ks != 1 && ks != 3) return;
+  if (cin % 8 != 0 || cin <= 0 || cout <= 0 || cout > 256) return;
+  if (n <= 0 || d <= 0 || h <= 0 || w <= 0) return;
   P.od = d + 2 * pd - (ks - 1);
   P.oh = h + 2 * ph - (ks - 1);
   P.ow = w + 2 * pw - (ks - 1);
-  if (P.od <= 0 || P.oh <= 0 || P.ow <= 0) return false;
-  if (pd > 8 || ph > 8 || pw > 8 || pd < -8 || ph < -8 || pw < -8) return false;
+  if (P.od <= 0 || P.oh <= 0 || P.ow <= 0) return;
+  if (pd > 8 || ph > 8 || pw > 8 || pd < -8 || ph < -8 || pw < -8) return;
   P.n = n; P.d = d; P.h = h; P.w = w;
   P.cin = cin; P.cout = cout; P.ks = ks; P.pd = pd; P.ph = ph; P.pw = pw;
   P.c8 = cin / 8;
@@ -165,27 +202,41 @@ bool plan_conv(int n, int d, int h, int w, int cin, int cout, int ks, int pd, in
 
   std::vector<int> gs;
   if (P.c8 % 2 == 1) {
-    if (P.c8 > 13) return false;
+    if (P.c8 > 13) return;
     gs.push_back(P.c8);
   } else {
     for (int g = std::min(P.c8, 14); g >= 2; g -= 2)
       if (P.c8 % g == 0) gs.push_back(g);
   }
   const int wt_max = 254 - (ks - 1);
-  const int nw = (P.ow + wt_max - 1) / wt_max;
-  const int wt = (P.ow + nw - 1) / nw;
+  const int nw_min = (P.ow + wt_max - 1) / wt_max;
   const int sms = num_sms();
 
-  double best = 1e300;
   for (int G : gs) {
+    if (force.G && G != force.G) continue;
+    if (G_only > 0 && G != G_only) continue;
     const int nsteps = steps_per_stage(ks, G);
     if (nsteps > kMaxSteps) continue;
     const int ngroups = P.c8 / G;
     const int b_bytes = nsteps * 2 * ks * P.npad * 16;
     const int wbytes = ngroups * b_bytes;
-    for (int wres = 1; wres >= 0; --wres) {
+    // a brick row (wt + k - 1 positions x G chunks) must fit the producers'
+    // fixed per-thread copy slots
+    const int wt_cap = kMaxEntries * kProducerThreads / G - (ks - 1);
+    if (wt_cap < 1) continue;
+    const int nw_lo = std::max(nw_min, (P.ow + wt_cap - 1) / wt_cap);
+    const int nw_a = force.nw ? force.nw : nw_lo, nw_b = force.nw ? force.nw : nw_lo + 8;
+    for (int nw = nw_a; nw <= nw_b && nw <= P.ow; ++nw) {
+     const int wt = (P.ow + nw - 1) / nw;
+     // the kernel decodes ceil(ow / wt) tiles per row; skip counts that differ
+     if ((P.ow + wt - 1) / wt != nw) continue;
+     const int entries = ((wt + ks - 1) * G + kProducerThreads - 1) / kProducerThreads;
+     if (entries > kMaxEntries) continue;
+     for (int wres = 1; wres >= 0; --wres) {
+      if (force.wres >= 0 && wres != force.wres) continue;
       if (wres && wbytes > 96 * 1024) continue;
       for (int ht = 1; ht <= P.oh && ht <= 254 - (ks - 1); ++ht) {
+        if (force.ht && ht != force.ht) continue;
         const int pitch_w = wt + ks - 1, pitch_h = ht + ks - 1;
         const int span = (ht - 1) * pitch_w + wt;
         const int mtiles = (span + 127) / 128;
@@ -197,11 +248,12 @@ bool plan_conv(int n, int d, int h, int w, int cin, int cout, int ks, int pd, in
         const int avail = kSmemMax - kHeader - (wres ? round_up(wbytes, 128) : 0);
         const int tiles_h = (P.oh + ht - 1) / ht;
         for (int Pb = 1; Pb <= std::min(P.od, 16); ++Pb) {
+          if (force.P && Pb != force.P) continue;
           // a stage holds the A brick and, unless resident, the weight slots
           // of the output planes its input plane feeds (at most min(ks, Pb))
           const int sb = std::min(ks, Pb) * nsteps * 2 * P.npad * 16;
           const int stage = round_up(a_bytes + (wres ? 0 : sb), 128);
-          const int stages = std::min(kMaxStages, avail / stage);
+          const int stages = std::min(force.stages ? force.stages : kMaxStages, std::min(kMaxStages, avail / stage));
           if (stages < 2) break;
           int nsets = 2;
           if (2 * Pb * P.npad * mtiles > 512) nsets = 1;
@@ -220,17 +272,25 @@ bool plan_conv(int n, int d, int h, int w, int cin, int cout, int ks, int pd, in
             }
             mma += t * nsteps * mtiles * ngroups;
           }
-          const double load = (double)nin * ngroups * (G * pitch_h * pitch_w * 16.0 + (wres ? 0.0 : sb)) / 64.0;
-          const double epi = (double)Pb * mtiles * (P.npad / 16.0) * 40.0;
-          double t_unit = std::max(mma, load) + 150.0 * nin * ngroups;
+          // producer clocks per stage (measured on B200): the halo brick
+          // arrives by 16-byte cp.async at ~3 B/clk per producer warp that
+          // has copies in a brick row (11.4 B/clk per SM with four), plus
+          // ~40 clk of addressing per row; the staged weight slots arrive by
+          // bulk copies at ~30 B/clk, in parallel
+          const int busy_warps = std::min(kProducerWarps, (pitch_w * G + 31) / 32);
+          const double cp_rate = std::min(11.4, 3.0 * busy_warps);
+          const double load =
+              (double)nin * ngroups *
+              (std::max(G * pitch_h * pitch_w * 16.0 / cp_rate + 40.0 * pitch_h, wres ? 0.0 : sb / 30.0) + 150.0);
+          // epilogue clocks per unit: per (tile, plane) the TMEM reads (one
+          // wait per 32 columns), 16-byte stores of 8 channels, addressing
+          const double epi = (double)Pb * mtiles * (((P.npad + 31) / 32) * 100.0 + ((cout + 7) / 8) * 12.0 + 40.0);
+          double t_unit = std::max(mma, load) + 100.0 * nin * ngroups;
           t_unit = nsets == 2 ? std::max(t_unit, epi) : t_unit + epi;
           const long long units = (long long)n * ((P.od + Pb - 1) / Pb) * tiles_h * nw;
           const long long waves = (units + sms - 1) / sms;
-          // streaming the weights per stage competes with the tensor core for
-          // shared-memory bandwidth even when it hides under the MMAs
-          const double est = (double)waves * (t_unit + (wres ? 0.0 : 0.1 * load));
-          if (est < best) {
-            best = est;
+          const double est = (double)waves * t_unit;
+          {
             P.G = G; P.ngroups = ngroups; P.nsteps = nsteps;
             P.wt = wt; P.ht = ht; P.pitch_w = pitch_w; P.pitch_h = pitch_h;
             P.cpb = cpb; P.mtiles = mtiles; P.nsets = nsets;
@@ -246,14 +306,78 @@ bool plan_conv(int n, int d, int h, int w, int cin, int cout, int ks, int pd, in
             P.grid = (int)std::min<long long>(units, sms);
             P.est_cycles = est;
             P.ok = true;
+            visit(static_cast<const ConvPlan&>(P));
           }
         }
       }
+     }
     }
   }
-  if (!P.ok) return false;
-  if (pl) *pl = P;
+}
+
+struct PlanKey {
+  int v[12];
+  bool operator<(const PlanKey& o) const { return std::lexicographical_compare(v, v + 12, o.v, o.v + 12); }
+};
+
+// Best plan by the cost model; cached per shape and device (the search
+// visits thousands of candidates) unless the tuning override is set.
+bool plan_conv(int n, int d, int h, int w, int cin, int cout, int ks, int pd, int ph, int pw, ConvPlan* pl) {
+  static std::map<PlanKey, ConvPlan> cache;
+  static std::mutex mu;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const PlanKey key{{n, d, h, w, cin, cout, ks, pd, ph, pw, dev, 0}};
+  const PlanForce force = plan_force();
+  const bool forced = getenv("R4C_TC_PLAN") != nullptr;
+  if (!forced) {
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) {
+      if (!it->second.ok) return false;
+      if (pl) *pl = it->second;
+      return true;
+    }
+  }
+  ConvPlan best{};
+  best.ok = false;
+  enumerate_plans(n, d, h, w, cin, cout, ks, pd, ph, pw, 0, force, [&](const ConvPlan& c) {
+    if (!best.ok || c.est_cycles < best.est_cycles) best = c;
+  });
+  if (!forced) {
+    std::lock_guard<std::mutex> lk(mu);
+    cache[key] = best;
+  }
+  if (!best.ok) return false;
+  if (pl) *pl = best;
   return true;
+}
+
+// Candidates for on-device tuning: the plans with the model's chunk group
+// size G (same packed weights, bit-identical results) ranked by modelled
+// cost, top `k_top`, plus the cheapest of each brick-row count so that a
+// model error in the halo/row trade-off cannot hide the fastest shape.
+static std::vector<ConvPlan> plan_candidates(const ConvPlan& m, int k_top) {
+  std::vector<ConvPlan> all;
+  PlanForce none;
+  enumerate_plans(m.n, m.d, m.h, m.w, m.cin, m.cout, m.ks, m.pd, m.ph, m.pw, m.G, none,
+                  [&](const ConvPlan& c) { all.push_back(c); });
+  std::sort(all.begin(), all.end(), [](const ConvPlan& a, const ConvPlan& b) { return a.est_cycles < b.est_cycles; });
+  std::vector<ConvPlan> out;
+  auto same = [](const ConvPlan& a, const ConvPlan& b) {
+    return a.ht == b.ht && a.wt == b.wt && a.P == b.P && a.wres == b.wres && a.stages == b.stages;
+  };
+  auto add = [&](const ConvPlan& c) {
+    for (const ConvPlan& o : out)
+      if (same(o, c)) return;
+    out.push_back(c);
+  };
+  for (size_t i = 0; i < all.size() && (int)out.size() < k_top; ++i) add(all[i]);
+  for (int ht : {1, 2, 4, 8, 16}) {
+    for (const ConvPlan& c : all)
+      if (c.ht == ht) { add(c); break; }
+  }
+  return out;
 }
 
 size_t packed_bytes(const ConvPlan& P) { return (size_t)P.ngroups * P.b_bytes; }
@@ -362,76 +486,83 @@ __device__ __forceinline__ void store_row(T* dst, const float (&v)[NV], const fl
   }
 }
 
-// MMA issue for K steps [s0, s1) of one stage. MT tiles x NS slot segments
-// per step, fully unrolled, and the step loop unrolled so that every loop
-// iteration carries at least four MMAs: the issuing thread's scalar work for
-// one MMA (descriptor arithmetic, the table load, the uniform-register moves)
-// is a dependent chain of ~100 clocks, so MMAs issued one per iteration run
-// at that rate instead of the tensor pipe's 45-64 clocks; an unrolled block
-// lets those chains overlap.
+// MMA issue for the nsteps K steps of one stage (one thread). MT tiles x NS slot segments per step are
+// fully unrolled and four steps go per loop iteration: a loop iteration
+// costs the issuing warp a ~40-clock bubble (branch resolution after an
+// MMA), which straight-line MMAs hide, so one MMA per iteration runs at
+// ~105 clocks instead of the tensor pipe's 56-64 (measured on B200).
 //   adlo[s]  : low descriptor word of step s (A address field, biased by one
 //              16-byte unit, and LBO), relative to the stage base sA4
 //   bd0      : B descriptor of step 0; step s adds s * bstep
-//   d[k], bo[k], id[k], acc[k]: TMEM column, B offset (16-byte units),
-//              instruction descriptor and accumulate flag of segment k
-struct Segs {
-  uint32_t d[4];
-  uint32_t bo[4];
-  uint32_t id[4];
-  uint32_t acc[4];
-};
-
+//   dk, bk, ik: TMEM column offset, B offset (16-byte units) and
+//              instruction descriptor of slot segment k
+// Every MMA accumulates: the epilogue zeroes the accumulators it drains.
 template <int MT, int NS>
-__device__ __forceinline__ void issue_steps(const uint32_t* __restrict__ adlo, int s0, int s1, uint32_t sA4,
+__device__ __forceinline__ void issue_steps(const uint32_t* __restrict__ adlo, int nsteps, uint32_t sA4,
                                             uint64_t bd0, uint64_t bstep, uint32_t dbase, uint32_t tile_cols,
-                                            const Segs& sg) {
+                                            uint32_t d0, uint32_t d1, uint32_t d2, uint32_t b0, uint32_t b1,
+                                            uint32_t b2, uint32_t i0, uint32_t i1, uint32_t i2) {
   constexpr uint64_t kAHi = (uint64_t)((128u >> 4) | (1u << 14)) << 32;  // SBO 128 B, version 1
   constexpr int U = (MT * NS >= 4) ? 1 : ((MT * NS >= 2) ? 2 : 4);
-  uint32_t d[NS], bo[NS], id[NS], acc[NS];
+  const uint32_t dk[3] = {dbase + d0, dbase + d1, dbase + d2};
+  const uint32_t bk[3] = {b0, b1, b2};
+  const uint32_t ik[3] = {i0, i1, i2};
+  int s = 0;
+#pragma unroll 1
+  for (; s + U <= nsteps; s += U) {
 #pragma unroll
-  for (int k = 0; k < NS; ++k) {
-    d[k] = dbase + sg.d[k];
-    bo[k] = sg.bo[k];
-    id[k] = sg.id[k];
-    acc[k] = sg.acc[k];
+    for (int q = 0; q < U; ++q) {
+      const uint64_t ad = kAHi | (uint64_t)(adlo[s + q] + sA4);
+      const uint64_t bd = bd0 + (uint64_t)(s + q) * bstep;
+#pragma unroll
+      for (int t = 0; t < MT; ++t)
+#pragma unroll
+        for (int k = 0; k < NS; ++k)
+          mma_f16_ss(dk[k] + (uint32_t)t * tile_cols, ad + (uint64_t)(t * 128), bd + bk[k], ik[k], 1u);
+    }
   }
-#pragma unroll U
-  for (int s = s0; s < s1; ++s) {
+#pragma unroll 1
+  for (; s < nsteps; ++s) {
     const uint64_t ad = kAHi | (uint64_t)(adlo[s] + sA4);
     const uint64_t bd = bd0 + (uint64_t)s * bstep;
 #pragma unroll
     for (int t = 0; t < MT; ++t)
 #pragma unroll
       for (int k = 0; k < NS; ++k)
-        mma_f16_ss(d[k] + (uint32_t)t * tile_cols, ad + (uint64_t)(t * 128), bd + bo[k], id[k], acc[k]);
+        mma_f16_ss(dk[k] + (uint32_t)t * tile_cols, ad + (uint64_t)(t * 128), bd + bk[k], ik[k], 1u);
   }
 }
+
+#define R4C_ISSUE_ARGS adlo, nsteps, sA4, bd0, bstep, dbase, tile_cols, d0, d1, d2, b0, b1, b2, i0, i1, i2
 
 template <int MT>
-__device__ __forceinline__ void issue_ns(int ns, const uint32_t* adlo, int s0, int s1, uint32_t sA4, uint64_t bd0,
-                                         uint64_t bstep, uint32_t dbase, uint32_t tile_cols, const Segs& sg) {
+__device__ __forceinline__ void issue_ns(int ns, const uint32_t* adlo, int nsteps, uint32_t sA4, uint64_t bd0,
+                                         uint64_t bstep, uint32_t dbase, uint32_t tile_cols, uint32_t d0,
+                                         uint32_t d1, uint32_t d2, uint32_t b0, uint32_t b1, uint32_t b2,
+                                         uint32_t i0, uint32_t i1, uint32_t i2) {
   switch (ns) {
-    case 1: issue_steps<MT, 1>(adlo, s0, s1, sA4, bd0, bstep, dbase, tile_cols, sg); break;
-    case 2: issue_steps<MT, 2>(adlo, s0, s1, sA4, bd0, bstep, dbase, tile_cols, sg); break;
-    case 3: issue_steps<MT, 3>(adlo, s0, s1, sA4, bd0, bstep, dbase, tile_cols, sg); break;
-    default: issue_steps<MT, 4>(adlo, s0, s1, sA4, bd0, bstep, dbase, tile_cols, sg); break;
+    case 1: issue_steps<MT, 1>(R4C_ISSUE_ARGS); break;
+    case 2: issue_steps<MT, 2>(R4C_ISSUE_ARGS); break;
+    default: issue_steps<MT, 3>(R4C_ISSUE_ARGS); break;
   }
 }
 
-__device__ __forceinline__ void issue(int mt, int ns, const uint32_t* adlo, int s0, int s1, uint32_t sA4,
-                                      uint64_t bd0, uint64_t bstep, uint32_t dbase, uint32_t tile_cols,
-                                      const Segs& sg) {
+__device__ __forceinline__ void issue(int mt, int ns, const uint32_t* adlo, int nsteps, uint32_t sA4, uint64_t bd0,
+                                      uint64_t bstep, uint32_t dbase, uint32_t tile_cols, uint32_t d0, uint32_t d1,
+                                      uint32_t d2, uint32_t b0, uint32_t b1, uint32_t b2, uint32_t i0, uint32_t i1,
+                                      uint32_t i2) {
   switch (mt) {
-    case 1: issue_ns<1>(ns, adlo, s0, s1, sA4, bd0, bstep, dbase, tile_cols, sg); break;
-    case 2: issue_ns<2>(ns, adlo, s0, s1, sA4, bd0, bstep, dbase, tile_cols, sg); break;
-    case 3: issue_ns<3>(ns, adlo, s0, s1, sA4, bd0, bstep, dbase, tile_cols, sg); break;
-    case 4: issue_ns<4>(ns, adlo, s0, s1, sA4, bd0, bstep, dbase, tile_cols, sg); break;
-    case 5: issue_ns<5>(ns, adlo, s0, s1, sA4, bd0, bstep, dbase, tile_cols, sg); break;
-    case 6: issue_ns<6>(ns, adlo, s0, s1, sA4, bd0, bstep, dbase, tile_cols, sg); break;
-    case 7: issue_ns<7>(ns, adlo, s0, s1, sA4, bd0, bstep, dbase, tile_cols, sg); break;
-    default: issue_ns<8>(ns, adlo, s0, s1, sA4, bd0, bstep, dbase, tile_cols, sg); break;
+    case 1: issue_ns<1>(ns, R4C_ISSUE_ARGS); break;
+    case 2: issue_ns<2>(ns, R4C_ISSUE_ARGS); break;
+    case 3: issue_ns<3>(ns, R4C_ISSUE_ARGS); break;
+    case 4: issue_ns<4>(ns, R4C_ISSUE_ARGS); break;
+    case 5: issue_ns<5>(ns, R4C_ISSUE_ARGS); break;
+    case 6: issue_ns<6>(ns, R4C_ISSUE_ARGS); break;
+    case 7: issue_ns<7>(ns, R4C_ISSUE_ARGS); break;
+    default: issue_ns<8>(ns, R4C_ISSUE_ARGS); break;
   }
 }
+#undef R4C_ISSUE_ARGS
 
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1) tc_conv_kernel(const __grid_constant__ TcConvArgs a) {
@@ -490,7 +621,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_conv_kernel(const __grid_const
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 4) {
+  if (warp == kMmaWarp) {
     tmem_alloc(tmem_slot, (uint32_t)a.tmem_cols);
     tmem_relinquish();
   }
@@ -523,13 +654,29 @@ __global__ void __launch_bounds__(kThreads, 1) tc_conv_kernel(const __grid_const
   };
   const int set_cols = a.P * a.slot_w * a.mtiles;
 
-  if (warp < 4) {
+  if (warp < kProducerWarps) {
     // ---------------- producers: cp.async gather of the halo bricks ----------------
     const int pt = threadIdx.x;
     const T* __restrict__ x = static_cast<const T*>(a.x);
+    // A brick row is pitch_w positions x G chunks = per_row 16-byte copies;
+    // copy q goes to thread q % 128 as its entry q / 128 (at most kMaxEntries,
+    // which the planner guarantees). Consecutive threads take consecutive
+    // chunks of a position, so a warp reads 512 contiguous bytes. The
+    // shared/global offsets of every entry are fixed for the whole kernel,
+    // so a copy costs a handful of independent instructions.
     const int per_row = a.pitch_w * a.G;
-    const int q0w = pt / a.G, q0c = pt - (pt / a.G) * a.G;
-    const int dw128 = kProducerThreads / a.G, dc128 = kProducerThreads - dw128 * a.G;
+    uint32_t soff[kMaxEntries];
+    int goff[kMaxEntries], wpos[kMaxEntries];
+    uint32_t qmask = 0;
+#pragma unroll
+    for (int e = 0; e < kMaxEntries; ++e) {
+      const int q = pt + e * kProducerThreads;
+      const int ww = q / a.G, c = q - (q / a.G) * a.G;
+      soff[e] = (uint32_t)(c * a.cpb + ww * 16);
+      goff[e] = ww * a.cin + c * 8;
+      wpos[e] = ww;
+      if (q < per_row) qmask |= 1u << e;
+    }
     if (pt == 0 && a.wres) {
       const uint32_t wb = (uint32_t)(a.ngroups * a.b_bytes);
       mbar_arrive_expect_tx(wbar, wb);
@@ -537,7 +684,6 @@ __global__ void __launch_bounds__(kThreads, 1) tc_conv_kernel(const __grid_const
     }
     int stage = 0;
     uint32_t epar = 1;
-    long long k = 0;
     bool ok = true;
     for (long long u = blockIdx.x; u < units && ok; u += gridDim.x) {
       const int wi = (int)(u % a.nwt);
@@ -546,6 +692,14 @@ __global__ void __launch_bounds__(kThreads, 1) tc_conv_kernel(const __grid_const
       const int zb = (int)(r % a.nzb);
       const int nb = (int)(r / a.nzb);
       const int h0 = hi * a.ht - a.ph, w0 = wi * a.wt - a.pw;
+      // entries whose input column lies inside the image for this unit
+      uint32_t wmask = 0;
+#pragma unroll
+      for (int e = 0; e < kMaxEntries; ++e) {
+        const int iw = w0 + wpos[e];
+        if (((qmask >> e) & 1u) && iw >= 0 && iw < a.w) wmask |= 1u << e;
+      }
+      const long long wofs = (long long)w0 * a.cin;  // may be negative; only added to in-image offsets
       for (int j = 0; j < a.nin && ok; ++j) {
         const int iz = zb * a.P - a.pd + j;
         const bool z_ok = iz >= 0 && iz < a.d;
@@ -559,18 +713,17 @@ __global__ void __launch_bounds__(kThreads, 1) tc_conv_kernel(const __grid_const
           for (int hh = 0; hh < a.pitch_h; ++hh) {
             const int ih = h0 + hh;
             const bool r_ok = z_ok && ih >= 0 && ih < a.h;
-            const T* xrow = x + ((((long long)nb * a.d + (r_ok ? iz : 0)) * a.h + (r_ok ? ih : 0)) * a.w) * a.cin +
-                            g * a.G * 8;
+            const uint32_t m = r_ok ? wmask : 0u;
+            const long long rbase =
+                (((long long)nb * a.d + (r_ok ? iz : 0)) * a.h + (r_ok ? ih : 0)) * a.w * a.cin + wofs + g * a.G * 8;
             const uint32_t drow = sA + (uint32_t)(hh * a.pitch_w * 16);
-            int ww = q0w, c = q0c;
-            for (int q = pt; q < per_row; q += kProducerThreads) {
-              const int iw = w0 + ww;
-              const bool ok2 = r_ok && iw >= 0 && iw < a.w;
-              const T* src = ok2 ? xrow + (long long)iw * a.cin + c * 8 : x;
-              cp_async_16(drow + (uint32_t)(c * a.cpb + ww * 16), src, ok2 ? 16u : 0u);
-              ww += dw128;
-              c += dc128;
-              if (c >= a.G) { c -= a.G; ++ww; }
+#pragma unroll
+            for (int e = 0; e < kMaxEntries; ++e) {
+              if ((qmask >> e) & 1u) {
+                const bool v = (m >> e) & 1u;
+                const T* src = v ? x + (rbase + goff[e]) : x;
+                cp_async_16(drow + soff[e], src, v ? 16u : 0u);
+              }
             }
           }
           cp_async_commit();
@@ -589,7 +742,6 @@ __global__ void __launch_bounds__(kThreads, 1) tc_conv_kernel(const __grid_const
           }
           // this thread's copies of the stage arrive on its full barrier when they land
           cp_async_arrive_noinc(&full[stage]);
-          ++k;
           if (++stage == a.stages) { stage = 0; epar ^= 1; }
         }
       }
@@ -602,96 +754,90 @@ __global__ void __launch_bounds__(kThreads, 1) tc_conv_kernel(const __grid_const
       while (!mbar_try_wait(wbar, 0) && global_timer_ns() < dl) {
       }
     }
-  } else if (warp == 4) {
-    // ---------------- MMA issuer ----------------
+  } else if (warp == kMmaWarp) {
+    // ---------------- MMA issuer (lane 0) ----------------
+    // One thread issues. A warp-wide issuer (elected lane, uniform
+    // descriptors) issues each MMA slightly faster in isolation, but its 31
+    // idle lanes wait in warp-synchronous instructions that take issue slots
+    // from the producer warp sharing the sub-partition; measured slower.
     if (lane == 0) {
-      int stage = 0;
-      uint32_t fpar = 0;
-      uint32_t tpar[2] = {1, 1};
-      int set = 0;
-      bool ok = true;
-      if (a.wres && !wait(wbar, 0)) ok = false;
-      const uint32_t bslot = (uint32_t)(a.slot_w * 16);           // bytes of one slot's B rows
-      const int ks = a.ks, Pb = a.P, slot_w = a.slot_w, mtiles = a.mtiles, nsteps = a.nsteps;
-      const int fold = a.fold, ngroups = a.ngroups, nin = a.nin;
-      const uint32_t tile_cols = (uint32_t)(Pb * slot_w);
-      for (long long u = blockIdx.x; u < units && ok; u += gridDim.x) {
-        if (!wait(&tempty[set], tpar[set])) { ok = false; break; }
-        tpar[set] ^= 1;
-        tc_fence_after();
-        const uint32_t dset = tmem + (uint32_t)(set * set_cols);
-        for (int j = 0; j < nin && ok; ++j) {
-          const int lo = max(0, j - ks + 1), hi = min(Pb - 1, j);
-          const int b0 = (ks - 1) - (j - lo);
-          const int nsl = hi - lo + 1;
-          const bool has_new = j < Pb;  // slot j (== hi) gets its first product here
-          // Steady segments: slots lo..hi in runs of at most `fold` slots, one
-          // MMA each. The first K step of the stage that brings a new slot
-          // (g == 0) runs apart: slots lo..hi-1 accumulate, the new slot hi
-          // starts from zero (accumulate = 0) in an MMA of its own.
-          Segs steady, first;
-          int nst = 0, nfi = 0;
-          for (int o = lo; o <= hi && nst < 4; ++nst) {
-            const int n = min(fold, hi - o + 1);
-            steady.d[nst] = (uint32_t)(o * slot_w);
-            steady.bo[nst] = (uint32_t)(((o - lo) * bslot) >> 4);
-            steady.id[nst] = a.idesc[n];
-            steady.acc[nst] = 1u;
-            o += n;
-          }
-          if (has_new) {
-            for (int o = lo; o <= hi - 1 && nfi < 3; ++nfi) {
-              const int n = min(fold, hi - o);
-              first.d[nfi] = (uint32_t)(o * slot_w);
-              first.bo[nfi] = (uint32_t)(((o - lo) * bslot) >> 4);
-              first.id[nfi] = a.idesc[n];
-              first.acc[nfi] = 1u;
-              o += n;
-            }
-            first.d[nfi] = (uint32_t)(hi * slot_w);
-            first.bo[nfi] = (uint32_t)(((hi - lo) * bslot) >> 4);
-            first.id[nfi] = a.idesc[1];
-            first.acc[nfi] = 0u;
-            ++nfi;
-          }
-          // resident weights keep all ks slots per (step, half); staged ones
-          // only the nsl slots of this input plane
-          const int bslots = a.wres ? ks : nsl;
-          const uint64_t bstep = (uint64_t)((2 * bslots * bslot) >> 4);
-          const uint32_t blbo = (uint32_t)(bslots * bslot);
-          for (int g = 0; g < ngroups; ++g) {
-            if (!wait(&full[stage], fpar)) { ok = false; break; }
-            tc_fence_after();
-            // stage A base in 16-byte units, minus the one-unit bias of s_adlo
-            const uint32_t sA4 = ((smem_u32(stage0 + (size_t)stage * a.stage_bytes) + 128u) >> 4) - 1u;
-            const uint32_t sB = a.wres ? smem_u32(wres_smem + (size_t)g * a.b_bytes) + (uint32_t)b0 * bslot
-                                       : smem_u32(stage0 + (size_t)stage * a.stage_bytes + a.a_bytes);
-            const uint64_t bdesc = smem_desc(sB, blbo, 128);
-            int s0 = 0;
-            if (has_new && g == 0) {
-              issue(mtiles, nfi, s_adlo, 0, 1, sA4, bdesc, bstep, dset, tile_cols, first);
-              s0 = 1;
-            }
-            issue(mtiles, nst, s_adlo, s0, nsteps, sA4, bdesc, bstep, dset, tile_cols, steady);
-            mma_commit(&empty[stage]);
-            if (++stage == a.stages) { stage = 0; fpar ^= 1; }
-          }
+    int stage = 0;
+    uint32_t fpar = 0;
+    uint32_t tpar[2] = {0, 0};  // phase 0 of tempty = the epilogue's initial zeroing
+    int set = 0;
+    bool ok = true;
+    if (a.wres && !wait(wbar, 0)) ok = false;
+    const uint32_t bslot = (uint32_t)(a.slot_w * 16);  // bytes of one slot's B rows
+    const int ks = a.ks, Pb = a.P, slot_w = a.slot_w, mtiles = a.mtiles, nsteps = a.nsteps;
+    const int fold = a.fold, ngroups = a.ngroups, nin = a.nin;
+    const uint32_t tile_cols = (uint32_t)(Pb * slot_w);
+    for (long long u = blockIdx.x; u < units && ok; u += gridDim.x) {
+      if (!wait(&tempty[set], tpar[set])) { ok = false; break; }
+      tpar[set] ^= 1;
+      tc_fence_after();
+      const uint32_t dset = tmem + (uint32_t)(set * set_cols);
+      for (int j = 0; j < nin && ok; ++j) {
+        // input plane j feeds output slots lo..hi; one MMA per run of at
+        // most `fold` slots (their B rows are adjacent: slot o uses the
+        // weights of kd = j - o, stored in reverse kd order)
+        const int lo = max(0, j - ks + 1), hi = min(Pb - 1, j);
+        const int b0 = (ks - 1) - (j - lo);
+        const int nsl = hi - lo + 1;
+        uint32_t dd[3] = {0, 0, 0}, bb[3] = {0, 0, 0}, ii[3] = {0, 0, 0};
+        int ns = 0;
+        for (int o = lo; o <= hi && ns < 3; ++ns) {
+          const int n = min(fold, hi - o + 1);
+          dd[ns] = (uint32_t)(o * slot_w);
+          bb[ns] = (uint32_t)(((o - lo) * bslot) >> 4);
+          ii[ns] = a.idesc[n];
+          o += n;
         }
-        if (!ok) break;
-        mma_commit(&tfull[set]);
-        if (a.nsets == 2) set ^= 1;
+        // resident weights keep all ks slots per (step, half); staged ones
+        // only the nsl slots of this input plane
+        const int bslots = a.wres ? ks : nsl;
+        const uint64_t bstep = (uint64_t)((2 * bslots * bslot) >> 4);
+        const uint32_t blbo = (uint32_t)(bslots * bslot);
+        for (int g = 0; g < ngroups; ++g) {
+          if (!wait(&full[stage], fpar)) { ok = false; break; }
+          tc_fence_after();
+          // stage A base in 16-byte units, minus the one-unit bias of s_adlo
+          const uint32_t sA4 = ((smem_u32(stage0 + (size_t)stage * a.stage_bytes) + 128u) >> 4) - 1u;
+          const uint32_t sB = a.wres ? smem_u32(wres_smem + (size_t)g * a.b_bytes) + (uint32_t)b0 * bslot
+                                     : smem_u32(stage0 + (size_t)stage * a.stage_bytes + a.a_bytes);
+          const uint64_t bdesc = smem_desc(sB, blbo, 128);
+          issue(mtiles, ns, s_adlo, nsteps, sA4, bdesc, bstep, dset, tile_cols, dd[0], dd[1], dd[2], bb[0], bb[1],
+                bb[2], ii[0], ii[1], ii[2]);
+          mma_commit(&empty[stage]);
+          if (++stage == a.stages) { stage = 0; fpar ^= 1; }
+        }
       }
-      mma_commit(mdone);
-      wait(mdone, 0);
+      if (!ok) break;
+      mma_commit(&tfull[set]);
+      if (a.nsets == 2) set ^= 1;
+    }
+    mma_commit(mdone);
+    wait(mdone, 0);
     }
   } else {
-    // ---------------- epilogue (warps 5..8) ----------------
+    // ---------------- epilogue (warps 9..12) ----------------
     const int q = warp & 3;
     const int row = q * 32 + lane;
     T* __restrict__ y = static_cast<T*>(a.y);
     const bool vec_ok = (a.cout % 8) == 0;
     uint32_t fpar[2] = {0, 0};
     int set = 0;
+    // Every MMA accumulates, so the accumulators start at zero: this warp
+    // zeroes its lane quarter of every set now and of each set it drains,
+    // and releases a set (tempty) only after those stores completed.
+    const uint32_t tq = tmem + ((uint32_t)(q * 32) << 16);
+    for (int c = 0; c < a.nsets * set_cols; c += 16) tmem_zero_16(tq + (uint32_t)c);
+    tmem_wait_st();
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) {
+      mbar_arrive(&tempty[0]);
+      mbar_arrive(&tempty[1]);
+    }
     for (long long u = blockIdx.x; u < units; u += gridDim.x) {
       const int wi = (int)(u % a.nwt);
       long long r = u / a.nwt;
@@ -705,30 +851,36 @@ __global__ void __launch_bounds__(kThreads, 1) tc_conv_kernel(const __grid_const
       if (!got) break;
       fpar[set] ^= 1;
       tc_fence_after();
+      const long long plane = (long long)a.oh * a.ow * a.cout;  // elements per output plane
+      T* const yu = y + ((((long long)nb * a.od + z0) * a.oh + h0) * a.ow + w0) * a.cout;
+      const int nz = min(a.P, a.od - z0);
       for (int t = 0; t < a.mtiles; ++t) {
         const int p = t * 128 + row;
         const int hh = p / a.pitch_w;
         const int ww = p - hh * a.pitch_w;
         const bool pos_ok = hh < a.ht && ww < a.wt && (h0 + hh) < a.oh && (w0 + ww) < a.ow;
-        for (int o = 0; o < a.P; ++o) {
-          const int z = z0 + o;
-          const bool valid = pos_ok && z < a.od;
-          T* dst = y + ((((long long)nb * a.od + z) * a.oh + (h0 + hh)) * a.ow + (w0 + ww)) * a.cout;
+        T* dst = yu + ((long long)hh * a.ow + ww) * a.cout;
+        for (int o = 0; o < a.P; ++o, dst += plane) {
+          const bool valid = pos_ok && o < nz;
           const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) +
                               (uint32_t)(set * set_cols + t * a.P * a.slot_w + o * a.slot_w);
           int cc = 0;
           for (; cc + 32 <= a.slot_w; cc += 32) {
             float v[32];
             tmem_ld_32(tb + (uint32_t)cc, v);
+            tmem_zero_16(tb + (uint32_t)cc);
+            tmem_zero_16(tb + (uint32_t)cc + 16u);
             if (valid) store_row<T, 32>(dst, v, sbias, cc, a.cout, vec_ok);
           }
           if (cc < a.slot_w) {
             float v[16];
             tmem_ld_16(tb + (uint32_t)cc, v);
+            tmem_zero_16(tb + (uint32_t)cc);
             if (valid) store_row<T, 16>(dst, v, sbias, cc, a.cout, vec_ok);
           }
         }
       }
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[set]);
@@ -738,7 +890,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_conv_kernel(const __grid_const
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 4) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, (uint32_t)a.tmem_cols);
   }
@@ -780,6 +932,10 @@ int launch_conv(const ConvPlan& P, const void* x, const void* w_packed, const vo
   a.nht = (P.oh + P.ht - 1) / P.ht;
   a.nwt = (P.ow + P.wt - 1) / P.wt;
   a.nzb = (P.od + P.P - 1) / P.P;
+  // the kernel's fixed-size per-thread tables and unrolled issue blocks
+  if ((long long)P.n * a.nzb * a.nht * a.nwt != P.work_units) return R4C_ERR_INVALID;
+  if ((P.pitch_w * P.G + kProducerThreads - 1) / kProducerThreads > kMaxEntries) return R4C_ERR_INVALID;
+  if (P.mtiles < 1 || P.mtiles > kMaxMt) return R4C_ERR_INVALID;
   a.pitch_w = P.pitch_w; a.pitch_h = P.pitch_h;
   a.slot_w = P.npad; a.P = P.P; a.nin = P.nin; a.fold = P.fold;
   a.G = P.G; a.ngroups = P.ngroups; a.nsteps = (int)steps.size();
@@ -807,6 +963,69 @@ int launch_conv(const ConvPlan& P, const void* x, const void* w_packed, const vo
   note_launches(1);
   e = cudaGetLastError();
   return e == cudaSuccess ? R4C_OK : R4C_ERR_CUDA;
+}
+
+// Launch with the fastest plan measured on this device for this shape.
+// The first call per (shape, dtype, device) times up to a dozen candidate
+// plans that share the model plan's packed-weight layout (so results are
+// bit-identical whichever wins) on the caller's buffers and stream, then
+// caches the winner; the model's plan is used as is while the stream is
+// being captured, when R4C_AUTOTUNE=0, or when R4C_TC_PLAN forces a plan.
+int launch_conv_tuned(const ConvPlan& model, const void* x, const void* w_packed, const void* bias, void* y, int dtype,
+                      cudaStream_t st) {
+  static std::map<PlanKey, ConvPlan> tuned;
+  static std::mutex mu;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const PlanKey key{{model.n, model.d, model.h, model.w, model.cin, model.cout, model.ks, model.pd, model.ph,
+                     model.pw, dev, dtype}};
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = tuned.find(key);
+    if (it != tuned.end()) return launch_conv(it->second, x, w_packed, bias, y, dtype, st);
+  }
+  const char* at = getenv("R4C_AUTOTUNE");
+  if (getenv("R4C_TC_PLAN") || (at && at[0] == '0')) return launch_conv(model, x, w_packed, bias, y, dtype, st);
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone)
+    return launch_conv(model, x, w_packed, bias, y, dtype, st);
+
+  std::vector<ConvPlan> cands = plan_candidates(model, 8);
+  if (cands.empty()) cands.push_back(model);
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  if (cudaEventCreate(&e0) != cudaSuccess || cudaEventCreate(&e1) != cudaSuccess) {
+    if (e0) cudaEventDestroy(e0);
+    return launch_conv(model, x, w_packed, bias, y, dtype, st);
+  }
+  ConvPlan best = model;
+  float best_ms = 1e30f;
+  int rc = R4C_OK;
+  for (const ConvPlan& c : cands) {
+    rc = launch_conv(c, x, w_packed, bias, y, dtype, st);  // warm-up (and module load)
+    if (rc != R4C_OK) break;
+    float ms = 1e30f;
+    for (int rep = 0; rep < 2 && rc == R4C_OK; ++rep) {
+      cudaEventRecord(e0, st);
+      rc = launch_conv(c, x, w_packed, bias, y, dtype, st);
+      cudaEventRecord(e1, st);
+      if (cudaEventSynchronize(e1) != cudaSuccess) rc = R4C_ERR_CUDA;
+      float t = 0.f;
+      if (rc == R4C_OK && cudaEventElapsedTime(&t, e0, e1) == cudaSuccess) ms = std::min(ms, t);
+    }
+    if (rc != R4C_OK) break;
+    if (ms < best_ms) {
+      best_ms = ms;
+      best = c;
+    }
+  }
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  if (rc != R4C_OK) return rc;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    tuned[key] = best;
+  }
+  return launch_conv(best, x, w_packed, bias, y, dtype, st);
 }
 
 // Device address of the error flag for the current device, for kernels in

@@ -142,7 +142,7 @@ static bool plan_dw(int n, int d, int h, int w, int cin, int cout, int ks, int p
       if (cout % nn) continue;
       int npad = round_up(nn, 16);
       if (npad > 256) continue;
-      for (int mtn = P.mtiles; mtn >= 1; --mtn) {
+      for (int mtn = std::min(P.mtiles, 8); mtn >= 1; --mtn) {
         int cols = kwn * mtn * npad;
         if (cols > 512) continue;
         int ntask_m = (P.mtiles + mtn - 1) / mtn;
@@ -206,6 +206,56 @@ template <> struct OneBits<__half> { static constexpr uint32_t v = 0x3C003C00u; 
 struct TaskTable {
   int mt0[128], mtn[128], n0[128], kw0[128];
 };
+
+// MMA issue for one output row (ksteps K steps of 16 positions): every
+// (kw, M tile) accumulator takes one MMA per K step. The (kw, tile) block is
+// fully unrolled and K steps are unrolled so that a loop iteration carries
+// at least four MMAs: the issuing thread's per-iteration bubble (~40 clk)
+// otherwise dominates (one MMA per iteration ran at ~210 clk per MMA).
+template <int MTN, int KWN>
+__device__ __forceinline__ void dw_step(int ks, uint64_t a0, uint64_t b0, uint32_t tmem, uint32_t npad,
+                                        uint64_t a_tile, uint32_t idesc, uint32_t acc) {
+  const uint64_t b = b0 + (uint64_t)(ks * 16);  // 256 B per K step
+#pragma unroll
+  for (int kw = 0; kw < KWN; ++kw)
+#pragma unroll
+    for (int t = 0; t < MTN; ++t)
+      mma_f16_ss(tmem + (uint32_t)(kw * MTN + t) * npad, a0 + (uint64_t)(ks * 16 + kw) + (uint64_t)t * a_tile, b,
+                 idesc, acc);
+}
+
+template <int MTN, int KWN>
+__device__ __forceinline__ void dw_issue_row(uint64_t a0, uint64_t b0, uint32_t tmem, uint32_t npad, uint64_t a_tile,
+                                             int ksteps, uint32_t idesc, bool first) {
+  constexpr int U = (MTN * KWN >= 4) ? 1 : ((MTN * KWN >= 2) ? 2 : 4);
+  int ks = 0;
+  if (first && ksteps > 0) {  // the task's first K step initialises every accumulator
+    dw_step<MTN, KWN>(0, a0, b0, tmem, npad, a_tile, idesc, 0u);
+    ks = 1;
+  }
+#pragma unroll 1
+  for (; ks + U <= ksteps; ks += U) {
+#pragma unroll
+    for (int u = 0; u < U; ++u) dw_step<MTN, KWN>(ks + u, a0, b0, tmem, npad, a_tile, idesc, 1u);
+  }
+#pragma unroll 1
+  for (; ks < ksteps; ++ks) dw_step<MTN, KWN>(ks, a0, b0, tmem, npad, a_tile, idesc, 1u);
+}
+
+template <int KWN>
+__device__ __forceinline__ void dw_issue_mt(int mtn, uint64_t a0, uint64_t b0, uint32_t tmem, uint32_t npad,
+                                            uint64_t a_tile, int ksteps, uint32_t idesc, bool first) {
+  switch (mtn) {
+    case 1: dw_issue_row<1, KWN>(a0, b0, tmem, npad, a_tile, ksteps, idesc, first); break;
+    case 2: dw_issue_row<2, KWN>(a0, b0, tmem, npad, a_tile, ksteps, idesc, first); break;
+    case 3: dw_issue_row<3, KWN>(a0, b0, tmem, npad, a_tile, ksteps, idesc, first); break;
+    case 4: dw_issue_row<4, KWN>(a0, b0, tmem, npad, a_tile, ksteps, idesc, first); break;
+    case 5: dw_issue_row<5, KWN>(a0, b0, tmem, npad, a_tile, ksteps, idesc, first); break;
+    case 6: dw_issue_row<6, KWN>(a0, b0, tmem, npad, a_tile, ksteps, idesc, first); break;
+    case 7: dw_issue_row<7, KWN>(a0, b0, tmem, npad, a_tile, ksteps, idesc, first); break;
+    default: dw_issue_row<8, KWN>(a0, b0, tmem, npad, a_tile, ksteps, idesc, first); break;
+  }
+}
 
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -341,16 +391,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint64_t a0 = smem_desc(sA + (uint32_t)(rel0 * sbo_a) + (uint32_t)(kw0 * 16), 128, (uint32_t)sbo_a);
         const uint64_t b0 = smem_desc(sA + (uint32_t)a.a_bytes, 128, (uint32_t)(a.kpad * 16));
         const int ksteps = a.kpad / 16;
-        for (int ks = 0; ks < ksteps; ++ks) {
-          const uint32_t acc = (first && ks == 0) ? 0u : 1u;
-          const uint64_t b = b0 + (uint64_t)(ks * 16);  // 256 B per K step
-          for (int kw = 0; kw < a.kwn; ++kw) {
-            const uint64_t akw = a0 + (uint64_t)(ks * 16 + kw);
-            const uint32_t dk = tmem + (uint32_t)(kw * mtn * npad);
-            for (int t = 0; t < mtn; ++t)
-              mma_f16_ss(dk + (uint32_t)(t * npad), akw + (uint64_t)(t * a_tile), b, a.idesc, acc);
-          }
-        }
+        if (a.kwn == 3)
+          dw_issue_mt<3>(mtn, a0, b0, tmem, (uint32_t)npad, (uint64_t)a_tile, ksteps, a.idesc, first);
+        else
+          dw_issue_mt<1>(mtn, a0, b0, tmem, (uint32_t)npad, (uint64_t)a_tile, ksteps, a.idesc, first);
         first = false;
         mma_commit(&empty[stage]);
         if (++stage == a.stages) { stage = 0; fpar ^= 1; }

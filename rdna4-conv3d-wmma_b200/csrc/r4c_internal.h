@@ -90,6 +90,8 @@ int launch_conv(const ConvPlan& pl, const void* x, const void* w_packed, const v
 // (timed on the first call, then cached); same packed weights as `pl`.
 int launch_conv_tuned(const ConvPlan& pl, const void* x, const void* w_packed, const void* bias,
                       void* y, int dtype, cudaStream_t st);
+// The plan launch_conv_tuned settled on for this shape, if it ran already.
+bool tuned_plan(const ConvPlan& pl, int dtype, ConvPlan* out);
 
 // Device address of the kernels' bounded-wait error flag (current device).
 int* device_error_flag();

@@ -971,10 +971,25 @@ int launch_conv(const ConvPlan& P, const void* x, const void* w_packed, const vo
 // bit-identical whichever wins) on the caller's buffers and stream, then
 // caches the winner; the model's plan is used as is while the stream is
 // being captured, when R4C_AUTOTUNE=0, or when R4C_TC_PLAN forces a plan.
+static std::map<PlanKey, ConvPlan> g_tuned;
+static std::mutex g_tuned_mu;
+
+bool tuned_plan(const ConvPlan& model, int dtype, ConvPlan* out) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const PlanKey key{{model.n, model.d, model.h, model.w, model.cin, model.cout, model.ks, model.pd, model.ph,
+                     model.pw, dev, dtype}};
+  std::lock_guard<std::mutex> lk(g_tuned_mu);
+  auto it = g_tuned.find(key);
+  if (it == g_tuned.end()) return false;
+  if (out) *out = it->second;
+  return true;
+}
+
 int launch_conv_tuned(const ConvPlan& model, const void* x, const void* w_packed, const void* bias, void* y, int dtype,
                       cudaStream_t st) {
-  static std::map<PlanKey, ConvPlan> tuned;
-  static std::mutex mu;
+  std::map<PlanKey, ConvPlan>& tuned = g_tuned;
+  std::mutex& mu = g_tuned_mu;
   int dev = 0;
   cudaGetDevice(&dev);
   const PlanKey key{{model.n, model.d, model.h, model.w, model.cin, model.cout, model.ks, model.pd, model.ph,

@@ -113,8 +113,8 @@ def halo_exchange(x: torch.Tensor, halo: int = 1, group=None) -> torch.Tensor:
     n, c, d, h, w = x.shape
     if d < halo:
         raise ValueError("depth slab thinner than the halo")
-    out = torch.zeros((n, c, d + 2 * halo, h, w), dtype=x.dtype, device=x.device,
-                      memory_format=torch.channels_last_3d)
+    out = torch.empty((n, c, d + 2 * halo, h, w), dtype=x.dtype, device=x.device,
+                      memory_format=torch.channels_last_3d).zero_()
     out[:, :, halo:halo + d] = x
     ops = []
     lo = torch.empty((n, c, halo, h, w), dtype=x.dtype, device=x.device) if prev_r is not None else None
@@ -191,8 +191,9 @@ class DepthShardedConv3dFn(torch.autograd.Function):
         if xp.is_cuda and cw._wmma_hw():
             dw, db = cw._launch_wgrad(xp, go, weight.shape, (0, 1, 1), ctx.has_bias)
         else:
-            dw = torch.nn.grad.conv3d_weight(xp.float(), weight.shape, go.float(), 1, (0, 1, 1))
-            db = go.float().sum(dim=(0, 2, 3, 4)) if ctx.has_bias else None
+            acc = torch.promote_types(xp.dtype, torch.float32)  # fp32 accumulation, fp64 kept
+            dw = torch.nn.grad.conv3d_weight(xp.to(acc), weight.shape, go.to(acc), 1, (0, 1, 1))
+            db = go.to(acc).sum(dim=(0, 2, 3, 4)) if ctx.has_bias else None
         red = GradAllReducer(group, average=False)
         pending = red.reduce_async([dw, db])
         if xp.is_cuda and cw._wmma_hw():

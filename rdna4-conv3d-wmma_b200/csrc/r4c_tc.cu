@@ -9,32 +9,36 @@
 //
 //  * Work unit = a block of P consecutive output planes of one (ht x wt)
 //    plane tile. Persistent CTAs (one per SM) walk the units.
-//  * Each input plane of the block (P + k - 1 of them) is loaded ONCE, as
-//    "chunk planes": for every 8-channel chunk, the (ht+k-1) x (wt+k-1) halo
-//    brick with 16 bytes per position. Four producer warps gather it with
-//    coalesced 16-byte cp.async copies (zero fill = the conv padding); TMA is
-//    not used for activations because its rate is about one box row per
-//    clock and the rows here are only 16 bytes wide.
+//  * Each input plane of the block (P + k - 1 of them) is loaded ONCE by TMA
+//    as an (ht+k-1) x (wt+k-1) halo brick, one box per channel group. Cin is
+//    split into groups of 64/32/16/8 channels (24 = 16 + 8, 96 = 64 + 32);
+//    a group's box lands as rows of cw*2 bytes with the matching TMA swizzle
+//    (128/64/32 B, none for 8 channels), so TMA moves one wide row per
+//    position instead of one 16-byte row per 8 channels. Out-of-bounds fill
+//    supplies the conv padding, whole missing planes included.
 //  * GEMM rows are brick positions p = hh*(wt+k-1) + ww ("padded grid"): a tap
-//    (kh, kw) is a constant shift of the A start address, so the k*k taps of
-//    a plane read the same brick. Rows with ww >= wt or hh >= ht are junk.
+//    (kh, kw) is a constant shift of the A start address. The MMA applies the
+//    swizzle on absolute shared-memory address bits, so a row-shifted start
+//    of a swizzled K-major operand reads the data TMA wrote (measured exact
+//    with descriptor base offset 0). Rows with ww >= wt or hh >= ht are junk.
+//  * K = 16 per MMA: for a group of >= 16 channels each tap contributes cw/16
+//    steps (32-byte moves along the swizzled row). An 8-channel group pairs
+//    taps instead: (kw, kw+1) are 16 B apart, (kh, kh+1) one brick row
+//    apart, and a last single tap pairs with a zero-weight half.
 //  * kd is folded into N: input plane j feeds output planes j-kd (kd = 0..k-1)
 //    of the block, so one tcgen05.mma (M = 128, N = slots * Cout_pad <= 256)
 //    updates up to three output-plane accumulators. This matters because an
 //    M=128 K=16 MMA costs ~45 SM clocks whatever N <= 48 is (shared-memory
 //    operand fetch), so N=32 alone would cap the tensor pipe near 35%.
-//  * K = 16 = two 8-channel core-matrix columns at distance LBO. Even chunk
-//    counts pair (c, c+1); odd chunk counts (Cin = 24) pair taps instead:
-//    (kw, kw+1) are 16 B apart, (kh, kh+1) one brick row apart; a final single
-//    chunk pairs with a zero-weight half.
 //  * fp32 accumulators live in TMEM ([set][tile][slot][Cout_pad] columns,
 //    double-buffered when they fit); four epilogue warps read them with
-//    tcgen05.ld, add bias, round and store NDHWC.
+//    tcgen05.ld, add bias, round, store NDHWC and write the columns back to
+//    zero, so that every MMA accumulates.
 //
-// Warp roles (416 threads): warps 0-7 producers, warp 8 MMA issuer + TMEM
-// owner, warps 9-12 epilogue (TMEM lane quarter = warp % 4). Every wait is
-// bounded (1 s); a timeout sets the device error flag and the kernel winds
-// down (copies drained, TMEM released) instead of hanging.
+// Warp roles (192 threads): warp 0 TMA producer (lane 0), warp 1 MMA issuer
+// (lane 0) + TMEM owner, warps 2-5 epilogue (TMEM lane quarter = warp % 4).
+// Every wait is bounded (1 s); a timeout sets the device error flag and the
+// kernel winds down (copies drained, TMEM released) instead of hanging.
 #include <cuda.h>
 
 #include <algorithm>
@@ -54,19 +58,17 @@ __device__ int g_r4c_dev_error = 0;
 
 namespace tc {
 
-constexpr int kMaxSteps = 64;
+constexpr int kMaxSteps = 128;
 constexpr int kMaxStages = 8;
-constexpr int kMaxMt = 8;  // M tiles per unit (the issue loop is unrolled over them)
-constexpr int kMaxEntries = 8;  // 16-byte copies per producer thread per brick row
-constexpr int kProducerWarps = 4;  // 8 warps copy faster alone (15.2 vs 11.4 B/clk/SM) but measured no faster in the kernel
-constexpr int kProducerThreads = 32 * kProducerWarps;
-constexpr int kMmaWarp = kProducerWarps;
-constexpr int kThreads = kProducerThreads + 32 + 128;
+constexpr int kMaxMt = 8;    // M tiles per unit (the issue loop is unrolled over them)
+constexpr int kMaxChg = 16;  // channel groups per stage
+constexpr int kThreads = 192;
+constexpr int kMmaWarp = 1;
 constexpr int kSmemMax = 232448;  // 227 KB opt-in dynamic shared memory
-constexpr int kHeader = 2048;     // barriers + bias
+constexpr int kHeader = 4096;     // barriers, bias, descriptor tables
 
-struct TcConvArgs {
-  const void* x;
+struct alignas(64) TcConvArgs {
+  CUtensorMap maps[4];  // x: dims (cin, w, h, d, n), box (cw, pitch_w, pitch_h, 1, 1); cw = 64/32/16/8
   const uint8_t* wpack;
   const void* bias;
   void* y;
@@ -76,66 +78,127 @@ struct TcConvArgs {
   int ht, wt, nht, nwt, nzb;
   int pitch_w, pitch_h;
   int slot_w, P, nin, fold;
-  int G, ngroups, nsteps;
+  int ngroups, nsteps;  // stages per input plane, K steps per stage
+  int nchg;             // channel groups per stage
+  int chg_c0[kMaxChg], chg_map[kMaxChg], chg_roff[kMaxChg];
+  int stage_c0;         // channel offset between consecutive stages of a plane
   int mtiles, nsets;
-  int cpb, a_bytes, b_bytes, stage_bytes, stages;
+  int a_bytes, a_tx, b_bytes, stage_bytes, stages;
   int wres, wres_bytes;
   int tmem_cols;
   long long units;
   uint32_t idesc[4];  // N = 1..3 slots
-  int a_off[kMaxSteps];
-  int lbo[kMaxSteps];
+  // per K step: low descriptor word relative to the stage base (address, LBO),
+  // high word (SBO, version, layout), M-tile stride in 16-byte units
+  uint32_t dlo[kMaxSteps], dhi[kMaxSteps], dts[kMaxSteps];
 };
 
+// ---------------------------------------------------------------------------
+// Channel groups, stage layout and K steps (host).
+// ---------------------------------------------------------------------------
+static int round_up(int v, int a) { return (v + a - 1) / a * a; }
+
+struct Chg {
+  int c0, cw;
+};
+
+// Cin in groups of 64, then at most one each of 32, 16, 8 channels.
+static int channel_groups(int cin, Chg* out) {
+  int n = 0, c = 0;
+  for (int wdt : {64, 32, 16, 8})
+    while (cin - c >= wdt) {
+      if (n == kMaxChg) return -1;
+      out[n++] = Chg{c, wdt};
+      c += wdt;
+    }
+  return c == cin ? n : -1;
+}
+static int map_index(int cw) { return cw == 64 ? 0 : cw == 32 ? 1 : cw == 16 ? 2 : 3; }
+// tcgen05 smem descriptor layout codes: 0 none, 2 = 128 B, 4 = 64 B, 6 = 32 B swizzle
+static int layout_code(int cw) { return cw == 64 ? 2 : cw == 32 ? 4 : cw == 16 ? 6 : 0; }
+
+struct StageLayout {
+  int nchg;
+  Chg g[kMaxChg];     // channels relative to the stage's first channel
+  int roff[kMaxChg];  // region offset in the stage (1024-aligned)
+  int a_bytes;        // all regions
+  int a_tx;           // bytes TMA writes per stage (full boxes)
+  int stage_c0;       // channels between consecutive stages of a plane
+  int ngroups;        // stages per input plane
+};
+
+// Rows a region must hold: the TMA box, and every row an MMA reads: 128 per
+// M tile plus the largest tap shift plus one (the zero-weight half of an
+// 8-channel pair reads the next position).
+static int region_rows(int mtiles, int ks, int pitch_w, int pitch_h) {
+  return std::max(pitch_h * pitch_w, 128 * mtiles + (ks - 1) * (pitch_w + 1) + 1);
+}
+
+// split_w = 0: every channel group of a plane in one stage; otherwise the
+// plane's channels in stages of one split_w-wide group each (split_w divides
+// Cin), which keeps the weight slice staged with each stage small.
+static bool stage_layout(int cin, int split_w, int mtiles, int ks, int pitch_w, int pitch_h, StageLayout* L) {
+  Chg all[kMaxChg];
+  const int rows = region_rows(mtiles, ks, pitch_w, pitch_h);
+  L->a_bytes = 0;
+  L->a_tx = 0;
+  if (split_w) {
+    if (cin % split_w != 0 || cin / split_w < 2) return false;
+    L->nchg = 1;
+    L->g[0] = Chg{0, split_w};
+    L->stage_c0 = split_w;
+    L->ngroups = cin / split_w;
+  } else {
+    const int n = channel_groups(cin, all);
+    if (n <= 0) return false;
+    L->nchg = n;
+    for (int i = 0; i < n; ++i) L->g[i] = all[i];
+    L->stage_c0 = 0;
+    L->ngroups = 1;
+  }
+  for (int i = 0; i < L->nchg; ++i) {
+    L->roff[i] = L->a_bytes;
+    L->a_bytes += round_up(rows * L->g[i].cw * 2, 1024);
+    L->a_tx += pitch_h * pitch_w * L->g[i].cw * 2;
+  }
+  return true;
+}
+
 struct HalfRef {
-  int kh, kw, c, zero;
+  int kh, kw, c, zero;  // c: 8-channel chunk relative to the stage's first channel
 };
 struct Step {
   HalfRef h[2];
-  int a_off;
-  int lbo;
+  int a_off;    // bytes from the stage base
+  int lbo;      // bytes between the two K halves (no-swizzle regions)
+  int sbo;      // bytes between 8-row groups
+  int layout;   // descriptor layout code
+  int tstride;  // bytes between M tiles (128 rows)
 };
 
-static int steps_per_stage(int ks, int G) {
-  if (G % 2 == 0) return ks * ks * G / 2;
-  return ks == 3 ? 4 * G + (G + 1) / 2 : (G + 1) / 2;
-}
-
-// K steps of one (input plane, chunk group) stage: which two 8-channel
-// halves each K=16 step reads, the A offset of its first half and the
-// distance (LBO) to its second half.
-static void build_steps(int ks, int G, int pitch_w, int cpb, std::vector<Step>& st) {
+static void build_steps(const StageLayout& L, int ks, int pitch_w, std::vector<Step>& st) {
   st.clear();
-  auto off = [&](int kh, int kw, int c) { return c * cpb + (kh * pitch_w + kw) * 16; };
   auto ref = [](int kh, int kw, int c) { return HalfRef{kh, kw, c, 0}; };
   const HalfRef zero{0, 0, 0, 1};
-  if (G % 2 == 0) {
-    for (int kh = 0; kh < ks; ++kh)
-      for (int kw = 0; kw < ks; ++kw)
-        for (int j = 0; j < G / 2; ++j)
-          st.push_back(Step{{ref(kh, kw, 2 * j), ref(kh, kw, 2 * j + 1)}, off(kh, kw, 2 * j), cpb});
-    return;
-  }
-  if (ks == 3) {
-    for (int kh = 0; kh < 3; ++kh)
-      for (int c = 0; c < G; ++c)
-        st.push_back(Step{{ref(kh, 0, c), ref(kh, 1, c)}, off(kh, 0, c), 16});
-    for (int c = 0; c < G; ++c)
-      st.push_back(Step{{ref(0, 2, c), ref(1, 2, c)}, off(0, 2, c), pitch_w * 16});
-    for (int j = 0; j < (G - 1) / 2; ++j)
-      st.push_back(Step{{ref(2, 2, 2 * j), ref(2, 2, 2 * j + 1)}, off(2, 2, 2 * j), cpb});
-    st.push_back(Step{{zero, ref(2, 2, G - 1)}, off(2, 2, G - 1) - 16, 16});
-  } else {
-    for (int j = 0; j < (G - 1) / 2; ++j)
-      st.push_back(Step{{ref(0, 0, 2 * j), ref(0, 0, 2 * j + 1)}, off(0, 0, 2 * j), cpb});
-    st.push_back(Step{{zero, ref(0, 0, G - 1)}, off(0, 0, G - 1) - 16, 16});
+  for (int gi = 0; gi < L.nchg; ++gi) {
+    const int cw = L.g[gi].cw, rb = cw * 2, ch0 = L.g[gi].c0 / 8, ro = L.roff[gi];
+    auto off = [&](int kh, int kw) { return ro + (kh * pitch_w + kw) * rb; };
+    if (cw >= 16) {
+      for (int kh = 0; kh < ks; ++kh)
+        for (int kw = 0; kw < ks; ++kw)
+          for (int kk = 0; kk < cw / 16; ++kk)
+            st.push_back(Step{{ref(kh, kw, ch0 + 2 * kk), ref(kh, kw, ch0 + 2 * kk + 1)}, off(kh, kw) + kk * 32, 16,
+                              8 * rb, layout_code(cw), 128 * rb});
+    } else if (ks == 3) {
+      for (int kh = 0; kh < 3; ++kh)
+        st.push_back(Step{{ref(kh, 0, ch0), ref(kh, 1, ch0)}, off(kh, 0), 16, 128, 0, 2048});
+      st.push_back(Step{{ref(0, 2, ch0), ref(1, 2, ch0)}, off(0, 2), pitch_w * 16, 128, 0, 2048});
+      st.push_back(Step{{ref(2, 2, ch0), zero}, off(2, 2), 16, 128, 0, 2048});
+    } else {
+      st.push_back(Step{{ref(0, 0, ch0), zero}, off(0, 0), 16, 128, 0, 2048});
+    }
   }
 }
-
-// ---------------------------------------------------------------------------
-// Planner (host only).
-// ---------------------------------------------------------------------------
-static int round_up(int v, int a) { return (v + a - 1) / a * a; }
 
 static int num_sms() {
   static int cached[64] = {0};
@@ -155,7 +218,8 @@ static double mma_clk(int n) { return std::max({n / 2.0, 40.0 + n / 6.0, 45.0});
 
 // Tuning override: R4C_TC_PLAN="ht=4,nw=8,P=8,G=3,wres=1,stages=4" limits
 // the search to candidates with the given values (any subset of the keys;
-// stages caps the stage count). Unset keys are searched as usual.
+// G = 8-channel chunks per stage, stages caps the stage count). Unset keys
+// are searched as usual.
 struct PlanForce {
   int ht = 0, nw = 0, P = 0, G = 0, wres = -1, stages = 0;
 };
@@ -179,8 +243,8 @@ static PlanForce plan_force() {
 }
 
 // Every feasible plan of the conv, with its modelled cost in est_cycles, is
-// passed to visit(). G_only > 0 restricts the chunk group size (the packed
-// weight layout depends on G only).
+// passed to visit(). G_only > 0 restricts the chunks per stage (the packed
+// weight layout depends on it only).
 template <typename F>
 static void enumerate_plans(int n, int d, int h, int w, int cin, int cout, int ks, int pd, int ph, int pw, int G_only,
                             const PlanForce& force, F&& visit) {
@@ -199,61 +263,56 @@ static void enumerate_plans(int n, int d, int h, int w, int cin, int cout, int k
   P.c8 = cin / 8;
   P.npad = round_up(cout, 16);
   P.fold = std::max(1, std::min(ks, 256 / P.npad));
+  P.cpb = 0;
 
-  std::vector<int> gs;
-  if (P.c8 % 2 == 1) {
-    if (P.c8 > 13) return;
-    gs.push_back(P.c8);
-  } else {
-    for (int g = std::min(P.c8, 14); g >= 2; g -= 2)
-      if (P.c8 % g == 0) gs.push_back(g);
-  }
   const int wt_max = 254 - (ks - 1);
   const int nw_min = (P.ow + wt_max - 1) / wt_max;
   const int sms = num_sms();
 
-  for (int G : gs) {
+  for (int split : {0, 64, 32, 16, 8}) {
+    if (split && (cin % split != 0 || cin / split < 2)) continue;
+    const int G = split ? split / 8 : P.c8;
     if (force.G && G != force.G) continue;
     if (G_only > 0 && G != G_only) continue;
-    const int nsteps = steps_per_stage(ks, G);
-    if (nsteps > kMaxSteps) continue;
-    const int ngroups = P.c8 / G;
-    const int b_bytes = nsteps * 2 * ks * P.npad * 16;
-    const int wbytes = ngroups * b_bytes;
-    // a brick row (wt + k - 1 positions x G chunks) must fit the producers'
-    // fixed per-thread copy slots
-    const int wt_cap = kMaxEntries * kProducerThreads / G - (ks - 1);
-    if (wt_cap < 1) continue;
-    const int nw_lo = std::max(nw_min, (P.ow + wt_cap - 1) / wt_cap);
-    const int nw_a = force.nw ? force.nw : nw_lo, nw_b = force.nw ? force.nw : nw_lo + 8;
+    const int nw_a = force.nw ? force.nw : nw_min, nw_b = force.nw ? force.nw : nw_min + 8;
     for (int nw = nw_a; nw <= nw_b && nw <= P.ow; ++nw) {
      const int wt = (P.ow + nw - 1) / nw;
      // the kernel decodes ceil(ow / wt) tiles per row; skip counts that differ
      if ((P.ow + wt - 1) / wt != nw) continue;
-     const int entries = ((wt + ks - 1) * G + kProducerThreads - 1) / kProducerThreads;
-     if (entries > kMaxEntries) continue;
      for (int wres = 1; wres >= 0; --wres) {
       if (force.wres >= 0 && wres != force.wres) continue;
-      if (wres && wbytes > 96 * 1024) continue;
       for (int ht = 1; ht <= P.oh && ht <= 254 - (ks - 1); ++ht) {
         if (force.ht && ht != force.ht) continue;
         const int pitch_w = wt + ks - 1, pitch_h = ht + ks - 1;
         const int span = (ht - 1) * pitch_w + wt;
         const int mtiles = (span + 127) / 128;
         if (mtiles * P.npad > 512 || mtiles > kMaxMt) break;
-        const int cpb = round_up(pitch_h * pitch_w * 16, 128);
-        const int maxrow = 128 * mtiles - 1 + (ks - 1) * (pitch_w + 1);
-        const int pad = round_up(std::max(0, (maxrow + 1) * 16 - cpb), 128);
-        const int a_bytes = 128 + G * cpb + pad;
-        const int avail = kSmemMax - kHeader - (wres ? round_up(wbytes, 128) : 0);
+        StageLayout L;
+        if (!stage_layout(cin, split, mtiles, ks, pitch_w, pitch_h, &L)) break;
+        std::vector<Step> steps;
+        build_steps(L, ks, pitch_w, steps);
+        const int nsteps = (int)steps.size();
+        if (nsteps > kMaxSteps) break;
+        const int ngroups = L.ngroups;
+        const int b_bytes = nsteps * 2 * ks * P.npad * 16;
+        const int wbytes = ngroups * b_bytes;
+        if (wres && wbytes > 96 * 1024) continue;
+        const int wres_bytes = wres ? round_up(wbytes, 1024) : 0;
+        const int avail = kSmemMax - kHeader - wres_bytes;
         const int tiles_h = (P.oh + ht - 1) / ht;
+        // TMA rows per stage: one per brick position and channel group, about
+        // one row per clock (~105 B/clk for 128-byte rows)
+        double rows_clk = 0.0;
+        for (int gi = 0; gi < L.nchg; ++gi)
+          rows_clk += (double)pitch_h * pitch_w * std::max(1.0, L.g[gi].cw * 2 / 105.0);
         for (int Pb = 1; Pb <= std::min(P.od, 16); ++Pb) {
           if (force.P && Pb != force.P) continue;
-          // a stage holds the A brick and, unless resident, the weight slots
-          // of the output planes its input plane feeds (at most min(ks, Pb))
+          // a stage holds the A regions and, unless resident, the weight
+          // slots of the output planes its input plane feeds (<= min(ks, Pb))
           const int sb = std::min(ks, Pb) * nsteps * 2 * P.npad * 16;
-          const int stage = round_up(a_bytes + (wres ? 0 : sb), 128);
-          const int stages = std::min(force.stages ? force.stages : kMaxStages, std::min(kMaxStages, avail / stage));
+          const int stage = round_up(L.a_bytes + (wres ? 0 : sb), 1024);
+          const int stages =
+              std::min(force.stages ? force.stages : kMaxStages, std::min(kMaxStages, avail / stage));
           if (stages < 2) break;
           int nsets = 2;
           if (2 * Pb * P.npad * mtiles > 512) nsets = 1;
@@ -272,19 +331,11 @@ static void enumerate_plans(int n, int d, int h, int w, int cin, int cout, int k
             }
             mma += t * nsteps * mtiles * ngroups;
           }
-          // producer clocks per stage (measured on B200): the halo brick
-          // arrives by 16-byte cp.async at ~3 B/clk per producer warp that
-          // has copies in a brick row (11.4 B/clk per SM with four), plus
-          // ~40 clk of addressing per row; the staged weight slots arrive by
-          // bulk copies at ~30 B/clk, in parallel
-          const int busy_warps = std::min(kProducerWarps, (pitch_w * G + 31) / 32);
-          const double cp_rate = std::min(11.4, 3.0 * busy_warps);
-          const double load =
-              (double)nin * ngroups *
-              (std::max(G * pitch_h * pitch_w * 16.0 / cp_rate + 40.0 * pitch_h, wres ? 0.0 : sb / 30.0) + 150.0);
+          const double load = (double)nin * ngroups * (std::max(rows_clk, wres ? 0.0 : sb / 30.0) + 150.0);
           // epilogue clocks per unit: per (tile, plane) the TMEM reads (one
           // wait per 32 columns), 16-byte stores of 8 channels, addressing
-          const double epi = (double)Pb * mtiles * (((P.npad + 31) / 32) * 100.0 + ((cout + 7) / 8) * 12.0 + 40.0);
+          const double epi =
+              (double)Pb * mtiles * (((P.npad + 31) / 32) * 100.0 + ((cout + 7) / 8) * 12.0 + 40.0);
           double t_unit = std::max(mma, load) + 100.0 * nin * ngroups;
           t_unit = nsets == 2 ? std::max(t_unit, epi) : t_unit + epi;
           const long long units = (long long)n * ((P.od + Pb - 1) / Pb) * tiles_h * nw;
@@ -293,11 +344,11 @@ static void enumerate_plans(int n, int d, int h, int w, int cin, int cout, int k
           {
             P.G = G; P.ngroups = ngroups; P.nsteps = nsteps;
             P.wt = wt; P.ht = ht; P.pitch_w = pitch_w; P.pitch_h = pitch_h;
-            P.cpb = cpb; P.mtiles = mtiles; P.nsets = nsets;
+            P.mtiles = mtiles; P.nsets = nsets;
             P.P = Pb; P.nin = nin;
-            P.a_bytes = a_bytes; P.b_bytes = b_bytes; P.stage_bytes = stage; P.stages = stages;
-            P.wres = wres; P.wres_bytes = wres ? round_up(wbytes, 128) : 0;
-            P.smem_bytes = kHeader + P.wres_bytes + stages * stage;
+            P.a_bytes = L.a_bytes; P.b_bytes = b_bytes; P.stage_bytes = stage; P.stages = stages;
+            P.wres = wres; P.wres_bytes = wres_bytes;
+            P.smem_bytes = kHeader + wres_bytes + stages * stage;
             const int cols = nsets * Pb * P.npad * mtiles;
             int alloc = 32;
             while (alloc < cols) alloc *= 2;
@@ -353,8 +404,8 @@ bool plan_conv(int n, int d, int h, int w, int cin, int cout, int ks, int pd, in
   return true;
 }
 
-// Candidates for on-device tuning: the plans with the model's chunk group
-// size G (same packed weights, bit-identical results) ranked by modelled
+// Candidates for on-device tuning: the plans with the model's chunks per
+// stage (same packed weights, bit-identical results) ranked by modelled
 // cost, top `k_top`, plus the cheapest of each brick-row count so that a
 // model error in the halo/row trade-off cannot hide the fastest shape.
 static std::vector<ConvPlan> plan_candidates(const ConvPlan& m, int k_top) {
@@ -382,8 +433,15 @@ static std::vector<ConvPlan> plan_candidates(const ConvPlan& m, int k_top) {
 
 size_t packed_bytes(const ConvPlan& P) { return (size_t)P.ngroups * P.b_bytes; }
 
+static bool plan_layout(const ConvPlan& P, StageLayout* L, std::vector<Step>* steps) {
+  if (!stage_layout(P.cin, P.ngroups > 1 ? P.G * 8 : 0, P.mtiles, P.ks, P.pitch_w, P.pitch_h, L)) return false;
+  if (L->ngroups != P.ngroups) return false;
+  build_steps(*L, P.ks, P.pitch_w, *steps);
+  return (int)steps->size() == P.nsteps;
+}
+
 // ---------------------------------------------------------------------------
-// Weight pack: PyTorch OIDHW -> per chunk group, per K step:
+// Weight pack: PyTorch OIDHW -> per stage of a plane, per K step:
 // [half][slot b (kd = ks-1-b)][npad rows][8 elements]
 // ---------------------------------------------------------------------------
 struct PackArgs {
@@ -426,8 +484,9 @@ __global__ void pack_tc_kernel(const void* __restrict__ src, int sdt, TO* __rest
 
 cudaError_t pack_weight(const ConvPlan& P, bool flip, int cin_real, const void* w_src, int src_dtype,
                         void* w_packed, int dtype, cudaStream_t st) {
+  StageLayout L;
   std::vector<Step> steps;
-  build_steps(P.ks, P.G, P.pitch_w, P.cpb, steps);
+  if (!plan_layout(P, &L, &steps)) return cudaErrorInvalidValue;
   PackArgs a{};
   a.ks = P.ks; a.G = P.G; a.ngroups = P.ngroups; a.nsteps = (int)steps.size();
   a.npad = P.npad; a.cin = P.cin; a.cout = P.cout; a.flip = flip ? 1 : 0;
@@ -486,23 +545,24 @@ __device__ __forceinline__ void store_row(T* dst, const float (&v)[NV], const fl
   }
 }
 
-// MMA issue for the nsteps K steps of one stage (one thread). MT tiles x NS slot segments per step are
-// fully unrolled and four steps go per loop iteration: a loop iteration
-// costs the issuing warp a ~40-clock bubble (branch resolution after an
-// MMA), which straight-line MMAs hide, so one MMA per iteration runs at
-// ~105 clocks instead of the tensor pipe's 56-64 (measured on B200).
-//   adlo[s]  : low descriptor word of step s (A address field, biased by one
-//              16-byte unit, and LBO), relative to the stage base sA4
-//   bd0      : B descriptor of step 0; step s adds s * bstep
-//   dk, bk, ik: TMEM column offset, B offset (16-byte units) and
-//              instruction descriptor of slot segment k
+// MMA issue for the nsteps K steps of one stage (one thread). MT tiles x NS
+// slot segments per step are fully unrolled and K steps are unrolled so that
+// a loop iteration carries at least four MMAs: a loop iteration costs the
+// issuing thread a ~40-clock bubble (branch resolution after an MMA), which
+// straight-line MMAs hide, so one MMA per iteration runs at ~105 clocks
+// instead of the tensor pipe's 56-64 (measured on B200).
+//   tlo/thi/tts[s]: step s's A descriptor low word relative to the stage base
+//                   sA4, its high word, and its M-tile stride (16-byte units)
+//   bd0           : B descriptor of step 0; step s adds s * bstep
+//   dk, bk, ik    : TMEM column offset, B offset (16-byte units) and
+//                   instruction descriptor of slot segment k
 // Every MMA accumulates: the epilogue zeroes the accumulators it drains.
 template <int MT, int NS>
-__device__ __forceinline__ void issue_steps(const uint32_t* __restrict__ adlo, int nsteps, uint32_t sA4,
+__device__ __forceinline__ void issue_steps(const uint32_t* __restrict__ tlo, const uint32_t* __restrict__ thi,
+                                            const uint32_t* __restrict__ tts, int nsteps, uint32_t sA4,
                                             uint64_t bd0, uint64_t bstep, uint32_t dbase, uint32_t tile_cols,
                                             uint32_t d0, uint32_t d1, uint32_t d2, uint32_t b0, uint32_t b1,
                                             uint32_t b2, uint32_t i0, uint32_t i1, uint32_t i2) {
-  constexpr uint64_t kAHi = (uint64_t)((128u >> 4) | (1u << 14)) << 32;  // SBO 128 B, version 1
   constexpr int U = (MT * NS >= 4) ? 1 : ((MT * NS >= 2) ? 2 : 4);
   const uint32_t dk[3] = {dbase + d0, dbase + d1, dbase + d2};
   const uint32_t bk[3] = {b0, b1, b2};
@@ -512,34 +572,37 @@ __device__ __forceinline__ void issue_steps(const uint32_t* __restrict__ adlo, i
   for (; s + U <= nsteps; s += U) {
 #pragma unroll
     for (int q = 0; q < U; ++q) {
-      const uint64_t ad = kAHi | (uint64_t)(adlo[s + q] + sA4);
+      const uint64_t ad = ((uint64_t)thi[s + q] << 32) | (uint64_t)(tlo[s + q] + sA4);
+      const uint64_t ts = MT > 1 ? (uint64_t)tts[s + q] : 0ull;
       const uint64_t bd = bd0 + (uint64_t)(s + q) * bstep;
 #pragma unroll
       for (int t = 0; t < MT; ++t)
 #pragma unroll
         for (int k = 0; k < NS; ++k)
-          mma_f16_ss(dk[k] + (uint32_t)t * tile_cols, ad + (uint64_t)(t * 128), bd + bk[k], ik[k], 1u);
+          mma_f16_ss(dk[k] + (uint32_t)t * tile_cols, ad + (uint64_t)t * ts, bd + bk[k], ik[k], 1u);
     }
   }
 #pragma unroll 1
   for (; s < nsteps; ++s) {
-    const uint64_t ad = kAHi | (uint64_t)(adlo[s] + sA4);
+    const uint64_t ad = ((uint64_t)thi[s] << 32) | (uint64_t)(tlo[s] + sA4);
+    const uint64_t ts = MT > 1 ? (uint64_t)tts[s] : 0ull;
     const uint64_t bd = bd0 + (uint64_t)s * bstep;
 #pragma unroll
     for (int t = 0; t < MT; ++t)
 #pragma unroll
       for (int k = 0; k < NS; ++k)
-        mma_f16_ss(dk[k] + (uint32_t)t * tile_cols, ad + (uint64_t)(t * 128), bd + bk[k], ik[k], 1u);
+        mma_f16_ss(dk[k] + (uint32_t)t * tile_cols, ad + (uint64_t)t * ts, bd + bk[k], ik[k], 1u);
   }
 }
 
-#define R4C_ISSUE_ARGS adlo, nsteps, sA4, bd0, bstep, dbase, tile_cols, d0, d1, d2, b0, b1, b2, i0, i1, i2
+#define R4C_ISSUE_ARGS tlo, thi, tts, nsteps, sA4, bd0, bstep, dbase, tile_cols, d0, d1, d2, b0, b1, b2, i0, i1, i2
+#define R4C_ISSUE_PARAMS                                                                                        \
+  const uint32_t *tlo, const uint32_t *thi, const uint32_t *tts, int nsteps, uint32_t sA4, uint64_t bd0,      \
+      uint64_t bstep, uint32_t dbase, uint32_t tile_cols, uint32_t d0, uint32_t d1, uint32_t d2, uint32_t b0, \
+      uint32_t b1, uint32_t b2, uint32_t i0, uint32_t i1, uint32_t i2
 
 template <int MT>
-__device__ __forceinline__ void issue_ns(int ns, const uint32_t* adlo, int nsteps, uint32_t sA4, uint64_t bd0,
-                                         uint64_t bstep, uint32_t dbase, uint32_t tile_cols, uint32_t d0,
-                                         uint32_t d1, uint32_t d2, uint32_t b0, uint32_t b1, uint32_t b2,
-                                         uint32_t i0, uint32_t i1, uint32_t i2) {
+__device__ __forceinline__ void issue_ns(int ns, R4C_ISSUE_PARAMS) {
   switch (ns) {
     case 1: issue_steps<MT, 1>(R4C_ISSUE_ARGS); break;
     case 2: issue_steps<MT, 2>(R4C_ISSUE_ARGS); break;
@@ -547,10 +610,7 @@ __device__ __forceinline__ void issue_ns(int ns, const uint32_t* adlo, int nstep
   }
 }
 
-__device__ __forceinline__ void issue(int mt, int ns, const uint32_t* adlo, int nsteps, uint32_t sA4, uint64_t bd0,
-                                      uint64_t bstep, uint32_t dbase, uint32_t tile_cols, uint32_t d0, uint32_t d1,
-                                      uint32_t d2, uint32_t b0, uint32_t b1, uint32_t b2, uint32_t i0, uint32_t i1,
-                                      uint32_t i2) {
+__device__ __forceinline__ void issue(int mt, int ns, R4C_ISSUE_PARAMS) {
   switch (mt) {
     case 1: issue_ns<1>(ns, R4C_ISSUE_ARGS); break;
     case 2: issue_ns<2>(ns, R4C_ISSUE_ARGS); break;
@@ -563,6 +623,7 @@ __device__ __forceinline__ void issue(int mt, int ns, const uint32_t* adlo, int 
   }
 }
 #undef R4C_ISSUE_ARGS
+#undef R4C_ISSUE_PARAMS
 
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1) tc_conv_kernel(const __grid_constant__ TcConvArgs a) {
@@ -575,27 +636,27 @@ __global__ void __launch_bounds__(kThreads, 1) tc_conv_kernel(const __grid_const
   uint64_t* wbar = mdone + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(wbar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* sbias = reinterpret_cast<float*>(smem + 1024);
-  // low 32 bits of each K step's A descriptor relative to the stage base:
-  // ((a_off + 16) >> 4) in the address field (offsets start at -16 B, so they
-  // are biased by one 16-byte unit to stay non-negative) and the step's LBO
-  uint32_t* s_adlo = reinterpret_cast<uint32_t*>(smem + 512);
+  float* sbias = reinterpret_cast<float*>(smem + 1024);        // 256 floats
+  uint32_t* s_lo = reinterpret_cast<uint32_t*>(smem + 2048);   // kMaxSteps each
+  uint32_t* s_hi = s_lo + kMaxSteps;
+  uint32_t* s_ts = s_hi + kMaxSteps;
   uint8_t* wres_smem = smem + kHeader;
   uint8_t* stage0 = smem + kHeader + a.wres_bytes;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  // Bulk copies need 16-byte aligned shared memory; keep the whole layout on
-  // 128-byte boundaries from the base.
-  if ((smem_u32(smem) & 127u) != 0u || a.tmem_cols > 512) {
+  // Swizzled TMA boxes and the MMA's address-based swizzle need the stage
+  // regions on 1024-byte boundaries: the layout is built on a 1024-aligned
+  // base.
+  if ((smem_u32(smem) & 1023u) != 0u || a.tmem_cols > 512) {
     if (threadIdx.x == 0) atomicExch(&g_r4c_dev_error, 2);
     return;
   }
 
-  // One-time set-up: zero the stage buffers (guard rows, inter-plane gaps and
-  // the overrun pad are read by junk GEMM rows only, but keep them finite),
-  // stage the bias as fp32, init barriers, allocate TMEM.
+  // One-time set-up: zero the stage buffers (rows past the TMA boxes are
+  // read by junk GEMM rows only, but must be finite), stage the bias as fp32
+  // and the descriptor tables, init barriers, allocate TMEM.
   {
     const uint4 z = make_uint4(0, 0, 0, 0);
     const int total = a.stages * a.stage_bytes;
@@ -603,13 +664,15 @@ __global__ void __launch_bounds__(kThreads, 1) tc_conv_kernel(const __grid_const
     const T* bias = static_cast<const T*>(a.bias);
     for (int i = threadIdx.x; i < a.slot_w; i += kThreads)
       sbias[i] = (bias != nullptr && i < a.cout) ? Elem<T>::to_f(bias[i]) : 0.f;
-    for (int i = threadIdx.x; i < a.nsteps; i += kThreads)
-      s_adlo[i] = (uint32_t)(((a.a_off[i] + 16) >> 4) & 0x3FFF) | ((uint32_t)((a.lbo[i] >> 4) & 0x3FFF) << 16);
+    for (int i = threadIdx.x; i < a.nsteps; i += kThreads) {
+      s_lo[i] = a.dlo[i];
+      s_hi[i] = a.dhi[i];
+      s_ts[i] = a.dts[i];
+    }
   }
   if (threadIdx.x == 0) {
     for (int s = 0; s < a.stages; ++s) {
-      // one (asynchronous) arrival per producer thread, plus the weight copy
-      mbar_init(&full[s], kProducerThreads + (a.wres ? 0 : 1));
+      mbar_init(&full[s], 1);  // the producer's expect_tx arrival; TMA bytes complete it
       mbar_init(&empty[s], 1);
     }
     for (int s = 0; s < 2; ++s) {
@@ -634,8 +697,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_conv_kernel(const __grid_const
   const long long units = a.units;
   const uint64_t kWaitNs = 1000000000ull;  // 1 s per wait
   // Bounded wait. `nap` > 0 makes the polling thread sleep between polls so
-  // that warps which only wait (producers, epilogue) leave issue slots to the
-  // MMA warp; the MMA issuer polls without sleeping.
+  // that warps which only wait leave issue slots to the MMA thread.
   auto wait = [&](uint64_t* bar, uint32_t par, uint32_t nap = 0) -> bool {
     const uint64_t deadline = global_timer_ns() + kWaitNs;
     uint32_t spins = 0;
@@ -654,172 +716,133 @@ __global__ void __launch_bounds__(kThreads, 1) tc_conv_kernel(const __grid_const
   };
   const int set_cols = a.P * a.slot_w * a.mtiles;
 
-  if (warp < kProducerWarps) {
-    // ---------------- producers: cp.async gather of the halo bricks ----------------
-    const int pt = threadIdx.x;
-    const T* __restrict__ x = static_cast<const T*>(a.x);
-    // A brick row is pitch_w positions x G chunks = per_row 16-byte copies;
-    // copy q goes to thread q % 128 as its entry q / 128 (at most kMaxEntries,
-    // which the planner guarantees). Consecutive threads take consecutive
-    // chunks of a position, so a warp reads 512 contiguous bytes. The
-    // shared/global offsets of every entry are fixed for the whole kernel,
-    // so a copy costs a handful of independent instructions.
-    const int per_row = a.pitch_w * a.G;
-    uint32_t soff[kMaxEntries];
-    int goff[kMaxEntries], wpos[kMaxEntries];
-    uint32_t qmask = 0;
-#pragma unroll
-    for (int e = 0; e < kMaxEntries; ++e) {
-      const int q = pt + e * kProducerThreads;
-      const int ww = q / a.G, c = q - (q / a.G) * a.G;
-      soff[e] = (uint32_t)(c * a.cpb + ww * 16);
-      goff[e] = ww * a.cin + c * 8;
-      wpos[e] = ww;
-      if (q < per_row) qmask |= 1u << e;
-    }
-    if (pt == 0 && a.wres) {
-      const uint32_t wb = (uint32_t)(a.ngroups * a.b_bytes);
-      mbar_arrive_expect_tx(wbar, wb);
-      bulk_load(wres_smem, a.wpack, wb, wbar);
-    }
-    int stage = 0;
-    uint32_t epar = 1;
-    bool ok = true;
-    for (long long u = blockIdx.x; u < units && ok; u += gridDim.x) {
-      const int wi = (int)(u % a.nwt);
-      long long r = u / a.nwt;
-      const int hi = (int)(r % a.nht); r /= a.nht;
-      const int zb = (int)(r % a.nzb);
-      const int nb = (int)(r / a.nzb);
-      const int h0 = hi * a.ht - a.ph, w0 = wi * a.wt - a.pw;
-      // entries whose input column lies inside the image for this unit
-      uint32_t wmask = 0;
-#pragma unroll
-      for (int e = 0; e < kMaxEntries; ++e) {
-        const int iw = w0 + wpos[e];
-        if (((qmask >> e) & 1u) && iw >= 0 && iw < a.w) wmask |= 1u << e;
+  if (warp == 0) {
+    // ---------------- TMA producer (lane 0) ----------------
+    if (lane == 0) {
+      for (int m = 0; m < 4; ++m) prefetch_tmap(&a.maps[m]);
+      if (a.wres) {
+        const uint32_t wb = (uint32_t)(a.ngroups * a.b_bytes);
+        mbar_arrive_expect_tx(wbar, wb);
+        bulk_load(wres_smem, a.wpack, wb, wbar);
       }
-      const long long wofs = (long long)w0 * a.cin;  // may be negative; only added to in-image offsets
-      for (int j = 0; j < a.nin && ok; ++j) {
-        const int iz = zb * a.P - a.pd + j;
-        const bool z_ok = iz >= 0 && iz < a.d;
-        for (int g = 0; g < a.ngroups; ++g) {
-          int got = 1;
-          if (lane == 0) got = wait(&empty[stage], epar, 64) ? 1 : 0;
-          got = __shfl_sync(0xffffffffu, got, 0);
-          if (!got) { ok = false; break; }
-          uint8_t* sbase = stage0 + (size_t)stage * a.stage_bytes;
-          const uint32_t sA = smem_u32(sbase) + 128u;
-          for (int hh = 0; hh < a.pitch_h; ++hh) {
-            const int ih = h0 + hh;
-            const bool r_ok = z_ok && ih >= 0 && ih < a.h;
-            const uint32_t m = r_ok ? wmask : 0u;
-            const long long rbase =
-                (((long long)nb * a.d + (r_ok ? iz : 0)) * a.h + (r_ok ? ih : 0)) * a.w * a.cin + wofs + g * a.G * 8;
-            const uint32_t drow = sA + (uint32_t)(hh * a.pitch_w * 16);
-#pragma unroll
-            for (int e = 0; e < kMaxEntries; ++e) {
-              if ((qmask >> e) & 1u) {
-                const bool v = (m >> e) & 1u;
-                const T* src = v ? x + (rbase + goff[e]) : x;
-                cp_async_16(drow + soff[e], src, v ? 16u : 0u);
-              }
+      int stage = 0;
+      uint32_t epar = 1;
+      bool pending[kMaxStages];
+      uint32_t last_par[kMaxStages];
+      for (int s = 0; s < kMaxStages; ++s) { pending[s] = false; last_par[s] = 0; }
+      const uint32_t slot_bytes = (uint32_t)(a.slot_w * 16);
+      bool ok = true;
+      for (long long u = blockIdx.x; u < units && ok; u += gridDim.x) {
+        const int wi = (int)(u % a.nwt);
+        long long r = u / a.nwt;
+        const int hi = (int)(r % a.nht); r /= a.nht;
+        const int zb = (int)(r % a.nzb);
+        const int nb = (int)(r / a.nzb);
+        const int h0 = hi * a.ht - a.ph, w0 = wi * a.wt - a.pw;
+        for (int j = 0; j < a.nin && ok; ++j) {
+          const int iz = zb * a.P - a.pd + j;  // outside [0, d): TMA fills zeros
+          const int lo = max(0, j - a.ks + 1), hs = min(a.P - 1, j);
+          const int nsl = hs - lo + 1, b0 = (a.ks - 1) - (j - lo);
+          for (int g = 0; g < a.ngroups; ++g) {
+            if (!wait(&empty[stage], epar)) { ok = false; break; }
+            uint8_t* sbase = stage0 + (size_t)stage * a.stage_bytes;
+            const uint32_t wtx = a.wres ? 0u : (uint32_t)(a.nsteps * 2 * nsl) * slot_bytes;
+            mbar_arrive_expect_tx(&full[stage], (uint32_t)a.a_tx + wtx);
+            for (int gi = 0; gi < a.nchg; ++gi)
+              tma_load_5d(sbase + a.chg_roff[gi], &a.maps[a.chg_map[gi]], &full[stage], a.chg_c0[gi] + g * a.stage_c0,
+                          w0, h0, iz, nb);
+            if (!a.wres) {
+              // weight rows of slots [lo, hs] for every K step and half:
+              // global [g][step][half][ks slots][rows] -> smem [step][half][nsl slots][rows]
+              const uint8_t* gsrc = a.wpack + (size_t)g * a.b_bytes + (size_t)b0 * slot_bytes;
+              uint8_t* sdst = sbase + a.a_bytes;
+              for (int sh = 0; sh < 2 * a.nsteps; ++sh)
+                bulk_load(sdst + (size_t)sh * nsl * slot_bytes, gsrc + (size_t)sh * a.ks * slot_bytes,
+                          (uint32_t)nsl * slot_bytes, &full[stage]);
             }
+            pending[stage] = true;
+            last_par[stage] = epar ^ 1;
+            if (++stage == a.stages) { stage = 0; epar ^= 1; }
           }
-          cp_async_commit();
-          if (pt == 0 && !a.wres) {
-            // weight rows of slots [lo, hi] for every K step and half:
-            // global [g][step][half][ks slots][rows] -> smem [step][half][nsl slots][rows]
-            const int lo = max(0, j - a.ks + 1), hi = min(a.P - 1, j);
-            const int nsl = hi - lo + 1, b0 = (a.ks - 1) - (j - lo);
-            const uint32_t slot_bytes = (uint32_t)(a.slot_w * 16);
-            mbar_arrive_expect_tx(&full[stage], (uint32_t)(a.nsteps * 2 * nsl) * slot_bytes);
-            const uint8_t* gsrc = a.wpack + (size_t)g * a.b_bytes + (size_t)b0 * slot_bytes;
-            uint8_t* sdst = sbase + a.a_bytes;
-            for (int sh = 0; sh < 2 * a.nsteps; ++sh)
-              bulk_load(sdst + (size_t)sh * nsl * slot_bytes, gsrc + (size_t)sh * a.ks * slot_bytes,
-                        (uint32_t)nsl * slot_bytes, &full[stage]);
-          }
-          // this thread's copies of the stage arrive on its full barrier when they land
-          cp_async_arrive_noinc(&full[stage]);
-          if (++stage == a.stages) { stage = 0; epar ^= 1; }
         }
       }
-    }
-    // no copy may outlive the CTA
-    cp_async_wait<0>();
-    if (pt == 0 && a.wres) {
-      // no bulk copy may outlive the CTA: wait (bounded) for the weight copy
-      const uint64_t dl = global_timer_ns() + kWaitNs;
-      while (!mbar_try_wait(wbar, 0) && global_timer_ns() < dl) {
+      // no copy may outlive the CTA: wait (bounded) for every stage's last fill
+      for (int s = 0; s < a.stages; ++s) {
+        if (!pending[s]) continue;
+        const uint64_t dl = global_timer_ns() + kWaitNs;
+        while (!mbar_try_wait(&full[s], last_par[s]) && global_timer_ns() < dl) {
+        }
+      }
+      if (a.wres) {
+        const uint64_t dl = global_timer_ns() + kWaitNs;
+        while (!mbar_try_wait(wbar, 0) && global_timer_ns() < dl) {
+        }
       }
     }
   } else if (warp == kMmaWarp) {
     // ---------------- MMA issuer (lane 0) ----------------
     // One thread issues. A warp-wide issuer (elected lane, uniform
-    // descriptors) issues each MMA slightly faster in isolation, but its 31
-    // idle lanes wait in warp-synchronous instructions that take issue slots
-    // from the producer warp sharing the sub-partition; measured slower.
+    // descriptors) issues each MMA slightly faster in isolation but measured
+    // slower inside the pipelined kernel.
     if (lane == 0) {
-    int stage = 0;
-    uint32_t fpar = 0;
-    uint32_t tpar[2] = {0, 0};  // phase 0 of tempty = the epilogue's initial zeroing
-    int set = 0;
-    bool ok = true;
-    if (a.wres && !wait(wbar, 0)) ok = false;
-    const uint32_t bslot = (uint32_t)(a.slot_w * 16);  // bytes of one slot's B rows
-    const int ks = a.ks, Pb = a.P, slot_w = a.slot_w, mtiles = a.mtiles, nsteps = a.nsteps;
-    const int fold = a.fold, ngroups = a.ngroups, nin = a.nin;
-    const uint32_t tile_cols = (uint32_t)(Pb * slot_w);
-    for (long long u = blockIdx.x; u < units && ok; u += gridDim.x) {
-      if (!wait(&tempty[set], tpar[set])) { ok = false; break; }
-      tpar[set] ^= 1;
-      tc_fence_after();
-      const uint32_t dset = tmem + (uint32_t)(set * set_cols);
-      for (int j = 0; j < nin && ok; ++j) {
-        // input plane j feeds output slots lo..hi; one MMA per run of at
-        // most `fold` slots (their B rows are adjacent: slot o uses the
-        // weights of kd = j - o, stored in reverse kd order)
-        const int lo = max(0, j - ks + 1), hi = min(Pb - 1, j);
-        const int b0 = (ks - 1) - (j - lo);
-        const int nsl = hi - lo + 1;
-        uint32_t dd[3] = {0, 0, 0}, bb[3] = {0, 0, 0}, ii[3] = {0, 0, 0};
-        int ns = 0;
-        for (int o = lo; o <= hi && ns < 3; ++ns) {
-          const int n = min(fold, hi - o + 1);
-          dd[ns] = (uint32_t)(o * slot_w);
-          bb[ns] = (uint32_t)(((o - lo) * bslot) >> 4);
-          ii[ns] = a.idesc[n];
-          o += n;
+      int stage = 0;
+      uint32_t fpar = 0;
+      uint32_t tpar[2] = {0, 0};  // phase 0 of tempty = the epilogue's initial zeroing
+      int set = 0;
+      bool ok = true;
+      if (a.wres && !wait(wbar, 0)) ok = false;
+      const uint32_t bslot = (uint32_t)(a.slot_w * 16);  // bytes of one slot's B rows
+      const int ks = a.ks, Pb = a.P, slot_w = a.slot_w, mtiles = a.mtiles, nsteps = a.nsteps;
+      const int fold = a.fold, ngroups = a.ngroups, nin = a.nin;
+      const uint32_t tile_cols = (uint32_t)(Pb * slot_w);
+      for (long long u = blockIdx.x; u < units && ok; u += gridDim.x) {
+        if (!wait(&tempty[set], tpar[set])) { ok = false; break; }
+        tpar[set] ^= 1;
+        tc_fence_after();
+        const uint32_t dset = tmem + (uint32_t)(set * set_cols);
+        for (int j = 0; j < nin && ok; ++j) {
+          // input plane j feeds output slots lo..hi; one MMA per run of at
+          // most `fold` slots (their B rows are adjacent: slot o uses the
+          // weights of kd = j - o, stored in reverse kd order)
+          const int lo = max(0, j - ks + 1), hi = min(Pb - 1, j);
+          const int b0 = (ks - 1) - (j - lo);
+          const int nsl = hi - lo + 1;
+          uint32_t dd[3] = {0, 0, 0}, bb[3] = {0, 0, 0}, ii[3] = {0, 0, 0};
+          int ns = 0;
+          for (int o = lo; o <= hi && ns < 3; ++ns) {
+            const int n = min(fold, hi - o + 1);
+            dd[ns] = (uint32_t)(o * slot_w);
+            bb[ns] = (uint32_t)(((o - lo) * bslot) >> 4);
+            ii[ns] = a.idesc[n];
+            o += n;
+          }
+          // resident weights keep all ks slots per (step, half); staged ones
+          // only the nsl slots of this input plane
+          const int bslots = a.wres ? ks : nsl;
+          const uint64_t bstep = (uint64_t)((2 * bslots * bslot) >> 4);
+          const uint32_t blbo = (uint32_t)(bslots * bslot);
+          for (int g = 0; g < ngroups; ++g) {
+            if (!wait(&full[stage], fpar)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t sA4 = smem_u32(stage0 + (size_t)stage * a.stage_bytes) >> 4;
+            const uint32_t sB = a.wres ? smem_u32(wres_smem + (size_t)g * a.b_bytes) + (uint32_t)b0 * bslot
+                                       : smem_u32(stage0 + (size_t)stage * a.stage_bytes + a.a_bytes);
+            const uint64_t bdesc = smem_desc(sB, blbo, 128);
+            issue(mtiles, ns, s_lo, s_hi, s_ts, nsteps, sA4, bdesc, bstep, dset, tile_cols, dd[0], dd[1], dd[2],
+                  bb[0], bb[1], bb[2], ii[0], ii[1], ii[2]);
+            mma_commit(&empty[stage]);
+            if (++stage == a.stages) { stage = 0; fpar ^= 1; }
+          }
         }
-        // resident weights keep all ks slots per (step, half); staged ones
-        // only the nsl slots of this input plane
-        const int bslots = a.wres ? ks : nsl;
-        const uint64_t bstep = (uint64_t)((2 * bslots * bslot) >> 4);
-        const uint32_t blbo = (uint32_t)(bslots * bslot);
-        for (int g = 0; g < ngroups; ++g) {
-          if (!wait(&full[stage], fpar)) { ok = false; break; }
-          tc_fence_after();
-          // stage A base in 16-byte units, minus the one-unit bias of s_adlo
-          const uint32_t sA4 = ((smem_u32(stage0 + (size_t)stage * a.stage_bytes) + 128u) >> 4) - 1u;
-          const uint32_t sB = a.wres ? smem_u32(wres_smem + (size_t)g * a.b_bytes) + (uint32_t)b0 * bslot
-                                     : smem_u32(stage0 + (size_t)stage * a.stage_bytes + a.a_bytes);
-          const uint64_t bdesc = smem_desc(sB, blbo, 128);
-          issue(mtiles, ns, s_adlo, nsteps, sA4, bdesc, bstep, dset, tile_cols, dd[0], dd[1], dd[2], bb[0], bb[1],
-                bb[2], ii[0], ii[1], ii[2]);
-          mma_commit(&empty[stage]);
-          if (++stage == a.stages) { stage = 0; fpar ^= 1; }
-        }
+        if (!ok) break;
+        mma_commit(&tfull[set]);
+        if (a.nsets == 2) set ^= 1;
       }
-      if (!ok) break;
-      mma_commit(&tfull[set]);
-      if (a.nsets == 2) set ^= 1;
-    }
-    mma_commit(mdone);
-    wait(mdone, 0);
+      mma_commit(mdone);
+      wait(mdone, 0);
     }
   } else {
-    // ---------------- epilogue (warps 9..12) ----------------
+    // ---------------- epilogue (warps 2..5) ----------------
     const int q = warp & 3;
     const int row = q * 32 + lane;
     T* __restrict__ y = static_cast<T*>(a.y);
@@ -913,15 +936,52 @@ static cudaError_t set_smem_attr() {
   return e;
 }
 
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, []() {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// NDHWC activation map, box (cw channels, bw, bh, 1, 1), swizzle by width.
+static bool encode_act(CUtensorMap* m, const void* base, int dtype, int c, int w, int h, int d, int n, int cw, int bw,
+                       int bh) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return false;
+  const cuuint64_t e = 2;
+  cuuint64_t dims[5] = {(cuuint64_t)c, (cuuint64_t)w, (cuuint64_t)h, (cuuint64_t)d, (cuuint64_t)n};
+  cuuint64_t str[4] = {c * e, (cuuint64_t)w * c * e, (cuuint64_t)h * w * c * e, (cuuint64_t)d * h * w * c * e};
+  cuuint32_t box[5] = {(cuuint32_t)cw, (cuuint32_t)bw, (cuuint32_t)bh, 1, 1};
+  cuuint32_t es[5] = {1, 1, 1, 1, 1};
+  const CUtensorMapSwizzle sw = cw == 64   ? CU_TENSOR_MAP_SWIZZLE_128B
+                                : cw == 32 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                : cw == 16 ? CU_TENSOR_MAP_SWIZZLE_32B
+                                           : CU_TENSOR_MAP_SWIZZLE_NONE;
+  return enc(m, dtype == R4C_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5,
+             const_cast<void*>(base), dims, str, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 int launch_conv(const ConvPlan& P, const void* x, const void* w_packed, const void* bias, void* y, int dtype,
                 cudaStream_t st) {
   if (((uintptr_t)x & 15) || ((uintptr_t)w_packed & 15)) return R4C_ERR_ALIGN;
   static_assert(sizeof(TcConvArgs) <= 4096, "kernel argument block too large");
+  StageLayout L;
+  std::vector<Step> steps;
+  if (!plan_layout(P, &L, &steps)) return R4C_ERR_INVALID;
   TcConvArgs a;
   memset(&a, 0, sizeof(a));
-  std::vector<Step> steps;
-  build_steps(P.ks, P.G, P.pitch_w, P.cpb, steps);
-  a.x = x;
   a.wpack = static_cast<const uint8_t*>(w_packed);
   a.bias = bias;
   a.y = y;
@@ -932,23 +992,39 @@ int launch_conv(const ConvPlan& P, const void* x, const void* w_packed, const vo
   a.nht = (P.oh + P.ht - 1) / P.ht;
   a.nwt = (P.ow + P.wt - 1) / P.wt;
   a.nzb = (P.od + P.P - 1) / P.P;
-  // the kernel's fixed-size per-thread tables and unrolled issue blocks
+  // the kernel's fixed-size tables and unrolled issue blocks
   if ((long long)P.n * a.nzb * a.nht * a.nwt != P.work_units) return R4C_ERR_INVALID;
-  if ((P.pitch_w * P.G + kProducerThreads - 1) / kProducerThreads > kMaxEntries) return R4C_ERR_INVALID;
-  if (P.mtiles < 1 || P.mtiles > kMaxMt) return R4C_ERR_INVALID;
+  if (P.mtiles < 1 || P.mtiles > kMaxMt || P.nsteps > kMaxSteps || P.stages > kMaxStages) return R4C_ERR_INVALID;
+  if (P.pitch_w > 256 || P.pitch_h > 256) return R4C_ERR_INVALID;  // TMA box dimensions
   a.pitch_w = P.pitch_w; a.pitch_h = P.pitch_h;
   a.slot_w = P.npad; a.P = P.P; a.nin = P.nin; a.fold = P.fold;
-  a.G = P.G; a.ngroups = P.ngroups; a.nsteps = (int)steps.size();
+  a.ngroups = P.ngroups; a.nsteps = P.nsteps;
+  a.nchg = L.nchg;
+  bool have[4] = {false, false, false, false};
+  for (int gi = 0; gi < L.nchg; ++gi) {
+    a.chg_c0[gi] = L.g[gi].c0;
+    a.chg_map[gi] = map_index(L.g[gi].cw);
+    a.chg_roff[gi] = L.roff[gi];
+    if (!have[a.chg_map[gi]]) {
+      if (!encode_act(&a.maps[a.chg_map[gi]], x, dtype, P.cin, P.w, P.h, P.d, P.n, L.g[gi].cw, P.pitch_w, P.pitch_h))
+        return R4C_ERR_INVALID;
+      have[a.chg_map[gi]] = true;
+    }
+  }
+  a.stage_c0 = L.stage_c0;
   a.mtiles = P.mtiles; a.nsets = P.nsets;
-  a.cpb = P.cpb; a.a_bytes = P.a_bytes; a.b_bytes = P.b_bytes; a.stage_bytes = P.stage_bytes; a.stages = P.stages;
+  a.a_bytes = L.a_bytes; a.a_tx = L.a_tx;
+  a.b_bytes = P.b_bytes; a.stage_bytes = P.stage_bytes; a.stages = P.stages;
   a.wres = P.wres; a.wres_bytes = P.wres_bytes;
   a.tmem_cols = P.tmem_cols;
   a.units = P.work_units;
   for (int k = 1; k <= 3; ++k)
     a.idesc[k] = sm100::instr_desc_f16(dtype == R4C_BF16, 128, std::min(256, k * P.npad), 0, 0);
-  for (int j = 0; j < a.nsteps; ++j) {
-    a.a_off[j] = steps[j].a_off;
-    a.lbo[j] = steps[j].lbo;
+  for (int j = 0; j < P.nsteps; ++j) {
+    const Step& s = steps[j];
+    a.dlo[j] = (uint32_t)((s.a_off >> 4) & 0x3FFF) | ((uint32_t)((s.lbo >> 4) & 0x3FFF) << 16);
+    a.dhi[j] = (uint32_t)((s.sbo >> 4) & 0x3FFF) | (1u << 14) | ((uint32_t)s.layout << 29);
+    a.dts[j] = (uint32_t)(s.tstride >> 4);
   }
   cudaError_t e;
   if (dtype == R4C_BF16) {
@@ -965,12 +1041,6 @@ int launch_conv(const ConvPlan& P, const void* x, const void* w_packed, const vo
   return e == cudaSuccess ? R4C_OK : R4C_ERR_CUDA;
 }
 
-// Launch with the fastest plan measured on this device for this shape.
-// The first call per (shape, dtype, device) times up to a dozen candidate
-// plans that share the model plan's packed-weight layout (so results are
-// bit-identical whichever wins) on the caller's buffers and stream, then
-// caches the winner; the model's plan is used as is while the stream is
-// being captured, when R4C_AUTOTUNE=0, or when R4C_TC_PLAN forces a plan.
 static std::map<PlanKey, ConvPlan> g_tuned;
 static std::mutex g_tuned_mu;
 

@@ -72,6 +72,7 @@ struct ConvPlan {
   int wres;              // 1: the whole packed weight stays resident in smem
   int wres_bytes;        // its size (ks * ngroups * b_bytes) when resident
   int tmem_cols;
+  int stg_bytes;         // output staging buffer (one of two) for TMA stores; 0: per-thread stores
   double est_cycles;     // planner's cost-model estimate for the whole launch
   int64_t work_units;    // n * ceil(od / P) * tiles_h * tiles_w
   int grid;

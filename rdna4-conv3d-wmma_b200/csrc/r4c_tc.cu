@@ -47,6 +47,8 @@
 #include <cstring>
 #include <map>
 #include <mutex>
+#include <numeric>
+#include <string>
 #include <vector>
 
 #include "r4c_internal.h"
@@ -69,6 +71,7 @@ constexpr int kHeader = 4096;     // barriers, bias, descriptor tables
 
 struct alignas(64) TcConvArgs {
   CUtensorMap maps[4];  // x: dims (cin, w, h, d, n), box (cw, pitch_w, pitch_h, 1, 1); cw = 64/32/16/8
+  CUtensorMap ymap;     // y: dims (cout, ow, oh, od, n), box (cout, wt, ht, 1, 1) (TMA-store epilogue)
   const uint8_t* wpack;
   const void* bias;
   void* y;
@@ -86,6 +89,7 @@ struct alignas(64) TcConvArgs {
   int a_bytes, a_tx, b_bytes, stage_bytes, stages;
   int wres, wres_bytes;
   int tmem_cols;
+  int stg_bytes;  // one output staging buffer (two follow the weights); 0: per-thread stores
   long long units;
   uint32_t idesc[4];  // N = 1..3 slots
   // per K step: low descriptor word relative to the stage base (address, LBO),
@@ -221,7 +225,7 @@ static double mma_clk(int n) { return std::max({n / 2.0, 40.0 + n / 6.0, 45.0});
 // G = 8-channel chunks per stage, stages caps the stage count). Unset keys
 // are searched as usual.
 struct PlanForce {
-  int ht = 0, nw = 0, P = 0, G = 0, wres = -1, stages = 0;
+  int ht = 0, nw = 0, P = 0, G = 0, wres = -1, stages = 0, stg = -1;
 };
 static PlanForce plan_force() {
   PlanForce f;
@@ -236,6 +240,7 @@ static PlanForce plan_force() {
     else if (!strcmp(key, "G")) f.G = val;
     else if (!strcmp(key, "wres")) f.wres = val;
     else if (!strcmp(key, "stages")) f.stages = val;
+    else if (!strcmp(key, "stg")) f.stg = val;
     e += used;
     while (*e == ',' || *e == ' ') ++e;
   }
@@ -281,6 +286,11 @@ static void enumerate_plans(int n, int d, int h, int w, int cin, int cout, int k
      if ((P.ow + wt - 1) / wt != nw) continue;
      for (int wres = 1; wres >= 0; --wres) {
       if (force.wres >= 0 && wres != force.wres) continue;
+      // so = 1: TMA-store epilogue through two [ht][wt][cout] staging tiles
+      // (cout % 8 == 0); so = 0: per-thread stores from the TMEM rows
+      for (int so = 1; so >= 0; --so) {
+      if (force.stg >= 0 && so != force.stg) continue;
+      if (so && cout % 8 != 0) continue;
       for (int ht = 1; ht <= P.oh && ht <= 254 - (ks - 1); ++ht) {
         if (force.ht && ht != force.ht) continue;
         const int pitch_w = wt + ks - 1, pitch_h = ht + ks - 1;
@@ -298,7 +308,9 @@ static void enumerate_plans(int n, int d, int h, int w, int cin, int cout, int k
         const int wbytes = ngroups * b_bytes;
         if (wres && wbytes > 96 * 1024) continue;
         const int wres_bytes = wres ? round_up(wbytes, 1024) : 0;
-        const int avail = kSmemMax - kHeader - wres_bytes;
+        const int stg = so ? round_up(ht * wt * cout * 2, 1024) : 0;
+        const int avail = kSmemMax - kHeader - wres_bytes - 2 * stg;
+        if (avail <= 0) continue;
         const int tiles_h = (P.oh + ht - 1) / ht;
         // TMA rows per stage: one per brick position and channel group, about
         // one row per clock (~105 B/clk for 128-byte rows)
@@ -333,9 +345,15 @@ static void enumerate_plans(int n, int d, int h, int w, int cin, int cout, int k
           }
           const double load = (double)nin * ngroups * (std::max(rows_clk, wres ? 0.0 : sb / 30.0) + 150.0);
           // epilogue clocks per unit: per (tile, plane) the TMEM reads (one
-          // wait per 32 columns), 16-byte stores of 8 channels, addressing
+          // wait per 32 columns), 16-byte stores of 8 channels (to global
+          // memory, or to the staging tile with the bank conflicts of its
+          // cout-element row stride, plus a barrier pair and the TMA store
+          // per plane), addressing
+          const int conflict = so ? std::gcd(std::max(cout / 8, 1), 8) : 0;
           const double epi =
-              (double)Pb * mtiles * (((P.npad + 31) / 32) * 100.0 + ((cout + 7) / 8) * 12.0 + 40.0);
+              so ? (double)Pb * (mtiles * (((P.npad + 31) / 32) * 100.0 + ((cout + 7) / 8) * 4.0 * conflict + 40.0) +
+                                 150.0)
+                 : (double)Pb * mtiles * (((P.npad + 31) / 32) * 100.0 + ((cout + 7) / 8) * 12.0 + 40.0);
           double t_unit = std::max(mma, load) + 100.0 * nin * ngroups;
           t_unit = nsets == 2 ? std::max(t_unit, epi) : t_unit + epi;
           const long long units = (long long)n * ((P.od + Pb - 1) / Pb) * tiles_h * nw;
@@ -348,7 +366,8 @@ static void enumerate_plans(int n, int d, int h, int w, int cin, int cout, int k
             P.P = Pb; P.nin = nin;
             P.a_bytes = L.a_bytes; P.b_bytes = b_bytes; P.stage_bytes = stage; P.stages = stages;
             P.wres = wres; P.wres_bytes = wres_bytes;
-            P.smem_bytes = kHeader + wres_bytes + stages * stage;
+            P.smem_bytes = kHeader + wres_bytes + 2 * stg + stages * stage;
+            P.stg_bytes = stg;
             const int cols = nsets * Pb * P.npad * mtiles;
             int alloc = 32;
             while (alloc < cols) alloc *= 2;
@@ -361,6 +380,7 @@ static void enumerate_plans(int n, int d, int h, int w, int cin, int cout, int k
           }
         }
       }
+      }
      }
     }
   }
@@ -371,17 +391,18 @@ struct PlanKey {
   bool operator<(const PlanKey& o) const { return std::lexicographical_compare(v, v + 12, o.v, o.v + 12); }
 };
 
-// Best plan by the cost model; cached per shape and device (the search
-// visits thousands of candidates) unless the tuning override is set.
+// Best plan by the cost model; cached per shape, device and tuning override
+// (the search visits thousands of candidates).
 bool plan_conv(int n, int d, int h, int w, int cin, int cout, int ks, int pd, int ph, int pw, ConvPlan* pl) {
   static std::map<PlanKey, ConvPlan> cache;
   static std::mutex mu;
   int dev = 0;
   cudaGetDevice(&dev);
-  const PlanKey key{{n, d, h, w, cin, cout, ks, pd, ph, pw, dev, 0}};
-  const PlanForce force = plan_force();
-  const bool forced = getenv("R4C_TC_PLAN") != nullptr;
-  if (!forced) {
+  // the tuning override is part of the key (it is read once per call)
+  const char* fs = getenv("R4C_TC_PLAN");
+  const int fh = fs ? (int)(std::hash<std::string>()(std::string(fs)) & 0x7fffffff) | 1 : 0;
+  const PlanKey key{{n, d, h, w, cin, cout, ks, pd, ph, pw, dev, fh}};
+  {
     std::lock_guard<std::mutex> lk(mu);
     auto it = cache.find(key);
     if (it != cache.end()) {
@@ -390,12 +411,13 @@ bool plan_conv(int n, int d, int h, int w, int cin, int cout, int ks, int pd, in
       return true;
     }
   }
+  const PlanForce force = plan_force();
   ConvPlan best{};
   best.ok = false;
   enumerate_plans(n, d, h, w, cin, cout, ks, pd, ph, pw, 0, force, [&](const ConvPlan& c) {
     if (!best.ok || c.est_cycles < best.est_cycles) best = c;
   });
-  if (!forced) {
+  {
     std::lock_guard<std::mutex> lk(mu);
     cache[key] = best;
   }
@@ -406,8 +428,9 @@ bool plan_conv(int n, int d, int h, int w, int cin, int cout, int ks, int pd, in
 
 // Candidates for on-device tuning: the plans with the model's chunks per
 // stage (same packed weights, bit-identical results) ranked by modelled
-// cost, top `k_top`, plus the cheapest of each brick-row count so that a
-// model error in the halo/row trade-off cannot hide the fastest shape.
+// cost, top `k_top`, plus, for each epilogue kind, the cheapest plan of each
+// planes-per-unit count and of each brick-row count, so that an error of the
+// model in the depth/halo/row trade-offs cannot hide the fastest shape.
 static std::vector<ConvPlan> plan_candidates(const ConvPlan& m, int k_top) {
   std::vector<ConvPlan> all;
   PlanForce none;
@@ -416,7 +439,8 @@ static std::vector<ConvPlan> plan_candidates(const ConvPlan& m, int k_top) {
   std::sort(all.begin(), all.end(), [](const ConvPlan& a, const ConvPlan& b) { return a.est_cycles < b.est_cycles; });
   std::vector<ConvPlan> out;
   auto same = [](const ConvPlan& a, const ConvPlan& b) {
-    return a.ht == b.ht && a.wt == b.wt && a.P == b.P && a.wres == b.wres && a.stages == b.stages;
+    return a.ht == b.ht && a.wt == b.wt && a.P == b.P && a.wres == b.wres && a.stages == b.stages &&
+           a.stg_bytes == b.stg_bytes;
   };
   auto add = [&](const ConvPlan& c) {
     for (const ConvPlan& o : out)
@@ -424,9 +448,13 @@ static std::vector<ConvPlan> plan_candidates(const ConvPlan& m, int k_top) {
     out.push_back(c);
   };
   for (size_t i = 0; i < all.size() && (int)out.size() < k_top; ++i) add(all[i]);
-  for (int ht : {1, 2, 4, 8, 16}) {
-    for (const ConvPlan& c : all)
-      if (c.ht == ht) { add(c); break; }
+  for (int so = 0; so <= 1; ++so) {
+    for (int Pb : {1, 2, 3, 4, 5, 6, 8, 12, 16})
+      for (const ConvPlan& c : all)
+        if ((c.stg_bytes > 0) == (so == 1) && c.P == Pb) { add(c); break; }
+    for (int ht : {1, 2, 4, 8, 16})
+      for (const ConvPlan& c : all)
+        if ((c.stg_bytes > 0) == (so == 1) && c.ht == ht) { add(c); break; }
   }
   return out;
 }
@@ -625,6 +653,9 @@ __device__ __forceinline__ void issue(int mt, int ns, R4C_ISSUE_PARAMS) {
 #undef R4C_ISSUE_ARGS
 #undef R4C_ISSUE_PARAMS
 
+// Barrier among the four epilogue warps only (threads 64..191).
+__device__ __forceinline__ void epi_bar_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1) tc_conv_kernel(const __grid_constant__ TcConvArgs a) {
   extern __shared__ __align__(1024) uint8_t smem[];
@@ -636,12 +667,14 @@ __global__ void __launch_bounds__(kThreads, 1) tc_conv_kernel(const __grid_const
   uint64_t* wbar = mdone + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(wbar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* epi_ok = reinterpret_cast<volatile int*>(smem + 256);  // one flag per epilogue warp
   float* sbias = reinterpret_cast<float*>(smem + 1024);        // 256 floats
   uint32_t* s_lo = reinterpret_cast<uint32_t*>(smem + 2048);   // kMaxSteps each
   uint32_t* s_hi = s_lo + kMaxSteps;
   uint32_t* s_ts = s_hi + kMaxSteps;
   uint8_t* wres_smem = smem + kHeader;
-  uint8_t* stage0 = smem + kHeader + a.wres_bytes;
+  uint8_t* stg0 = smem + kHeader + a.wres_bytes;  // two output staging tiles when stg_bytes > 0
+  uint8_t* stage0 = stg0 + 2 * a.stg_bytes;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -849,6 +882,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_conv_kernel(const __grid_const
     const bool vec_ok = (a.cout % 8) == 0;
     uint32_t fpar[2] = {0, 0};
     int set = 0;
+    int sbuf = 0;  // staging tile of the TMA-store epilogue
     // Every MMA accumulates, so the accumulators start at zero: this warp
     // zeroes its lane quarter of every set now and of each set it drains,
     // and releases a set (tempty) only after those stores completed.
@@ -871,12 +905,66 @@ __global__ void __launch_bounds__(kThreads, 1) tc_conv_kernel(const __grid_const
       int got = 1;
       if (lane == 0) got = wait(&tfull[set], fpar[set], 128) ? 1 : 0;
       got = __shfl_sync(0xffffffffu, got, 0);
+      if (a.stg_bytes) {
+        // The TMA-store path synchronises the four epilogue warps on a named
+        // barrier, so they leave the loop together: agree on the wait results.
+        if (lane == 0) epi_ok[q] = got;
+        epi_bar_sync();
+        got = epi_ok[0] & epi_ok[1] & epi_ok[2] & epi_ok[3];
+      }
       if (!got) break;
       fpar[set] ^= 1;
       tc_fence_after();
+      const int nz = min(a.P, a.od - z0);
+      if (a.stg_bytes) {
+        // Per output plane: TMEM -> bias, rounding -> staging tile
+        // [ht][wt][cout] in shared memory -> one TMA store, which clips the
+        // positions outside the volume. Two staging tiles alternate; a tile is
+        // rewritten only after the store issued from it two planes earlier has
+        // finished reading it. Planes past the volume's depth are only zeroed.
+        for (int o = 0; o < a.P; ++o) {
+          const bool live = o < nz;
+          if (live) {
+            if (threadIdx.x == 64) bulk_wait_read<1>();
+            epi_bar_sync();
+          }
+          T* sb = reinterpret_cast<T*>(stg0 + (size_t)sbuf * a.stg_bytes);
+          for (int t = 0; t < a.mtiles; ++t) {
+            const int p = t * 128 + row;
+            const int hh = p / a.pitch_w;
+            const int ww = p - hh * a.pitch_w;
+            const bool valid = live && hh < a.ht && ww < a.wt;
+            T* dst = sb + ((size_t)hh * a.wt + ww) * a.cout;
+            const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) +
+                                (uint32_t)(set * set_cols + t * a.P * a.slot_w + o * a.slot_w);
+            int cc = 0;
+            for (; cc + 32 <= a.slot_w; cc += 32) {
+              float v[32];
+              tmem_ld_32(tb + (uint32_t)cc, v);
+              tmem_zero_16(tb + (uint32_t)cc);
+              tmem_zero_16(tb + (uint32_t)cc + 16u);
+              if (valid) store_row<T, 32>(dst, v, sbias, cc, a.cout, true);
+            }
+            if (cc < a.slot_w) {
+              float v[16];
+              tmem_ld_16(tb + (uint32_t)cc, v);
+              tmem_zero_16(tb + (uint32_t)cc);
+              if (valid) store_row<T, 16>(dst, v, sbias, cc, a.cout, true);
+            }
+          }
+          if (live) {
+            fence_proxy_async_smem();  // staging writes become visible to the TMA engine
+            epi_bar_sync();
+            if (threadIdx.x == 64) {
+              tma_store_5d(&a.ymap, sb, 0, w0, h0, z0 + o, nb);
+              bulk_commit_group();
+            }
+            sbuf ^= 1;
+          }
+        }
+      } else {
       const long long plane = (long long)a.oh * a.ow * a.cout;  // elements per output plane
       T* const yu = y + ((((long long)nb * a.od + z0) * a.oh + h0) * a.ow + w0) * a.cout;
-      const int nz = min(a.P, a.od - z0);
       for (int t = 0; t < a.mtiles; ++t) {
         const int p = t * 128 + row;
         const int hh = p / a.pitch_w;
@@ -903,12 +991,15 @@ __global__ void __launch_bounds__(kThreads, 1) tc_conv_kernel(const __grid_const
           }
         }
       }
+      }
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[set]);
       if (a.nsets == 2) set ^= 1;
     }
+    // the TMA stores must have finished before the CTA exits
+    if (a.stg_bytes && threadIdx.x == 64) bulk_wait<0>();
   }
 
   tc_fence_before();
@@ -1018,6 +1109,25 @@ int launch_conv(const ConvPlan& P, const void* x, const void* w_packed, const vo
   a.wres = P.wres; a.wres_bytes = P.wres_bytes;
   a.tmem_cols = P.tmem_cols;
   a.units = P.work_units;
+  // Output map for the TMA-store epilogue: box (cout, wt, ht, 1, 1) over the
+  // NDHWC output. Without it (unaligned output, odd sizes) the epilogue stores
+  // per thread and the staging space stays unused.
+  a.stg_bytes = 0;
+  if (P.stg_bytes > 0 && ((uintptr_t)y & 15) == 0 && P.cout % 8 == 0 && P.cout <= 256 && P.wt <= 256 &&
+      P.ht <= 256 && P.stg_bytes >= P.ht * P.wt * P.cout * 2) {
+    EncodeTiledFn enc = get_encode_fn();
+    const cuuint64_t e = 2;
+    cuuint64_t dims[5] = {(cuuint64_t)P.cout, (cuuint64_t)P.ow, (cuuint64_t)P.oh, (cuuint64_t)P.od,
+                          (cuuint64_t)P.n};
+    cuuint64_t str[4] = {(cuuint64_t)P.cout * e, (cuuint64_t)P.ow * P.cout * e,
+                         (cuuint64_t)P.oh * P.ow * P.cout * e, (cuuint64_t)P.od * P.oh * P.ow * P.cout * e};
+    cuuint32_t box[5] = {(cuuint32_t)P.cout, (cuuint32_t)P.wt, (cuuint32_t)P.ht, 1, 1};
+    cuuint32_t es[5] = {1, 1, 1, 1, 1};
+    if (enc && enc(&a.ymap, dtype == R4C_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5,
+                   y, dims, str, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                   CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS)
+      a.stg_bytes = P.stg_bytes;
+  }
   for (int k = 1; k <= 3; ++k)
     a.idesc[k] = sm100::instr_desc_f16(dtype == R4C_BF16, 128, std::min(256, k * P.npad), 0, 0);
   for (int j = 0; j < P.nsteps; ++j) {

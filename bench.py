@@ -369,7 +369,11 @@ def main():
         run_step(layers, reducer, legs=legs)
     torch.cuda.synchronize()
 
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in layers]
+    # per step, per layer: events around the fwd / dW / dX legs; the host runs
+    # ahead of the GPU (no synchronize inside the timed loop), so a leg's time
+    # is the GPU's and holds no host launch latency
+    evs = [[[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in layers]
+           for _ in range(args.steps)]
     leg_ms = [[0.0, 0.0, 0.0] for _ in layers]
     sampler = ClockSampler(local)
     barrier(world)
@@ -379,14 +383,14 @@ def main():
     n_launch0 = _native.launch_count()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record()
-    for _ in range(args.steps):
-        run_step(layers, reducer, ev, legs=legs)
-        torch.cuda.synchronize()
+    for s in range(args.steps):
+        run_step(layers, reducer, evs[s], legs=legs)
+    t1.record()
+    torch.cuda.synchronize()
+    for ev in evs:
         for i in range(len(layers)):
             for j in range(3):
                 leg_ms[i][j] += ev[i][j].elapsed_time(ev[i][j + 1])
-    t1.record()
-    torch.cuda.synchronize()
     launches = _native.launch_count() - n_launch0
     clocks = sampler.stop()
     ms_total = max_over_ranks(t0.elapsed_time(t1), world)

@@ -144,6 +144,12 @@ cudaError_t launch_cpad(const void* x, void* xp, const Geom& g, int dtype, cudaS
   return cudaGetLastError();
 }
 
+// Forward of a k=3 layer with 1..4 input channels: the stem kernel.
+bool use_stem(const r4c_conv_desc* ds, int leg, const Geom& g) {
+  if (ds->force_kernel == R4C_KERNEL_GENERIC || leg != R4C_LEG_FWD) return false;
+  return stem::supported(g.n, g.d, g.h, g.w, g.cin, g.cout, g.k, g.pd, g.ph, g.pw);
+}
+
 bool use_tc(const r4c_conv_desc* ds, int leg, const Geom& g, tc::ConvPlan* pl) {
   if (ds->force_kernel == R4C_KERNEL_GENERIC) return false;
   if (leg == R4C_LEG_FWD)
@@ -193,7 +199,7 @@ int r4c_plan_kernel(const r4c_conv_desc* desc, int leg) {
   int st = check_desc(desc, leg, &g);
   if (st != R4C_OK) return st;
   tc::ConvPlan pl;
-  if (use_tc(desc, leg, g, &pl)) return R4C_KERNEL_TC;
+  if (use_stem(desc, leg, g) || use_tc(desc, leg, g, &pl)) return R4C_KERNEL_TC;
   return R4C_KERNEL_GENERIC;
 }
 
@@ -205,7 +211,10 @@ int r4c_describe_plan(const r4c_conv_desc* desc, int leg, char* buf, size_t len)
     snprintf(tmp, sizeof(tmp), "invalid: %s", r4c_strerror(st));
   } else {
     tc::ConvPlan pl;
-    if (leg == R4C_LEG_DW && use_tc(desc, leg, g, &pl)) {
+    if (use_stem(desc, leg, g)) {
+      stem::describe(g.n, g.d, g.h, g.w, g.cin, g.cout, g.pd, g.ph, g.pw, tmp, sizeof(tmp));
+      st = R4C_KERNEL_TC;
+    } else if (leg == R4C_LEG_DW && use_tc(desc, leg, g, &pl)) {
       tc::dw_describe(g.n, g.d, g.h, g.w, cin_eff(g), g.cout, g.k, g.pd, g.ph, g.pw, tmp, sizeof(tmp));
       if (needs_cpad(g)) strncat(tmp, " (input channels padded to a multiple of 8)", sizeof(tmp) - strlen(tmp) - 1);
       st = R4C_KERNEL_TC;
@@ -241,6 +250,7 @@ int r4c_describe_plan(const r4c_conv_desc* desc, int leg, char* buf, size_t len)
 size_t r4c_packed_weight_bytes(const r4c_conv_desc* desc, int leg) {
   Geom g;
   if (check_desc(desc, leg, &g) != R4C_OK) return 0;
+  if (use_stem(desc, leg, g)) return stem::packed_bytes(g.cin, g.cout);
   tc::ConvPlan pl;
   if (use_tc(desc, leg, g, &pl)) return tc::packed_bytes(pl);
   int taps = (leg == R4C_LEG_TFWD || leg == R4C_LEG_TDX) ? 8 : g.k * g.k * g.k;
@@ -255,6 +265,7 @@ size_t r4c_workspace_size(const r4c_conv_desc* desc, int leg) {
     if (use_tc(desc, leg, g, &pl)) return cpad_bytes(g) + tc_dw_ws(g, nullptr);
   }
   if (leg == R4C_LEG_FWD) {
+    if (use_stem(desc, leg, g)) return 0;
     tc::ConvPlan pl;
     if (use_tc(desc, leg, g, &pl)) return cpad_bytes(g);
   }
@@ -275,6 +286,10 @@ int r4c_pack_weight(const r4c_conv_desc* desc, int leg, const void* w_src, int s
   if (src_dtype != R4C_F32 && src_dtype != R4C_BF16 && src_dtype != R4C_F16) return R4C_ERR_INVALID;
   if (!w_src || !w_packed) return R4C_ERR_INVALID;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (use_stem(desc, leg, g)) {
+    if ((reinterpret_cast<uintptr_t>(w_packed) & 15) != 0) return R4C_ERR_ALIGN;
+    return cuda_status(stem::pack_weight(g.cin, g.cout, w_src, src_dtype, w_packed, desc->dtype, s));
+  }
   tc::ConvPlan pl;
   if (use_tc(desc, leg, g, &pl)) {
     if ((reinterpret_cast<uintptr_t>(w_packed) & 15) != 0) return R4C_ERR_ALIGN;
@@ -303,6 +318,9 @@ int r4c_conv3d_fwd(const r4c_conv_desc* desc, const void* x, const void* w_packe
   if (g.out_vox() == 0) return R4C_OK;
   if (!x || !w_packed || !y) return R4C_ERR_INVALID;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (use_stem(desc, R4C_LEG_FWD, g))
+    return stem::launch_fwd(g.n, g.d, g.h, g.w, g.cin, g.cout, g.pd, g.ph, g.pw, x, w_packed, bias, y,
+                            desc->dtype, s);
   tc::ConvPlan pl;
   if (use_tc(desc, R4C_LEG_FWD, g, &pl)) {
     const void* xin = x;

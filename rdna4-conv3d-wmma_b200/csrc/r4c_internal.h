@@ -109,4 +109,16 @@ int launch_dw(int n, int d, int h, int w, int cin, int cin_real, int cout, int k
 
 }  // namespace tc
 
+// tcgen05 forward conv for k=3 layers with 1..4 input channels (r4c_tc_stem.cu):
+// raw input brick by TMA, im2col rows built in shared memory, K = 27*Cin.
+namespace stem {
+bool supported(int n, int d, int h, int w, int cin, int cout, int ks, int pd, int ph, int pw);
+size_t packed_bytes(int cin, int cout);
+cudaError_t pack_weight(int cin, int cout, const void* w_src, int src_dtype, void* w_packed, int dtype,
+                        cudaStream_t st);
+int launch_fwd(int n, int d, int h, int w, int cin, int cout, int pd, int ph, int pw, const void* x,
+               const void* w_packed, const void* bias, void* y, int dtype, cudaStream_t st);
+int describe(int n, int d, int h, int w, int cin, int cout, int pd, int ph, int pw, char* buf, size_t len);
+}  // namespace stem
+
 }  // namespace r4c

@@ -47,6 +47,16 @@ CONV_CASES = [
     (1, 16, 200, 3, 4, 5, 3, 1),       # Cout not a multiple of 16
     (1, 32, 256, 2, 4, 8, 3, 1),       # Cout = 256
     (0, 24, 24, 4, 4, 4, 3, 1),        # empty batch
+    # stem kernel (forward, 1..4 input channels, W*Cin a multiple of 8)
+    (2, 2, 16, 5, 9, 12, 3, 1),
+    (1, 3, 8, 4, 6, 8, 3, 0),
+    (1, 4, 32, 3, 5, 10, 3, 2),
+    (1, 1, 24, 3, 4, 200, 3, 1),       # brick row of 200 columns
+    (1, 1, 24, 2, 3, 296, 3, 1),       # two brick columns
+    (1, 4, 24, 2, 3, 100, 3, 1),       # Cin=4: 50-column bricks
+    (1, 1, 48, 6, 7, 16, 3, 1),        # Cout 48: five M tiles per unit
+    (1, 1, 7, 3, 5, 8, 3, 1),          # Cout 7: scalar stores
+    (1, 2, 256, 2, 3, 8, 3, 1),        # Cout 256
 ]
 TCONV_CASES = [
     (2, 16, 8, 3, 4, 5),

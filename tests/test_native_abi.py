@@ -61,6 +61,28 @@ def test_plan_families():
     assert "tcgen05" in _native.describe_plan(_d(), _native.LEG_FWD)
 
 
+def test_stem_family():
+    # k=3 forward with 1..4 input channels (and W*Cin a multiple of 8): the stem
+    # kernel, no channel-padding workspace, weight image [16-padded Cout][K]
+    # with K = 9 groups of 4*Cin (3*Cin taps + Cin zeros) rounded up to 16
+    for cin, cout, w, kpad in ((1, 24, 32, 48), (2, 16, 12, 80), (3, 8, 8, 112), (4, 200, 10, 144)):
+        dsc = _d(cin=cin, cout=cout, w=w)
+        assert _native.plan_kernel(dsc, _native.LEG_FWD) == _native.KERNEL_TC
+        assert "stem" in _native.describe_plan(dsc, _native.LEG_FWD)
+        assert _native.workspace_bytes(dsc, _native.LEG_FWD) == 0
+        assert _native.packed_weight_bytes(dsc, _native.LEG_FWD) == (cout + 15) // 16 * 16 * kpad * 2
+        # the other legs of the layer keep their kernels
+        assert "stem" not in _native.describe_plan(dsc, _native.LEG_DW)
+        assert "stem" not in _native.describe_plan(dsc, _native.LEG_DX)
+    # rows whose byte stride is not a multiple of 16, k=1 and 5+ channels stay
+    # on the general kernel; forcing the SIMT family still works
+    assert "stem" not in _native.describe_plan(_d(cin=3, w=30), _native.LEG_FWD)
+    assert _native.workspace_bytes(_d(cin=3, w=30), _native.LEG_FWD) > 0
+    assert "stem" not in _native.describe_plan(_d(cin=2, k=1, p=0), _native.LEG_FWD)
+    assert "stem" not in _native.describe_plan(_d(cin=5, w=8), _native.LEG_FWD)
+    assert _native.plan_kernel(_d(cin=1, force=1), _native.LEG_FWD) == _native.KERNEL_GENERIC
+
+
 def test_descriptor_validation():
     assert _native.plan_kernel(_d(k=5), _native.LEG_FWD) == -2       # unsupported
     assert _native.plan_kernel(_d(k=3), _native.LEG_TFWD) == -2      # tconv needs k=2

@@ -383,8 +383,10 @@ def main():
     n_launch0 = _native.launch_count()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record()
+    h0 = time.perf_counter()
     for s in range(args.steps):
         run_step(layers, reducer, evs[s], legs=legs)
+    host_ms = (time.perf_counter() - h0) * 1e3 / args.steps  # host time to issue a step
     t1.record()
     torch.cuda.synchronize()
     for ev in evs:
@@ -463,7 +465,7 @@ def main():
                        "l2": "no flush: each step streams ~1.7 GB of activations, far above the 126 MB L2"},
             "gflop_per_step_per_gpu": round(step_flops / 1e9, 2),
             "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": int(launches),
-            "clocks": clocks, "layers": breakdown,
+            "clocks": clocks, "host_issue_ms_per_step": round(host_ms, 3), "layers": breakdown,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

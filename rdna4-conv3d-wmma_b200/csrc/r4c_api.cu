@@ -150,6 +150,12 @@ bool use_stem(const r4c_conv_desc* ds, int leg, const Geom& g) {
   return stem::supported(g.n, g.d, g.h, g.w, g.cin, g.cout, g.k, g.pd, g.ph, g.pw);
 }
 
+// Weight gradient of the same layers (Cout a multiple of 8): the stem dW kernel.
+bool use_stem_dw(const r4c_conv_desc* ds, int leg, const Geom& g) {
+  if (ds->force_kernel == R4C_KERNEL_GENERIC || leg != R4C_LEG_DW) return false;
+  return stem::dw_supported(g.n, g.d, g.h, g.w, g.cin, g.cout, g.k, g.pd, g.ph, g.pw);
+}
+
 bool use_tc(const r4c_conv_desc* ds, int leg, const Geom& g, tc::ConvPlan* pl) {
   if (ds->force_kernel == R4C_KERNEL_GENERIC) return false;
   if (leg == R4C_LEG_FWD)
@@ -199,7 +205,7 @@ int r4c_plan_kernel(const r4c_conv_desc* desc, int leg) {
   int st = check_desc(desc, leg, &g);
   if (st != R4C_OK) return st;
   tc::ConvPlan pl;
-  if (use_stem(desc, leg, g) || use_tc(desc, leg, g, &pl)) return R4C_KERNEL_TC;
+  if (use_stem(desc, leg, g) || use_stem_dw(desc, leg, g) || use_tc(desc, leg, g, &pl)) return R4C_KERNEL_TC;
   return R4C_KERNEL_GENERIC;
 }
 
@@ -213,6 +219,9 @@ int r4c_describe_plan(const r4c_conv_desc* desc, int leg, char* buf, size_t len)
     tc::ConvPlan pl;
     if (use_stem(desc, leg, g)) {
       stem::describe(g.n, g.d, g.h, g.w, g.cin, g.cout, g.pd, g.ph, g.pw, tmp, sizeof(tmp));
+      st = R4C_KERNEL_TC;
+    } else if (use_stem_dw(desc, leg, g)) {
+      stem::dw_describe(g.n, g.d, g.h, g.w, g.cin, g.cout, g.pd, g.ph, g.pw, tmp, sizeof(tmp));
       st = R4C_KERNEL_TC;
     } else if (leg == R4C_LEG_DW && use_tc(desc, leg, g, &pl)) {
       tc::dw_describe(g.n, g.d, g.h, g.w, cin_eff(g), g.cout, g.k, g.pd, g.ph, g.pw, tmp, sizeof(tmp));
@@ -261,6 +270,7 @@ size_t r4c_workspace_size(const r4c_conv_desc* desc, int leg) {
   Geom g;
   if (check_desc(desc, leg, &g) != R4C_OK) return 0;
   if (leg == R4C_LEG_DW) {
+    if (use_stem_dw(desc, leg, g)) return stem::dw_workspace(g.n, g.d, g.h, g.w, g.cin, g.cout, g.pd, g.ph, g.pw);
     tc::ConvPlan pl;
     if (use_tc(desc, leg, g, &pl)) return cpad_bytes(g) + tc_dw_ws(g, nullptr);
   }
@@ -371,6 +381,11 @@ int r4c_conv3d_dw(const r4c_conv_desc* desc, const void* x, const void* go, floa
   if (!dw) return R4C_ERR_INVALID;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const int taps = g.k * g.k * g.k;
+  if (g.out_vox() > 0 && use_stem_dw(desc, R4C_LEG_DW, g)) {
+    if (!x || !go) return R4C_ERR_INVALID;
+    return stem::launch_dw(g.n, g.d, g.h, g.w, g.cin, g.cout, g.pd, g.ph, g.pw, x, go, dw, db, workspace, ws_bytes,
+                           desc->dtype, s);
+  }
   tc::ConvPlan tcp;
   if (g.out_vox() > 0 && use_tc(desc, R4C_LEG_DW, g, &tcp)) {
     size_t part_bytes = 0;

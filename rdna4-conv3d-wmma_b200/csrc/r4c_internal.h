@@ -119,6 +119,13 @@ cudaError_t pack_weight(int cin, int cout, const void* w_src, int src_dtype, voi
 int launch_fwd(int n, int d, int h, int w, int cin, int cout, int pd, int ph, int pw, const void* x,
                const void* w_packed, const void* bias, void* y, int dtype, cudaStream_t st);
 int describe(int n, int d, int h, int w, int cin, int cout, int pd, int ph, int pw, char* buf, size_t len);
+// Weight gradient (dW fp32 OIDHW, db fp32 when non-null) of the same layers,
+// Cout a multiple of 8; `ws` holds one fp32 partial per CTA.
+bool dw_supported(int n, int d, int h, int w, int cin, int cout, int ks, int pd, int ph, int pw);
+size_t dw_workspace(int n, int d, int h, int w, int cin, int cout, int pd, int ph, int pw);
+int dw_describe(int n, int d, int h, int w, int cin, int cout, int pd, int ph, int pw, char* buf, size_t len);
+int launch_dw(int n, int d, int h, int w, int cin, int cout, int pd, int ph, int pw, const void* x, const void* go,
+              float* dw, float* db, void* ws, size_t ws_bytes, int dtype, cudaStream_t st);
 }  // namespace stem
 
 }  // namespace r4c

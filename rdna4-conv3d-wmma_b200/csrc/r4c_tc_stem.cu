@@ -131,7 +131,7 @@ template <int C> struct StemK {
 // (m%8)*16).
 template <int C>
 __device__ __forceinline__ void build_row(uint8_t* slot, int m, const uint16_t* raw, int row_elems, int plane_elems,
-                                          uint32_t odd, bool live) {
+                                          uint32_t odd, bool live, uint32_t one = 0u) {
   using K = StemK<C>;
   uint32_t wr[K::WORDS];
 #pragma unroll
@@ -160,12 +160,44 @@ __device__ __forceinline__ void build_row(uint8_t* slot, int m, const uint16_t* 
         wr[g * K::GW + (3 * C - 1) / 2] = __byte_perm(v[NL - 1], 0u, odd ? 0x4432u : 0x4410u);
       }
     }
+    // the weight gradient's db slot: element 3C (the first zero slot of
+    // group 0) holds `one` (the 16-bit pattern of 1.0; 0 for the forward)
+    wr[(3 * C) / 2] |= one << (16 * ((3 * C) & 1));
   }
   uint8_t* base = slot + (m >> 3) * (K::KPAD * 16) + (m & 7) * 16;
 #pragma unroll
   for (int j = 0; j < K::KPAD / 8; ++j)
     *reinterpret_cast<uint4*>(base + j * 128) = make_uint4(wr[4 * j], wr[4 * j + 1], wr[4 * j + 2], wr[4 * j + 3]);
 }
+
+// This CTA's units u = blockIdx.x, + gridDim.x, ... as (nb, zb, hi, wi), wi
+// fastest, advanced by carries (one add and compare per digit) rather than
+// four divisions per unit in every role.
+struct UnitWalk {
+  int wi, hi, zb, nb, gw, gh, gz, gn;
+  template <class Args> __device__ void init(const Args& a) {
+    int u = blockIdx.x;
+    wi = u % a.nwt; u /= a.nwt;
+    hi = u % a.nht; u /= a.nht;
+    zb = u % a.nzb; nb = u / a.nzb;
+    int g = gridDim.x;
+    gw = g % a.nwt; g /= a.nwt;
+    gh = g % a.nht; g /= a.nht;
+    gz = g % a.nzb; gn = g / a.nzb;
+  }
+  template <class Args> __device__ void next(const Args& a) {
+    wi += gw;
+    int c = wi >= a.nwt;
+    if (c) wi -= a.nwt;
+    hi += gh + c;
+    c = hi >= a.nht;
+    if (c) hi -= a.nht;
+    zb += gz + c;
+    c = zb >= a.nzb;
+    if (c) zb -= a.nzb;
+    nb += gn + c;
+  }
+};
 
 template <typename T, int C>
 __global__ void __launch_bounds__(kThreads, 1) stem_fwd_kernel(const __grid_constant__ StemArgs a) {
@@ -241,34 +273,6 @@ __global__ void __launch_bounds__(kThreads, 1) stem_fwd_kernel(const __grid_cons
       }
     }
     return true;
-  };
-  // This CTA's units u = blockIdx.x, + gridDim.x, ... as (nb, zb, hi, wi),
-  // wi fastest, advanced by carries (one add and compare per digit) rather
-  // than four divisions per unit in every role.
-  struct UnitWalk {
-    int wi, hi, zb, nb, gw, gh, gz, gn;
-    __device__ void init(const StemArgs& a) {
-      int u = blockIdx.x;
-      wi = u % a.nwt; u /= a.nwt;
-      hi = u % a.nht; u /= a.nht;
-      zb = u % a.nzb; nb = u / a.nzb;
-      int g = gridDim.x;
-      gw = g % a.nwt; g /= a.nwt;
-      gh = g % a.nht; g /= a.nht;
-      gz = g % a.nzb; gn = g / a.nzb;
-    }
-    __device__ void next(const StemArgs& a) {
-      wi += gw;
-      int c = wi >= a.nwt;
-      if (c) wi -= a.nwt;
-      hi += gh + c;
-      c = hi >= a.nht;
-      if (c) hi -= a.nht;
-      zb += gz + c;
-      c = zb >= a.nzb;
-      if (c) zb -= a.nzb;
-      nb += gn + c;
-    }
   };
   UnitWalk uw;
   uw.init(a);
@@ -450,6 +454,287 @@ __global__ void __launch_bounds__(kThreads, 1) stem_fwd_kernel(const __grid_cons
     tc_fence_after();
     tmem_dealloc(tmem, (uint32_t)a.tmem_cols);
   }
+}
+
+// ---------------------------------------------------------------------------
+// Weight gradient of the stem conv (k=3, 1..4 input channels):
+//   dW[co][c][kd][kh][kw] = sum_v dY[v][co] * x[v + (kd,kh,kw) - pad][c]
+//   db[co]                = sum_v dY[v][co]
+// as D[k][co] += A[k][v] * B[v][co] over the output positions v of each work
+// unit (reference counterpart: the _wgrad_kernel GEMM with K = voxels and the
+// separate db sum). A is the unit's im2col rows, built exactly as for the
+// forward and read here as an MN-major operand (M = the StemK slots k, K =
+// positions; slot 3C of group 0 holds ones, so D row 3C is db). B is the
+// unit's dY brick: one TMA box of whole-channel rows (Cout*2 bytes, one TMA
+// row per position) that the builders re-lay into 8-channel planes (MN-major,
+// N = Cout). Each CTA accumulates all its units in one TMEM accumulator and
+// writes it once as an fp32 partial; stem_dw_reduce sums the partials in CTA
+// order (deterministic).
+// Warps: 0 TMA producer, 1 MMA issuer, 2..9 builders (and, at the end, 2..5
+// read the accumulator, one TMEM lane quarter each).
+constexpr int kDwBuildWarps = 8;
+constexpr int kDwThreads = 64 + 32 * kDwBuildWarps;
+constexpr int kDwMaxStages = 16;
+constexpr int kDwMaxBufs = 3;  // A+B buffer pairs: builders up to two units ahead of the MMA
+
+struct StemDwArgs {
+  CUtensorMap xmap;  // as StemArgs::xmap
+  CUtensorMap gmap;  // dY: (Cout, OW, OH, OD, N), box (Cout, bw, bh, P, 1)
+  float* part;       // [gridDim.x][kpad][npad] fp32
+  int* err;
+  int n, d, h, w, cin, cout;
+  int od, oh, ow, pd, ph, pw;
+  int bw, bh, P, wb, walign;
+  int nwt, nht, nzb;
+  int units;
+  int mtiles, npad, kpad, mk;    // mk: 128-row M tiles over the kpad slots
+  int raw_bytes, raw_tx, g_tx;   // stage = raw brick (raw_bytes) + dY brick
+  int stage_bytes, nstages;
+  int a_bytes, abuf_bytes;       // A tile (128 positions x kpad), A buffer (mtiles tiles)
+  int plane_bytes, bbuf_bytes;   // B: npad/8 planes of mtiles*128 positions x 16 B
+  int nbufs;                     // A+B buffer pairs (2 or 3)
+  int tmem_cols;
+  uint32_t idesc;
+  uint32_t one;                  // 16-bit pattern of 1.0 in the element type
+};
+
+template <int C>
+__global__ void __launch_bounds__(kDwThreads, 1) stem_dw_kernel(const __grid_constant__ StemDwArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint64_t* in_full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* in_empty = in_full + kDwMaxStages;
+  uint64_t* b_full = in_empty + kDwMaxStages;  // A+B buffer pair ready
+  uint64_t* b_empty = b_full + kDwMaxBufs;
+  uint64_t* mdone = b_empty + kDwMaxBufs;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mdone + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint8_t* st0 = smem + kHeader;                         // input stages
+  uint8_t* abuf0 = st0 + a.nstages * a.stage_bytes;      // nbufs A buffers
+  uint8_t* bbuf0 = abuf0 + a.nbufs * a.abuf_bytes;       // nbufs B buffers (also take the M=128
+                                                         // over-read of the last A buffer)
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  if ((smem_u32(smem) & 1023u) != 0u || a.tmem_cols > 512) {
+    if (threadIdx.x == 0) atomicExch(a.err, 2);
+    return;
+  }
+  // B planes for channels at or above Cout (npad padding) stay zero
+  for (int bi = 0; bi < a.nbufs; ++bi)
+    for (int pl = a.cout / 8; pl < a.npad / 8; ++pl)
+      for (int i = threadIdx.x * 16; i < a.plane_bytes; i += kDwThreads * 16)
+        *reinterpret_cast<uint4*>(bbuf0 + (size_t)bi * a.bbuf_bytes + (size_t)pl * a.plane_bytes + i) =
+            make_uint4(0, 0, 0, 0);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kDwMaxStages; ++s) {
+      mbar_init(&in_full[s], 1);
+      mbar_init(&in_empty[s], kDwBuildWarps);
+    }
+    for (int s = 0; s < kDwMaxBufs; ++s) {
+      mbar_init(&b_full[s], kDwBuildWarps);
+      mbar_init(&b_empty[s], 1);
+    }
+    mbar_init(mdone, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, (uint32_t)a.tmem_cols);
+    tmem_relinquish();
+  }
+  fence_proxy_async_smem();  // the zeroed B planes, for the tensor core
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  const uint64_t kWaitNs = 1000000000ull;
+  auto wait = [&](uint64_t* bar, uint32_t par, uint32_t nap = 0) -> bool {
+    const uint64_t deadline = global_timer_ns() + kWaitNs;
+    uint32_t spins = 0;
+    while (!mbar_try_wait(bar, par)) {
+      if (nap) __nanosleep(nap);
+      if (((++spins) & 63u) == 0) {
+        if (*abort_flag) return false;
+        if (global_timer_ns() > deadline) {
+          *abort_flag = 1;
+          atomicExch(a.err, 1);
+          return false;
+        }
+      }
+    }
+    return true;
+  };
+  UnitWalk uw;
+  uw.init(a);
+
+  if (warp == 0) {
+    // ---------------- TMA producer: raw x brick + dY brick per unit ----------------
+    if (lane == 0) {
+      prefetch_tmap(&a.xmap);
+      prefetch_tmap(&a.gmap);
+      int s = 0;
+      uint32_t epar = 1;
+      uint32_t pending = 0u, last_par = 0u;  // per stage bits
+      for (int u = blockIdx.x; u < a.units; u += gridDim.x, uw.next(a)) {
+        const int nb = uw.nb, z0 = uw.zb * a.P, y0 = uw.hi * a.bh, x0 = uw.wi * a.bw;
+        if (!wait(&in_empty[s], epar, 64)) break;
+        const int ws = (x0 - a.pw) & -a.walign;  // floor to a multiple of walign (a power of two)
+        uint8_t* sb = st0 + (size_t)s * a.stage_bytes;
+        mbar_arrive_expect_tx(&in_full[s], (uint32_t)(a.raw_tx + a.g_tx));
+        tma_load_5d(sb, &a.xmap, &in_full[s], ws * a.cin, y0 - a.ph, z0 - a.pd, nb, 0);
+        tma_load_5d(sb + a.raw_bytes, &a.gmap, &in_full[s], 0, x0, y0, z0, nb);
+        pending |= 1u << s;
+        last_par = (last_par & ~(1u << s)) | ((epar ^ 1u) << s);
+        if (++s == a.nstages) { s = 0; epar ^= 1; }
+      }
+      // no copy may outlive the CTA (matters only after an abort)
+      const uint64_t deadline = global_timer_ns() + kWaitNs;
+      for (int i = 0; i < a.nstages; ++i)
+        if ((pending >> i) & 1u) mbar_wait_bounded(&in_full[i], (last_par >> i) & 1u, deadline);
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer: D[k][co] += A[k][v] B[v][co] ----------------
+    if (lane == 0) {
+      uint32_t fpar = 0u;  // b_full phase bits
+      int ab = 0;
+      uint32_t acc = 0u;   // the CTA's first K step starts the accumulator
+      const int ksteps = a.mtiles * 8;  // 16 positions per K step
+      for (int u = blockIdx.x; u < a.units; u += gridDim.x) {
+        if (!wait(&b_full[ab], (fpar >> ab) & 1u)) break;
+        fpar ^= 1u << ab;
+        tc_fence_after();
+        // MN-major, no swizzle: A: LBO = 8-position group (kpad*16 B), SBO =
+        // 8-slot group (128 B); B: LBO = 8-position group (128 B), SBO = plane
+        const uint64_t ad0 = smem_desc(smem_u32(abuf0 + (size_t)ab * a.abuf_bytes), (uint32_t)a.kpad * 16u, 128u);
+        const uint64_t bd0 = smem_desc(smem_u32(bbuf0 + (size_t)ab * a.bbuf_bytes), 128u, (uint32_t)a.plane_bytes);
+        // K steps in blocks of 8 (ksteps = 8 * mtiles), unrolled: an MMA per
+        // loop iteration would cost a branch bubble each
+        constexpr int MK = (StemK<C>::KPAD + 127) / 128;  // 128-slot M tiles
+        constexpr uint32_t KG = 2u * StemK<C>::KPAD;      // K step of A in 16-byte units
+        for (int kb = 0; kb < ksteps; kb += 8) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const uint64_t ad = ad0 + (uint64_t)((kb + j) * KG);  // + ks * 2 groups * kpad*16 B
+            const uint64_t bd = bd0 + (uint64_t)((kb + j) * 16);  // + ks * 256 B
+#pragma unroll
+            for (int mk = 0; mk < MK; ++mk)  // slots 128*mk..: + 16 groups of 128 B
+              mma_f16_ss(tmem + (uint32_t)(mk * a.npad), ad + (uint64_t)(mk * 128), bd, a.idesc, acc);
+            acc = 1u;
+          }
+        }
+        mma_commit(&b_empty[ab]);
+        if (++ab == a.nbufs) ab = 0;
+      }
+      mma_commit(mdone);
+    }
+  } else {
+    // ---------------- builders (warps 2..9): A = im2col rows, B = dY planes ----------------
+    const int bt = threadIdx.x - 64;
+    const int m = bt & 127;       // A row / position within a tile
+    const int t_first = bt >> 7;  // tiles t_first, t_first + 2, ...
+    const int per_plane = a.bh * a.bw;
+    const int total = a.P * per_plane;
+    const int row_elems = a.wb * C;
+    const int plane_elems = (a.bh + 2) * row_elems;
+    const int nc8 = a.cout / 8;
+    int s = 0, ab = 0;
+    uint32_t rpar = 0u, epar = (1u << kDwMaxBufs) - 1u;  // in_full phase; b_empty phase bits
+    for (int u = blockIdx.x; u < a.units; u += gridDim.x, uw.next(a)) {
+      const int x0 = uw.wi * a.bw;
+      const int xs = x0 - a.pw;
+      const int off = xs - (xs & -a.walign);  // first needed column within the box
+      int got = 1;
+      if (lane == 0) got = (wait(&in_full[s], rpar, 32) && wait(&b_empty[ab], (epar >> ab) & 1u, 32)) ? 1 : 0;
+      got = __shfl_sync(0xffffffffu, got, 0);
+      if (!got) break;
+      epar ^= 1u << ab;
+      const uint16_t* raw = reinterpret_cast<const uint16_t*>(st0 + (size_t)s * a.stage_bytes);
+      const uint8_t* gsrc = st0 + (size_t)s * a.stage_bytes + a.raw_bytes;
+      uint8_t* abuf = abuf0 + (size_t)ab * a.abuf_bytes;
+      uint8_t* bbuf = bbuf0 + (size_t)ab * a.bbuf_bytes;
+      for (int t = t_first; t < a.mtiles; t += 2) {
+        const int l = t * 128 + m;
+        const bool live = l < total;
+        const int lc = live ? l : 0;
+        const int zo = lc / per_plane;
+        const int rem = lc - zo * per_plane;
+        const int yo = rem / a.bw;
+        const int xo = rem - yo * a.bw;
+        const int e0 = zo * plane_elems + yo * row_elems + (off + xo) * C;  // rows and planes are even
+        build_row<C>(abuf + (size_t)t * a.a_bytes, m, raw + e0, row_elems, plane_elems, (uint32_t)e0 & 1u, live,
+                     a.one);
+        // dY row of position l (Cout channels, dense) -> 8-channel planes
+        const uint8_t* gr = gsrc + (size_t)lc * a.cout * 2;
+        for (int c8 = 0; c8 < nc8; ++c8) {
+          const uint4 v = live ? *reinterpret_cast<const uint4*>(gr + c8 * 16) : make_uint4(0, 0, 0, 0);
+          *reinterpret_cast<uint4*>(bbuf + (size_t)c8 * a.plane_bytes + (size_t)l * 16) = v;
+        }
+      }
+      fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&b_full[ab]);
+        mbar_arrive(&in_empty[s]);
+      }
+      if (++ab == a.nbufs) ab = 0;
+      if (++s == a.nstages) { s = 0; rpar ^= 1u; }
+    }
+    // ---------------- accumulator -> fp32 partial (warps 2..5) ----------------
+    if (warp < 6) {
+      const int q = warp & 3;
+      int got = 1;
+      if (lane == 0) got = wait(mdone, 0, 64) ? 1 : 0;
+      got = __shfl_sync(0xffffffffu, got, 0);
+      if (got) {
+        tc_fence_after();
+        for (int mk = 0; mk < a.mk; ++mk) {
+          const int k = mk * 128 + q * 32 + lane;  // slot row of D
+          float* dst = a.part + ((size_t)blockIdx.x * a.kpad + k) * a.npad;
+          for (int cc = 0; cc < a.npad; cc += 16) {
+            float v[16];
+            tmem_ld_16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(mk * a.npad + cc), v);
+            if (k < a.kpad) {
+#pragma unroll
+              for (int i = 0; i < 16; i += 4)
+                *reinterpret_cast<float4*>(dst + cc + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+            }
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, (uint32_t)a.tmem_cols);
+  }
+}
+
+// Sum of the CTA partials in CTA order: dW in OIDHW fp32 (slot k of tap
+// (kd,kh,kw), channel c: k = (kd*3+kh)*4*cin + kw*cin + c) and db (slot 3*cin).
+__global__ void stem_dw_reduce(const float* __restrict__ part, int nparts, int kpad, int npad, int cin, int cout,
+                               float* __restrict__ dw, float* __restrict__ db) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  const int nw = cout * cin * 27;
+  int k, co;
+  if (i < nw) {
+    co = i / (cin * 27);
+    const int r = i - co * cin * 27;
+    const int c = r / 27, tap = r - c * 27;
+    k = (tap / 3) * 4 * cin + (tap % 3) * cin + c;
+  } else if (db != nullptr && i < nw + cout) {
+    co = i - nw;
+    k = 3 * cin;
+  } else {
+    return;
+  }
+  float s = 0.f;
+  for (int b = 0; b < nparts; ++b) s += part[((size_t)b * kpad + k) * npad + co];
+  if (i < nw) dw[i] = s;
+  else db[co] = s;
 }
 
 // ---------------------------------------------------------------------------
@@ -690,6 +975,184 @@ int launch_fwd(int n, int d, int h, int w, int cin, int cout, int pd, int ph, in
   }
   note_launches(1);
   return ce == cudaSuccess ? R4C_OK : R4C_ERR_CUDA;
+}
+
+
+// ---------------------------------------------------------------------------
+// Weight gradient host side.
+// ---------------------------------------------------------------------------
+struct StemDwPlan {
+  int bw, bh, P, wb, walign, mtiles, npad, kpad, mk;
+  int raw_bytes, g_bytes, stage_bytes, nstages, a_bytes, abuf_bytes, plane_bytes, bbuf_bytes, nbufs, smem, tmem_cols;
+  long long units;
+};
+
+// Units of at most two M tiles (256 positions): two A and two B buffers stay
+// small enough for at least 6 input stages (raw brick + dY brick) in flight.
+static bool make_dw_plan(int n, int d, int h, int w, int cin, int cout, int pd, int ph, int pw, StemDwPlan* sp) {
+  if (!supported(n, d, h, w, cin, cout, 3, pd, ph, pw) || cout % 8 != 0) return false;
+  const int od = d + 2 * pd - 2, oh = h + 2 * ph - 2, ow = w + 2 * pw - 2;
+  StemDwPlan p{};
+  p.walign = walign_of(cin);
+  p.npad = npad_of(cout);
+  p.kpad = kpad_of(cin);
+  p.mk = (p.kpad + 127) / 128;
+  if (p.mk * p.npad > 512) return false;
+  p.a_bytes = 128 * p.kpad * 2;
+  int bw = ow;
+  auto box_w = [&](int b) { return (b + 2 + p.walign - 1 + p.walign - 1) / p.walign * p.walign; };
+  while (bw > 1 && (box_w(bw) * cin > 256 || bw > 256)) bw = (bw + 1) / 2;
+  if (box_w(bw) * cin > 256) return false;
+  p.bw = bw;
+  p.wb = box_w(bw);
+  p.mtiles = 0;
+  for (int mt = 2; mt >= 1 && p.mtiles == 0; --mt) {
+    const int cap = mt * 128;
+    const int bh = std::max(1, std::min(oh, cap / bw));
+    const int P = std::max(1, std::min(od, cap / (bw * bh)));
+    if (P + 2 > 256 || bh + 2 > 256) continue;
+    const int mtiles = (P * bh * bw + 127) / 128;
+    if (mtiles > mt) continue;
+    const int raw = ((P + 2) * (bh + 2) * p.wb * cin * 2 + 1023) / 1024 * 1024;
+    const int gb = (P * bh * bw * cout * 2 + 1023) / 1024 * 1024;
+    const int abuf = mtiles * p.a_bytes;
+    const int plane = mtiles * 128 * 16;
+    const int bbuf = (p.npad / 8) * plane;
+    // three buffer pairs when at least four input stages still fit, else two
+    int nb = kDwMaxBufs, nst = 0;
+    for (; nb >= 2; --nb) {
+      nst = std::min(kDwMaxStages, (kSmemMax - kHeader - nb * (abuf + bbuf)) / (raw + gb));
+      if (nst >= (nb == 2 ? 3 : 4)) break;
+    }
+    if (nb < 2) continue;
+    const int fixed = kHeader + nb * (abuf + bbuf);
+    p.bh = bh; p.P = P; p.mtiles = mtiles;
+    p.raw_bytes = raw; p.g_bytes = gb; p.stage_bytes = raw + gb; p.nstages = nst;
+    p.abuf_bytes = abuf; p.plane_bytes = plane; p.bbuf_bytes = bbuf; p.nbufs = nb;
+    p.smem = fixed + nst * (raw + gb);
+  }
+  if (p.mtiles < 1) return false;
+  int alloc = 32;
+  while (alloc < p.mk * p.npad) alloc *= 2;
+  p.tmem_cols = alloc;
+  p.units = (long long)n * ((od + p.P - 1) / p.P) * ((oh + p.bh - 1) / p.bh) * ((ow + bw - 1) / bw);
+  if (p.units >= (1ll << 31)) return false;
+  *sp = p;
+  return true;
+}
+
+bool dw_supported(int n, int d, int h, int w, int cin, int cout, int ks, int pd, int ph, int pw) {
+  StemDwPlan p;
+  return ks == 3 && make_dw_plan(n, d, h, w, cin, cout, pd, ph, pw, &p);
+}
+
+size_t dw_workspace(int n, int d, int h, int w, int cin, int cout, int pd, int ph, int pw) {
+  StemDwPlan p;
+  if (!make_dw_plan(n, d, h, w, cin, cout, pd, ph, pw, &p)) return 0;
+  const long long grid = std::min<long long>(p.units, 1024);  // upper bound of the CTA count
+  return (size_t)grid * p.kpad * p.npad * sizeof(float);
+}
+
+int dw_describe(int n, int d, int h, int w, int cin, int cout, int pd, int ph, int pw, char* buf, size_t len) {
+  StemDwPlan p;
+  if (!make_dw_plan(n, d, h, w, cin, cout, pd, ph, pw, &p)) return snprintf(buf, len, "stem dW: no plan");
+  return snprintf(buf, len,
+                  "tcgen05 stem dW (im2col in smem, dY planes re-laid in smem): cin=%d cout=%d(npad %d) K=%d "
+                  "brick=%dx%dx%d mtiles=%d stages=%d (raw %dB + dY %dB) buffers=%d smem=%dB tmem=%d units=%lld",
+                  cin, cout, p.npad, p.kpad, p.P, p.bh, p.bw, p.mtiles, p.nstages, p.raw_bytes, p.g_bytes, p.nbufs,
+                  p.smem,
+                  p.tmem_cols, p.units);
+}
+
+template <int C>
+static cudaError_t launch_dw_typed(const StemDwArgs& a, int grid, int smem, cudaStream_t st) {
+  static bool done[64] = {false};
+  static std::mutex mu;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (dev >= 0 && dev < 64 && !done[dev]) {
+      e = cudaFuncSetAttribute(stem_dw_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
+      if (e != cudaSuccess) return e;
+      done[dev] = true;
+    }
+  }
+  stem_dw_kernel<C><<<grid, kDwThreads, smem, st>>>(a);
+  return cudaGetLastError();
+}
+
+int launch_dw(int n, int d, int h, int w, int cin, int cout, int pd, int ph, int pw, const void* x, const void* go,
+              float* dw, float* db, void* ws, size_t ws_bytes, int dtype, cudaStream_t st) {
+  StemDwPlan p;
+  if (!make_dw_plan(n, d, h, w, cin, cout, pd, ph, pw, &p)) return R4C_ERR_UNSUPPORTED;
+  if (((uintptr_t)x & 15) || ((uintptr_t)go & 15) || ((uintptr_t)ws & 15)) return R4C_ERR_ALIGN;
+  const int grid = (int)std::min<long long>(p.units, num_sms());
+  if (!ws || ws_bytes < (size_t)grid * p.kpad * p.npad * sizeof(float)) return R4C_ERR_WORKSPACE;
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return R4C_ERR_CUDA;
+  StemDwArgs a;
+  memset(&a, 0, sizeof(a));
+  const int od = d + 2 * pd - 2, oh = h + 2 * ph - 2, ow = w + 2 * pw - 2;
+  const CUtensorMapDataType dt = dtype == R4C_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const cuuint64_t e = 2;
+  {
+    cuuint64_t dims[5] = {(cuuint64_t)w * cin, (cuuint64_t)h, (cuuint64_t)d, (cuuint64_t)n, 1};
+    cuuint64_t str[4] = {(cuuint64_t)w * cin * e, (cuuint64_t)h * w * cin * e, (cuuint64_t)d * h * w * cin * e,
+                         (cuuint64_t)n * d * h * w * cin * e};
+    cuuint32_t box[5] = {(cuuint32_t)(p.wb * cin), (cuuint32_t)(p.bh + 2), (cuuint32_t)(p.P + 2), 1, 1};
+    cuuint32_t es[5] = {1, 1, 1, 1, 1};
+    if (enc(&a.xmap, dt, 5, const_cast<void*>(x), dims, str, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
+        CUDA_SUCCESS)
+      return R4C_ERR_INVALID;
+  }
+  {
+    cuuint64_t dims[5] = {(cuuint64_t)cout, (cuuint64_t)ow, (cuuint64_t)oh, (cuuint64_t)od, (cuuint64_t)n};
+    cuuint64_t str[4] = {(cuuint64_t)cout * e, (cuuint64_t)ow * cout * e, (cuuint64_t)oh * ow * cout * e,
+                         (cuuint64_t)od * oh * ow * cout * e};
+    cuuint32_t box[5] = {(cuuint32_t)cout, (cuuint32_t)p.bw, (cuuint32_t)p.bh, (cuuint32_t)p.P, 1};
+    cuuint32_t es[5] = {1, 1, 1, 1, 1};
+    if (enc(&a.gmap, dt, 5, const_cast<void*>(go), dims, str, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
+        CUDA_SUCCESS)
+      return R4C_ERR_INVALID;
+  }
+  a.part = static_cast<float*>(ws);
+  a.err = tc::device_error_flag();
+  if (!a.err) return R4C_ERR_CUDA;
+  a.n = n; a.d = d; a.h = h; a.w = w; a.cin = cin; a.cout = cout;
+  a.od = od; a.oh = oh; a.ow = ow; a.pd = pd; a.ph = ph; a.pw = pw;
+  a.bw = p.bw; a.bh = p.bh; a.P = p.P; a.wb = p.wb; a.walign = p.walign;
+  a.nwt = (ow + p.bw - 1) / p.bw;
+  a.nht = (oh + p.bh - 1) / p.bh;
+  a.nzb = (od + p.P - 1) / p.P;
+  a.units = (int)p.units;
+  a.mtiles = p.mtiles; a.npad = p.npad; a.kpad = p.kpad; a.mk = p.mk;
+  a.raw_bytes = p.raw_bytes;
+  a.raw_tx = (p.P + 2) * (p.bh + 2) * p.wb * cin * 2;
+  a.g_tx = p.P * p.bh * p.bw * cout * 2;
+  a.stage_bytes = p.stage_bytes; a.nstages = p.nstages;
+  a.a_bytes = p.a_bytes; a.abuf_bytes = p.abuf_bytes;
+  a.plane_bytes = p.plane_bytes; a.bbuf_bytes = p.bbuf_bytes; a.nbufs = p.nbufs;
+  a.tmem_cols = p.tmem_cols;
+  a.idesc = instr_desc_f16(dtype == R4C_BF16, 128, p.npad, 1, 1);
+  a.one = dtype == R4C_BF16 ? 0x3F80u : 0x3C00u;
+  const int smem = std::max(p.smem, kSmemMax / 2 + 1024);  // one CTA per SM (TMEM)
+  cudaError_t ce;
+  switch (cin) {
+    case 1: ce = launch_dw_typed<1>(a, grid, smem, st); break;
+    case 2: ce = launch_dw_typed<2>(a, grid, smem, st); break;
+    case 3: ce = launch_dw_typed<3>(a, grid, smem, st); break;
+    default: ce = launch_dw_typed<4>(a, grid, smem, st); break;
+  }
+  note_launches(1);
+  if (ce != cudaSuccess) return R4C_ERR_CUDA;
+  const int nout = cout * cin * 27 + cout;
+  stem_dw_reduce<<<(nout + 127) / 128, 128, 0, st>>>(a.part, grid, p.kpad, p.npad, cin, cout, dw, db);
+  note_launches(1);
+  return cudaGetLastError() == cudaSuccess ? R4C_OK : R4C_ERR_CUDA;
 }
 
 }  // namespace stem

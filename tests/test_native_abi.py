@@ -71,9 +71,14 @@ def test_stem_family():
         assert "stem" in _native.describe_plan(dsc, _native.LEG_FWD)
         assert _native.workspace_bytes(dsc, _native.LEG_FWD) == 0
         assert _native.packed_weight_bytes(dsc, _native.LEG_FWD) == (cout + 15) // 16 * 16 * kpad * 2
-        # the other legs of the layer keep their kernels
-        assert "stem" not in _native.describe_plan(dsc, _native.LEG_DW)
+        # dX keeps the general kernel; dW takes the stem dW kernel when Cout
+        # is a multiple of 8 and its buffers fit shared memory
         assert "stem" not in _native.describe_plan(dsc, _native.LEG_DX)
+        if cout % 8 == 0 and cout <= 32:
+            assert "stem dW" in _native.describe_plan(dsc, _native.LEG_DW)
+            assert _native.workspace_bytes(dsc, _native.LEG_DW) > 0
+    # Cout not a multiple of 8: the dW leaves the stem kernel
+    assert "stem" not in _native.describe_plan(_d(cin=1, cout=7, w=32), _native.LEG_DW)
     # rows whose byte stride is not a multiple of 16, k=1 and 5+ channels stay
     # on the general kernel; forcing the SIMT family still works
     assert "stem" not in _native.describe_plan(_d(cin=3, w=30), _native.LEG_FWD)

@@ -29,6 +29,7 @@
 
 #include <stdio.h>
 #include <string.h>
+#include <stdlib.h>
 
 #include <algorithm>
 #include <mutex>
@@ -64,14 +65,26 @@ struct alignas(64) DwArgs {
   long long rows_per_split;
   int ntasks;
   uint32_t idesc;
+  // wide mode: input channel groups of cw (16/32/64) in the swizzled MN-major
+  // layout, one TMA box (cw, pitch_w, k, k) per group and row: an M tile is
+  // apt = 128/cw consecutive (kd, kh) planes of one group (MN atoms, LBO =
+  // plane), K groups of 8 positions at SBO = 16*cw bytes. dY boxes of cwb
+  // channels, swizzled likewise (cwb = 8: the no-swizzle chunk layout).
+  int wide;
+  int cw, apt, plane_bytes, lay_a;
+  int cwb, b_region, lay_b;
+  int tail_bytes;                    // zeroed bytes past the last stage (M tile over-read)
 };
 
 struct Task {
   int mt0, mtn, n0, nn, kw0, kwn;
+  int g;  // wide mode: input channel group (mt0 counts M tiles within it)
 };
 
 struct DwPlan {
   bool ok;
+  bool wide;
+  int cw, apt, tpg, ng, plane_bytes, region_bytes, cwb, tail_bytes;
   int n, d, h, w, od, oh, ow, cin, cout, ks, pd, ph, pw;
   int c8, groups, mtiles, pitch_w, kpad, wt, nwt;
   int mtn, nn, kwn;  // task shape
@@ -104,6 +117,14 @@ static void chunk_range(int mt0, int mtn, int k2, int c8, int* lo, int* hi) {
   *hi = std::min(g1 / k2, c8 - 1);
 }
 
+// Clocks per M=128 x N x K=16 MMA with MN-major operands, issued back to back
+// from the dW issue loop (measured on B200: ~70-80 for N <= 48; the A read
+// bounds small N).
+static double dw_mma_clk(int npad) { return std::max(72.0, 40.0 + npad / 2.0); }
+// Load-to-use latency of a stage's TMA boxes under the kernel's own load
+// (measured on B200 with per-row clock stamps: 2-3 us).
+constexpr double kTmaLatencyClk = 5000.0;
+
 static bool plan_dw(int n, int d, int h, int w, int cin, int cout, int ks, int pd, int ph, int pw, DwPlan* out) {
   DwPlan P{};
   P.ok = false;
@@ -133,65 +154,167 @@ static bool plan_dw(int n, int d, int h, int w, int cin, int cout, int ks, int p
   P.rows = (long long)n * P.od * P.oh * P.nwt;
   const int sms = num_sms();
 
+  // R4C_DW_WIDE=0 / =1 restricts the search to the 8-channel chunk layout /
+  // to the wide channel-group layout when the layer allows it.
+  const char* wenv = getenv("R4C_DW_WIDE");
+  const int wide_force = (wenv && wenv[0] == '0') ? 0 : (wenv && wenv[0] == '1') ? 1 : -1;
+  const int cw_ok = cin % 64 == 0 ? 64 : cin % 32 == 0 ? 32 : cin % 16 == 0 ? 16 : 0;
+  // Automatic choice: the wide layout for 64-channel groups only. Measured on
+  // B200 (trunk layers, batch 4): 192->192 k3 254 -> 210 us and 192->96 k1
+  // 83 -> 67 us with 64-channel groups, while 32- and 16-channel groups lost
+  // to the chunk layout (96->96 206 -> 238 us, 48->48 248 -> 314 us: more M
+  // tiles per K step outweigh the fewer TMA rows). R4C_DW_WIDE=1 enables the
+  // narrower groups, =0 disables the wide layout.
+  const bool wide_auto = wide_force == -1 && cw_ok == 64 && cin >= 64;
+  const bool chunk_allowed = !((wide_force == 1 && cw_ok && cin >= 32) || wide_auto);
+
   // Task shape: largest N split and M-tile group that fits TMEM (512 cols)
   // with all kw in one task when possible.
   double best = 1e300;
-  for (int kwn : {ks, 1}) {
-    if (ks % kwn) continue;
-    for (int nn = cout; nn >= 8; nn -= 8) {
-      if (cout % nn) continue;
-      int npad = round_up(nn, 16);
-      if (npad > 256) continue;
-      for (int mtn = std::min(P.mtiles, 8); mtn >= 1; --mtn) {
-        int cols = kwn * mtn * npad;
-        if (cols > 512) continue;
-        int ntask_m = (P.mtiles + mtn - 1) / mtn;
-        int ntasks = ntask_m * (cout / nn) * (ks / kwn);
-        // stage bytes: chunks touched by an M group of mtn tiles
-        int lo, hi;
-        chunk_range(0, mtn, k2, P.c8, &lo, &hi);
-        int nch = hi - lo + 2;  // +1 slack for a straddling group range
-        if (nch > P.c8) nch = P.c8;
-        int a_bytes = (nch * k2 + 1) * P.pitch_w * 16;
-        a_bytes = round_up(a_bytes, 128);
-        int g_bytes = (nn / 8) * P.kpad * 16;
-        int stage = round_up(a_bytes + g_bytes, 128);
-        int tail = 16 * mtn * P.pitch_w * 16 + 256;
-        int stages = std::min(kMaxStages, (kSmemMax - kHeader - tail) / stage);
-        if (stages < 2) continue;
-        // cost per row per task
-        double t_mma = std::max({npad / 2.0, (4096.0 + 32.0 * npad) / 128.0, 44.6});
-        double mma = (double)(P.kpad / 16) * kwn * mtn * t_mma;
-        double load = (double)(nch * k2 * P.pitch_w * 16 + g_bytes) / 48.0;
-        double per_row = std::max(mma, load) + 60.0;
-        // split so that tasks * S ~ a few waves
-        int S = (int)std::max<long long>(1, std::min<long long>(P.rows, (2LL * sms + ntasks - 1) / ntasks));
-        long long rps = (P.rows + S - 1) / S;
-        S = (int)((P.rows + rps - 1) / rps);
-        long long ctas = (long long)ntasks * S;
-        long long waves = (ctas + sms - 1) / sms;
-        double est = waves * (rps * per_row + 3000.0);
-        if (est < best) {
-          best = est;
-          P.mtn = mtn; P.nn = nn; P.kwn = kwn;
-          P.S = S; P.rows_per_split = rps;
-          P.stages = stages; P.stage_bytes = stage;
-          P.smem_bytes = kHeader + stages * stage + tail;
-          int alloc = 32;
-          while (alloc < cols) alloc *= 2;
-          P.tmem_cols = alloc;
-          P.est = est;
-          P.ok = true;
+  // W tile candidates: the widest, and its half (twice the stages in flight)
+  for (int wtc : {wt}) {
+    const int nwt_c = (P.ow + wtc - 1) / wtc;
+    const int kpad_c = round_up(wtc, 16);
+    const int pitch_c = round_up(kpad_c + ks - 1, 8);
+    const long long rows_c = (long long)n * P.od * P.oh * nwt_c;
+    for (int kwn : {ks, 1}) {
+      if (!chunk_allowed) break;
+      if (ks % kwn) continue;
+      for (int nn = cout; nn >= 8; nn -= 8) {
+        if (cout % nn) continue;
+        int npad = round_up(nn, 16);
+        if (npad > 256) continue;
+        for (int mtn = std::min(P.mtiles, 8); mtn >= 1; --mtn) {
+          int cols = kwn * mtn * npad;
+          if (cols > 512) continue;
+          int ntask_m = (P.mtiles + mtn - 1) / mtn;
+          int ntasks = ntask_m * (cout / nn) * (ks / kwn);
+          // stage bytes: chunks touched by an M group of mtn tiles
+          int lo, hi;
+          chunk_range(0, mtn, k2, P.c8, &lo, &hi);
+          int nch = hi - lo + 2;  // +1 slack for a straddling group range
+          if (nch > P.c8) nch = P.c8;
+          int a_bytes = (nch * k2 + 1) * pitch_c * 16;
+          a_bytes = round_up(a_bytes, 128);
+          int g_bytes = (nn / 8) * kpad_c * 16;
+          int stage = round_up(a_bytes + g_bytes, 128);
+          int tail = 16 * mtn * pitch_c * 16 + 256;
+          int stages = std::min(kMaxStages, (kSmemMax - kHeader - tail) / stage);
+          if (stages < 2) continue;
+          // cost per row per task
+          double t_mma = std::max({npad / 2.0, (4096.0 + 32.0 * npad) / 128.0, 44.6});
+          double mma = (double)(kpad_c / 16) * kwn * mtn * t_mma;
+          double load = (double)(nch * k2 * pitch_c * 16 + g_bytes) / 48.0;
+          double per_row = std::max(mma, load) + 60.0;
+          // split so that tasks * S ~ a few waves
+          int S = (int)std::max<long long>(1, std::min<long long>(rows_c, (2LL * sms + ntasks - 1) / ntasks));
+          long long rps = (rows_c + S - 1) / S;
+          S = (int)((rows_c + rps - 1) / rps);
+          long long ctas = (long long)ntasks * S;
+          long long waves = (ctas + sms - 1) / sms;
+          double est = waves * (rps * per_row + 3000.0);
+          if (est < best) {
+            best = est;
+            P.wide = false;
+            P.wt = wtc; P.nwt = nwt_c; P.kpad = kpad_c; P.pitch_w = pitch_c; P.rows = rows_c;
+            P.mtn = mtn; P.nn = nn; P.kwn = kwn;
+            P.S = S; P.rows_per_split = rps;
+            P.stages = stages; P.stage_bytes = stage;
+            P.smem_bytes = kHeader + stages * stage + tail;
+            int alloc = 32;
+            while (alloc < cols) alloc *= 2;
+            P.tmem_cols = alloc;
+            P.est = est;
+            P.ok = true;
+          }
+        }
+      }
+    }
+  }
+  // Wide mode (Cin a multiple of 16, at least 32): one swizzled box per
+  // channel group and row instead of one 16-byte-row box per 8 channels.
+  const int cw = cw_ok;
+  if (cw && cin >= 32 && (wide_force == 1 || wide_auto)) {
+    const int apt = 128 / cw, atoms = k2 + 1;  // + the ones (group 0) / zero plane
+    const int tpg = (atoms + apt - 1) / apt, ng = cin / cw;
+    // W tile: the chunk layout's, halved until two stages fit
+    int wt_w = P.wt;
+    auto plane_of = [&](int t) { return round_up(round_up(t, 16) + ks - 1, 8) * cw * 2; };
+    while (wt_w > 16 && kHeader + 2 * (round_up(atoms * plane_of(wt_w), 1024) +
+                                       round_up(cout * round_up(wt_w, 16) * 2, 1024)) +
+                            (tpg * apt - atoms) * plane_of(wt_w) + 1024 > kSmemMax)
+      wt_w = round_up((wt_w + 1) / 2, 16);
+    const int nwt_w = (P.ow + wt_w - 1) / wt_w;
+    const int kpad_w = round_up(wt_w, 16);
+    const int pitch_ww = round_up(kpad_w + ks - 1, 8);
+    const long long rows_w = (long long)n * P.od * P.oh * nwt_w;
+    const int plane = pitch_ww * cw * 2;
+    const int region = round_up(atoms * plane, 1024);
+    const int tail = (tpg * apt - atoms) * plane + 1024;
+    for (int kwn : {1}) {  // one kw per task: keeps the wide issue code (runtime steps) small
+      for (int nn = cout; nn >= 8; nn -= 8) {
+        if (cout % nn) continue;
+        const int npad = round_up(nn, 16);
+        if (npad > 256) continue;
+        const int cwb = nn % 64 == 0 ? 64 : nn % 32 == 0 ? 32 : nn % 16 == 0 ? 16 : 8;
+        // the last stage's over-reads past its end stay inside the zeroed
+        // tail: A tiles past the group's planes, B chunks past nn (npad > nn)
+        const int tail_nn = std::max(tail, (npad - nn) / 8 * kpad_w * 16 + 1024);
+        for (int mtn = std::min(tpg, 5); mtn >= 1; --mtn) {
+          const int cols = kwn * mtn * npad;
+          if (cols > 512) continue;
+          const int ntasks = ng * ((tpg + mtn - 1) / mtn) * (cout / nn) * (ks / kwn);
+          if (ntasks > 128) continue;
+          const int stage = region + round_up(nn * kpad_w * 2, 1024);
+          const int stages = std::min(kMaxStages, (kSmemMax - kHeader - tail_nn) / stage);
+          if (stages < 2) continue;
+          const double t_mma = dw_mma_clk(npad);
+          const double mma = (double)(kpad_w / 16) * kwn * mtn * t_mma;
+          const double rows = (double)k2 * pitch_ww + (double)(nn / cwb) * kpad_w;
+          const double bytes = (double)k2 * plane + (double)nn * kpad_w * 2;
+          const double load = std::max(bytes / 48.0, rows * 2.2);
+          const double per_row = std::max(std::max(mma, load) + 60.0, (kTmaLatencyClk + mma) / stages);
+          int S = (int)std::max<long long>(1, std::min<long long>(rows_w, (2LL * sms + ntasks - 1) / ntasks));
+          const long long rps = (rows_w + S - 1) / S;
+          S = (int)((rows_w + rps - 1) / rps);
+          const long long ctas = (long long)ntasks * S;
+          const long long waves = (ctas + sms - 1) / sms;
+          const double est = waves * (rps * per_row + 3000.0);
+          if (est < best) {
+            best = est;
+            P.wide = true;
+            P.wt = wt_w; P.nwt = nwt_w; P.kpad = kpad_w; P.pitch_w = pitch_ww; P.rows = rows_w;
+            P.cw = cw; P.apt = apt; P.tpg = tpg; P.ng = ng; P.plane_bytes = plane; P.region_bytes = region;
+            P.cwb = cwb; P.tail_bytes = tail_nn;
+            P.mtn = mtn; P.nn = nn; P.kwn = kwn;
+            P.S = S; P.rows_per_split = rps;
+            P.stages = stages; P.stage_bytes = stage;
+            P.smem_bytes = kHeader + stages * stage + tail_nn;
+            int alloc = 32;
+            while (alloc < cols) alloc *= 2;
+            P.tmem_cols = alloc;
+            P.est = est;
+            P.db_in_kernel = true;
+            P.ok = true;
+          }
         }
       }
     }
   }
   if (!P.ok) return false;
   P.tasks.clear();
-  for (int mt0 = 0; mt0 < P.mtiles; mt0 += P.mtn)
-    for (int n0 = 0; n0 < cout; n0 += P.nn)
-      for (int kw0 = 0; kw0 < ks; kw0 += P.kwn)
-        P.tasks.push_back(Task{mt0, std::min(P.mtn, P.mtiles - mt0), n0, P.nn, kw0, P.kwn});
+  if (P.wide) {
+    for (int g = 0; g < P.ng; ++g)
+      for (int mt0 = 0; mt0 < P.tpg; mt0 += P.mtn)
+        for (int n0 = 0; n0 < cout; n0 += P.nn)
+          for (int kw0 = 0; kw0 < ks; kw0 += P.kwn)
+            P.tasks.push_back(Task{mt0, std::min(P.mtn, P.tpg - mt0), n0, P.nn, kw0, P.kwn, g});
+  } else {
+    for (int mt0 = 0; mt0 < P.mtiles; mt0 += P.mtn)
+      for (int n0 = 0; n0 < cout; n0 += P.nn)
+        for (int kw0 = 0; kw0 < ks; kw0 += P.kwn)
+          P.tasks.push_back(Task{mt0, std::min(P.mtn, P.mtiles - mt0), n0, P.nn, kw0, P.kwn, 0});
+  }
   if (out) *out = P;
   return true;
 }
@@ -204,56 +327,69 @@ template <> struct OneBits<__nv_bfloat16> { static constexpr uint32_t v = 0x3F80
 template <> struct OneBits<__half> { static constexpr uint32_t v = 0x3C003C00u; };         // fp16 1.0 x2
 
 struct TaskTable {
-  int mt0[128], mtn[128], n0[128], kw0[128];
+  int mt0[128], mtn[128], n0[128], kw0[128], g[128];
 };
+
+__device__ __forceinline__ uint64_t desc_layout(uint32_t addr, uint32_t lbo, uint32_t sbo, uint32_t layout) {
+  return smem_desc(addr, lbo, sbo) | ((uint64_t)(layout & 7u) << 61);
+}
 
 // MMA issue for one output row (ksteps K steps of 16 positions): every
 // (kw, M tile) accumulator takes one MMA per K step. The (kw, tile) block is
 // fully unrolled and K steps are unrolled so that a loop iteration carries
 // at least four MMAs: the issuing thread's per-iteration bubble (~40 clk)
 // otherwise dominates (one MMA per iteration ran at ~210 clk per MMA).
-template <int MTN, int KWN>
+// Descriptor start-address steps (16-byte units) of one operand layout: a K
+// step of 16 positions for A and B, a kw shift of A (one position), an M tile.
+struct DwSteps {
+  uint32_t ks_a, kw_a, tile_a, ks_b;
+};
+
+// WIDE = false: the chunk layout's steps are compile-time constants (256 B
+// per K step, 16 B per kw), which keeps the issue loop short.
+template <int MTN, int KWN, bool WIDE>
 __device__ __forceinline__ void dw_step(int ks, uint64_t a0, uint64_t b0, uint32_t tmem, uint32_t npad,
-                                        uint64_t a_tile, uint32_t idesc, uint32_t acc) {
-  const uint64_t b = b0 + (uint64_t)(ks * 16);  // 256 B per K step
+                                        const DwSteps& st, uint32_t idesc, uint32_t acc) {
+  const uint32_t ks_a = WIDE ? st.ks_a : 16u, kw_a = WIDE ? st.kw_a : 1u, ks_b = WIDE ? st.ks_b : 16u;
+  const uint64_t b = b0 + (uint64_t)(ks * ks_b);
 #pragma unroll
   for (int kw = 0; kw < KWN; ++kw)
 #pragma unroll
     for (int t = 0; t < MTN; ++t)
-      mma_f16_ss(tmem + (uint32_t)(kw * MTN + t) * npad, a0 + (uint64_t)(ks * 16 + kw) + (uint64_t)t * a_tile, b,
-                 idesc, acc);
+      mma_f16_ss(tmem + (uint32_t)(kw * MTN + t) * npad,
+                 a0 + (uint64_t)(ks * ks_a + kw * kw_a) + (uint64_t)t * st.tile_a, b, idesc, acc);
 }
 
-template <int MTN, int KWN>
-__device__ __forceinline__ void dw_issue_row(uint64_t a0, uint64_t b0, uint32_t tmem, uint32_t npad, uint64_t a_tile,
-                                             int ksteps, uint32_t idesc, bool first) {
+template <int MTN, int KWN, bool WIDE>
+__device__ __forceinline__ void dw_issue_row(uint64_t a0, uint64_t b0, uint32_t tmem, uint32_t npad,
+                                             const DwSteps& a_tile, int ksteps, uint32_t idesc, bool first) {
   constexpr int U = (MTN * KWN >= 4) ? 1 : ((MTN * KWN >= 2) ? 2 : 4);
   int ks = 0;
   if (first && ksteps > 0) {  // the task's first K step initialises every accumulator
-    dw_step<MTN, KWN>(0, a0, b0, tmem, npad, a_tile, idesc, 0u);
+    dw_step<MTN, KWN, WIDE>(0, a0, b0, tmem, npad, a_tile, idesc, 0u);
     ks = 1;
   }
 #pragma unroll 1
   for (; ks + U <= ksteps; ks += U) {
 #pragma unroll
-    for (int u = 0; u < U; ++u) dw_step<MTN, KWN>(ks + u, a0, b0, tmem, npad, a_tile, idesc, 1u);
+    for (int u = 0; u < U; ++u) dw_step<MTN, KWN, WIDE>(ks + u, a0, b0, tmem, npad, a_tile, idesc, 1u);
   }
 #pragma unroll 1
-  for (; ks < ksteps; ++ks) dw_step<MTN, KWN>(ks, a0, b0, tmem, npad, a_tile, idesc, 1u);
+  for (; ks < ksteps; ++ks) dw_step<MTN, KWN, WIDE>(ks, a0, b0, tmem, npad, a_tile, idesc, 1u);
 }
 
-template <int KWN>
+template <int KWN, bool WIDE>
 __device__ __forceinline__ void dw_issue_mt(int mtn, uint64_t a0, uint64_t b0, uint32_t tmem, uint32_t npad,
-                                            uint64_t a_tile, int ksteps, uint32_t idesc, bool first) {
+                                            const DwSteps& a_tile, int ksteps, uint32_t idesc, bool first) {
   switch (mtn) {
-    case 1: dw_issue_row<1, KWN>(a0, b0, tmem, npad, a_tile, ksteps, idesc, first); break;
-    case 2: dw_issue_row<2, KWN>(a0, b0, tmem, npad, a_tile, ksteps, idesc, first); break;
-    case 3: dw_issue_row<3, KWN>(a0, b0, tmem, npad, a_tile, ksteps, idesc, first); break;
-    case 4: dw_issue_row<4, KWN>(a0, b0, tmem, npad, a_tile, ksteps, idesc, first); break;
-    case 5: dw_issue_row<5, KWN>(a0, b0, tmem, npad, a_tile, ksteps, idesc, first); break;
-    case 6: dw_issue_row<6, KWN>(a0, b0, tmem, npad, a_tile, ksteps, idesc, first); break;
-    case 7: dw_issue_row<7, KWN>(a0, b0, tmem, npad, a_tile, ksteps, idesc, first); break;
-    default: dw_issue_row<8, KWN>(a0, b0, tmem, npad, a_tile, ksteps, idesc, first); break;
+    case 1: dw_issue_row<1, KWN, WIDE>(a0, b0, tmem, npad, a_tile, ksteps, idesc, first); break;
+    case 2: dw_issue_row<2, KWN, WIDE>(a0, b0, tmem, npad, a_tile, ksteps, idesc, first); break;
+    case 3: dw_issue_row<3, KWN, WIDE>(a0, b0, tmem, npad, a_tile, ksteps, idesc, first); break;
+    case 4: dw_issue_row<4, KWN, WIDE>(a0, b0, tmem, npad, a_tile, ksteps, idesc, first); break;
+    case 5: dw_issue_row<5, KWN, WIDE>(a0, b0, tmem, npad, a_tile, ksteps, idesc, first); break;
+    case 6: dw_issue_row<6, KWN, WIDE>(a0, b0, tmem, npad, a_tile, ksteps, idesc, first); break;
+    case 7: dw_issue_row<7, KWN, WIDE>(a0, b0, tmem, npad, a_tile, ksteps, idesc, first); break;
+    default: dw_issue_row<8, KWN, WIDE>(a0, b0, tmem, npad, a_tile, ksteps, idesc, first); break;
   }
 }
 
@@ -270,31 +406,42 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  if ((smem_u32(smem) & 127u) != 0u) {
+  if ((smem_u32(smem) & (a.wide ? 1023u : 127u)) != 0u) {  // swizzled boxes need 1024-byte alignment
     if (threadIdx.x == 0) atomicExch(a.err, 2);
     return;
   }
   const int task = blockIdx.x % a.ntasks;
   const int split = blockIdx.x / a.ntasks;
   const int mt0 = tt.mt0[task], mtn = tt.mtn[task], n0 = tt.n0[task], kw0 = tt.kw0[task];
+  const int grp = tt.g[task];
   const int k2 = a.ks * a.ks;
   int c_lo = min((16 * mt0) / k2, a.c8 - 1);
   int c_hi = min((16 * (mt0 + mtn) - 1) / k2, a.c8 - 1);
   const int nch = c_hi - c_lo + 1;
   const int sbo_a = a.pitch_w * 16;
   // group g (absolute) lives at row block (g - c_lo*k2) of the stage's A region
-  const bool has_ones = a.ones_group >= 16 * mt0 && a.ones_group < 16 * (mt0 + mtn) && kw0 == 0 &&
-                        a.dbpart != nullptr;
+  // wide mode: plane k2 of group 0 holds ones (its D rows are db)
+  const bool has_ones = a.wide ? (grp == 0 && kw0 == 0 && a.dbpart != nullptr && k2 >= mt0 * a.apt &&
+                                  k2 < (mt0 + mtn) * a.apt)
+                               : (a.ones_group >= 16 * mt0 && a.ones_group < 16 * (mt0 + mtn) && kw0 == 0 &&
+                                  a.dbpart != nullptr);
   const int npad = (a.nn + 15) / 16 * 16;
-  const uint32_t tx_bytes = (uint32_t)(nch * k2 * sbo_a + (a.nn / 8) * a.kpad * 16);
+  const uint32_t tx_bytes = a.wide ? (uint32_t)(k2 * a.plane_bytes + a.nn * a.kpad * 2)
+                                   : (uint32_t)(nch * k2 * sbo_a + (a.nn / 8) * a.kpad * 16);
 
   // zero the whole dynamic region (finite junk rows), then the ones rows
   {
-    const int total = a.stages * a.stage_bytes + 16 * mtn * sbo_a + 256;
+    const int total = a.stages * a.stage_bytes + (a.wide ? a.tail_bytes : 16 * mtn * sbo_a + 256);
     uint4 z = make_uint4(0, 0, 0, 0);
     for (int i = threadIdx.x * 16; i < total; i += kThreads * 16) *reinterpret_cast<uint4*>(stage0 + i) = z;
     __syncthreads();
-    if (a.ones_group >= 0) {
+    if (a.wide) {
+      if (grp == 0 && a.dbpart != nullptr)
+        for (int s = 0; s < a.stages; ++s) {
+          uint32_t* o = reinterpret_cast<uint32_t*>(stage0 + (size_t)s * a.stage_bytes + (size_t)k2 * a.plane_bytes);
+          for (int i = threadIdx.x; i < a.plane_bytes / 4; i += kThreads) o[i] = OneBits<T>::v;
+        }
+    } else if (a.ones_group >= 0) {
       const int rel = a.ones_group - c_lo * k2;
       if (rel >= 0 && (rel + 1) * sbo_a <= a.a_bytes) {
         for (int s = 0; s < a.stages; ++s) {
@@ -361,11 +508,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!wait(&empty[stage], epar)) break;
         uint8_t* sA = stage0 + (size_t)stage * a.stage_bytes;
         mbar_arrive_expect_tx(&full[stage], tx_bytes);
-        for (int c = 0; c < nch; ++c)
-          tma_load_5d(sA + (size_t)c * k2 * sbo_a, &a.tx, &full[stage], (c_lo + c) * 8, w0 - a.pw, y - a.ph,
-                      z - a.pd, nb);
-        for (int c = 0; c < a.nn / 8; ++c)
-          tma_load_5d(sA + a.a_bytes + (size_t)c * a.kpad * 16, &a.tg, &full[stage], n0 + c * 8, w0, y, z, nb);
+        if (a.wide) {
+          // the k x k input rows of the group: planes [kd][kh] of pitch_w positions
+          tma_load_5d(sA, &a.tx, &full[stage], grp * a.cw, w0 - a.pw, y - a.ph, z - a.pd, nb);
+          for (int c = 0; c < a.nn / a.cwb; ++c)
+            tma_load_5d(sA + a.a_bytes + (size_t)c * a.b_region, &a.tg, &full[stage], n0 + c * a.cwb, w0, y, z, nb);
+        } else {
+          for (int c = 0; c < nch; ++c)
+            tma_load_5d(sA + (size_t)c * k2 * sbo_a, &a.tx, &full[stage], (c_lo + c) * 8, w0 - a.pw, y - a.ph,
+                        z - a.pd, nb);
+          for (int c = 0; c < a.nn / 8; ++c)
+            tma_load_5d(sA + a.a_bytes + (size_t)c * a.kpad * 16, &a.tg, &full[stage], n0 + c * 8, w0, y, z, nb);
+        }
         pending[stage] = true;
         last_par[stage] = epar ^ 1;
         if (++stage == a.stages) { stage = 0; epar ^= 1; }
@@ -382,19 +536,43 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t fpar = 0;
       bool first = true;
-      const uint32_t a_tile = (uint32_t)(16 * sbo_a) >> 4;       // descriptor units
-      const int rel0 = 16 * mt0 - c_lo * k2;                     // first group of the task
+      const int rel0 = 16 * mt0 - c_lo * k2;                     // first group of the task (chunk mode)
+      // descriptor steps (16-byte units): K step, kw shift, M tile, B K step
+      const DwSteps stp = a.wide ? DwSteps{(uint32_t)(2 * a.cw), (uint32_t)(a.cw / 8),
+                                           (uint32_t)(a.apt * a.plane_bytes / 16), (uint32_t)(2 * a.cwb)}
+                                 : DwSteps{16u, 1u, (uint32_t)(16 * sbo_a) >> 4, 16u};
       for (long long r = r_beg; r < r_end; ++r) {
         if (!wait(&full[stage], fpar)) break;
         tc_fence_after();
         const uint32_t sA = smem_u32(stage0 + (size_t)stage * a.stage_bytes);
-        const uint64_t a0 = smem_desc(sA + (uint32_t)(rel0 * sbo_a) + (uint32_t)(kw0 * 16), 128, (uint32_t)sbo_a);
-        const uint64_t b0 = smem_desc(sA + (uint32_t)a.a_bytes, 128, (uint32_t)(a.kpad * 16));
+        uint64_t a0, b0;
+        if (a.wide) {
+          // swizzled MN-major: LBO = MN atom stride, SBO = 8-position K group
+          a0 = desc_layout(sA + (uint32_t)(mt0 * a.apt * a.plane_bytes) + (uint32_t)(kw0 * a.cw * 2),
+                           (uint32_t)a.plane_bytes, (uint32_t)(16 * a.cw), (uint32_t)a.lay_a);
+          b0 = a.cwb > 8 ? desc_layout(sA + (uint32_t)a.a_bytes, (uint32_t)a.b_region, (uint32_t)(16 * a.cwb),
+                                       (uint32_t)a.lay_b)
+                         : smem_desc(sA + (uint32_t)a.a_bytes, 128, (uint32_t)(a.kpad * 16));
+        } else {
+          // no swizzle MN-major: LBO = K group (128 B), SBO = MN group
+          a0 = smem_desc(sA + (uint32_t)(rel0 * sbo_a) + (uint32_t)(kw0 * 16), 128, (uint32_t)sbo_a);
+          b0 = smem_desc(sA + (uint32_t)a.a_bytes, 128, (uint32_t)(a.kpad * 16));
+        }
         const int ksteps = a.kpad / 16;
-        if (a.kwn == 3)
-          dw_issue_mt<3>(mtn, a0, b0, tmem, (uint32_t)npad, (uint64_t)a_tile, ksteps, a.idesc, first);
-        else
-          dw_issue_mt<1>(mtn, a0, b0, tmem, (uint32_t)npad, (uint64_t)a_tile, ksteps, a.idesc, first);
+        if (a.wide) {  // wide tasks: one kw, at most 5 M tiles (10 planes / 2 per tile)
+          switch (mtn) {
+            case 1: dw_issue_row<1, 1, true>(a0, b0, tmem, (uint32_t)npad, stp, ksteps, a.idesc, first); break;
+            case 2: dw_issue_row<2, 1, true>(a0, b0, tmem, (uint32_t)npad, stp, ksteps, a.idesc, first); break;
+            case 3: dw_issue_row<3, 1, true>(a0, b0, tmem, (uint32_t)npad, stp, ksteps, a.idesc, first); break;
+            case 4: dw_issue_row<4, 1, true>(a0, b0, tmem, (uint32_t)npad, stp, ksteps, a.idesc, first); break;
+            default: dw_issue_row<5, 1, true>(a0, b0, tmem, (uint32_t)npad, stp, ksteps, a.idesc, first); break;
+          }
+        } else {
+          if (a.kwn == 3)
+            dw_issue_mt<3, false>(mtn, a0, b0, tmem, (uint32_t)npad, stp, ksteps, a.idesc, first);
+          else
+            dw_issue_mt<1, false>(mtn, a0, b0, tmem, (uint32_t)npad, stp, ksteps, a.idesc, first);
+        }
         first = false;
         mma_commit(&empty[stage]);
         if (++stage == a.stages) { stage = 0; fpar ^= 1; }
@@ -409,16 +587,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int row = q * 32 + lane;
       for (int kw = 0; kw < a.kwn; ++kw) {
         for (int t = 0; t < mtn; ++t) {
-          const int g = 16 * (mt0 + t) + row / 8;  // absolute group
-          const int ci8 = row % 8;
+          // chunk mode: absolute 8-channel group (c, kd, kh) and channel in it;
+          // wide mode: (kd, kh) plane (atom) of group grp and channel in it
+          const int g = a.wide ? (mt0 + t) * a.apt + row / a.cw : 16 * (mt0 + t) + row / 8;
+          const int ci8 = a.wide ? row % a.cw : row % 8;
           const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)((kw * mtn + t) * npad);
           for (int cc = 0; cc < npad; cc += 16) {
             float v[16];
             tmem_ld_16(tb + (uint32_t)cc, v);
-            if (g < k2 * a.c8) {
-              const int c = g / k2, rem = g % k2;
+            if (a.wide ? g < k2 : g < k2 * a.c8) {
+              const int c = a.wide ? grp : g / k2, rem = a.wide ? g : g % k2;
               const int kd = rem / a.ks, kh = rem % a.ks;
-              const int ci = c * 8 + ci8;
+              const int ci = c * (a.wide ? a.cw : 8) + ci8;
               const int tap = (kd * a.ks + kh) * a.ks + (kw0 + kw);
               const int ntap = k2 * a.ks;
               float* dst = a.part + (size_t)split * a.cout * a.cin * ntap;
@@ -427,7 +607,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int co = n0 + cc + i;
                 if (cc + i < a.nn) dst[((size_t)co * a.cin + ci) * ntap + tap] = v[i];
               }
-            } else if (has_ones && g == a.ones_group && ci8 == 0 && kw == 0) {
+            } else if (has_ones && g == (a.wide ? k2 : a.ones_group) && ci8 == 0 && kw == 0) {
 #pragma unroll
               for (int i = 0; i < 16; ++i)
                 if (cc + i < a.nn) a.dbpart[(size_t)split * a.cout + n0 + cc + i] = v[i];
@@ -491,17 +671,23 @@ static EncodeTiledFn get_encode_fn() {
   return fn;
 }
 
+// NDHWC map, box (bc channels, bx, by, bz, 1), swizzled by the box row width
+// (bc*2 = 32/64/128 bytes; 16 bytes: no swizzle).
 static bool encode_ndhwc(CUtensorMap* m, const void* base, int dtype, int c, int w, int h, int d, int n,
-                         int bx, int by, int bz) {
+                         int bx, int by, int bz, int bc = 8) {
   EncodeTiledFn enc = get_encode_fn();
   if (!enc) return false;
   const cuuint64_t e = 2;
   cuuint64_t dims[5] = {(cuuint64_t)c, (cuuint64_t)w, (cuuint64_t)h, (cuuint64_t)d, (cuuint64_t)n};
   cuuint64_t str[4] = {c * e, (cuuint64_t)w * c * e, (cuuint64_t)h * w * c * e, (cuuint64_t)d * h * w * c * e};
-  cuuint32_t box[5] = {8, (cuuint32_t)bx, (cuuint32_t)by, (cuuint32_t)bz, 1};
+  cuuint32_t box[5] = {(cuuint32_t)bc, (cuuint32_t)bx, (cuuint32_t)by, (cuuint32_t)bz, 1};
   cuuint32_t es[5] = {1, 1, 1, 1, 1};
+  const CUtensorMapSwizzle sw = bc == 64   ? CU_TENSOR_MAP_SWIZZLE_128B
+                                : bc == 32 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                : bc == 16 ? CU_TENSOR_MAP_SWIZZLE_32B
+                                           : CU_TENSOR_MAP_SWIZZLE_NONE;
   return enc(m, dtype == R4C_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5,
-             const_cast<void*>(base), dims, str, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+             const_cast<void*>(base), dims, str, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
              CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -542,11 +728,19 @@ int dw_describe(int n, int d, int h, int w, int cin, int cout, int ks, int pd, i
                 size_t len) {
   tcdw::DwPlan P;
   if (!tcdw::plan_dw(n, d, h, w, cin, cout, ks, pd, ph, pw, &P)) return 0;
-  snprintf(buf, len,
-           "tcgen05 dW: groups=%d mtiles=%d task(mt=%d n=%d kw=%d) tasks=%d splits=%d rows/split=%lld "
-           "wt=%d kpad=%d pitch=%d stages=%d stage=%dB smem=%dB tmem=%d db_in_kernel=%d est=%.0fus",
-           P.groups, P.mtiles, P.mtn, P.nn, P.kwn, (int)P.tasks.size(), P.S, P.rows_per_split, P.wt, P.kpad,
-           P.pitch_w, P.stages, P.stage_bytes, P.smem_bytes, P.tmem_cols, (int)P.db_in_kernel, P.est / 1.9e3);
+  if (P.wide)
+    snprintf(buf, len,
+             "tcgen05 dW (wide: %d-channel swizzled groups x%d, M tiles/group=%d, dY boxes of %d): "
+             "task(mt=%d n=%d kw=%d) tasks=%d splits=%d rows/split=%lld wt=%d kpad=%d pitch=%d stages=%d "
+             "stage=%dB smem=%dB tmem=%d est=%.0fus",
+             P.cw, P.ng, P.tpg, P.cwb, P.mtn, P.nn, P.kwn, (int)P.tasks.size(), P.S, P.rows_per_split, P.wt,
+             P.kpad, P.pitch_w, P.stages, P.stage_bytes, P.smem_bytes, P.tmem_cols, P.est / 1.9e3);
+  else
+    snprintf(buf, len,
+             "tcgen05 dW: groups=%d mtiles=%d task(mt=%d n=%d kw=%d) tasks=%d splits=%d rows/split=%lld "
+             "wt=%d kpad=%d pitch=%d stages=%d stage=%dB smem=%dB tmem=%d db_in_kernel=%d est=%.0fus",
+             P.groups, P.mtiles, P.mtn, P.nn, P.kwn, (int)P.tasks.size(), P.S, P.rows_per_split, P.wt, P.kpad,
+             P.pitch_w, P.stages, P.stage_bytes, P.smem_bytes, P.tmem_cols, (int)P.db_in_kernel, P.est / 1.9e3);
   return 1;
 }
 
@@ -564,8 +758,9 @@ int launch_dw(int n, int d, int h, int w, int cin, int cin_real, int cout, int k
   if (ws_bytes < need || ws == nullptr) return R4C_ERR_WORKSPACE;
   DwArgs a;
   memset(&a, 0, sizeof(a));
-  if (!encode_ndhwc(&a.tx, x, dtype, cin, w, h, d, n, P.pitch_w, ks, ks)) return R4C_ERR_INVALID;
-  if (!encode_ndhwc(&a.tg, go, dtype, cout, P.ow, P.oh, P.od, n, P.kpad, 1, 1)) return R4C_ERR_INVALID;
+  if (!encode_ndhwc(&a.tx, x, dtype, cin, w, h, d, n, P.pitch_w, ks, ks, P.wide ? P.cw : 8)) return R4C_ERR_INVALID;
+  if (!encode_ndhwc(&a.tg, go, dtype, cout, P.ow, P.oh, P.od, n, P.kpad, 1, 1, P.wide ? P.cwb : 8))
+    return R4C_ERR_INVALID;
   a.part = static_cast<float*>(ws);
   a.err = device_error_flag();
   if (!a.err) return R4C_ERR_CUDA;
@@ -584,6 +779,15 @@ int launch_dw(int n, int d, int h, int w, int cin, int cin_real, int cout, int k
     a.a_bytes = round_up((nch * ks * ks + 1) * P.pitch_w * 16, 128);
   }
   a.g_bytes = (P.nn / 8) * P.kpad * 16;
+  if (P.wide) {
+    auto lay = [](int c) { return c == 64 ? 2 : c == 32 ? 4 : c == 16 ? 6 : 0; };
+    a.wide = 1;
+    a.cw = P.cw; a.apt = P.apt; a.plane_bytes = P.plane_bytes; a.lay_a = lay(P.cw);
+    a.cwb = P.cwb; a.b_region = P.kpad * P.cwb * 2; a.lay_b = lay(P.cwb);
+    a.a_bytes = P.region_bytes;
+    a.tail_bytes = P.tail_bytes;
+    a.ones_group = -1;
+  }
   a.tmem_cols = P.tmem_cols;
   a.rows = P.rows;
   a.rows_per_split = P.rows_per_split;
@@ -593,6 +797,7 @@ int launch_dw(int n, int d, int h, int w, int cin, int cin_real, int cout, int k
   memset(&tt, 0, sizeof(tt));
   for (size_t i = 0; i < P.tasks.size(); ++i) {
     tt.mt0[i] = P.tasks[i].mt0; tt.mtn[i] = P.tasks[i].mtn; tt.n0[i] = P.tasks[i].n0; tt.kw0[i] = P.tasks[i].kw0;
+    tt.g[i] = P.tasks[i].g;
   }
   const unsigned grid = (unsigned)(P.tasks.size() * P.S);
   cudaError_t e;

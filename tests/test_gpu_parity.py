@@ -125,6 +125,36 @@ def test_conv_legs_match_oracle(cuda_ready, case, dtype, force, monkeypatch):
     assert O.norm_rel(dw, dwr) <= 1e-4
 
 
+# dW in both layouts of the tcgen05 weight-gradient kernel: 8-channel chunks
+# and wide swizzled channel groups (R4C_DW_WIDE forces one; Cin a multiple of
+# 16, >= 32, for the wide one)
+DW_CASES = [
+    (1, 48, 48, 4, 8, 8, 3, 1),
+    (1, 32, 16, 3, 5, 20, 3, 1),       # one 32-channel group, ragged W
+    (2, 96, 96, 3, 6, 10, 3, 1),
+    (1, 192, 192, 2, 4, 8, 3, 1),
+    (1, 64, 24, 3, 4, 9, 3, 0),        # pad 0, Cout 24 (8-channel dY chunks)
+    (1, 192, 96, 4, 8, 8, 1, 0),       # k1
+    (1, 48, 24, 4, 8, 8, 1, 0),
+    (1, 128, 40, 2, 3, 140, 3, 1),     # W split into two tiles
+]
+
+
+@pytest.mark.parametrize("wide", ["0", "1"], ids=["chunks", "wide"])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16], ids=["bf16", "fp16"])
+@pytest.mark.parametrize("case", DW_CASES, ids=_ids(DW_CASES))
+def test_dw_layouts_match_oracle(cuda_ready, case, dtype, wide, monkeypatch):
+    n, cin, cout, d, h, w, k, pad = case
+    monkeypatch.setenv("R4C_DW_WIDE", wide)
+    cw = _cw()
+    x, wt, b, go = _inputs(*case, dtype)
+    dw, db = cw._launch_wgrad(x.cuda(), go.cuda(), wt.shape, (pad,) * 3, True)
+    torch.cuda.synchronize()
+    dwr = O.torch_conv_dw(x, go, wt.shape, pad)
+    assert O.norm_rel(dw.cpu(), dwr) <= 1e-4
+    assert O.norm_rel(db.cpu(), go.float().sum(dim=(0, 2, 3, 4))) <= 1e-4
+
+
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16], ids=["bf16", "fp16"])
 @pytest.mark.parametrize("case", TCONV_CASES, ids=_ids(TCONV_CASES))
 def test_tconv_legs_match_oracle(cuda_ready, case, dtype):

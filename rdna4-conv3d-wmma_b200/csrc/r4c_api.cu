@@ -230,10 +230,11 @@ int r4c_describe_plan(const r4c_conv_desc* desc, int leg, char* buf, size_t len)
     } else if (use_tc(desc, leg, g, &pl)) {
       snprintf(tmp, sizeof(tmp),
                "tcgen05 conv: cin=%d cout=%d(npad %d) k=%d planes/unit=%d fold=%d tile=%dx%d pitch=%dx%d G=%d groups=%d "
-               "steps=%d mtiles=%d sets=%d stages=%d stage=%dB wres=%d stg=%d smem=%dB tmem=%d units=%lld grid=%d "
-               "est=%.0fus",
+               "padg=%d steps=%d mtiles=%d sets=%d stages=%d stage=%dB wres=%d stg=%d smem=%dB tmem=%d units=%lld "
+               "grid=%d est=%.0fus",
                pl.cin, pl.cout, pl.npad, pl.ks, pl.P, pl.fold, pl.ht, pl.wt, pl.pitch_h, pl.pitch_w, pl.G, pl.ngroups,
-               pl.nsteps, pl.mtiles, pl.nsets, pl.stages, pl.stage_bytes, pl.wres_bytes, pl.stg_bytes, pl.smem_bytes,
+               pl.padg, pl.nsteps, pl.mtiles, pl.nsets, pl.stages, pl.stage_bytes, pl.wres_bytes, pl.stg_bytes,
+               pl.smem_bytes,
                pl.tmem_cols, (long long)pl.work_units, pl.grid, pl.est_cycles / 1.9e3);
       tc::ConvPlan tp;
       if (tc::tuned_plan(pl, desc->dtype, &tp)) {

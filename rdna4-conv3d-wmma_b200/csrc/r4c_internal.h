@@ -63,6 +63,7 @@ struct ConvPlan {
   int nin;               // input planes per unit: P + ks - 1
   int fold;              // output-plane slots one MMA may cover (kd folded into N)
   int G, ngroups;        // chunks per pipeline stage, stages per kd plane
+  int padg;              // 1: the last channel group is padded up to a swizzle width (TMA zero fill past Cin)
   int nsteps;            // 16-wide K steps per stage
   int wt, ht;            // output tile (cols, rows) of one plane
   int pitch_w, pitch_h;  // brick pitches: wt + ks - 1, ht + ks - 1

@@ -104,15 +104,36 @@ static int round_up(int v, int a) { return (v + a - 1) / a * a; }
 
 struct Chg {
   int c0, cw;
+  int creal;  // channels of the group inside Cin (< cw: the rest is TMA zero fill)
 };
 
-// Cin in groups of 64, then at most one each of 32, 16, 8 channels.
-static int channel_groups(int cin, Chg* out) {
+// Cin in groups of 64, then at most one each of 32, 16, 8 channels (pad =
+// false); or, with pad, groups of 64 and one last group of the remaining r
+// channels padded up to 16, 32 or 64: one TMA row per position and group
+// instead of one per power-of-two part of r (24 channels: one 32-channel
+// group instead of 16 + 8). The padding channels are read as zeros (the box
+// passes the tensor's channel extent) and get zero weights.
+static int channel_groups(int cin, Chg* out, bool pad = false) {
   int n = 0, c = 0;
+  if (pad) {
+    while (cin - c >= 64) {
+      if (n == kMaxChg) return -1;
+      out[n++] = Chg{c, 64, 64};
+      c += 64;
+    }
+    const int r = cin - c;
+    if (r > 0) {
+      if (n == kMaxChg) return -1;
+      const int wdt = r <= 8 ? 8 : r <= 16 ? 16 : r <= 32 ? 32 : 64;
+      out[n++] = Chg{c, wdt, r};
+      c = cin;
+    }
+    return n;
+  }
   for (int wdt : {64, 32, 16, 8})
     while (cin - c >= wdt) {
       if (n == kMaxChg) return -1;
-      out[n++] = Chg{c, wdt};
+      out[n++] = Chg{c, wdt, wdt};
       c += wdt;
     }
   return c == cin ? n : -1;
@@ -141,7 +162,8 @@ static int region_rows(int mtiles, int ks, int pitch_w, int pitch_h) {
 // split_w = 0: every channel group of a plane in one stage; otherwise the
 // plane's channels in stages of one split_w-wide group each (split_w divides
 // Cin), which keeps the weight slice staged with each stage small.
-static bool stage_layout(int cin, int split_w, int mtiles, int ks, int pitch_w, int pitch_h, StageLayout* L) {
+static bool stage_layout(int cin, int split_w, int mtiles, int ks, int pitch_w, int pitch_h, StageLayout* L,
+                         bool pad = false) {
   Chg all[kMaxChg];
   const int rows = region_rows(mtiles, ks, pitch_w, pitch_h);
   L->a_bytes = 0;
@@ -149,11 +171,11 @@ static bool stage_layout(int cin, int split_w, int mtiles, int ks, int pitch_w, 
   if (split_w) {
     if (cin % split_w != 0 || cin / split_w < 2) return false;
     L->nchg = 1;
-    L->g[0] = Chg{0, split_w};
+    L->g[0] = Chg{0, split_w, split_w};
     L->stage_c0 = split_w;
     L->ngroups = cin / split_w;
   } else {
-    const int n = channel_groups(cin, all);
+    const int n = channel_groups(cin, all, pad);
     if (n <= 0) return false;
     L->nchg = n;
     for (int i = 0; i < n; ++i) L->g[i] = all[i];
@@ -188,9 +210,10 @@ static void build_steps(const StageLayout& L, int ks, int pitch_w, std::vector<S
     const int cw = L.g[gi].cw, rb = cw * 2, ch0 = L.g[gi].c0 / 8, ro = L.roff[gi];
     auto off = [&](int kh, int kw) { return ro + (kh * pitch_w + kw) * rb; };
     if (cw >= 16) {
+      const int nk = (L.g[gi].creal + 15) / 16;  // K steps over the group's real channels
       for (int kh = 0; kh < ks; ++kh)
         for (int kw = 0; kw < ks; ++kw)
-          for (int kk = 0; kk < cw / 16; ++kk)
+          for (int kk = 0; kk < nk; ++kk)
             st.push_back(Step{{ref(kh, kw, ch0 + 2 * kk), ref(kh, kw, ch0 + 2 * kk + 1)}, off(kh, kw) + kk * 32, 16,
                               8 * rb, layout_code(cw), 128 * rb});
     } else if (ks == 3) {
@@ -225,7 +248,7 @@ static double mma_clk(int n) { return std::max({n / 2.0, 40.0 + n / 6.0, 45.0});
 // G = 8-channel chunks per stage, stages caps the stage count). Unset keys
 // are searched as usual.
 struct PlanForce {
-  int ht = 0, nw = 0, P = 0, G = 0, wres = -1, stages = 0, stg = -1;
+  int ht = 0, nw = 0, P = 0, G = 0, wres = -1, stages = 0, stg = -1, pad = -1;
 };
 static PlanForce plan_force() {
   PlanForce f;
@@ -241,6 +264,7 @@ static PlanForce plan_force() {
     else if (!strcmp(key, "wres")) f.wres = val;
     else if (!strcmp(key, "stages")) f.stages = val;
     else if (!strcmp(key, "stg")) f.stg = val;
+    else if (!strcmp(key, "pad")) f.pad = val;
     e += used;
     while (*e == ',' || *e == ' ') ++e;
   }
@@ -274,9 +298,16 @@ static void enumerate_plans(int n, int d, int h, int w, int cin, int cout, int k
   const int nw_min = (P.ow + wt_max - 1) / wt_max;
   const int sms = num_sms();
 
-  for (int split : {0, 64, 32, 16, 8}) {
-    if (split && (cin % split != 0 || cin / split < 2)) continue;
-    const int G = split ? split / 8 : P.c8;
+  for (int split : {-1, 0, 64, 32, 16, 8}) {  // -1: all groups in one stage, last one padded
+    if (split > 0 && (cin % split != 0 || cin / split < 2)) continue;
+    const bool padg = split < 0;
+    if (padg) {  // only when padding changes the grouping
+      Chg a1[kMaxChg], a2[kMaxChg];
+      const int n1 = channel_groups(cin, a1, false), n2 = channel_groups(cin, a2, true);
+      if (n2 <= 0 || n2 == n1) continue;
+    }
+    if (force.pad >= 0 && (int)padg != force.pad) continue;
+    const int G = split > 0 ? split / 8 : P.c8;
     if (force.G && G != force.G) continue;
     if (G_only > 0 && G != G_only) continue;
     const int nw_a = force.nw ? force.nw : nw_min, nw_b = force.nw ? force.nw : nw_min + 8;
@@ -298,7 +329,7 @@ static void enumerate_plans(int n, int d, int h, int w, int cin, int cout, int k
         const int mtiles = (span + 127) / 128;
         if (mtiles * P.npad > 512 || mtiles > kMaxMt) break;
         StageLayout L;
-        if (!stage_layout(cin, split, mtiles, ks, pitch_w, pitch_h, &L)) break;
+        if (!stage_layout(cin, split > 0 ? split : 0, mtiles, ks, pitch_w, pitch_h, &L, padg)) break;
         std::vector<Step> steps;
         build_steps(L, ks, pitch_w, steps);
         const int nsteps = (int)steps.size();
@@ -360,7 +391,7 @@ static void enumerate_plans(int n, int d, int h, int w, int cin, int cout, int k
           const long long waves = (units + sms - 1) / sms;
           const double est = (double)waves * t_unit;
           {
-            P.G = G; P.ngroups = ngroups; P.nsteps = nsteps;
+            P.G = G; P.ngroups = ngroups; P.nsteps = nsteps; P.padg = padg ? 1 : 0;
             P.wt = wt; P.ht = ht; P.pitch_w = pitch_w; P.pitch_h = pitch_h;
             P.mtiles = mtiles; P.nsets = nsets;
             P.P = Pb; P.nin = nin;
@@ -434,8 +465,10 @@ bool plan_conv(int n, int d, int h, int w, int cin, int cout, int ks, int pd, in
 static std::vector<ConvPlan> plan_candidates(const ConvPlan& m, int k_top) {
   std::vector<ConvPlan> all;
   PlanForce none;
-  enumerate_plans(m.n, m.d, m.h, m.w, m.cin, m.cout, m.ks, m.pd, m.ph, m.pw, m.G, none,
-                  [&](const ConvPlan& c) { all.push_back(c); });
+  // same packed weights: same chunks per stage and the same channel grouping
+  enumerate_plans(m.n, m.d, m.h, m.w, m.cin, m.cout, m.ks, m.pd, m.ph, m.pw, m.G, none, [&](const ConvPlan& c) {
+    if (c.padg == m.padg) all.push_back(c);
+  });
   std::sort(all.begin(), all.end(), [](const ConvPlan& a, const ConvPlan& b) { return a.est_cycles < b.est_cycles; });
   std::vector<ConvPlan> out;
   auto same = [](const ConvPlan& a, const ConvPlan& b) {
@@ -462,7 +495,8 @@ static std::vector<ConvPlan> plan_candidates(const ConvPlan& m, int k_top) {
 size_t packed_bytes(const ConvPlan& P) { return (size_t)P.ngroups * P.b_bytes; }
 
 static bool plan_layout(const ConvPlan& P, StageLayout* L, std::vector<Step>* steps) {
-  if (!stage_layout(P.cin, P.ngroups > 1 ? P.G * 8 : 0, P.mtiles, P.ks, P.pitch_w, P.pitch_h, L)) return false;
+  if (!stage_layout(P.cin, P.ngroups > 1 ? P.G * 8 : 0, P.mtiles, P.ks, P.pitch_w, P.pitch_h, L, P.padg != 0))
+    return false;
   if (L->ngroups != P.ngroups) return false;
   build_steps(*L, P.ks, P.pitch_w, *steps);
   return (int)steps->size() == P.nsteps;
@@ -548,27 +582,34 @@ using namespace r4c::sm100;
 // Store NV (16 or 32) accumulator columns starting at channel cc of one
 // output row: bias added, rounded to T; every complete 8-channel group inside
 // cout goes out as one 16-byte store when the row is 16-byte aligned.
+template <typename T> __device__ __forceinline__ uint32_t pack2(float a, float b);
+template <> __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);  // one paired conversion
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+template <> __device__ __forceinline__ uint32_t pack2<__half>(float a, float b) {
+  __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
 template <typename T, int NV>
 __device__ __forceinline__ void store_row(T* dst, const float (&v)[NV], const float* bias, int cc, int cout,
                                           bool vec_ok) {
+  const float4* bias4 = reinterpret_cast<const float4*>(bias);  // 16-byte aligned, npad entries
 #pragma unroll
   for (int g = 0; g < NV / 8; ++g) {
     const int c0 = cc + 8 * g;
     if (c0 >= cout) break;
+    const float4 b0 = bias4[c0 / 4], b1 = bias4[c0 / 4 + 1];
+    const float f[8] = {v[8 * g] + b0.x,     v[8 * g + 1] + b0.y, v[8 * g + 2] + b0.z, v[8 * g + 3] + b0.w,
+                        v[8 * g + 4] + b1.x, v[8 * g + 5] + b1.y, v[8 * g + 6] + b1.z, v[8 * g + 7] + b1.w};
     if (vec_ok && c0 + 8 <= cout) {
-      uint32_t pk[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        T lo = Elem<T>::from_f(v[8 * g + 2 * i] + bias[c0 + 2 * i]);
-        T hi = Elem<T>::from_f(v[8 * g + 2 * i + 1] + bias[c0 + 2 * i + 1]);
-        pk[i] = (uint32_t)(*reinterpret_cast<uint16_t*>(&lo)) |
-                ((uint32_t)(*reinterpret_cast<uint16_t*>(&hi)) << 16);
-      }
-      *reinterpret_cast<uint4*>(dst + c0) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      *reinterpret_cast<uint4*>(dst + c0) =
+          make_uint4(pack2<T>(f[0], f[1]), pack2<T>(f[2], f[3]), pack2<T>(f[4], f[5]), pack2<T>(f[6], f[7]));
     } else {
 #pragma unroll
       for (int i = 0; i < 8; ++i)
-        if (c0 + i < cout) dst[c0 + i] = Elem<T>::from_f(v[8 * g + i] + bias[c0 + i]);
+        if (c0 + i < cout) dst[c0 + i] = Elem<T>::from_f(f[i]);
     }
   }
 }

@@ -31,12 +31,14 @@
 //    M=128 K=16 MMA costs ~45 SM clocks whatever N <= 48 is (shared-memory
 //    operand fetch), so N=32 alone would cap the tensor pipe near 35%.
 //  * fp32 accumulators live in TMEM ([set][tile][slot][Cout_pad] columns,
-//    double-buffered when they fit); four epilogue warps read them with
-//    tcgen05.ld, add bias, round, store NDHWC and write the columns back to
-//    zero, so that every MMA accumulates.
+//    double-buffered when they fit); eight epilogue warps (two per TMEM lane
+//    quarter, alternate (tile, plane) slots: the epilogue is instruction-
+//    bound per thread, and two warps per sub-partition hide each other's
+//    latency) read them with tcgen05.ld, add bias, round, store NDHWC and
+//    write the columns back to zero, so that every MMA accumulates.
 //
-// Warp roles (192 threads): warp 0 TMA producer (lane 0), warp 1 MMA issuer
-// (lane 0) + TMEM owner, warps 2-5 epilogue (TMEM lane quarter = warp % 4).
+// Warp roles (320 threads): warp 0 TMA producer (lane 0), warp 1 MMA issuer
+// (lane 0) + TMEM owner, warps 2-9 epilogue (TMEM lane quarter = warp % 4).
 // Every wait is bounded (1 s); a timeout sets the device error flag and the
 // kernel winds down (copies drained, TMEM released) instead of hanging.
 #include <cuda.h>
@@ -64,7 +66,8 @@ constexpr int kMaxSteps = 128;
 constexpr int kMaxStages = 8;
 constexpr int kMaxMt = 8;    // M tiles per unit (the issue loop is unrolled over them)
 constexpr int kMaxChg = 16;  // channel groups per stage
-constexpr int kThreads = 192;
+constexpr int kEpiWarps = 8;  // two per TMEM lane quarter (alternate (tile, plane) slots)
+constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kMmaWarp = 1;
 constexpr int kSmemMax = 232448;  // 227 KB opt-in dynamic shared memory
 constexpr int kHeader = 4096;     // barriers, bias, descriptor tables
@@ -694,8 +697,8 @@ __device__ __forceinline__ void issue(int mt, int ns, R4C_ISSUE_PARAMS) {
 #undef R4C_ISSUE_ARGS
 #undef R4C_ISSUE_PARAMS
 
-// Barrier among the four epilogue warps only (threads 64..191).
-__device__ __forceinline__ void epi_bar_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// Barrier among the epilogue warps only (threads 64..64 + 32*kEpiWarps - 1).
+__device__ __forceinline__ void epi_bar_sync() { asm volatile("bar.sync 1, %0;" ::"n"(32 * kEpiWarps) : "memory"); }
 
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1) tc_conv_kernel(const __grid_constant__ TcConvArgs a) {
@@ -751,7 +754,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_conv_kernel(const __grid_const
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&tfull[s], 1);
-      mbar_init(&tempty[s], 4);
+      mbar_init(&tempty[s], kEpiWarps);
     }
     mbar_init(mdone, 1);
     mbar_init(wbar, 1);
@@ -916,8 +919,9 @@ __global__ void __launch_bounds__(kThreads, 1) tc_conv_kernel(const __grid_const
       wait(mdone, 0);
     }
   } else {
-    // ---------------- epilogue (warps 2..5) ----------------
-    const int q = warp & 3;
+    // ---------------- epilogue (warps 2..9) ----------------
+    const int q = warp & 3;                // TMEM lane quarter this warp may read
+    const int half = (warp - 2) >> 2;      // which of the two warps of the quarter
     const int row = q * 32 + lane;
     T* __restrict__ y = static_cast<T*>(a.y);
     const bool vec_ok = (a.cout % 8) == 0;
@@ -928,7 +932,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_conv_kernel(const __grid_const
     // zeroes its lane quarter of every set now and of each set it drains,
     // and releases a set (tempty) only after those stores completed.
     const uint32_t tq = tmem + ((uint32_t)(q * 32) << 16);
-    for (int c = 0; c < a.nsets * set_cols; c += 16) tmem_zero_16(tq + (uint32_t)c);
+    for (int c = 16 * half; c < a.nsets * set_cols; c += 32) tmem_zero_16(tq + (uint32_t)c);
     tmem_wait_st();
     tc_fence_before();
     __syncwarp();
@@ -947,11 +951,13 @@ __global__ void __launch_bounds__(kThreads, 1) tc_conv_kernel(const __grid_const
       if (lane == 0) got = wait(&tfull[set], fpar[set], 128) ? 1 : 0;
       got = __shfl_sync(0xffffffffu, got, 0);
       if (a.stg_bytes) {
-        // The TMA-store path synchronises the four epilogue warps on a named
+        // The TMA-store path synchronises the epilogue warps on a named
         // barrier, so they leave the loop together: agree on the wait results.
-        if (lane == 0) epi_ok[q] = got;
+        if (lane == 0) epi_ok[warp - 2] = got;
         epi_bar_sync();
-        got = epi_ok[0] & epi_ok[1] & epi_ok[2] & epi_ok[3];
+        got = 1;
+#pragma unroll
+        for (int i = 0; i < kEpiWarps; ++i) got &= epi_ok[i];
       }
       if (!got) break;
       fpar[set] ^= 1;
@@ -970,7 +976,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_conv_kernel(const __grid_const
             epi_bar_sync();
           }
           T* sb = reinterpret_cast<T*>(stg0 + (size_t)sbuf * a.stg_bytes);
-          for (int t = 0; t < a.mtiles; ++t) {
+          for (int t = half; t < a.mtiles; t += 2) {
             const int p = t * 128 + row;
             const int hh = p / a.pitch_w;
             const int ww = p - hh * a.pitch_w;
@@ -1012,7 +1018,10 @@ __global__ void __launch_bounds__(kThreads, 1) tc_conv_kernel(const __grid_const
         const int ww = p - hh * a.pitch_w;
         const bool pos_ok = hh < a.ht && ww < a.wt && (h0 + hh) < a.oh && (w0 + ww) < a.ow;
         T* dst = yu + ((long long)hh * a.ow + ww) * a.cout;
-        for (int o = 0; o < a.P; ++o, dst += plane) {
+        // this warp's (tile, plane) slots: t*P + o of its parity
+        const int o0 = (t * a.P + half) & 1;
+        dst += (long long)o0 * plane;
+        for (int o = o0; o < a.P; o += 2, dst += 2 * plane) {
           const bool valid = pos_ok && o < nz;
           const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) +
                               (uint32_t)(set * set_cols + t * a.P * a.slot_w + o * a.slot_w);

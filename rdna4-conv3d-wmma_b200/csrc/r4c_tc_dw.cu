@@ -73,6 +73,7 @@ struct alignas(64) DwArgs {
   int wide;
   int cw, apt, plane_bytes, lay_a;
   int cwb, b_region, lay_b;
+  int nbox, npad_w;                  // dY boxes per stage, MMA N
   int tail_bytes;                    // zeroed bytes past the last stage (M tile over-read)
 };
 
@@ -84,7 +85,7 @@ struct Task {
 struct DwPlan {
   bool ok;
   bool wide;
-  int cw, apt, tpg, ng, plane_bytes, region_bytes, cwb, tail_bytes;
+  int cw, apt, tpg, ng, plane_bytes, region_bytes, cwb, nbox, npad_w, tail_bytes;
   int n, d, h, w, od, oh, ow, cin, cout, ks, pd, ph, pw;
   int c8, groups, mtiles, pitch_w, kpad, wt, nwt;
   int mtn, nn, kwn;  // task shape
@@ -165,8 +166,13 @@ static bool plan_dw(int n, int d, int h, int w, int cin, int cout, int ks, int p
   // to the chunk layout (96->96 206 -> 238 us, 48->48 248 -> 314 us: more M
   // tiles per K step outweigh the fewer TMA rows). R4C_DW_WIDE=1 enables the
   // narrower groups, =0 disables the wide layout.
-  const bool wide_auto = wide_force == -1 && cw_ok == 64 && cin >= 64;
-  const bool chunk_allowed = !((wide_force == 1 && cw_ok && cin >= 32) || wide_auto);
+  // k1 layers (a plain GEMM over positions, TMA-row-bound in the chunk
+  // layout) take the wide layout with the channel groups padded up to 64 /
+  // 32 / 16 (the TMA zero-fills channels past Cin): one TMA row per position
+  // and group.
+  const int cw_pad = cin >= 48 ? 64 : cin > 16 ? 32 : 16;
+  const bool wide_auto = wide_force == -1 && ((cw_ok == 64 && cin >= 64) || (ks == 1 && cin >= 16));
+  const bool chunk_allowed = !((wide_force == 1 && cin >= 16) || wide_auto);
 
   // Task shape: largest N split and M-tile group that fits TMEM (512 cols)
   // with all kw in one task when possible.
@@ -233,10 +239,10 @@ static bool plan_dw(int n, int d, int h, int w, int cin, int cout, int ks, int p
   }
   // Wide mode (Cin a multiple of 16, at least 32): one swizzled box per
   // channel group and row instead of one 16-byte-row box per 8 channels.
-  const int cw = cw_ok;
-  if (cw && cin >= 32 && (wide_force == 1 || wide_auto)) {
+  const int cw = (wide_force == 1 || ks == 1) ? cw_pad : cw_ok;
+  if (cin >= 16 && (wide_force == 1 || wide_auto)) {
     const int apt = 128 / cw, atoms = k2 + 1;  // + the ones (group 0) / zero plane
-    const int tpg = (atoms + apt - 1) / apt, ng = cin / cw;
+    const int tpg = (atoms + apt - 1) / apt, ng = (cin + cw - 1) / cw;
     // W tile: the chunk layout's, halved until two stages fit
     int wt_w = P.wt;
     auto plane_of = [&](int t) { return round_up(round_up(t, 16) + ks - 1, 8) * cw * 2; };
@@ -254,24 +260,27 @@ static bool plan_dw(int n, int d, int h, int w, int cin, int cout, int ks, int p
     for (int kwn : {1}) {  // one kw per task: keeps the wide issue code (runtime steps) small
       for (int nn = cout; nn >= 8; nn -= 8) {
         if (cout % nn) continue;
-        const int npad = round_up(nn, 16);
+        // dY boxes of cwb channels, the last padded (channels past nn are
+        // computed and dropped, past Cout zero-filled); MMA N = the boxes
+        const int cwb = nn % 64 == 0 ? 64 : nn % 32 == 0 ? 32 : nn % 16 == 0 ? 16 : nn <= 16 ? 16 : nn <= 32 ? 32 : 64;
+        const int nbox = (nn + cwb - 1) / cwb;
+        const int npad = round_up(nbox * cwb, 16);
         if (npad > 256) continue;
-        const int cwb = nn % 64 == 0 ? 64 : nn % 32 == 0 ? 32 : nn % 16 == 0 ? 16 : 8;
         // the last stage's over-reads past its end stay inside the zeroed
-        // tail: A tiles past the group's planes, B chunks past nn (npad > nn)
-        const int tail_nn = std::max(tail, (npad - nn) / 8 * kpad_w * 16 + 1024);
+        // tail: A tiles past the group's planes, B chunks past the boxes
+        const int tail_nn = std::max(tail, (npad - nbox * cwb) / 8 * kpad_w * 16 + 1024);
         for (int mtn = std::min(tpg, 5); mtn >= 1; --mtn) {
           const int cols = kwn * mtn * npad;
           if (cols > 512) continue;
           const int ntasks = ng * ((tpg + mtn - 1) / mtn) * (cout / nn) * (ks / kwn);
           if (ntasks > 128) continue;
-          const int stage = region + round_up(nn * kpad_w * 2, 1024);
+          const int stage = region + round_up(nbox * cwb * kpad_w * 2, 1024);
           const int stages = std::min(kMaxStages, (kSmemMax - kHeader - tail_nn) / stage);
           if (stages < 2) continue;
           const double t_mma = dw_mma_clk(npad);
           const double mma = (double)(kpad_w / 16) * kwn * mtn * t_mma;
-          const double rows = (double)k2 * pitch_ww + (double)(nn / cwb) * kpad_w;
-          const double bytes = (double)k2 * plane + (double)nn * kpad_w * 2;
+          const double rows = (double)k2 * pitch_ww + (double)nbox * kpad_w;
+          const double bytes = (double)k2 * plane + (double)nbox * cwb * kpad_w * 2;
           const double load = std::max(bytes / 48.0, rows * 2.2);
           const double per_row = std::max(std::max(mma, load) + 60.0, (kTmaLatencyClk + mma) / stages);
           int S = (int)std::max<long long>(1, std::min<long long>(rows_w, (2LL * sms + ntasks - 1) / ntasks));
@@ -285,7 +294,7 @@ static bool plan_dw(int n, int d, int h, int w, int cin, int cout, int ks, int p
             P.wide = true;
             P.wt = wt_w; P.nwt = nwt_w; P.kpad = kpad_w; P.pitch_w = pitch_ww; P.rows = rows_w;
             P.cw = cw; P.apt = apt; P.tpg = tpg; P.ng = ng; P.plane_bytes = plane; P.region_bytes = region;
-            P.cwb = cwb; P.tail_bytes = tail_nn;
+            P.cwb = cwb; P.nbox = nbox; P.npad_w = npad; P.tail_bytes = tail_nn;
             P.mtn = mtn; P.nn = nn; P.kwn = kwn;
             P.S = S; P.rows_per_split = rps;
             P.stages = stages; P.stage_bytes = stage;
@@ -425,8 +434,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                                   k2 < (mt0 + mtn) * a.apt)
                                : (a.ones_group >= 16 * mt0 && a.ones_group < 16 * (mt0 + mtn) && kw0 == 0 &&
                                   a.dbpart != nullptr);
-  const int npad = (a.nn + 15) / 16 * 16;
-  const uint32_t tx_bytes = a.wide ? (uint32_t)(k2 * a.plane_bytes + a.nn * a.kpad * 2)
+  // MMA N. Kept as arithmetic on the task width: loading it as a plain
+  // argument changes the issue loop's register allocation (96 registers, no
+  // descriptor reuse) and measured 9 % slower at 24->24.
+  const int npad = ((a.wide ? a.nbox * a.cwb : a.nn) + 15) / 16 * 16;
+  const uint32_t tx_bytes = a.wide ? (uint32_t)(k2 * a.plane_bytes + a.nbox * a.cwb * a.kpad * 2)
                                    : (uint32_t)(nch * k2 * sbo_a + (a.nn / 8) * a.kpad * 16);
 
   // zero the whole dynamic region (finite junk rows), then the ones rows
@@ -511,7 +523,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (a.wide) {
           // the k x k input rows of the group: planes [kd][kh] of pitch_w positions
           tma_load_5d(sA, &a.tx, &full[stage], grp * a.cw, w0 - a.pw, y - a.ph, z - a.pd, nb);
-          for (int c = 0; c < a.nn / a.cwb; ++c)
+          for (int c = 0; c < a.nbox; ++c)
             tma_load_5d(sA + a.a_bytes + (size_t)c * a.b_region, &a.tg, &full[stage], n0 + c * a.cwb, w0, y, z, nb);
         } else {
           for (int c = 0; c < nch; ++c)
@@ -595,7 +607,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int cc = 0; cc < npad; cc += 16) {
             float v[16];
             tmem_ld_16(tb + (uint32_t)cc, v);
-            if (a.wide ? g < k2 : g < k2 * a.c8) {
+            const bool real_ci = !a.wide || grp * a.cw + ci8 < a.cin;  // padded group channels
+            if ((a.wide ? g < k2 : g < k2 * a.c8) && real_ci) {
               const int c = a.wide ? grp : g / k2, rem = a.wide ? g : g % k2;
               const int kd = rem / a.ks, kh = rem % a.ks;
               const int ci = c * (a.wide ? a.cw : 8) + ci8;
@@ -625,28 +638,49 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// dw[co][ci][tap] (ci < cin_real) = sum over splits, in split order, of the
-// partials laid out with cin_pad input channels.
-__global__ void dw_reduce_kernel(const float* __restrict__ part, int S, int cout, int cin_pad, int cin_real,
-                                 int ntap, float* __restrict__ dw, const float* __restrict__ dbpart,
-                                 float* __restrict__ db) {
+// dw[co][ci][tap] (ci < cin_real) = sum over splits of the partials laid out
+// with cin_pad input channels. A block covers 32 outputs with LANES lanes
+// each: lane j sums splits j, j+LANES, ... in order, then the lane sums are
+// added in a fixed tree — a fixed association, so reruns are bitwise
+// identical. LANES = 8 keeps 8x the loads in flight when S is large (one
+// thread per output was latency-bound at S ~ 100-300 splits); LANES = 1 for
+// few splits over many outputs.
+template <int LANES>
+__global__ void __launch_bounds__(256) dw_reduce_kernel(const float* __restrict__ part, int S, int cout,
+                                                               int cin_pad, int cin_real, int ntap,
+                                                               float* __restrict__ dw,
+                                                               const float* __restrict__ dbpart,
+                                                               float* __restrict__ db) {
+  __shared__ float red[8][33];
   const long long total_pad = (long long)cout * cin_pad * ntap;
   const long long total = (long long)cout * cin_real * ntap;
-  long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < total) {
+  constexpr int OPB = 256 / LANES;  // outputs per block
+  const int o = threadIdx.x % OPB, lj = threadIdx.x / OPB;
+  const long long i = (long long)blockIdx.x * OPB + o;
+  // outputs [0, total) are dW; [total, total + cout) are db (when requested)
+  const bool is_dw = i < total;
+  const bool is_db = !is_dw && db != nullptr && dbpart != nullptr && i < total + cout;
+  float s = 0.f;
+  if (is_dw) {
     const int tap = (int)(i % ntap);
     const long long r = i / ntap;
     const int ci = (int)(r % cin_real);
     const int co = (int)(r / cin_real);
     const long long j = ((long long)co * cin_pad + ci) * ntap + tap;
-    float s = 0.f;
-    for (int k = 0; k < S; ++k) s += part[(size_t)k * total_pad + j];
-    dw[i] = s;
+    for (int k = lj; k < S; k += LANES) s += part[(size_t)k * total_pad + j];
+  } else if (is_db) {
+    const long long c = i - total;
+    for (int k = lj; k < S; k += LANES) s += dbpart[(size_t)k * cout + c];
   }
-  if (db != nullptr && dbpart != nullptr && i < cout) {
-    float s = 0.f;
-    for (int k = 0; k < S; ++k) s += dbpart[(size_t)k * cout + i];
-    db[i] = s;
+  float t = s;
+  if (LANES > 1) {
+    red[lj][o] = s;
+    __syncthreads();
+    t = ((red[0][o] + red[1][o]) + (red[2][o] + red[3][o])) + ((red[4][o] + red[5][o]) + (red[6][o] + red[7][o]));
+  }
+  if (lj == 0 && (is_dw || is_db)) {
+    if (is_dw) dw[i] = t;
+    else db[i - total] = t;
   }
 }
 
@@ -784,6 +818,7 @@ int launch_dw(int n, int d, int h, int w, int cin, int cin_real, int cout, int k
     a.wide = 1;
     a.cw = P.cw; a.apt = P.apt; a.plane_bytes = P.plane_bytes; a.lay_a = lay(P.cw);
     a.cwb = P.cwb; a.b_region = P.kpad * P.cwb * 2; a.lay_b = lay(P.cwb);
+    a.nbox = P.nbox; a.npad_w = P.npad_w;
     a.a_bytes = P.region_bytes;
     a.tail_bytes = P.tail_bytes;
     a.ones_group = -1;
@@ -792,7 +827,7 @@ int launch_dw(int n, int d, int h, int w, int cin, int cin_real, int cout, int k
   a.rows = P.rows;
   a.rows_per_split = P.rows_per_split;
   a.ntasks = (int)P.tasks.size();
-  a.idesc = sm100::instr_desc_f16(dtype == R4C_BF16, 128, round_up(P.nn, 16), 1, 1);
+  a.idesc = sm100::instr_desc_f16(dtype == R4C_BF16, 128, P.wide ? P.npad_w : round_up(P.nn, 16), 1, 1);
   TaskTable tt;
   memset(&tt, 0, sizeof(tt));
   for (size_t i = 0; i < P.tasks.size(); ++i) {
@@ -812,8 +847,12 @@ int launch_dw(int n, int d, int h, int w, int cin, int cin_real, int cout, int k
   }
   if (cudaGetLastError() != cudaSuccess) return R4C_ERR_CUDA;
   const long long total = (long long)cout * cin_real * T;
-  const long long nthr = std::max<long long>(total, cout);
-  dw_reduce_kernel<<<(unsigned)((nthr + 255) / 256), 256, 0, st>>>(a.part, P.S, cout, cin, cin_real, (int)T, dw,
+  const long long nout = total + (a.dbpart ? cout : 0);
+  if (P.S >= 48)
+    dw_reduce_kernel<8><<<(unsigned)((nout + 31) / 32), 256, 0, st>>>(a.part, P.S, cout, cin, cin_real, (int)T, dw,
+                                                                      a.dbpart, a.dbpart ? db : nullptr);
+  else
+    dw_reduce_kernel<1><<<(unsigned)((nout + 255) / 256), 256, 0, st>>>(a.part, P.S, cout, cin, cin_real, (int)T, dw,
                                                                     a.dbpart, a.dbpart ? db : nullptr);
   note_launches(2);
   if (cudaGetLastError() != cudaSuccess) return R4C_ERR_CUDA;

@@ -713,13 +713,19 @@ __global__ void __launch_bounds__(kDwThreads, 1) stem_dw_kernel(const __grid_con
   }
 }
 
-// Sum of the CTA partials in CTA order: dW in OIDHW fp32 (slot k of tap
-// (kd,kh,kw), channel c: k = (kd*3+kh)*4*cin + kw*cin + c) and db (slot 3*cin).
-__global__ void stem_dw_reduce(const float* __restrict__ part, int nparts, int kpad, int npad, int cin, int cout,
-                               float* __restrict__ dw, float* __restrict__ db) {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+// Sum of the CTA partials: dW in OIDHW fp32 (slot k of tap (kd,kh,kw),
+// channel c: k = (kd*3+kh)*4*cin + kw*cin + c) and db (slot 3*cin). A block
+// covers 32 outputs with 8 lanes each (lane j sums partials j, j+8, ... in
+// order; the lane sums are added in a fixed tree): a fixed association
+// (bitwise-identical reruns) with 8 loads in flight per output.
+__global__ void __launch_bounds__(256) stem_dw_reduce(const float* __restrict__ part, int nparts, int kpad, int npad,
+                                                      int cin, int cout, float* __restrict__ dw,
+                                                      float* __restrict__ db) {
+  __shared__ float red[8][33];
+  const int o = threadIdx.x & 31, lj = threadIdx.x >> 5;
+  const int i = blockIdx.x * 32 + o;
   const int nw = cout * cin * 27;
-  int k, co;
+  int k = -1, co = 0;
   if (i < nw) {
     co = i / (cin * 27);
     const int r = i - co * cin * 27;
@@ -728,13 +734,18 @@ __global__ void stem_dw_reduce(const float* __restrict__ part, int nparts, int k
   } else if (db != nullptr && i < nw + cout) {
     co = i - nw;
     k = 3 * cin;
-  } else {
-    return;
   }
   float s = 0.f;
-  for (int b = 0; b < nparts; ++b) s += part[((size_t)b * kpad + k) * npad + co];
-  if (i < nw) dw[i] = s;
-  else db[co] = s;
+  if (k >= 0)
+    for (int b = lj; b < nparts; b += 8) s += part[((size_t)b * kpad + k) * npad + co];
+  red[lj][o] = s;
+  __syncthreads();
+  if (lj == 0 && k >= 0) {
+    const float t = ((red[0][o] + red[1][o]) + (red[2][o] + red[3][o])) +
+                    ((red[4][o] + red[5][o]) + (red[6][o] + red[7][o]));
+    if (i < nw) dw[i] = t;
+    else db[co] = t;
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -1150,7 +1161,7 @@ int launch_dw(int n, int d, int h, int w, int cin, int cout, int pd, int ph, int
   note_launches(1);
   if (ce != cudaSuccess) return R4C_ERR_CUDA;
   const int nout = cout * cin * 27 + cout;
-  stem_dw_reduce<<<(nout + 127) / 128, 128, 0, st>>>(a.part, grid, p.kpad, p.npad, cin, cout, dw, db);
+  stem_dw_reduce<<<(nout + 31) / 32, 256, 0, st>>>(a.part, grid, p.kpad, p.npad, cin, cout, dw, db);
   note_launches(1);
   return cudaGetLastError() == cudaSuccess ? R4C_OK : R4C_ERR_CUDA;
 }

@@ -485,11 +485,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   const long long r_beg = (long long)split * a.rows_per_split;
   const long long r_end = min(r_beg + a.rows_per_split, a.rows);
   const uint64_t kWaitNs = 1000000000ull;
-  auto wait = [&](uint64_t* bar, uint32_t par) -> bool {
+  // Bounded wait; `nap` > 0 sleeps between polls (waiting warps leave issue
+  // slots to the producer and MMA threads on their sub-partitions).
+  auto wait = [&](uint64_t* bar, uint32_t par, uint32_t nap = 0) -> bool {
     uint64_t deadline = global_timer_ns() + kWaitNs;
     uint32_t spins = 0;
     while (!mbar_try_wait(bar, par)) {
-      if (((++spins) & 255u) == 0) {
+      if (nap) __nanosleep(nap);
+      if (((++spins) & (nap ? 15u : 255u)) == 0) {
         if (*abort_flag) return false;
         if (global_timer_ns() > deadline) {
           *abort_flag = 1;
@@ -592,8 +595,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       mma_commit(done);
     }
   } else {
-    // epilogue: wait for every MMA, then write the fp32 partials of this task
-    if (wait(done, 0)) {
+    // epilogue: wait (lane 0, sleeping between polls) for every MMA, then
+    // write the fp32 partials of this task
+    int got = 1;
+    if (lane == 0) got = wait(done, 0, 256) ? 1 : 0;
+    got = __shfl_sync(0xffffffffu, got, 0);
+    if (got) {
       tc_fence_after();
       const int q = warp & 3;
       const int row = q * 32 + lane;

@@ -126,8 +126,8 @@ def test_conv_legs_match_oracle(cuda_ready, case, dtype, force, monkeypatch):
 
 
 # dW in both layouts of the tcgen05 weight-gradient kernel: 8-channel chunks
-# and wide swizzled channel groups (R4C_DW_WIDE forces one; Cin a multiple of
-# 16, >= 32, for the wide one)
+# and wide swizzled channel groups (R4C_DW_WIDE forces one; with the wide
+# one, groups and dY boxes past Cin / Cout are padded with zero channels)
 DW_CASES = [
     (1, 48, 48, 4, 8, 8, 3, 1),
     (1, 32, 16, 3, 5, 20, 3, 1),       # one 32-channel group, ragged W
@@ -137,6 +137,8 @@ DW_CASES = [
     (1, 192, 96, 4, 8, 8, 1, 0),       # k1
     (1, 48, 24, 4, 8, 8, 1, 0),
     (1, 128, 40, 2, 3, 140, 3, 1),     # W split into two tiles
+    (1, 40, 40, 3, 5, 16, 1, 0),       # padded channel group (40 of 64) and dY box (40 of 64)
+    (1, 24, 24, 3, 5, 16, 3, 1),       # padded 32-channel group and dY box (24 real)
 ]
 
 

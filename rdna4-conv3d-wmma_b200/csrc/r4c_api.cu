@@ -156,6 +156,12 @@ bool use_stem_dw(const r4c_conv_desc* ds, int leg, const Geom& g) {
   return stem::dw_supported(g.n, g.d, g.h, g.w, g.cin, g.cout, g.k, g.pd, g.ph, g.pw);
 }
 
+// Data gradient of the one-input-channel k=3 layers: the stem dX kernel.
+bool use_stem_dx(const r4c_conv_desc* ds, int leg, const Geom& g) {
+  if (ds->force_kernel == R4C_KERNEL_GENERIC || leg != R4C_LEG_DX) return false;
+  return stem::dx_supported(g.n, g.d, g.h, g.w, g.cin, g.cout, g.k, g.pd, g.ph, g.pw);
+}
+
 bool use_tc(const r4c_conv_desc* ds, int leg, const Geom& g, tc::ConvPlan* pl) {
   if (ds->force_kernel == R4C_KERNEL_GENERIC) return false;
   if (leg == R4C_LEG_FWD)
@@ -205,7 +211,8 @@ int r4c_plan_kernel(const r4c_conv_desc* desc, int leg) {
   int st = check_desc(desc, leg, &g);
   if (st != R4C_OK) return st;
   tc::ConvPlan pl;
-  if (use_stem(desc, leg, g) || use_stem_dw(desc, leg, g) || use_tc(desc, leg, g, &pl)) return R4C_KERNEL_TC;
+  if (use_stem(desc, leg, g) || use_stem_dw(desc, leg, g) || use_stem_dx(desc, leg, g) || use_tc(desc, leg, g, &pl))
+    return R4C_KERNEL_TC;
   return R4C_KERNEL_GENERIC;
 }
 
@@ -222,6 +229,9 @@ int r4c_describe_plan(const r4c_conv_desc* desc, int leg, char* buf, size_t len)
       st = R4C_KERNEL_TC;
     } else if (use_stem_dw(desc, leg, g)) {
       stem::dw_describe(g.n, g.d, g.h, g.w, g.cin, g.cout, g.pd, g.ph, g.pw, tmp, sizeof(tmp));
+      st = R4C_KERNEL_TC;
+    } else if (use_stem_dx(desc, leg, g)) {
+      stem::dx_describe(g.n, g.d, g.h, g.w, g.cout, tmp, sizeof(tmp));
       st = R4C_KERNEL_TC;
     } else if (leg == R4C_LEG_DW && use_tc(desc, leg, g, &pl)) {
       tc::dw_describe(g.n, g.d, g.h, g.w, cin_eff(g), g.cout, g.k, g.pd, g.ph, g.pw, tmp, sizeof(tmp));
@@ -261,6 +271,7 @@ size_t r4c_packed_weight_bytes(const r4c_conv_desc* desc, int leg) {
   Geom g;
   if (check_desc(desc, leg, &g) != R4C_OK) return 0;
   if (use_stem(desc, leg, g)) return stem::packed_bytes(g.cin, g.cout);
+  if (use_stem_dx(desc, leg, g)) return stem::dx_packed_bytes();
   tc::ConvPlan pl;
   if (use_tc(desc, leg, g, &pl)) return tc::packed_bytes(pl);
   int taps = (leg == R4C_LEG_TFWD || leg == R4C_LEG_TDX) ? 8 : g.k * g.k * g.k;
@@ -300,6 +311,10 @@ int r4c_pack_weight(const r4c_conv_desc* desc, int leg, const void* w_src, int s
   if (use_stem(desc, leg, g)) {
     if ((reinterpret_cast<uintptr_t>(w_packed) & 15) != 0) return R4C_ERR_ALIGN;
     return cuda_status(stem::pack_weight(g.cin, g.cout, w_src, src_dtype, w_packed, desc->dtype, s));
+  }
+  if (use_stem_dx(desc, leg, g)) {
+    if ((reinterpret_cast<uintptr_t>(w_packed) & 15) != 0) return R4C_ERR_ALIGN;
+    return cuda_status(stem::dx_pack_weight(g.cout, w_src, src_dtype, w_packed, desc->dtype, s));
   }
   tc::ConvPlan pl;
   if (use_tc(desc, leg, g, &pl)) {
@@ -360,6 +375,8 @@ int r4c_conv3d_dx(const r4c_conv_desc* desc, const void* go, const void* w_packe
   if (g.in_vox() == 0) return R4C_OK;
   if (!go || !w_packed || !dx) return R4C_ERR_INVALID;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (use_stem_dx(desc, R4C_LEG_DX, g))
+    return stem::launch_dx(g.n, g.d, g.h, g.w, g.cout, go, w_packed, dx, desc->dtype, s);
   tc::ConvPlan pl;
   if (use_tc(desc, R4C_LEG_DX, g, &pl))
     return tc::launch_conv_tuned(pl, go, w_packed, nullptr, dx, desc->dtype, s);

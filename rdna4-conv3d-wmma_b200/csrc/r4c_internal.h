@@ -127,6 +127,14 @@ size_t dw_workspace(int n, int d, int h, int w, int cin, int cout, int pd, int p
 int dw_describe(int n, int d, int h, int w, int cin, int cout, int pd, int ph, int pw, char* buf, size_t len);
 int launch_dw(int n, int d, int h, int w, int cin, int cout, int pd, int ph, int pw, const void* x, const void* go,
               float* dw, float* db, void* ws, size_t ws_bytes, int dtype, cudaStream_t st);
+// dX of k=3, pad 1 layers with one input channel and Cout a multiple of 4 up
+// to 32 (W even, <= 256); dY and dX NDHWC, packed weight dx_packed_bytes().
+bool dx_supported(int n, int d, int h, int w, int cin, int cout, int ks, int pd, int ph, int pw);
+size_t dx_packed_bytes();
+cudaError_t dx_pack_weight(int cout, const void* w_src, int src_dtype, void* w_packed, int dtype, cudaStream_t st);
+int dx_describe(int n, int d, int h, int w, int cout, char* buf, size_t len);
+int launch_dx(int n, int d, int h, int w, int cout, const void* go, const void* w_packed, void* dx, int dtype,
+              cudaStream_t st);
 }  // namespace stem
 
 }  // namespace r4c

@@ -57,6 +57,13 @@ CONV_CASES = [
     (1, 1, 48, 6, 7, 16, 3, 1),        # Cout 48: five M tiles per unit
     (1, 1, 7, 3, 5, 8, 3, 1),          # Cout 7: scalar stores
     (1, 2, 256, 2, 3, 8, 3, 1),        # Cout 256
+    # stem dX kernel (one input channel, Cout % 4 == 0 up to 32, pad 1, even W <= 256)
+    (2, 1, 24, 11, 37, 128, 3, 1),     # two rows per stage, ragged strips and plane slabs
+    (1, 1, 8, 5, 6, 64, 3, 1),         # four rows per stage
+    (1, 1, 32, 4, 9, 256, 3, 1),       # one row of 128 pairs per stage, 4 K steps
+    (1, 1, 12, 3, 3, 6, 3, 1),         # 12 rows per stage, pairs straddle warps
+    (1, 1, 4, 2, 2, 2, 3, 1),          # one pair per row
+    (1, 1, 20, 7, 10, 150, 3, 1),      # 75 pairs: idle lanes in every stage
 ]
 TCONV_CASES = [
     (2, 16, 8, 3, 4, 5),

@@ -71,14 +71,26 @@ def test_stem_family():
         assert "stem" in _native.describe_plan(dsc, _native.LEG_FWD)
         assert _native.workspace_bytes(dsc, _native.LEG_FWD) == 0
         assert _native.packed_weight_bytes(dsc, _native.LEG_FWD) == (cout + 15) // 16 * 16 * kpad * 2
-        # dX keeps the general kernel; dW takes the stem dW kernel when Cout
-        # is a multiple of 8 and its buffers fit shared memory
-        assert "stem" not in _native.describe_plan(dsc, _native.LEG_DX)
+        # dX: the stem dX kernel for one input channel (Cout a multiple of 4
+        # up to 32, pad 1, even W <= 256), else the general kernel; dW takes
+        # the stem dW kernel when Cout is a multiple of 8 and its buffers fit
+        if cin == 1 and cout <= 32:
+            assert "stem dX" in _native.describe_plan(dsc, _native.LEG_DX)
+            assert _native.packed_weight_bytes(dsc, _native.LEG_DX) == 96 * 128
+            assert _native.workspace_bytes(dsc, _native.LEG_DX) == 0
+        else:
+            assert "stem" not in _native.describe_plan(dsc, _native.LEG_DX)
         if cout % 8 == 0 and cout <= 32:
             assert "stem dW" in _native.describe_plan(dsc, _native.LEG_DW)
             assert _native.workspace_bytes(dsc, _native.LEG_DW) > 0
     # Cout not a multiple of 8: the dW leaves the stem kernel
     assert "stem" not in _native.describe_plan(_d(cin=1, cout=7, w=32), _native.LEG_DW)
+    # stem dX scope: Cout % 4, Cout <= 32, pad 1, even W up to 256
+    assert "stem dX" in _native.describe_plan(_d(cin=1, cout=4, w=2, h=1, d=1), _native.LEG_DX)
+    assert "stem dX" in _native.describe_plan(_d(cin=1, cout=32, w=256), _native.LEG_DX)
+    for bad in (_d(cin=1, cout=6), _d(cin=1, cout=48), _d(cin=1, w=31), _d(cin=1, w=258), _d(cin=1, p=0),
+                _d(cin=1, p=2), _d(cin=1, force=1)):
+        assert "stem dX" not in _native.describe_plan(bad, _native.LEG_DX)
     # rows whose byte stride is not a multiple of 16, k=1 and 5+ channels stay
     # on the general kernel; forcing the SIMT family still works
     assert "stem" not in _native.describe_plan(_d(cin=3, w=30), _native.LEG_FWD)

@@ -776,13 +776,16 @@ __global__ void __launch_bounds__(kThreads, 1) tc_conv_kernel(const __grid_const
   // Bounded wait. `nap` > 0 makes the polling thread sleep between polls so
   // that warps which only wait leave issue slots to the MMA thread.
   auto wait = [&](uint64_t* bar, uint32_t par, uint32_t nap = 0) -> bool {
-    const uint64_t deadline = global_timer_ns() + kWaitNs;
+    uint64_t deadline = 0;  // the clock is read only once a wait has lasted a while
     uint32_t spins = 0;
     while (!mbar_try_wait(bar, par)) {
       if (nap) __nanosleep(nap);
       if (((++spins) & 63u) == 0) {
         if (*abort_flag) return false;
-        if (global_timer_ns() > deadline) {
+        const uint64_t now = global_timer_ns();
+        if (deadline == 0) {
+          deadline = now + kWaitNs;
+        } else if (now > deadline) {
           *abort_flag = 1;
           atomicExch(&g_r4c_dev_error, 1);
           return false;

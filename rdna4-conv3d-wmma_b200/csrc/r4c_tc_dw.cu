@@ -488,13 +488,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   // Bounded wait; `nap` > 0 sleeps between polls (waiting warps leave issue
   // slots to the producer and MMA threads on their sub-partitions).
   auto wait = [&](uint64_t* bar, uint32_t par, uint32_t nap = 0) -> bool {
-    uint64_t deadline = global_timer_ns() + kWaitNs;
+    uint64_t deadline = 0;  // the clock is read only once a wait has lasted a while
     uint32_t spins = 0;
     while (!mbar_try_wait(bar, par)) {
       if (nap) __nanosleep(nap);
       if (((++spins) & (nap ? 15u : 255u)) == 0) {
         if (*abort_flag) return false;
-        if (global_timer_ns() > deadline) {
+        const uint64_t now = global_timer_ns();
+        if (deadline == 0) {
+          deadline = now + kWaitNs;
+        } else if (now > deadline) {
           *abort_flag = 1;
           atomicExch(a.err, 1);
           return false;

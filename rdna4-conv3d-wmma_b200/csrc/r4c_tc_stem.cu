@@ -259,13 +259,16 @@ __global__ void __launch_bounds__(kThreads, 1) stem_fwd_kernel(const __grid_cons
   // Bounded wait; `nap` > 0 makes the polling thread sleep between polls so
   // that waiting roles leave issue slots to the working ones.
   auto wait = [&](uint64_t* bar, uint32_t par, uint32_t nap = 0) -> bool {
-    const uint64_t deadline = global_timer_ns() + kWaitNs;
+    uint64_t deadline = 0;  // the clock is read only once a wait has lasted a while
     uint32_t spins = 0;
     while (!mbar_try_wait(bar, par)) {
       if (nap) __nanosleep(nap);
       if (((++spins) & 63u) == 0) {
         if (*abort_flag) return false;
-        if (global_timer_ns() > deadline) {
+        const uint64_t now = global_timer_ns();
+        if (deadline == 0) {
+          deadline = now + kWaitNs;
+        } else if (now > deadline) {
           *abort_flag = 1;
           atomicExch(a.err, 1);
           return false;
@@ -550,13 +553,16 @@ __global__ void __launch_bounds__(kDwThreads, 1) stem_dw_kernel(const __grid_con
 
   const uint64_t kWaitNs = 1000000000ull;
   auto wait = [&](uint64_t* bar, uint32_t par, uint32_t nap = 0) -> bool {
-    const uint64_t deadline = global_timer_ns() + kWaitNs;
+    uint64_t deadline = 0;  // the clock is read only once a wait has lasted a while
     uint32_t spins = 0;
     while (!mbar_try_wait(bar, par)) {
       if (nap) __nanosleep(nap);
       if (((++spins) & 63u) == 0) {
         if (*abort_flag) return false;
-        if (global_timer_ns() > deadline) {
+        const uint64_t now = global_timer_ns();
+        if (deadline == 0) {
+          deadline = now + kWaitNs;
+        } else if (now > deadline) {
           *abort_flag = 1;
           atomicExch(a.err, 1);
           return false;

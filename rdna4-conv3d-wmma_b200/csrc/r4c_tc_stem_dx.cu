@@ -66,12 +66,16 @@ constexpr int kDxGatherWarps = 8;
 constexpr int kDxThreads = 64 + 32 * kDxGatherWarps;
 constexpr int kDxHeader = 1024;
 constexpr int kDxWBytes = 96 * 128;        // weight image: 96 B rows x 64 K elements
-constexpr int kDxStageBytes = 128 * 128;   // one M tile of 128-byte rows
-constexpr int kDxMaxStages = 12;
-constexpr int kDxTSlots = 5;               // TMEM ring: 5 x 96 columns
-constexpr int kDxTCols = 96;
-constexpr int kDxSRing = 4;                // x-sum ring (stages)
-constexpr int kDxNStg = 9;                 // max stages per plane of a unit (accumulators per plane)
+// A stage is up to two M tiles (256 rows of 128 B = 32 KB): the TMA unit's
+// throughput per SM is set by the bytes of each mbarrier transaction (~0.55 us
+// per transaction up to ~32 KB, whatever the ring depth), so 16 KB stages
+// deliver ~4.3 TB/s over 148 SMs and 32 KB stages reach HBM speed.
+constexpr int kDxStageBytes = 256 * 128;
+constexpr int kDxMaxStages = 6;
+constexpr int kDxTSlots = 2;               // TMEM ring: 2 stages x 2 tiles x 96 columns
+constexpr int kDxTCols = 96;               // columns per M tile: D-1 (16), D0 (64), D+1 (16)
+constexpr int kDxSRing = 3;                // x-sum ring (stages); a stage's outputs read it and the one before
+constexpr int kDxNStg = 8;                 // max stages per plane of a unit (accumulators per plane)
 constexpr int kDxSmemMax = 232448;
 
 struct StemDxArgs {
@@ -80,9 +84,10 @@ struct StemDxArgs {
   void* dx;
   int* err;
   int n, d, h, w;
-  int pairs, rs, lanes;  // pairs per image row, rows per stage, rs * pairs
+  int pairs, rs, lanes;  // pairs per image row, rows per stage, rs * pairs (<= 256)
+  int mt;                // M tiles per stage (lanes / 128 rounded up)
   int R, Pz, nyt, nzt, units;
-  int ksteps;            // 16-channel K steps over 2*Cout
+  int ksteps;            // 16-channel K steps over 2*Cout (the kernel's KS)
   int nstages;
   int s_slot_floats;     // one x-sum ring slot: rs * 9 * W floats
   int ring_off;          // byte offset of the x-sum ring
@@ -142,7 +147,8 @@ __device__ __forceinline__ void tmem_ld_34(uint32_t t0, uint32_t t1, uint32_t t2
 
 }  // namespace
 
-template <typename T>
+// KS: 16-channel K steps over the 2*Cout channels of a position pair.
+template <typename T, int KS>
 __global__ void __launch_bounds__(kDxThreads, 1) stem_dx_kernel(const __grid_constant__ StemDxArgs a) {
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
@@ -155,7 +161,7 @@ __global__ void __launch_bounds__(kDxThreads, 1) stem_dx_kernel(const __grid_con
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   uint8_t* wsm = smem + kDxHeader;     // weight image (1024-aligned)
   uint8_t* st0 = wsm + kDxWBytes;      // dY stages (1024-aligned); the MMA of the -1 shift reads the
-                                       // 128 bytes before a stage, the +1 shift the 128 after it
+                                       // 128 bytes before a tile, the +1 shift the 128 after it
   float* sring = reinterpret_cast<float*>(smem + a.ring_off);
 
   const int warp = threadIdx.x >> 5;
@@ -189,13 +195,16 @@ __global__ void __launch_bounds__(kDxThreads, 1) stem_dx_kernel(const __grid_con
 
   const uint64_t kWaitNs = 1000000000ull;
   auto wait = [&](uint64_t* bar, uint32_t par, uint32_t nap = 0) -> bool {
-    const uint64_t deadline = global_timer_ns() + kWaitNs;
+    uint64_t deadline = 0;  // the clock is read only once a wait has lasted a while
     uint32_t spins = 0;
     while (!mbar_try_wait(bar, par)) {
       if (nap) __nanosleep(nap);
       if (((++spins) & 63u) == 0) {
         if (*abort_flag) return false;
-        if (global_timer_ns() > deadline) {
+        const uint64_t now = global_timer_ns();
+        if (deadline == 0) {
+          deadline = now + kWaitNs;
+        } else if (now > deadline) {
           *abort_flag = 1;
           atomicExch(a.err, 1);
           return false;
@@ -255,88 +264,115 @@ __global__ void __launch_bounds__(kDxThreads, 1) stem_dx_kernel(const __grid_con
         if ((pending >> i) & 1u) mbar_wait_bounded(&full[i], (last_par >> i) & 1u, deadline);
     }
   } else if (warp == 1) {
-    // ---------------- MMA issuer: three row shifts per K step ----------------
-    if (lane == 0) {
-      bool ok = wait(wbar, 0u);
-      const uint32_t wa = smem_u32(wsm);
+    // ---------------- MMA issuer: per M tile, three row shifts per K step ----------------
+    // The whole warp runs the loop (descriptors stay warp-uniform) and the
+    // elected lane issues: ~45 clk per MMA against ~70 from a lane-0 branch.
+    {
+      int ok0 = 1;
+      if (lane == 0) ok0 = wait(wbar, 0u) ? 1 : 0;
+      bool ok = __shfl_sync(0xffffffffu, ok0, 0) != 0;
+      // descriptors: the weight blocks are fixed; a tile's A descriptor moves
+      // by whole 128-byte rows (+-8 in 16-byte units) and 32-byte K steps
+      const uint64_t wd = sw128_desc(smem_u32(wsm));
+      uint64_t bd[3][KS];
+#pragma unroll
+      for (int kk = 0; kk < KS; ++kk) {
+        bd[0][kk] = wd + (uint64_t)(2 * kk);
+        bd[1][kk] = wd + (uint64_t)(2048 / 16 + 2 * kk);
+        bd[2][kk] = wd + (uint64_t)(10240 / 16 + 2 * kk);
+      }
+      const uint32_t i16 = a.idesc16, i64 = a.idesc64;
       int s = 0, ts = 0;
       uint32_t fpar = 0u, tbits = (1u << kDxTSlots) - 1u;
       for (int u = blockIdx.x; u < a.units && ok; u += gridDim.x) {
         int nb, z0, y0, pz, re;
         unit_of(u, nb, z0, y0, pz, re);
-        const int ns = (re + 2 + a.rs - 1) / a.rs;
-        for (int p = 0; p < pz + 2 && ok; ++p) {
-          for (int k = 0; k < ns; ++k) {
-            if (!wait(&full[s], fpar) || !wait(&tempty[ts], (tbits >> ts) & 1u)) {
-              ok = false;
-              break;
-            }
-            tbits ^= 1u << ts;
-            tc_fence_after();
-            const uint32_t sa = smem_u32(st0 + (size_t)s * kDxStageBytes);
-            const uint32_t d0 = tmem + (uint32_t)(ts * kDxTCols);
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-              if (kk < a.ksteps) {
-                const uint32_t acc = kk ? 1u : 0u;
-                const uint32_t ko = 32u * kk;  // 16 channels = 32 bytes of a swizzled row
-                mma_f16_ss(d0, sw128_desc(sa - 128u + ko), sw128_desc(wa + ko), a.idesc16, acc);
-                mma_f16_ss(d0 + 16u, sw128_desc(sa + ko), sw128_desc(wa + 2048u + ko), a.idesc64, acc);
-                mma_f16_ss(d0 + 80u, sw128_desc(sa + 128u + ko), sw128_desc(wa + 10240u + ko), a.idesc16, acc);
-              }
-            }
-            mma_commit(&empty[s]);
-            mma_commit(&tfull[ts]);
-            if (++s == a.nstages) {
-              s = 0;
-              fpar ^= 1u;
-            }
-            if (++ts == kDxTSlots) ts = 0;
+        const int nst = (pz + 2) * ((re + 2 + a.rs - 1) / a.rs);
+        for (int t = 0; t < nst; ++t) {
+          int okk = 1;
+          if (lane == 0) okk = (wait(&full[s], fpar) && wait(&tempty[ts], (tbits >> ts) & 1u)) ? 1 : 0;
+          if (!__shfl_sync(0xffffffffu, okk, 0)) {
+            ok = false;
+            break;
           }
+          tbits ^= 1u << ts;
+          tc_fence_after();
+          const uint64_t ad0 = sw128_desc(smem_u32(st0 + (size_t)s * kDxStageBytes));
+          for (int mi = 0; mi < a.mt; ++mi) {
+            const uint64_t ad = ad0 + (uint64_t)(mi * 1024);  // 128 rows of 128 B
+            const uint32_t d0 = tmem + (uint32_t)((ts * 2 + mi) * kDxTCols);
+#pragma unroll
+            for (int kk = 0; kk < KS; ++kk) {
+              const uint32_t acc = kk ? 1u : 0u;
+              mma_f16_ss_warp(d0, ad - 8u + (uint64_t)(2 * kk), bd[0][kk], i16, acc);
+              mma_f16_ss_warp(d0 + 16u, ad + (uint64_t)(2 * kk), bd[1][kk], i64, acc);
+              mma_f16_ss_warp(d0 + 80u, ad + (uint64_t)(8 + 2 * kk), bd[2][kk], i16, acc);
+            }
+          }
+          mma_commit_warp(&empty[s]);
+          mma_commit_warp(&tfull[ts]);
+          if (++s == a.nstages) {
+            s = 0;
+            fpar ^= 1u;
+          }
+          ts ^= 1;
         }
       }
       // every MMA of this CTA completes before TMEM is released
-      mma_commit(mdone);
-      mbar_wait_bounded(mdone, 0u, global_timer_ns() + kWaitNs);
+      mma_commit_warp(mdone);
+      if (lane == 0) mbar_wait_bounded(mdone, 0u, global_timer_ns() + kWaitNs);
+      __syncwarp();
     }
   } else {
     // ---------------- gather warps 2..9 ----------------
     const int gt = threadIdx.x - 64;
-    const int q = warp & 3;          // TMEM lane quarter this warp may read
+    const int q = warp & 3;            // TMEM lane quarter this warp may read
     const int hsel = (warp - 2) >> 2;  // 0: even outputs, 1: odd outputs
-    const int la = q * 32 + lane;    // TMEM lane = pair of the stage
-    const bool va = la < a.lanes;
-    const int ra = va ? la / a.pairs : 0;
-    const int pja = va ? la - ra * a.pairs : 0;
-    // the neighbour pair's term lies inside the image row (else x = -1 or W: zero)
-    const bool nbr = hsel == 0 ? (pja > 0) : (pja < a.pairs - 1);
     const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
     const uint32_t c0 = hsel == 0 ? 0u : 80u;   // D-1 / D+1
     const uint32_t c1 = hsel == 0 ? 16u : 48u;  // D0 columns 0..15 / 32..47
     const uint32_t c2 = hsel == 0 ? 32u : 64u;  // D0 columns 16..17 / 48..49
-    const int wa_idx = (ra * 18 + hsel) * a.pairs + pja;  // ring index of (row, i = 0, parity, pair)
     const int istep = 2 * a.pairs;
-    // output role: column x of row rb of each stage
-    const int pjb = gt % a.pairs;
-    const int ub = gt / a.pairs;
-    const int parb = ub & 1;
-    const int rb = ub >> 1;
-    const bool vb = rb < a.rs;
-    const int xb = 2 * pjb + parb;
-    int soff[3], rowoff[3];
+    // x-sum role, per M tile of the stage: pair b of the stage (TMEM lane)
+    bool va[2], nbr[2];
+    int wa_idx[2];
 #pragma unroll
-    for (int kh = 0; kh < 3; ++kh) {
-      // dY row of tap kh: stage offset and row within the stage (floor division)
-      const int dr = rb - kh;
-      const int so = dr >= 0 ? dr / a.rs : -((-dr + a.rs - 1) / a.rs);
-      soff[kh] = so;
-      rowoff[kh] = (((dr - so * a.rs) * 9 + kh) * 2 + parb) * a.pairs + pjb;
+    for (int mi = 0; mi < 2; ++mi) {
+      const int b = mi * 128 + q * 32 + lane;
+      va[mi] = b < a.lanes;
+      const int ra = va[mi] ? b / a.pairs : 0;
+      const int pja = va[mi] ? b - ra * a.pairs : 0;
+      // the neighbour pair's term lies inside the image row (else x = -1 or W: zero)
+      nbr[mi] = hsel == 0 ? (pja > 0) : (pja < a.pairs - 1);
+      wa_idx[mi] = (ra * 18 + hsel) * a.pairs + pja;  // ring index of (row, i = 0, parity, pair)
+    }
+    // output role: outputs gt and gt + 256 of each stage, (row, parity, pair) with the pair fastest
+    bool vb[2];
+    int rbo[2], xb[2], soff[2][3], rowoff[2][3];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int o = gt + 256 * j;
+      const int pjb = o % a.pairs;
+      const int ub = o / a.pairs;
+      const int parb = ub & 1;
+      const int rb = ub >> 1;
+      vb[j] = rb < a.rs;
+      rbo[j] = rb;
+      xb[j] = 2 * pjb + parb;
+#pragma unroll
+      for (int kh = 0; kh < 3; ++kh) {
+        // dY row of tap kh: this stage (0) or the one before (-1; rs >= 2), and its row there
+        const int dr = rb - kh;
+        const int so = dr >= 0 ? 0 : -1;
+        soff[j][kh] = so;
+        rowoff[j][kh] = (((dr - so * a.rs) * 9 + kh) * 2 + parb) * a.pairs + pjb;
+      }
     }
     const int kdstep = 3 * istep;
     T* dxp = static_cast<T*>(a.dx);
 
-    float acc[3][kDxNStg];
-    int g = 0, ts = 0;
+    float acc[3][kDxNStg][2];
+    int ts = 0, cur = 0;  // TMEM stage slot, x-sum ring slot of the current stage
     uint32_t tbits = 0u;
     bool bad = false;
     for (int u = blockIdx.x; u < a.units; u += gridDim.x) {
@@ -344,63 +380,80 @@ __global__ void __launch_bounds__(kDxThreads, 1) stem_dx_kernel(const __grid_con
       unit_of(u, nb, z0, y0, pz, re);
       const int ns = (re + 2 + a.rs - 1) / a.rs;
 #pragma unroll
-      for (int k = 0; k < kDxNStg; ++k) acc[0][k] = acc[1][k] = acc[2][k] = 0.f;
+      for (int k = 0; k < kDxNStg; ++k)
+#pragma unroll
+        for (int j = 0; j < 2; ++j) acc[0][k][j] = acc[1][k][j] = acc[2][k][j] = 0.f;
       for (int p = 0; p < pz + 2; ++p) {
 #pragma unroll
         for (int k = 0; k < kDxNStg; ++k) {
           if (k < ns) {
-            int got = 1;
-            if (lane == 0) got = wait(&tfull[ts], (tbits >> ts) & 1u, 32) ? 1 : 0;
-            got = __shfl_sync(0xffffffffu, got, 0);
+            // every lane polls; the vote keeps the warp's TMEM loads uniform
+            const int got = __all_sync(0xffffffffu, wait(&tfull[ts], (tbits >> ts) & 1u)) ? 1 : 0;
             tbits ^= 1u << ts;
             if (got) {
               tc_fence_after();
-              float v[34];
-              const uint32_t tb = lane_base + (uint32_t)(ts * kDxTCols);
-              tmem_ld_34(tb + c0, tb + c1, tb + c2, v);
+              float* sl = sring + cur * a.s_slot_floats;
+#pragma unroll
+              for (int mi = 0; mi < 2; ++mi) {
+                if (mi >= a.mt) break;
+                float v[34];
+                const uint32_t tb = lane_base + (uint32_t)((ts * 2 + mi) * kDxTCols);
+                tmem_ld_34(tb + c0, tb + c1, tb + c2, v);
+                if (va[mi]) {
+                  float* sw = sl + wa_idx[mi];
+#pragma unroll
+                  for (int i = 0; i < 9; ++i) sw[i * istep] = v[16 + i] + v[25 + i] + (nbr[mi] ? v[i] : 0.f);
+                }
+              }
               tc_fence_before();
               __syncwarp();
               if (lane == 0) mbar_arrive(&tempty[ts]);
-              if (va) {
-                float* sw = sring + (g & (kDxSRing - 1)) * a.s_slot_floats + wa_idx;
-#pragma unroll
-                for (int i = 0; i < 9; ++i) sw[i * istep] = v[16 + i] + v[25 + i] + (nbr ? v[i] : 0.f);
-              }
             }
             if (gather_bar_or(!got)) {
               bad = true;
               break;
             }
-            const int so_ = a.rs * k - 1 + rb;  // output row of the strip (1..re) this stage completes
-            if (vb && so_ >= 1 && so_ <= re) {
+            const int prev = cur == 0 ? kDxSRing - 1 : cur - 1;
 #pragma unroll
-              for (int kh = 0; kh < 3; ++kh) {
-                const float* sr = sring + ((g + soff[kh]) & (kDxSRing - 1)) * a.s_slot_floats + rowoff[kh];
+            for (int j = 0; j < 2; ++j) {
+              const int so_ = a.rs * k - 1 + rbo[j];  // output row of the strip (1..re) this stage completes
+              if (vb[j] && so_ >= 1 && so_ <= re) {
 #pragma unroll
-                for (int kd = 0; kd < 3; ++kd) acc[kd][k] += sr[kd * kdstep];
+                for (int kh = 0; kh < 3; ++kh) {
+                  const float* sr = sring + (soff[j][kh] ? prev : cur) * a.s_slot_floats + rowoff[j][kh];
+#pragma unroll
+                  for (int kd = 0; kd < 3; ++kd) acc[kd][k][j] += sr[kd * kdstep];
+                }
               }
             }
-            ++g;
-            if (++ts == kDxTSlots) ts = 0;
+            cur = cur == kDxSRing - 1 ? 0 : cur + 1;
+            ts ^= 1;
           }
         }
         if (bad) break;
         // output plane p-2 of the unit has had its last dY plane
         const int o = p - 2;
-        if (vb && o >= 0 && o < pz) {
-          const long long rowbase = ((long long)(nb * a.d + z0 + o) * a.h + (y0 - 1)) * a.w + xb;
+        if (o >= 0 && o < pz) {
 #pragma unroll
-          for (int k = 0; k < kDxNStg; ++k) {
-            const int so_ = a.rs * k - 1 + rb;
-            if (k < ns && so_ >= 1 && so_ <= re) dxp[rowbase + (long long)so_ * a.w] = Elem<T>::from_f(acc[0][k]);
+          for (int j = 0; j < 2; ++j) {
+            if (!vb[j]) continue;
+            const long long rowbase = ((long long)(nb * a.d + z0 + o) * a.h + (y0 - 1)) * a.w + xb[j];
+#pragma unroll
+            for (int k = 0; k < kDxNStg; ++k) {
+              const int so_ = a.rs * k - 1 + rbo[j];
+              if (k < ns && so_ >= 1 && so_ <= re)
+                dxp[rowbase + (long long)so_ * a.w] = Elem<T>::from_f(acc[0][k][j]);
+            }
           }
         }
 #pragma unroll
-        for (int k = 0; k < kDxNStg; ++k) {
-          acc[0][k] = acc[1][k];
-          acc[1][k] = acc[2][k];
-          acc[2][k] = 0.f;
-        }
+        for (int k = 0; k < kDxNStg; ++k)
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            acc[0][k][j] = acc[1][k][j];
+            acc[1][k][j] = acc[2][k][j];
+            acc[2][k][j] = 0.f;
+          }
       }
       if (bad) break;
     }
@@ -450,41 +503,53 @@ int dx_num_sms() {
 }
 
 struct DxPlan {
-  int pairs, rs, lanes, R, Pz, nyt, nzt, ns, nstages, slot_floats, ring_off, smem;
+  int pairs, rs, lanes, mt, R, Pz, nyt, nzt, ns, nstages, slot_floats, ring_off, smem;
   long long units;
 };
 
-// Stage = rs whole image rows (rs * W/2 <= 128 pairs); strip = up to
-// rs * 9 - 2 output rows (9 stages per plane); planes per unit chosen to
-// minimise the busiest CTA's stage count (units per CTA x stages per unit).
+// Stage = rs whole image rows with rs * W/2 <= 256 pairs (up to two M tiles)
+// and rs >= 2, so an output row's three dY rows lie in its stage and the one
+// before. Strip height R (ns = ceil((R+2)/rs) <= kDxNStg stages per plane)
+// and planes per unit Pz minimise the busiest CTA's stage count, then the
+// total.
 bool make_dx_plan(int n, int d, int h, int w, int sms, DxPlan* out) {
   DxPlan p{};
   p.pairs = w / 2;
-  p.rs = std::max(1, std::min(128 / p.pairs, h + 2));
+  p.rs = std::min(256 / p.pairs, h + 2);
+  if (p.rs < 2) return false;
   p.lanes = p.rs * p.pairs;
-  p.R = std::max(1, std::min(h, p.rs * kDxNStg - 2));
-  p.nyt = (h + p.R - 1) / p.R;
-  p.ns = (p.R + 2 + p.rs - 1) / p.rs;
-  if (p.ns > kDxNStg) return false;
-  long long best = -1;
-  for (int pz = 1; pz <= std::min(d, 64); ++pz) {
-    const long long nzt = (d + pz - 1) / pz;
-    const long long units = (long long)n * nzt * p.nyt;
-    const long long grid = std::min<long long>(units, sms);
-    const long long cost = (units + grid - 1) / grid * (long long)(pz + 2) * p.ns;
-    if (best < 0 || cost < best || (cost == best && pz > p.Pz)) {
-      best = cost;
-      p.Pz = pz;
+  p.mt = (p.lanes + 127) / 128;
+  long long best = -1, best_total = 0;
+  for (int ns = 1; ns <= kDxNStg; ++ns) {
+    const int R = std::min(h, p.rs * ns - 2);
+    if (R < 1 || (ns > 1 && R <= p.rs * (ns - 1) - 2)) continue;  // no taller strip than ns - 1 stages give
+    const long long nyt = (h + R - 1) / R;
+    for (int pz = 1; pz <= std::min(d, 64); ++pz) {
+      const long long nzt = (d + pz - 1) / pz;
+      const long long units = (long long)n * nzt * nyt;
+      const long long grid = std::min<long long>(units, sms);
+      const long long cost = (units + grid - 1) / grid * (long long)(pz + 2) * ns;
+      const long long total = units * (pz + 2) * ns;
+      if (best < 0 || cost < best || (cost == best && total < best_total)) {
+        best = cost;
+        best_total = total;
+        p.R = R;
+        p.Pz = pz;
+        p.ns = ns;
+      }
     }
   }
+  if (best < 0) return false;
+  p.nyt = (h + p.R - 1) / p.R;
   p.nzt = (d + p.Pz - 1) / p.Pz;
   p.units = (long long)n * p.nzt * p.nyt;
   if (p.units >= (1ll << 31)) return false;
   p.slot_floats = p.rs * 9 * w;
   const int ring_bytes = kDxSRing * p.slot_floats * 4;
+  // + 1024: the +1 row shift of a stage's last tile reads 128 bytes past it
   const int fixed = kDxHeader + kDxWBytes + 1024 + ring_bytes;
   p.nstages = std::min(kDxMaxStages, (kDxSmemMax - fixed) / kDxStageBytes);
-  if (p.nstages < 3) return false;
+  if (p.nstages < 2) return false;
   p.ring_off = kDxHeader + kDxWBytes + p.nstages * kDxStageBytes + 1024;
   p.smem = p.ring_off + ring_bytes;
   *out = p;
@@ -527,7 +592,7 @@ __global__ void pack_stem_dx_kernel(const void* __restrict__ src, int sdt, TO* _
   *reinterpret_cast<TO*>(reinterpret_cast<uint8_t*>(dst) + off) = Elem<TO>::from_f(v);
 }
 
-template <typename T>
+template <typename T, int KS>
 cudaError_t dx_launch_typed(const StemDxArgs& a, int grid, int smem, cudaStream_t st) {
   static bool done[64] = {false};
   static std::mutex mu;
@@ -537,12 +602,12 @@ cudaError_t dx_launch_typed(const StemDxArgs& a, int grid, int smem, cudaStream_
   {
     std::lock_guard<std::mutex> lk(mu);
     if (dev >= 0 && dev < 64 && !done[dev]) {
-      e = cudaFuncSetAttribute(stem_dx_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, kDxSmemMax);
+      e = cudaFuncSetAttribute(stem_dx_kernel<T, KS>, cudaFuncAttributeMaxDynamicSharedMemorySize, kDxSmemMax);
       if (e != cudaSuccess) return e;
       done[dev] = true;
     }
   }
-  stem_dx_kernel<T><<<grid, kDxThreads, smem, st>>>(a);
+  stem_dx_kernel<T, KS><<<grid, kDxThreads, smem, st>>>(a);
   return cudaGetLastError();
 }
 
@@ -564,8 +629,8 @@ int dx_describe(int n, int d, int h, int w, int cout, char* buf, size_t len) {
   if (!make_dx_plan(n, d, h, w, 148, &p)) return snprintf(buf, len, "stem dX: no plan");
   return snprintf(buf, len,
                   "tcgen05 stem dX (Z = dY.W^T per position pair, 27-point gather in smem): cout=%d pairs/row=%d "
-                  "rows/stage=%d strip=%d planes/unit=%d stages/plane=%d ring=%d smem=%dB units=%lld",
-                  cout, p.pairs, p.rs, p.R, p.Pz, p.ns, p.nstages, p.smem, p.units);
+                  "rows/stage=%d mtiles/stage=%d strip=%d planes/unit=%d stages/plane=%d ring=%d smem=%dB units=%lld",
+                  cout, p.pairs, p.rs, p.mt, p.R, p.Pz, p.ns, p.nstages, p.smem, p.units);
 }
 
 cudaError_t dx_pack_weight(int cout, const void* w_src, int src_dtype, void* w_packed, int dtype, cudaStream_t st) {
@@ -604,7 +669,7 @@ int launch_dx(int n, int d, int h, int w, int cout, const void* go, const void* 
   a.err = tc::device_error_flag();
   if (!a.err) return R4C_ERR_CUDA;
   a.n = n; a.d = d; a.h = h; a.w = w;
-  a.pairs = p.pairs; a.rs = p.rs; a.lanes = p.lanes;
+  a.pairs = p.pairs; a.rs = p.rs; a.lanes = p.lanes; a.mt = p.mt;
   a.R = p.R; a.Pz = p.Pz; a.nyt = p.nyt; a.nzt = p.nzt; a.units = (int)p.units;
   a.ksteps = (2 * cout + 15) / 16;
   a.nstages = p.nstages;
@@ -613,8 +678,14 @@ int launch_dx(int n, int d, int h, int w, int cout, const void* go, const void* 
   a.idesc16 = instr_desc_f16(dtype == R4C_BF16, 128, 16, 0, 0);
   a.idesc64 = instr_desc_f16(dtype == R4C_BF16, 128, 64, 0, 0);
   const int grid = (int)std::min<long long>(p.units, dx_num_sms());
-  const cudaError_t ce = dtype == R4C_BF16 ? dx_launch_typed<__nv_bfloat16>(a, grid, p.smem, st)
-                                           : dx_launch_typed<__half>(a, grid, p.smem, st);
+  const bool bf = dtype == R4C_BF16;
+  cudaError_t ce;
+  switch (a.ksteps) {
+    case 1: ce = bf ? dx_launch_typed<__nv_bfloat16, 1>(a, grid, p.smem, st) : dx_launch_typed<__half, 1>(a, grid, p.smem, st); break;
+    case 2: ce = bf ? dx_launch_typed<__nv_bfloat16, 2>(a, grid, p.smem, st) : dx_launch_typed<__half, 2>(a, grid, p.smem, st); break;
+    case 3: ce = bf ? dx_launch_typed<__nv_bfloat16, 3>(a, grid, p.smem, st) : dx_launch_typed<__half, 3>(a, grid, p.smem, st); break;
+    default: ce = bf ? dx_launch_typed<__nv_bfloat16, 4>(a, grid, p.smem, st) : dx_launch_typed<__half, 4>(a, grid, p.smem, st); break;
+  }
   note_launches(1);
   return ce == cudaSuccess ? R4C_OK : R4C_ERR_CUDA;
 }

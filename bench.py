@@ -41,6 +41,13 @@ TRUNK = [
     ("k1 96->48", 96, 48, (32, 64, 64), 1),
     ("k1 192->96", 192, 96, (16, 32, 32), 1),
 ]
+# ConvTranspose3d k=2 s=2 p=0 (name, cin, cout, input (D, H, W));
+# timed after the trunk, reported beside it, not part of `value`
+TCONV = [
+    ("T k2s2 192->96", 192, 96, (8, 16, 16)),
+    ("T k2s2 96->48", 96, 48, (16, 32, 32)),
+    ("T k2s2 48->24", 48, 24, (32, 64, 64)),
+]
 BATCH = 4
 METRIC = "conv TFLOP/s (fwd/dW/dX) vs bf16 peak; UNet3D ms/sample at 1/2/4/8 B200"
 
@@ -58,6 +65,15 @@ def layer_bytes(cin, cout, spatial, k, batch=BATCH, leg="fwd"):
     if leg == "dw":
         return 2 * v * (cin + cout) + 4 * wbytes
     return 2 * v * (cin + cout) + 2 * wbytes
+
+
+def tconv_bytes(cin, cout, spatial, leg, batch=BATCH):
+    """Minimum HBM bytes of one k2s2 transpose-conv leg (bf16, fp32 dW)."""
+    d, h, w = spatial
+    v = batch * d * h * w
+    if leg == "dw":
+        return 2 * v * cin + 2 * 8 * v * cout + 4 * 8 * cin * cout
+    return 2 * v * cin + 2 * 8 * v * cout + 2 * 8 * cin * cout
 
 
 def load_peaks():
@@ -289,6 +305,69 @@ def run_step(layers, reducer, ev=None, legs=("fwd", "dw", "dx")):
     return outs
 
 
+class TLayer:
+    def __init__(self, spec, device, seed):
+        import torch.nn as nn
+        self.name, self.cin, self.cout, self.spatial = spec
+        d, h, w = self.spatial
+        g = torch.Generator(device=device).manual_seed(seed)
+        cl = torch.channels_last_3d
+        self.x = torch.randn(BATCH, self.cin, d, h, w, device=device, generator=g).to(
+            torch.bfloat16).contiguous(memory_format=cl)
+        self.go = torch.randn(BATCH, self.cout, 2 * d, 2 * h, 2 * w, device=device, generator=g).to(
+            torch.bfloat16).contiguous(memory_format=cl)
+        conv = nn.ConvTranspose3d(self.cin, self.cout, 2, stride=2)
+        self.w = conv.weight.detach().to(device=device, dtype=torch.bfloat16)
+        self.b = conv.bias.detach().to(device=device, dtype=torch.bfloat16)
+        self.flops = 2.0 * BATCH * d * h * w * self.cin * self.cout * 8
+
+
+def time_tconv(device, steps, warmup, peaks):
+    """fwd / dX / dW(+db) of BASELINE configs[2] through the package's launch
+    path, CUDA events per leg; per leg: us, TFLOP/s and HBM GB/s of the
+    minimum bytes against the measured copy bandwidth."""
+    cw = sys.modules["rdna4_conv3d.conv3d_wmma"]
+    layers = [TLayer(spec, device, seed=500 + i) for i, spec in enumerate(TCONV)]
+
+    def step(evs=None):
+        for i, L in enumerate(layers):
+            if evs is not None:
+                evs[i][0].record()
+            cw.transpose_k2s2_fwd(L.x, L.w, L.b)
+            if evs is not None:
+                evs[i][1].record()
+            cw.transpose_k2s2_dx(L.x.shape, L.w, L.go)
+            if evs is not None:
+                evs[i][2].record()
+            cw.transpose_k2s2_dw(L.x, L.w.shape, L.go, True)
+            if evs is not None:
+                evs[i][3].record()
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    evs = [[[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in layers] for _ in range(steps)]
+    for s_ in range(steps):
+        step(evs[s_])
+    torch.cuda.synchronize()
+    from rdna4_conv3d import _native
+    rows = []
+    for i, L in enumerate(layers):
+        desc = _native.make_desc(BATCH, *L.spatial, L.cin, L.cout, 2, (0, 0, 0), torch.bfloat16, 0)
+        row = {"layer": L.name, "gflop_per_leg": round(L.flops / 1e9, 3)}
+        for j, (leg, code) in enumerate((("fwd", _native.LEG_TFWD), ("dx", _native.LEG_TDX),
+                                         ("dw", _native.LEG_TDW))):
+            ms = sum(ev[i][j].elapsed_time(ev[i][j + 1]) for ev in evs) / steps
+            gbs = tconv_bytes(L.cin, L.cout, L.spatial, leg) / (ms / 1e3) / 1e9
+            row[leg + "_us"] = round(ms * 1e3, 2)
+            row[leg + "_tflops"] = round(L.flops / (ms / 1e3) / 1e12, 2)
+            row[leg + "_hbm_gbs"] = round(gbs, 1)
+            row[leg + "_hbm_frac"] = round(gbs / peaks["hbm_gbs"], 4)
+            row[leg + "_kernel"] = "tcgen05" if _native.plan_kernel(desc, code) == _native.KERNEL_TC else "simt"
+        rows.append(row)
+    return rows
+
+
 def run_e2e(layers, host, steps, warmup, world):
     """Public-API legs with inputs copied from pinned host memory and results
     read back every step (wmma_fwd / wmma_dw / wmma_dx)."""
@@ -340,6 +419,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-tconv", action="store_true", help="skip the ConvTranspose3d k2s2 legs (configs[2])")
     ap.add_argument("--only", default=None, help="run one trunk layer, e.g. 'k3 24->24' (profiling)")
     ap.add_argument("--legs", default="fwd,dw,dx", help="comma list of legs to run (profiling)")
     args = ap.parse_args()
@@ -448,6 +528,10 @@ def main():
                "path": "public API wmma_fwd/wmma_dw/wmma_dx, pinned host inputs copied in and results copied "
                        "back inside the timed region"}
 
+    tconv = None
+    if args.only is None and len(legs) == 3 and not args.no_tconv:
+        tconv = time_tconv(dev, min(args.steps, 5), 2, peaks)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and args.only is None:
         cpu = cpu_baseline(TRUNK)
@@ -466,6 +550,10 @@ def main():
             "gflop_per_step_per_gpu": round(step_flops / 1e9, 2),
             "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": int(launches),
             "clocks": clocks, "host_issue_ms_per_step": round(host_ms, 3), "layers": breakdown,
+            "tconv_layers": tconv,
+            "tconv_note": "BASELINE configs[2] (ConvTranspose3d k2s2, batch 4, bf16), timed after the trunk "
+                          "with CUDA events per leg; not part of value; hbm_frac against the measured copy "
+                          "bandwidth for the minimum bytes of each leg",
         }
         print(json.dumps(line), flush=True)
     if world > 1:

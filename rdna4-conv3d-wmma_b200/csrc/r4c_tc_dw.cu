@@ -174,6 +174,26 @@ static bool plan_dw(int n, int d, int h, int w, int cin, int cout, int ks, int p
   const bool wide_auto = wide_force == -1 && ((cw_ok == 64 && cin >= 64) || (ks == 1 && cin >= 16));
   const bool chunk_allowed = !((wide_force == 1 && cin >= 16) || wide_auto);
 
+  // Splits of the output rows: one CTA per (task, split) at one CTA per SM,
+  // so the cost is waves x rows per split; the split counts that fill whole
+  // waves (1..4) are compared (rounding S up from 2 * SMs / tasks can add a
+  // nearly empty third wave).
+  auto pick_split = [&](long long rows, int ntasks, double per_row, int* S_out, long long* rps_out) {
+    double bc = 1e300;
+    for (int k = 1; k <= 4; ++k) {
+      int S = (int)std::max<long long>(1, std::min<long long>(rows, (long long)k * sms / ntasks));
+      const long long rps = (rows + S - 1) / S;
+      S = (int)((rows + rps - 1) / rps);
+      const long long waves = ((long long)ntasks * S + sms - 1) / sms;
+      const double c = waves * (rps * per_row + 3000.0);
+      if (c < bc) {
+        bc = c;
+        *S_out = S;
+        *rps_out = rps;
+      }
+    }
+    return bc;
+  };
   // Task shape: largest N split and M-tile group that fits TMEM (512 cols)
   // with all kw in one task when possible.
   double best = 1e300;
@@ -212,13 +232,9 @@ static bool plan_dw(int n, int d, int h, int w, int cin, int cout, int ks, int p
           double mma = (double)(kpad_c / 16) * kwn * mtn * t_mma;
           double load = (double)(nch * k2 * pitch_c * 16 + g_bytes) / 48.0;
           double per_row = std::max(mma, load) + 60.0;
-          // split so that tasks * S ~ a few waves
-          int S = (int)std::max<long long>(1, std::min<long long>(rows_c, (2LL * sms + ntasks - 1) / ntasks));
-          long long rps = (rows_c + S - 1) / S;
-          S = (int)((rows_c + rps - 1) / rps);
-          long long ctas = (long long)ntasks * S;
-          long long waves = (ctas + sms - 1) / sms;
-          double est = waves * (rps * per_row + 3000.0);
+          int S = 1;
+          long long rps = rows_c;
+          const double est = pick_split(rows_c, ntasks, per_row, &S, &rps);
           if (est < best) {
             best = est;
             P.wide = false;
@@ -283,12 +299,9 @@ static bool plan_dw(int n, int d, int h, int w, int cin, int cout, int ks, int p
           const double bytes = (double)k2 * plane + (double)nbox * cwb * kpad_w * 2;
           const double load = std::max(bytes / 48.0, rows * 2.2);
           const double per_row = std::max(std::max(mma, load) + 60.0, (kTmaLatencyClk + mma) / stages);
-          int S = (int)std::max<long long>(1, std::min<long long>(rows_w, (2LL * sms + ntasks - 1) / ntasks));
-          const long long rps = (rows_w + S - 1) / S;
-          S = (int)((rows_w + rps - 1) / rps);
-          const long long ctas = (long long)ntasks * S;
-          const long long waves = (ctas + sms - 1) / sms;
-          const double est = waves * (rps * per_row + 3000.0);
+          int S = 1;
+          long long rps = rows_w;
+          const double est = pick_split(rows_w, ntasks, per_row, &S, &rps);
           if (est < best) {
             best = est;
             P.wide = true;

@@ -162,6 +162,12 @@ bool use_stem_dx(const r4c_conv_desc* ds, int leg, const Geom& g) {
   return stem::dx_supported(g.n, g.d, g.h, g.w, g.cin, g.cout, g.k, g.pd, g.ph, g.pw);
 }
 
+// ConvTranspose3d k2s2 forward / dX: the tcgen05 transpose-conv kernel.
+bool use_tc_tconv(const r4c_conv_desc* ds, int leg, const Geom& g) {
+  if (ds->force_kernel == R4C_KERNEL_GENERIC || (leg != R4C_LEG_TFWD && leg != R4C_LEG_TDX)) return false;
+  return tconv::supported(leg == R4C_LEG_TFWD ? 0 : 1, g.n, g.d, g.h, g.w, g.cin, g.cout);
+}
+
 bool use_tc(const r4c_conv_desc* ds, int leg, const Geom& g, tc::ConvPlan* pl) {
   if (ds->force_kernel == R4C_KERNEL_GENERIC) return false;
   if (leg == R4C_LEG_FWD)
@@ -211,7 +217,8 @@ int r4c_plan_kernel(const r4c_conv_desc* desc, int leg) {
   int st = check_desc(desc, leg, &g);
   if (st != R4C_OK) return st;
   tc::ConvPlan pl;
-  if (use_stem(desc, leg, g) || use_stem_dw(desc, leg, g) || use_stem_dx(desc, leg, g) || use_tc(desc, leg, g, &pl))
+  if (use_stem(desc, leg, g) || use_stem_dw(desc, leg, g) || use_stem_dx(desc, leg, g) ||
+      use_tc_tconv(desc, leg, g) || use_tc(desc, leg, g, &pl))
     return R4C_KERNEL_TC;
   return R4C_KERNEL_GENERIC;
 }
@@ -232,6 +239,9 @@ int r4c_describe_plan(const r4c_conv_desc* desc, int leg, char* buf, size_t len)
       st = R4C_KERNEL_TC;
     } else if (use_stem_dx(desc, leg, g)) {
       stem::dx_describe(g.n, g.d, g.h, g.w, g.cout, tmp, sizeof(tmp));
+      st = R4C_KERNEL_TC;
+    } else if (use_tc_tconv(desc, leg, g)) {
+      tconv::describe(leg == R4C_LEG_TFWD ? 0 : 1, g.n, g.d, g.h, g.w, g.cin, g.cout, tmp, sizeof(tmp));
       st = R4C_KERNEL_TC;
     } else if (leg == R4C_LEG_DW && use_tc(desc, leg, g, &pl)) {
       tc::dw_describe(g.n, g.d, g.h, g.w, cin_eff(g), g.cout, g.k, g.pd, g.ph, g.pw, tmp, sizeof(tmp));
@@ -272,6 +282,8 @@ size_t r4c_packed_weight_bytes(const r4c_conv_desc* desc, int leg) {
   if (check_desc(desc, leg, &g) != R4C_OK) return 0;
   if (use_stem(desc, leg, g)) return stem::packed_bytes(g.cin, g.cout);
   if (use_stem_dx(desc, leg, g)) return stem::dx_packed_bytes();
+  if (use_tc_tconv(desc, leg, g))
+    return tconv::packed_bytes(leg == R4C_LEG_TFWD ? 0 : 1, g.n, g.d, g.h, g.w, g.cin, g.cout);
   tc::ConvPlan pl;
   if (use_tc(desc, leg, g, &pl)) return tc::packed_bytes(pl);
   int taps = (leg == R4C_LEG_TFWD || leg == R4C_LEG_TDX) ? 8 : g.k * g.k * g.k;
@@ -315,6 +327,11 @@ int r4c_pack_weight(const r4c_conv_desc* desc, int leg, const void* w_src, int s
   if (use_stem_dx(desc, leg, g)) {
     if ((reinterpret_cast<uintptr_t>(w_packed) & 15) != 0) return R4C_ERR_ALIGN;
     return cuda_status(stem::dx_pack_weight(g.cout, w_src, src_dtype, w_packed, desc->dtype, s));
+  }
+  if (use_tc_tconv(desc, leg, g)) {
+    if ((reinterpret_cast<uintptr_t>(w_packed) & 15) != 0) return R4C_ERR_ALIGN;
+    return cuda_status(tconv::pack_weight(leg == R4C_LEG_TFWD ? 0 : 1, g.n, g.d, g.h, g.w, g.cin, g.cout, w_src,
+                                          src_dtype, w_packed, desc->dtype, s));
   }
   tc::ConvPlan pl;
   if (use_tc(desc, leg, g, &pl)) {
@@ -462,6 +479,8 @@ int r4c_tconv_fwd(const r4c_conv_desc* desc, const void* x, const void* w_packed
   if (g.in_vox() == 0) return R4C_OK;
   if (!x || !w_packed || !y) return R4C_ERR_INVALID;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (use_tc_tconv(desc, R4C_LEG_TFWD, g))
+    return tconv::launch(0, g.n, g.d, g.h, g.w, g.cin, g.cout, x, w_packed, bias, y, desc->dtype, s);
   generic::FwdParams p{};
   p.a = x; p.b = w_packed; p.bias = bias; p.out = y;
   p.M = g.in_vox(); p.N = 8 * g.cout; p.K = g.cin;
@@ -480,6 +499,8 @@ int r4c_tconv_dx(const r4c_conv_desc* desc, const void* go, const void* w_packed
   if (g.in_vox() == 0) return R4C_OK;
   if (!go || !w_packed || !dx) return R4C_ERR_INVALID;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (use_tc_tconv(desc, R4C_LEG_TDX, g))
+    return tconv::launch(1, g.n, g.d, g.h, g.w, g.cin, g.cout, go, w_packed, nullptr, dx, desc->dtype, s);
   generic::FwdParams p{};
   p.a = go; p.b = w_packed; p.bias = nullptr; p.out = dx;
   p.M = g.in_vox(); p.N = g.cin; p.K = 8 * g.cout;

@@ -137,4 +137,17 @@ int launch_dx(int n, int d, int h, int w, int cout, const void* go, const void* 
               cudaStream_t st);
 }  // namespace stem
 
+// ConvTranspose3d k=2 s=2 p=0 forward (mode 0) and dX (mode 1) on tcgen05;
+// activations NDHWC, Cin and Cout multiples of 8. The packed weight is the
+// per-task shared-memory image of packed_bytes().
+namespace tconv {
+bool supported(int mode, int n, int d, int h, int w, int cin, int cout);
+size_t packed_bytes(int mode, int n, int d, int h, int w, int cin, int cout);
+int describe(int mode, int n, int d, int h, int w, int cin, int cout, char* buf, size_t len);
+cudaError_t pack_weight(int mode, int n, int d, int h, int w, int cin, int cout, const void* w_src, int src_dtype,
+                        void* w_packed, int dtype, cudaStream_t st);
+int launch(int mode, int n, int d, int h, int w, int cin, int cout, const void* in, const void* w_packed,
+           const void* bias, void* out, int dtype, cudaStream_t st);
+}  // namespace tconv
+
 }  // namespace r4c

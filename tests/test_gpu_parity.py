@@ -72,6 +72,13 @@ TCONV_CASES = [
     (1, 96, 48, 4, 4, 4),
     (1, 5, 3, 2, 3, 4),
     (0, 16, 8, 2, 2, 2),
+    # tcgen05 transpose conv (Cin, Cout multiples of 8): tiles of R rows x W,
+    # x segments for W > 128, N split into tasks, 2*Cout over two box groups
+    (1, 8, 16, 1, 3, 130),
+    (2, 48, 24, 2, 5, 64),
+    (1, 192, 96, 3, 8, 16),
+    (1, 96, 48, 2, 4, 32),
+    (1, 24, 40, 2, 3, 7),
 ]
 
 
@@ -164,11 +171,13 @@ def test_dw_layouts_match_oracle(cuda_ready, case, dtype, wide, monkeypatch):
     assert O.norm_rel(db.cpu(), go.float().sum(dim=(0, 2, 3, 4))) <= 1e-4
 
 
+@pytest.mark.parametrize("force", [0, 1], ids=["auto", "simt"])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16], ids=["bf16", "fp16"])
 @pytest.mark.parametrize("case", TCONV_CASES, ids=_ids(TCONV_CASES))
-def test_tconv_legs_match_oracle(cuda_ready, case, dtype):
+def test_tconv_legs_match_oracle(cuda_ready, case, dtype, force, monkeypatch):
     n, cin, cout, d, h, w = case
     cw = _cw()
+    monkeypatch.setattr(cw, "_FORCE_KERNEL", force)
     g = torch.Generator().manual_seed(0)
     x = torch.randn(n, cin, d, h, w, generator=g).to(dtype)
     wt = (torch.randn(cin, cout, 2, 2, 2, generator=g) / cin ** 0.5).to(dtype)

@@ -322,12 +322,12 @@ class TLayer:
         self.flops = 2.0 * BATCH * d * h * w * self.cin * self.cout * 8
 
 
-def time_tconv(device, steps, warmup, peaks):
+def time_tconv(device, steps, warmup, peaks, names=None):
     """fwd / dX / dW(+db) of BASELINE configs[2] through the package's launch
     path, CUDA events per leg; per leg: us, TFLOP/s and HBM GB/s of the
     minimum bytes against the measured copy bandwidth."""
     cw = sys.modules["rdna4_conv3d.conv3d_wmma"]
-    layers = [TLayer(spec, device, seed=500 + i) for i, spec in enumerate(TCONV)]
+    layers = [TLayer(spec, device, seed=500 + i) for i, spec in enumerate(TCONV) if names is None or spec[0] in names]
 
     def step(evs=None):
         for i, L in enumerate(layers):
@@ -420,7 +420,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-tconv", action="store_true", help="skip the ConvTranspose3d k2s2 legs (configs[2])")
-    ap.add_argument("--only", default=None, help="run one trunk layer, e.g. 'k3 24->24' (profiling)")
+    ap.add_argument("--only", default=None, help="run one trunk layer, e.g. 'k3 24->24', or one transpose-conv "
+                                                 "layer, e.g. 'T k2s2 48->24' (profiling)")
     ap.add_argument("--legs", default="fwd,dw,dx", help="comma list of legs to run (profiling)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -433,6 +434,13 @@ def main():
     from rdna4_conv3d import _native
     from rdna4_conv3d.conv3d_wmma import conv3d_kernels
     _native.lib()
+
+    if args.only in [t[0] for t in TCONV]:
+        # one transpose-conv layer (profiling): its legs only, one JSON line of per-leg times
+        rows = time_tconv(dev, args.steps, args.warmup, load_peaks(), names=[args.only])
+        if rank == 0:
+            print(json.dumps({"impl": "ours", "only": args.only, "tconv_layers": rows}), flush=True)
+        return 0
 
     specs = [t for t in TRUNK if args.only is None or t[0] == args.only]
     if not specs:

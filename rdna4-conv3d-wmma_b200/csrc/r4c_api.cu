@@ -168,6 +168,12 @@ bool use_tc_tconv(const r4c_conv_desc* ds, int leg, const Geom& g) {
   return tconv::supported(leg == R4C_LEG_TFWD ? 0 : 1, g.n, g.d, g.h, g.w, g.cin, g.cout);
 }
 
+// ConvTranspose3d k2s2 weight gradient: the tcgen05 transpose-conv dW kernel.
+bool use_tc_tconv_dw(const r4c_conv_desc* ds, int leg, const Geom& g) {
+  if (ds->force_kernel == R4C_KERNEL_GENERIC || leg != R4C_LEG_TDW) return false;
+  return tconv::dw_supported(g.n, g.d, g.h, g.w, g.cin, g.cout);
+}
+
 bool use_tc(const r4c_conv_desc* ds, int leg, const Geom& g, tc::ConvPlan* pl) {
   if (ds->force_kernel == R4C_KERNEL_GENERIC) return false;
   if (leg == R4C_LEG_FWD)
@@ -218,7 +224,7 @@ int r4c_plan_kernel(const r4c_conv_desc* desc, int leg) {
   if (st != R4C_OK) return st;
   tc::ConvPlan pl;
   if (use_stem(desc, leg, g) || use_stem_dw(desc, leg, g) || use_stem_dx(desc, leg, g) ||
-      use_tc_tconv(desc, leg, g) || use_tc(desc, leg, g, &pl))
+      use_tc_tconv(desc, leg, g) || use_tc_tconv_dw(desc, leg, g) || use_tc(desc, leg, g, &pl))
     return R4C_KERNEL_TC;
   return R4C_KERNEL_GENERIC;
 }
@@ -242,6 +248,9 @@ int r4c_describe_plan(const r4c_conv_desc* desc, int leg, char* buf, size_t len)
       st = R4C_KERNEL_TC;
     } else if (use_tc_tconv(desc, leg, g)) {
       tconv::describe(leg == R4C_LEG_TFWD ? 0 : 1, g.n, g.d, g.h, g.w, g.cin, g.cout, tmp, sizeof(tmp));
+      st = R4C_KERNEL_TC;
+    } else if (use_tc_tconv_dw(desc, leg, g)) {
+      tconv::dw_describe(g.n, g.d, g.h, g.w, g.cin, g.cout, tmp, sizeof(tmp));
       st = R4C_KERNEL_TC;
     } else if (leg == R4C_LEG_DW && use_tc(desc, leg, g, &pl)) {
       tc::dw_describe(g.n, g.d, g.h, g.w, cin_eff(g), g.cout, g.k, g.pd, g.ph, g.pw, tmp, sizeof(tmp));
@@ -302,6 +311,10 @@ size_t r4c_workspace_size(const r4c_conv_desc* desc, int leg) {
     if (use_stem(desc, leg, g)) return 0;
     tc::ConvPlan pl;
     if (use_tc(desc, leg, g, &pl)) return cpad_bytes(g);
+  }
+  if (leg == R4C_LEG_TDW && use_tc_tconv_dw(desc, leg, g)) {
+    WgradLayout L = wgrad_layout(g, true);
+    return tconv::dw_workspace(g.n, g.d, g.h, g.w, g.cin, g.cout) + L.db_bytes;
   }
   if (leg == R4C_LEG_DW || leg == R4C_LEG_TDW) {
     WgradLayout L = wgrad_layout(g, leg == R4C_LEG_TDW);
@@ -518,6 +531,15 @@ int r4c_tconv_dw(const r4c_conv_desc* desc, const void* x, const void* go, float
   if (!dw) return R4C_ERR_INVALID;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   WgradLayout L = wgrad_layout(g, true);
+  if (g.in_vox() > 0 && use_tc_tconv_dw(desc, R4C_LEG_TDW, g)) {
+    const size_t pb = tconv::dw_workspace(g.n, g.d, g.h, g.w, g.cin, g.cout);
+    if (!workspace || ws_bytes < pb + L.db_bytes) return R4C_ERR_WORKSPACE;
+    if (!x || !go) return R4C_ERR_INVALID;
+    int rc = tconv::launch_dw(g.n, g.d, g.h, g.w, g.cin, g.cout, x, go, dw, workspace, pb, desc->dtype, s);
+    if (rc != R4C_OK || !db) return rc;
+    float* part = reinterpret_cast<float*>(static_cast<char*>(workspace) + pb);
+    return cuda_status(generic::launch_db(go, 8 * g.in_vox(), g.cout, desc->dtype, part, db, s));
+  }
   if (ws_bytes < L.part_bytes + L.db_bytes || (!workspace && L.part_bytes + L.db_bytes))
     return R4C_ERR_WORKSPACE;
   if (g.in_vox() == 0) {

@@ -314,6 +314,56 @@ __global__ void __launch_bounds__(NT) db_partial_kernel(const T* __restrict__ go
   }
 }
 
+// C a multiple of 8: thread (r, g) of a block sums 8-channel group g of the
+// positions vbeg + r, vbeg + r + rows, ... with 16-byte loads (consecutive
+// threads read consecutive 16-byte groups of a position, then the next
+// position), four loads in flight; the block then adds its rows in a fixed
+// order. The scalar kernel above keeps ~10 two-byte loads in flight per
+// block and ran at ~0.3 TB/s.
+template <typename T>
+__global__ void __launch_bounds__(256) db_partial_vec_kernel(const T* __restrict__ go, int64_t V, int C,
+                                                             int64_t chunk, float* __restrict__ part) {
+  __shared__ float red[256 * 8];
+  const int G = C / 8;
+  const int rows = 256 / G;
+  const int tid = threadIdx.x;
+  const int r = tid / G, g = tid - r * G;
+  const int64_t vbeg = (int64_t)blockIdx.x * chunk;
+  const int64_t vend = min(vbeg + chunk, V);
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  if (r < rows) {
+    const T* base = go + 8 * g;
+    int64_t v = vbeg + r;
+    for (; v + 3 * rows < vend; v += 4 * rows) {
+      uint4 q[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) q[u] = *reinterpret_cast<const uint4*>(base + (v + u * rows) * C);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const T* e = reinterpret_cast<const T*>(&q[u]);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[i] += Elem<T>::to_f(e[i]);
+      }
+    }
+    for (; v < vend; v += rows) {
+      const uint4 q = *reinterpret_cast<const uint4*>(base + v * C);
+      const T* e = reinterpret_cast<const T*>(&q);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] += Elem<T>::to_f(e[i]);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) red[tid * 8 + i] = acc[i];
+  __syncthreads();
+  // thread (g, i) adds row r's value of channel 8g + i, rows in order
+  if (tid < C) {
+    const int gg = tid / 8, i = tid - gg * 8;
+    float sum = 0.f;
+    for (int rr = 0; rr < rows; ++rr) sum += red[(rr * G + gg) * 8 + i];
+    part[(int64_t)blockIdx.x * C + tid] = sum;
+  }
+}
+
 __global__ void db_reduce_kernel(const float* __restrict__ part, int S, int C, float* __restrict__ db) {
   int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= C) return;
@@ -394,7 +444,13 @@ cudaError_t launch_db(const void* go, int64_t V, int C, int dtype, float* part, 
     cudaError_t e = cudaMemsetAsync(db, 0, sizeof(float) * C, st);
     return e;
   }
-  if (dtype == R4C_BF16)
+  const bool vec = C % 8 == 0 && C <= 256 && (reinterpret_cast<uintptr_t>(go) & 15) == 0;
+  if (vec && dtype == R4C_BF16)
+    db_partial_vec_kernel<__nv_bfloat16><<<S, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(go), V, C, chunk,
+                                                             part);
+  else if (vec)
+    db_partial_vec_kernel<__half><<<S, 256, 0, st>>>(static_cast<const __half*>(go), V, C, chunk, part);
+  else if (dtype == R4C_BF16)
     db_partial_kernel<__nv_bfloat16><<<S, NT, 0, st>>>(static_cast<const __nv_bfloat16*>(go), V, C, chunk, part);
   else
     db_partial_kernel<__half><<<S, NT, 0, st>>>(static_cast<const __half*>(go), V, C, chunk, part);

@@ -148,6 +148,13 @@ cudaError_t pack_weight(int mode, int n, int d, int h, int w, int cin, int cout,
                         void* w_packed, int dtype, cudaStream_t st);
 int launch(int mode, int n, int d, int h, int w, int cin, int cout, const void* in, const void* w_packed,
            const void* bias, void* out, int dtype, cudaStream_t st);
+// dW (fp32, PyTorch ConvTranspose3d layout) from x and dY; `ws` holds the
+// split partials (dw_workspace() bytes).
+bool dw_supported(int n, int d, int h, int w, int cin, int cout);
+size_t dw_workspace(int n, int d, int h, int w, int cin, int cout);
+int dw_describe(int n, int d, int h, int w, int cin, int cout, char* buf, size_t len);
+int launch_dw(int n, int d, int h, int w, int cin, int cout, const void* x, const void* go, float* dw, void* ws,
+              size_t ws_bytes, int dtype, cudaStream_t st);
 }  // namespace tconv
 
 }  // namespace r4c

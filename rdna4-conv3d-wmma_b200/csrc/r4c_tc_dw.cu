@@ -75,6 +75,10 @@ struct alignas(64) DwArgs {
   int cwb, b_region, lay_b;
   int nbox, npad_w;                  // dY boxes per stage, MMA N
   int tail_bytes;                    // zeroed bytes past the last stage (M tile over-read)
+  // chunk layout with kw folded into N: B holds the dY row three times,
+  // shifted by kw = 0, 1, 2 positions (atoms kw * nn/8 + c), A the unshifted
+  // input rows; one MMA of N = 3 nn per (M tile, K step)
+  int fold;
 };
 
 struct Task {
@@ -85,6 +89,7 @@ struct Task {
 struct DwPlan {
   bool ok;
   bool wide;
+  bool fold;
   int cw, apt, tpg, ng, plane_bytes, region_bytes, cwb, nbox, npad_w, tail_bytes;
   int n, d, h, w, od, oh, ow, cin, cout, ks, pd, ph, pw;
   int c8, groups, mtiles, pitch_w, kpad, wt, nwt;
@@ -238,6 +243,7 @@ static bool plan_dw(int n, int d, int h, int w, int cin, int cout, int ks, int p
           if (est < best) {
             best = est;
             P.wide = false;
+            P.fold = false;
             P.wt = wtc; P.nwt = nwt_c; P.kpad = kpad_c; P.pitch_w = pitch_c; P.rows = rows_c;
             P.mtn = mtn; P.nn = nn; P.kwn = kwn;
             P.S = S; P.rows_per_split = rps;
@@ -253,10 +259,78 @@ static bool plan_dw(int n, int d, int h, int w, int cin, int cout, int ks, int p
       }
     }
   }
+  // kw folded into N (chunk layout, k = 3, one W tile per output row): the
+  // stage's B holds three copies of the dY row shifted by kw = 0, 1, 2
+  // positions (boxes of the same TMA transaction), A the unshifted input rows
+  // over K = ow + 2 positions, so each (M tile, K step) takes one MMA of
+  // N = 3 nn instead of three of N = nn. The MN-major A read bounds an MMA's
+  // cost (~72 clk up to N ~ 64), so at 24->24 this is 18 instead of 48 MMAs
+  // per output row.
+  // Opt-in (R4C_DW_FOLD=1, taken whenever the layer allows it): measured on
+  // B200 at 24->24 it ran 690 us against 546 for the chunk layout. The
+  // 8-channel boxes move 16-byte TMA rows, whose cost is per row (~1 row per
+  // clock), and the shifted copies add 28 % rows (5184 against 4056 per
+  // output row) while the fewer MMAs no longer bound the row.
+  const char* fenv = getenv("R4C_DW_FOLD");
+  const int fold_force = (fenv && fenv[0] == '0') ? 0 : (fenv && fenv[0] == '1') ? 1 : -1;
+  bool folded = false;
+  if (fold_force == 1 && chunk_allowed && ks == 3 && round_up(P.ow + 2, 16) <= 256) {
+    if (fold_force == 1) best = 1e300;
+    const int kp = round_up(P.ow + 2, 16);
+    const long long rows_f = (long long)n * P.od * P.oh;
+    for (int nn = cout; nn >= 8; nn -= 8) {
+      if (cout % nn) continue;
+      const int npad = round_up(3 * nn, 16);
+      if (npad > 256) continue;
+      for (int mtn = std::min(P.mtiles, 8); mtn >= 1; --mtn) {
+        const int cols = mtn * npad;
+        if (cols > 512) continue;
+        const int ntasks = ((P.mtiles + mtn - 1) / mtn) * (cout / nn);
+        int lo, hi;
+        chunk_range(0, mtn, k2, P.c8, &lo, &hi);
+        int nch = hi - lo + 2;
+        if (nch > P.c8) nch = P.c8;
+        const int a_bytes = round_up((nch * k2 + 1) * kp * 16, 128);
+        const int g_bytes = (npad / 8) * kp * 16;  // the shifted copies + the atoms the MMA's N reads past them
+        const int stage = round_up(a_bytes + g_bytes, 128);
+        // an M tile reads 16 row blocks from the task's first group, which
+        // lies less than k^2 blocks past the A base: the reads past the last
+        // stage stay within this zeroed tail
+        const int tail = std::max(0, (k2 + 16 * mtn) * kp * 16 - stage) + 256;
+        const int stages = std::min(kMaxStages, (kSmemMax - kHeader - tail) / stage);
+        if (stages < 2) continue;
+        // the chunk layout's MMA model, so that the two compare on one scale
+        const double t_mma = std::max({npad / 2.0, (4096.0 + 32.0 * npad) / 128.0, 44.6});
+        const double mma = (double)(kp / 16) * mtn * t_mma;
+        const double load = (double)(nch * k2 * kp * 16 + 3 * (nn / 8) * kp * 16) / 48.0;
+        const double per_row = std::max(mma, load) + 60.0;
+        int S = 1;
+        long long rps = rows_f;
+        const double est = pick_split(rows_f, ntasks, per_row, &S, &rps);
+        if (est < best) {
+          best = est;
+          P.wide = false;
+          P.fold = true;
+          P.wt = P.ow; P.nwt = 1; P.kpad = kp; P.pitch_w = kp; P.rows = rows_f;
+          P.mtn = mtn; P.nn = nn; P.kwn = 3;
+          P.S = S; P.rows_per_split = rps;
+          P.stages = stages; P.stage_bytes = stage;
+          P.smem_bytes = kHeader + stages * stage + tail;
+          P.tail_bytes = tail;
+          int alloc = 32;
+          while (alloc < cols) alloc *= 2;
+          P.tmem_cols = alloc;
+          P.est = est;
+          P.ok = true;
+          folded = true;
+        }
+      }
+    }
+  }
   // Wide mode (Cin a multiple of 16, at least 32): one swizzled box per
   // channel group and row instead of one 16-byte-row box per 8 channels.
   const int cw = (wide_force == 1 || ks == 1) ? cw_pad : cw_ok;
-  if (cin >= 16 && (wide_force == 1 || wide_auto)) {
+  if (cin >= 16 && (wide_force == 1 || wide_auto) && !(fold_force == 1 && folded)) {
     const int apt = 128 / cw, atoms = k2 + 1;  // + the ones (group 0) / zero plane
     const int tpg = (atoms + apt - 1) / apt, ng = (cin + cw - 1) / cw;
     // W tile: the chunk layout's, halved until two stages fit
@@ -305,6 +379,7 @@ static bool plan_dw(int n, int d, int h, int w, int cin, int cout, int ks, int p
           if (est < best) {
             best = est;
             P.wide = true;
+            P.fold = false;
             P.wt = wt_w; P.nwt = nwt_w; P.kpad = kpad_w; P.pitch_w = pitch_ww; P.rows = rows_w;
             P.cw = cw; P.apt = apt; P.tpg = tpg; P.ng = ng; P.plane_bytes = plane; P.region_bytes = region;
             P.cwb = cwb; P.nbox = nbox; P.npad_w = npad; P.tail_bytes = tail_nn;
@@ -415,7 +490,9 @@ __device__ __forceinline__ void dw_issue_mt(int mtn, uint64_t a0, uint64_t b0, u
   }
 }
 
-template <typename T>
+// FOLD: the kw-folded chunk layout (DwArgs::fold); a separate instantiation,
+// so that the other layouts' issue loop keeps its register allocation.
+template <typename T, bool FOLD>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_dw_kernel(const __grid_constant__ DwArgs a, const __grid_constant__ TaskTable tt) {
   extern __shared__ __align__(1024) uint8_t smem[];
@@ -450,13 +527,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   // MMA N. Kept as arithmetic on the task width: loading it as a plain
   // argument changes the issue loop's register allocation (96 registers, no
   // descriptor reuse) and measured 9 % slower at 24->24.
-  const int npad = ((a.wide ? a.nbox * a.cwb : a.nn) + 15) / 16 * 16;
+  const int npad = ((a.wide ? a.nbox * a.cwb : a.nn * (FOLD ? 3 : 1)) + 15) / 16 * 16;
   const uint32_t tx_bytes = a.wide ? (uint32_t)(k2 * a.plane_bytes + a.nbox * a.cwb * a.kpad * 2)
-                                   : (uint32_t)(nch * k2 * sbo_a + (a.nn / 8) * a.kpad * 16);
+                                   : (uint32_t)(nch * k2 * sbo_a + (FOLD ? 3 : 1) * (a.nn / 8) * a.kpad * 16);
 
   // zero the whole dynamic region (finite junk rows), then the ones rows
   {
-    const int total = a.stages * a.stage_bytes + (a.wide ? a.tail_bytes : 16 * mtn * sbo_a + 256);
+    const int total = a.stages * a.stage_bytes + ((a.wide || FOLD) ? a.tail_bytes : 16 * mtn * sbo_a + 256);
     uint4 z = make_uint4(0, 0, 0, 0);
     for (int i = threadIdx.x * 16; i < total; i += kThreads * 16) *reinterpret_cast<uint4*>(stage0 + i) = z;
     __syncthreads();
@@ -548,8 +625,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int c = 0; c < nch; ++c)
             tma_load_5d(sA + (size_t)c * k2 * sbo_a, &a.tx, &full[stage], (c_lo + c) * 8, w0 - a.pw, y - a.ph,
                         z - a.pd, nb);
-          for (int c = 0; c < a.nn / 8; ++c)
-            tma_load_5d(sA + a.a_bytes + (size_t)c * a.kpad * 16, &a.tg, &full[stage], n0 + c * 8, w0, y, z, nb);
+          // fold: copy kw starts kw positions early (position p of the K range
+          // holds dY[w0 + p - kw]; the TMA fills the out-of-range ones with zeros)
+          const int nkw = FOLD ? 3 : 1;
+          for (int kw = 0; kw < nkw; ++kw)
+            for (int c = 0; c < a.nn / 8; ++c)
+              tma_load_5d(sA + a.a_bytes + (size_t)(kw * (a.nn / 8) + c) * a.kpad * 16, &a.tg, &full[stage],
+                          n0 + c * 8, w0 - kw, y, z, nb);
         }
         pending[stage] = true;
         last_par[stage] = epar ^ 1;
@@ -599,7 +681,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             default: dw_issue_row<5, 1, true>(a0, b0, tmem, (uint32_t)npad, stp, ksteps, a.idesc, first); break;
           }
         } else {
-          if (a.kwn == 3)
+          if (FOLD)
+            dw_issue_mt<1, false>(mtn, a0, b0, tmem, (uint32_t)npad, stp, ksteps, a.idesc, first);
+          else if (a.kwn == 3)
             dw_issue_mt<3, false>(mtn, a0, b0, tmem, (uint32_t)npad, stp, ksteps, a.idesc, first);
           else
             dw_issue_mt<1, false>(mtn, a0, b0, tmem, (uint32_t)npad, stp, ksteps, a.idesc, first);
@@ -620,7 +704,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int q = warp & 3;
       const int row = q * 32 + lane;
-      for (int kw = 0; kw < a.kwn; ++kw) {
+      for (int kw = 0; kw < (FOLD ? 1 : a.kwn); ++kw) {
         for (int t = 0; t < mtn; ++t) {
           // chunk mode: absolute 8-channel group (c, kd, kh) and channel in it;
           // wide mode: (kd, kh) plane (atom) of group grp and channel in it
@@ -638,10 +722,19 @@ __global__ void __launch_bounds__(kThreads, 1)
               const int tap = (kd * a.ks + kh) * a.ks + (kw0 + kw);
               const int ntap = k2 * a.ks;
               float* dst = a.part + (size_t)split * a.cout * a.cin * ntap;
+              if (FOLD) {
+                // column j = kw * nn + channel
 #pragma unroll
-              for (int i = 0; i < 16; ++i) {
-                const int co = n0 + cc + i;
-                if (cc + i < a.nn) dst[((size_t)co * a.cin + ci) * ntap + tap] = v[i];
+                for (int i = 0; i < 16; ++i) {
+                  const int j = cc + i, kwi = j / a.nn, co = n0 + j - kwi * a.nn;
+                  if (kwi < 3) dst[((size_t)co * a.cin + ci) * ntap + tap + kwi] = v[i];
+                }
+              } else {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                  const int co = n0 + cc + i;
+                  if (cc + i < a.nn) dst[((size_t)co * a.cin + ci) * ntap + tap] = v[i];
+                }
               }
             } else if (has_ones && g == (a.wide ? k2 : a.ones_group) && ci8 == 0 && kw == 0) {
 #pragma unroll
@@ -748,7 +841,7 @@ static bool encode_ndhwc(CUtensorMap* m, const void* base, int dtype, int c, int
              CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <typename T>
+template <typename T, bool FOLD>
 static cudaError_t set_attr() {
   static bool done[64] = {false};
   static std::mutex mu;
@@ -757,7 +850,7 @@ static cudaError_t set_attr() {
   if (e != cudaSuccess) return e;
   std::lock_guard<std::mutex> lk(mu);
   if (dev >= 0 && dev < 64 && done[dev]) return cudaSuccess;
-  e = cudaFuncSetAttribute(tc_dw_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
+  e = cudaFuncSetAttribute(tc_dw_kernel<T, FOLD>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
   if (e == cudaSuccess && dev >= 0 && dev < 64) done[dev] = true;
   return e;
 }
@@ -794,9 +887,10 @@ int dw_describe(int n, int d, int h, int w, int cin, int cout, int ks, int pd, i
              P.kpad, P.pitch_w, P.stages, P.stage_bytes, P.smem_bytes, P.tmem_cols, P.est / 1.9e3);
   else
     snprintf(buf, len,
-             "tcgen05 dW: groups=%d mtiles=%d task(mt=%d n=%d kw=%d) tasks=%d splits=%d rows/split=%lld "
+             "tcgen05 dW%s: groups=%d mtiles=%d task(mt=%d n=%d kw=%d) tasks=%d splits=%d rows/split=%lld "
              "wt=%d kpad=%d pitch=%d stages=%d stage=%dB smem=%dB tmem=%d db_in_kernel=%d est=%.0fus",
-             P.groups, P.mtiles, P.mtn, P.nn, P.kwn, (int)P.tasks.size(), P.S, P.rows_per_split, P.wt, P.kpad,
+             P.fold ? " (kw folded into N)" : "", P.groups, P.mtiles, P.mtn, P.nn, P.kwn, (int)P.tasks.size(), P.S,
+             P.rows_per_split, P.wt, P.kpad,
              P.pitch_w, P.stages, P.stage_bytes, P.smem_bytes, P.tmem_cols, (int)P.db_in_kernel, P.est / 1.9e3);
   return 1;
 }
@@ -836,6 +930,8 @@ int launch_dw(int n, int d, int h, int w, int cin, int cin_real, int cout, int k
     a.a_bytes = round_up((nch * ks * ks + 1) * P.pitch_w * 16, 128);
   }
   a.g_bytes = (P.nn / 8) * P.kpad * 16;
+  a.fold = P.fold ? 1 : 0;
+  if (P.fold) a.tail_bytes = P.tail_bytes;
   if (P.wide) {
     auto lay = [](int c) { return c == 64 ? 2 : c == 32 ? 4 : c == 16 ? 6 : 0; };
     a.wide = 1;
@@ -850,7 +946,8 @@ int launch_dw(int n, int d, int h, int w, int cin, int cin_real, int cout, int k
   a.rows = P.rows;
   a.rows_per_split = P.rows_per_split;
   a.ntasks = (int)P.tasks.size();
-  a.idesc = sm100::instr_desc_f16(dtype == R4C_BF16, 128, P.wide ? P.npad_w : round_up(P.nn, 16), 1, 1);
+  a.idesc = sm100::instr_desc_f16(dtype == R4C_BF16, 128, P.wide ? P.npad_w : round_up(P.nn * (P.fold ? 3 : 1), 16),
+                                  1, 1);
   TaskTable tt;
   memset(&tt, 0, sizeof(tt));
   for (size_t i = 0; i < P.tasks.size(); ++i) {
@@ -859,14 +956,22 @@ int launch_dw(int n, int d, int h, int w, int cin, int cin_real, int cout, int k
   }
   const unsigned grid = (unsigned)(P.tasks.size() * P.S);
   cudaError_t e;
-  if (dtype == R4C_BF16) {
-    e = set_attr<__nv_bfloat16>();
+  if (dtype == R4C_BF16 && P.fold) {
+    e = set_attr<__nv_bfloat16, true>();
     if (e != cudaSuccess) return R4C_ERR_CUDA;
-    tc_dw_kernel<__nv_bfloat16><<<grid, kThreads, P.smem_bytes, st>>>(a, tt);
+    tc_dw_kernel<__nv_bfloat16, true><<<grid, kThreads, P.smem_bytes, st>>>(a, tt);
+  } else if (dtype == R4C_BF16) {
+    e = set_attr<__nv_bfloat16, false>();
+    if (e != cudaSuccess) return R4C_ERR_CUDA;
+    tc_dw_kernel<__nv_bfloat16, false><<<grid, kThreads, P.smem_bytes, st>>>(a, tt);
+  } else if (P.fold) {
+    e = set_attr<__half, true>();
+    if (e != cudaSuccess) return R4C_ERR_CUDA;
+    tc_dw_kernel<__half, true><<<grid, kThreads, P.smem_bytes, st>>>(a, tt);
   } else {
-    e = set_attr<__half>();
+    e = set_attr<__half, false>();
     if (e != cudaSuccess) return R4C_ERR_CUDA;
-    tc_dw_kernel<__half><<<grid, kThreads, P.smem_bytes, st>>>(a, tt);
+    tc_dw_kernel<__half, false><<<grid, kThreads, P.smem_bytes, st>>>(a, tt);
   }
   if (cudaGetLastError() != cudaSuccess) return R4C_ERR_CUDA;
   const long long total = (long long)cout * cin_real * T;

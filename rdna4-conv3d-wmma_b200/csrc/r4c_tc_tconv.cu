@@ -361,6 +361,216 @@ __global__ void __launch_bounds__(kThreads, 1) tconv_kernel(const __grid_constan
 }
 
 // ---------------------------------------------------------------------------
+// dW: D[ci][(a,b,c,co)] += sum_v X[v][ci] * dY[n, 2z+a, 2y+b, 2x+c, co]
+// over K = input positions, both operands MN-major from the same TMA boxes as
+// above (64 positions per K tile: an x box gives 64 ci of each position, a dY
+// box 64 elements (c, co) of one (a, b)): M = 128 ci (two x boxes; channels
+// past Cin are the zero fill), N = the task's (a, b) pairs x 64-element
+// groups. Split-K over positions, one fp32 partial per CTA, summed in split
+// order by tconv_dw_reduce (deterministic).
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr int kDwBox = 64 * 128;  // 64 positions x 128 bytes
+
+struct DwTArgs {
+  CUtensorMap xmap;  // x (Cin, W, H, D, N), box (64, wt, R, 1, 1)
+  CUtensorMap gmap;  // dY (2*Cout, W, 2, H, 2D*N), box (64, wt, 1, R, 1)
+  float* part;       // [task][S][128][ncol]
+  int* err;
+  int n, d, h, w, cin, cout;
+  int wt, R, nwt, nyb;
+  long long tiles;   // K tiles of 64 positions
+  int S, ntask, nabg, nab, ngb, ncol, nmma, mma_n;
+  int nbox;          // boxes per stage: 2 (x) + nab * ngb (dY)
+  int nstages;
+  int tmem_cols;
+  uint32_t idesc;
+};
+
+}  // namespace
+
+__global__ void __launch_bounds__(kThreads, 1) tconv_dw_kernel(const __grid_constant__ DwTArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* empty = full + kMaxStages;
+  uint64_t* mdone = empty + kMaxStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mdone + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint8_t* st0 = smem + kHeader;
+  const int stage_bytes = a.nbox * kDwBox;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  if ((smem_u32(smem) & 1023u) != 0u || a.tmem_cols > 512) {
+    if (threadIdx.x == 0) atomicExch(a.err, 2);
+    return;
+  }
+  const int task = (int)blockIdx.x / a.S;
+  const int split = (int)blockIdx.x - task * a.S;
+  const int mt = task / a.nabg, abg = task - mt * a.nabg;
+  const long long t0 = a.tiles * split / a.S, t1 = a.tiles * (split + 1) / a.S;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kMaxStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(mdone, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, (uint32_t)a.tmem_cols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  const uint64_t kWaitNs = 1000000000ull;
+  auto wait = [&](uint64_t* bar, uint32_t par, uint32_t nap = 0) -> bool {
+    uint64_t deadline = 0;  // the clock is read only once a wait has lasted a while
+    uint32_t spins = 0;
+    while (!mbar_try_wait(bar, par)) {
+      if (nap) __nanosleep(nap);
+      if (((++spins) & 63u) == 0) {
+        if (*abort_flag) return false;
+        const uint64_t now = global_timer_ns();
+        if (deadline == 0) {
+          deadline = now + kWaitNs;
+        } else if (now > deadline) {
+          *abort_flag = 1;
+          atomicExch(a.err, 1);
+          return false;
+        }
+      }
+    }
+    return true;
+  };
+
+  if (warp == 0) {
+    // ---------------- TMA producer: per K tile, 2 x boxes + the task's dY boxes ----------------
+    if (lane == 0) {
+      prefetch_tmap(&a.xmap);
+      prefetch_tmap(&a.gmap);
+      const uint32_t tx = (uint32_t)(a.nbox * 128 * a.R * a.wt);
+      int s = 0;
+      uint32_t epar = 1u, pending = 0u, last_par = 0u;
+      for (long long t = t0; t < t1; ++t) {
+        const int xs = (int)(t % a.nwt);
+        long long r = t / a.nwt;
+        const int yb = (int)(r % a.nyb);
+        r /= a.nyb;
+        const int z = (int)(r % a.d), nb = (int)(r / a.d);
+        const int x0 = xs * a.wt, y0 = yb * a.R;
+        if (!wait(&empty[s], epar, 32)) break;
+        mbar_arrive_expect_tx(&full[s], tx);
+        uint8_t* dst = st0 + (size_t)s * stage_bytes;
+        tma_load_5d(dst, &a.xmap, &full[s], 128 * mt, x0, y0, z, nb);
+        tma_load_5d(dst + kDwBox, &a.xmap, &full[s], 128 * mt + 64, x0, y0, z, nb);
+        int j = 2;
+        for (int ab = abg * a.nab; ab < (abg + 1) * a.nab; ++ab)
+          for (int g = 0; g < a.ngb; ++g, ++j)
+            tma_load_5d(dst + (size_t)j * kDwBox, &a.gmap, &full[s], 64 * g, x0, ab & 1, y0,
+                        nb * 2 * a.d + 2 * z + (ab >> 1));
+        pending |= 1u << s;
+        last_par = (last_par & ~(1u << s)) | ((epar ^ 1u) << s);
+        if (++s == a.nstages) {
+          s = 0;
+          epar ^= 1u;
+        }
+      }
+      const uint64_t deadline = global_timer_ns() + kWaitNs;
+      for (int i = 0; i < a.nstages; ++i)
+        if ((pending >> i) & 1u) mbar_wait_bounded(&full[i], (last_par >> i) & 1u, deadline);
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (whole warp; the elected lane issues) ----------------
+    // MN-major, 128-byte swizzle: LBO = the next 64-element MN atom (the
+    // next box), SBO = the next 8 positions (1024 B); a K step of 16
+    // positions moves the start by 2048 B (128 units of 16 B)
+    auto mn_desc = [](uint32_t addr) {
+      return smem_desc(addr, (uint32_t)kDwBox, 1024u) | ((uint64_t)2u << 61);
+    };
+    int s = 0;
+    uint32_t fpar = 0u, acc = 0u;
+    for (long long t = t0; t < t1; ++t) {
+      int okk = 1;
+      if (lane == 0) okk = wait(&full[s], fpar) ? 1 : 0;
+      if (!__shfl_sync(0xffffffffu, okk, 0)) break;
+      tc_fence_after();
+      const uint32_t sa = smem_u32(st0 + (size_t)s * stage_bytes);
+      const uint64_t ad = mn_desc(sa);
+      const uint64_t bd = mn_desc(sa + 2u * kDwBox);
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        for (int m = 0; m < a.nmma; ++m)
+          mma_f16_ss_warp(tmem + (uint32_t)(m * a.mma_n), ad + (uint64_t)(128 * kk),
+                          bd + (uint64_t)(128 * kk) + (uint64_t)(m * (a.mma_n / 64) * (kDwBox / 16)), a.idesc,
+                          acc);
+        acc = 1u;
+      }
+      mma_commit_warp(&empty[s]);
+      if (++s == a.nstages) {
+        s = 0;
+        fpar ^= 1u;
+      }
+    }
+    mma_commit_warp(mdone);
+  } else {
+    // ---------------- epilogue (warps 2..9): TMEM -> fp32 partial ----------------
+    const int q = warp & 3, half = (warp - 2) >> 2;
+    const int row = q * 32 + lane;
+    int got = 1;
+    if (lane == 0) got = wait(mdone, 0u, 256) ? 1 : 0;
+    got = __shfl_sync(0xffffffffu, got, 0);
+    if (got) {
+      tc_fence_after();
+      float* dst = a.part + (((size_t)task * a.S + split) * 128 + row) * a.ncol;
+      const bool any = t1 > t0;  // an empty split writes zeros
+      for (int g = half; g < a.ncol / 16; g += 2) {
+        float v[16];
+        tmem_ld_16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(g * 16), v);
+#pragma unroll
+        for (int i = 0; i < 16; i += 4)
+          *reinterpret_cast<float4*>(dst + g * 16 + i) =
+              any ? make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    if (lane == 0) mbar_wait_bounded(mdone, 0u, global_timer_ns() + kWaitNs);
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, (uint32_t)a.tmem_cols);
+  }
+}
+
+// dw[ci][co][a][b][c] (fp32, PyTorch ConvTranspose3d layout) = sum over the
+// splits, in split order, of the partials.
+__global__ void tconv_dw_reduce(const float* __restrict__ part, float* __restrict__ dw, int cin, int cout, int S,
+                                int nabg, int nab, int ngb, int ncol) {
+  const long long total = (long long)cin * cout * 8;
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= total) return;
+  const int tap = (int)(i % 8);
+  const long long r = i / 8;
+  const int co = (int)(r % cout), ci = (int)(r / cout);
+  const int ab = tap >> 1, c = tap & 1;
+  const int task = (ci >> 7) * nabg + ab / nab;
+  const int col = (ab % nab) * ngb * 64 + c * cout + co;
+  const float* p = part + ((size_t)task * S * 128 + (ci & 127)) * ncol + col;
+  float acc = 0.f;
+  for (int s = 0; s < S; ++s) acc += p[(size_t)s * 128 * ncol];
+  dw[i] = acc;
+}
+
+// ---------------------------------------------------------------------------
 // Host side.
 // ---------------------------------------------------------------------------
 namespace {
@@ -634,6 +844,146 @@ int launch(int mode, int n, int d, int h, int w, int cin, int cout, const void* 
                                            : launch_typed<__half>(a, grid, p.smem, st);
   note_launches(1);
   return ce == cudaSuccess ? R4C_OK : R4C_ERR_CUDA;
+}
+
+
+// ---------------------------------------------------------------------------
+// dW host side.
+// ---------------------------------------------------------------------------
+namespace {
+
+struct DwTPlan {
+  int wt, R, nwt, nyb;
+  long long tiles;
+  int S, ntask, nabg, nab, ngb, ncol, nmma, mma_n, nbox, nstages, tmem_cols, smem;
+  size_t part_bytes;
+};
+
+bool make_dw_plan(int n, int d, int h, int w, int cin, int cout, int sms, DwTPlan* out) {
+  if (n < 1 || d < 1 || h < 1 || w < 1) return false;
+  if (cin % 8 || cout % 8 || cin < 8 || cout < 8 || cout > 256) return false;
+  DwTPlan p{};
+  p.ngb = (2 * cout + 63) / 64;
+  p.nab = 4;
+  while (p.nab > 1 && p.nab * p.ngb * 64 > 512) p.nab /= 2;
+  p.ncol = p.nab * p.ngb * 64;
+  if (p.ncol > 512) return false;
+  p.mma_n = 64;
+  for (int k = 4; k >= 1; --k)
+    if (p.ncol % (64 * k) == 0) {
+      p.mma_n = 64 * k;
+      break;
+    }
+  p.nmma = p.ncol / p.mma_n;
+  p.nabg = 4 / p.nab;
+  p.ntask = ((cin + 127) / 128) * p.nabg;
+  p.nbox = 2 + p.nab * p.ngb;
+  p.nstages = std::min(kMaxStages, (kSmemMax - kHeader) / (p.nbox * kDwBox));
+  if (p.nstages < 2) return false;
+  p.smem = kHeader + p.nstages * p.nbox * kDwBox;
+  // K tile: 64 positions = R rows x wt columns (wt a power of two >= W, up
+  // to 64; columns past W and rows past H are the zero fill)
+  p.wt = 1;
+  while (p.wt < std::min(w, 64)) p.wt *= 2;
+  p.R = 64 / p.wt;
+  p.nwt = (w + p.wt - 1) / p.wt;
+  p.nyb = (h + p.R - 1) / p.R;
+  p.tiles = (long long)n * d * p.nyb * p.nwt;
+  p.S = (int)std::max<long long>(1, std::min<long long>(p.tiles, sms / p.ntask));
+  p.part_bytes = (size_t)p.ntask * p.S * 128 * p.ncol * sizeof(float);
+  int alloc = 32;
+  while (alloc < p.ncol) alloc *= 2;
+  p.tmem_cols = alloc;
+  *out = p;
+  return true;
+}
+
+}  // namespace
+
+bool dw_supported(int n, int d, int h, int w, int cin, int cout) {
+  DwTPlan p;
+  return make_dw_plan(n, d, h, w, cin, cout, 148, &p);
+}
+
+size_t dw_workspace(int n, int d, int h, int w, int cin, int cout) {
+  DwTPlan p;
+  if (!make_dw_plan(n, d, h, w, cin, cout, sm_count(), &p)) return 0;
+  return (p.part_bytes + 255) / 256 * 256;
+}
+
+int dw_describe(int n, int d, int h, int w, int cin, int cout, char* buf, size_t len) {
+  DwTPlan p;
+  if (!make_dw_plan(n, d, h, w, cin, cout, 148, &p)) return snprintf(buf, len, "tcgen05 tconv dW: no plan");
+  return snprintf(buf, len,
+                  "tcgen05 tconv dW (MN-major x and dY boxes, split-K over positions): K tile=%dx%d tasks=%d "
+                  "(a,b)/task=%d N/task=%d (%d MMAs of N=%d) boxes/stage=%d stages=%d splits=%d tiles=%lld",
+                  p.R, p.wt, p.ntask, p.nab, p.ncol, p.nmma, p.mma_n, p.nbox, p.nstages, p.S, p.tiles);
+}
+
+// x (NDHWC, Cin), go (NDHWC at 2x, Cout) -> dw fp32 (Cin, Cout, 2, 2, 2); ws >= dw_workspace().
+int launch_dw(int n, int d, int h, int w, int cin, int cout, const void* x, const void* go, float* dw, void* ws,
+              size_t ws_bytes, int dtype, cudaStream_t st) {
+  DwTPlan p;
+  if (!make_dw_plan(n, d, h, w, cin, cout, sm_count(), &p)) return R4C_ERR_UNSUPPORTED;
+  if (((uintptr_t)x & 15) || ((uintptr_t)go & 15)) return R4C_ERR_ALIGN;
+  if (!ws || ws_bytes < p.part_bytes) return R4C_ERR_WORKSPACE;
+  DwTArgs a;
+  memset(&a, 0, sizeof(a));
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return R4C_ERR_CUDA;
+  const CUtensorMapDataType dt = dtype == R4C_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const cuuint64_t e = 2;
+  cuuint32_t es[5] = {1, 1, 1, 1, 1};
+  {
+    const cuuint64_t c = (cuuint64_t)cin;
+    cuuint64_t dims[5] = {c, (cuuint64_t)w, (cuuint64_t)h, (cuuint64_t)d, (cuuint64_t)n};
+    cuuint64_t str[4] = {c * e, c * w * e, c * w * h * e, c * w * h * d * e};
+    cuuint32_t box[5] = {64, (cuuint32_t)p.wt, (cuuint32_t)p.R, 1, 1};
+    if (enc(&a.xmap, dt, 5, const_cast<void*>(x), dims, str, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return R4C_ERR_INVALID;
+  }
+  {
+    const cuuint64_t c2 = 2ull * cout, row = 2ull * w * cout * e;
+    cuuint64_t dims[5] = {c2, (cuuint64_t)w, 2, (cuuint64_t)h, 2ull * d * n};
+    cuuint64_t str[4] = {c2 * e, row, 2 * row, 2 * row * h};
+    cuuint32_t box[5] = {64, (cuuint32_t)p.wt, 1, (cuuint32_t)p.R, 1};
+    if (enc(&a.gmap, dt, 5, const_cast<void*>(go), dims, str, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return R4C_ERR_INVALID;
+  }
+  a.part = static_cast<float*>(ws);
+  a.err = tc::device_error_flag();
+  if (!a.err) return R4C_ERR_CUDA;
+  a.n = n; a.d = d; a.h = h; a.w = w; a.cin = cin; a.cout = cout;
+  a.wt = p.wt; a.R = p.R; a.nwt = p.nwt; a.nyb = p.nyb; a.tiles = p.tiles;
+  a.S = p.S; a.ntask = p.ntask; a.nabg = p.nabg; a.nab = p.nab; a.ngb = p.ngb;
+  a.ncol = p.ncol; a.nmma = p.nmma; a.mma_n = p.mma_n; a.nbox = p.nbox; a.nstages = p.nstages;
+  a.tmem_cols = p.tmem_cols;
+  a.idesc = instr_desc_f16(dtype == R4C_BF16, 128, p.mma_n, 1, 1);
+  static bool done[64] = {false};
+  static std::mutex mu;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return R4C_ERR_CUDA;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (dev >= 0 && dev < 64 && !done[dev]) {
+      if (cudaFuncSetAttribute(tconv_dw_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax) !=
+          cudaSuccess)
+        return R4C_ERR_CUDA;
+      done[dev] = true;
+    }
+  }
+  tconv_dw_kernel<<<p.ntask * p.S, kThreads, p.smem, st>>>(a);
+  note_launches(1);
+  if (cudaGetLastError() != cudaSuccess) return R4C_ERR_CUDA;
+  const long long total = (long long)cin * cout * 8;
+  tconv_dw_reduce<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(a.part, dw, cin, cout, p.S, p.nabg, p.nab, p.ngb,
+                                                                   p.ncol);
+  note_launches(1);
+  return cudaGetLastError() == cudaSuccess ? R4C_OK : R4C_ERR_CUDA;
 }
 
 }  // namespace tconv

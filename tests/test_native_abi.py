@@ -103,7 +103,8 @@ def test_stem_family():
 def test_tconv_family():
     # ConvTranspose3d k2s2 forward / dX with Cin, Cout multiples of 8: the
     # tcgen05 transpose-conv kernel, weights packed per task as 64-channel
-    # swizzled images (boxes x N columns x 128 B); dW stays SIMT
+    # swizzled images (boxes x N columns x 128 B); dW: the tcgen05 split-K
+    # kernel, its partials (plus the db partials) in the caller's workspace
     def t(n, cin, cout, d, h, w, force=0):
         return _native.make_desc(n, d, h, w, cin, cout, 2, (0, 0, 0), torch.bfloat16, force)
     for cin, cout, sp, fwd_b, dx_b in ((48, 24, (32, 64, 64), 1 * 192 * 128, 4 * 48 * 128),
@@ -115,11 +116,15 @@ def test_tconv_family():
             assert "tcgen05 tconv" in _native.describe_plan(dsc, leg)
             assert _native.packed_weight_bytes(dsc, leg) == nbytes
             assert _native.workspace_bytes(dsc, leg) == 0
-        assert _native.plan_kernel(dsc, _native.LEG_TDW) == _native.KERNEL_GENERIC
+        assert _native.plan_kernel(dsc, _native.LEG_TDW) == _native.KERNEL_TC
+        assert "tcgen05 tconv dW" in _native.describe_plan(dsc, _native.LEG_TDW)
+        assert _native.workspace_bytes(dsc, _native.LEG_TDW) > 0
     # channel counts off the multiple of 8, or the SIMT family forced
     assert _native.plan_kernel(t(1, 5, 3, 2, 3, 4), _native.LEG_TFWD) == _native.KERNEL_GENERIC
     assert _native.plan_kernel(t(1, 16, 12, 2, 3, 4), _native.LEG_TDX) == _native.KERNEL_GENERIC
     assert _native.plan_kernel(t(1, 16, 8, 2, 3, 4, force=1), _native.LEG_TFWD) == _native.KERNEL_GENERIC
+    assert _native.plan_kernel(t(1, 16, 12, 2, 3, 4), _native.LEG_TDW) == _native.KERNEL_GENERIC
+    assert _native.plan_kernel(t(1, 16, 8, 2, 3, 4, force=1), _native.LEG_TDW) == _native.KERNEL_GENERIC
 
 
 def test_descriptor_validation():

@@ -566,6 +566,8 @@ __global__ void tconv_dw_reduce(const float* __restrict__ part, float* __restric
   const int col = (ab % nab) * ngb * 64 + c * cout + co;
   const float* p = part + ((size_t)task * S * 128 + (ci & 127)) * ncol + col;
   float acc = 0.f;
+  // in split order, eight loads in flight
+#pragma unroll 8
   for (int s = 0; s < S; ++s) acc += p[(size_t)s * 128 * ncol];
   dw[i] = acc;
 }

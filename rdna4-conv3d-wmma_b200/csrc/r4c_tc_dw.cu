@@ -165,18 +165,22 @@ static bool plan_dw(int n, int d, int h, int w, int cin, int cout, int ks, int p
   const char* wenv = getenv("R4C_DW_WIDE");
   const int wide_force = (wenv && wenv[0] == '0') ? 0 : (wenv && wenv[0] == '1') ? 1 : -1;
   const int cw_ok = cin % 64 == 0 ? 64 : cin % 32 == 0 ? 32 : cin % 16 == 0 ? 16 : 0;
-  // Automatic choice: the wide layout for 64-channel groups only. Measured on
-  // B200 (trunk layers, batch 4): 192->192 k3 254 -> 210 us and 192->96 k1
-  // 83 -> 67 us with 64-channel groups, while 32- and 16-channel groups lost
-  // to the chunk layout (96->96 206 -> 238 us, 48->48 248 -> 314 us: more M
-  // tiles per K step outweigh the fewer TMA rows). R4C_DW_WIDE=1 enables the
-  // narrower groups, =0 disables the wide layout.
+  // Automatic choice of the wide layout. Measured on B200 (trunk layers,
+  // batch 4): 192->192 k3 254 -> 210 us and 192->96 k1 83 -> 67 us with
+  // 64-channel groups; with 32- and 16-channel groups the chunk layout first
+  // won (96->96 206 vs 238 us, 48->48 248 vs 314 us: more M tiles per K step
+  // outweigh the fewer TMA rows). R4C_DW_WIDE=1 enables the narrower groups,
+  // =0 disables the wide layout.
   // k1 layers (a plain GEMM over positions, TMA-row-bound in the chunk
   // layout) take the wide layout with the channel groups padded up to 64 /
   // 32 / 16 (the TMA zero-fills channels past Cin): one TMA row per position
   // and group.
   const int cw_pad = cin >= 48 ? 64 : cin > 16 ? 32 : 16;
-  const bool wide_auto = wide_force == -1 && ((cw_ok == 64 && cin >= 64) || (ks == 1 && cin >= 16));
+  // Re-measured with the wave-filling split counts: 96->96 k3 with 32-channel
+  // groups 223 -> 165 us (chunk -> wide), 48->48 with 16-channel groups still
+  // slower (260 vs 287 us); hence 32-channel groups from Cin = 96 up.
+  const bool wide_auto = wide_force == -1 &&
+                         ((cw_ok == 64 && cin >= 64) || (cw_ok == 32 && cin >= 96) || (ks == 1 && cin >= 16));
   const bool chunk_allowed = !((wide_force == 1 && cin >= 16) || wide_auto);
 
   // Splits of the output rows: one CTA per (task, split) at one CTA per SM,

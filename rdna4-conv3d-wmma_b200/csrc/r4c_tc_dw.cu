@@ -79,6 +79,7 @@ struct alignas(64) DwArgs {
   // shifted by kw = 0, 1, 2 positions (atoms kw * nn/8 + c), A the unshifted
   // input rows; one MMA of N = 3 nn per (M tile, K step)
   int fold;
+  int row_bytes;  // one output row's slot in a stage (stage_bytes / rows per stage)
 };
 
 struct Task {
@@ -90,6 +91,7 @@ struct DwPlan {
   bool ok;
   bool wide;
   bool fold;
+  int rpst;  // output rows per stage (wide layout: 2 when a row's boxes are under 32 KB)
   int cw, apt, tpg, ng, plane_bytes, region_bytes, cwb, nbox, npad_w, tail_bytes;
   int n, d, h, w, od, oh, ow, cin, cout, ks, pd, ph, pw;
   int c8, groups, mtiles, pitch_w, kpad, wt, nwt;
@@ -403,6 +405,24 @@ static bool plan_dw(int n, int d, int h, int w, int cin, int cout, int ks, int p
     }
   }
   if (!P.ok) return false;
+  // Two output rows per stage in the wide layout when a row's boxes move less
+  // than 32 KB: the TMA's throughput per SM is set by the bytes of each
+  // mbarrier transaction (~0.55 us per transaction below ~32 KB). k1 layers
+  // (16-24 KB per row) are the ones this reaches. R4C_DW_ROWS=1 keeps one.
+  P.rpst = 1;
+  {
+    const char* re = getenv("R4C_DW_ROWS");
+    if (P.wide && P.stage_bytes < 32768 && !(re && re[0] == '1')) {
+      const int row = P.stage_bytes;
+      const int st2 = std::min(kMaxStages, (kSmemMax - kHeader - P.tail_bytes) / (2 * row));
+      if (st2 >= 3) {
+        P.rpst = 2;
+        P.stage_bytes = 2 * row;
+        P.stages = st2;
+        P.smem_bytes = kHeader + st2 * 2 * row + P.tail_bytes;
+      }
+    }
+  }
   P.tasks.clear();
   if (P.wide) {
     for (int g = 0; g < P.ng; ++g)
@@ -494,9 +514,10 @@ __device__ __forceinline__ void dw_issue_mt(int mtn, uint64_t a0, uint64_t b0, u
   }
 }
 
-// FOLD: the kw-folded chunk layout (DwArgs::fold); a separate instantiation,
-// so that the other layouts' issue loop keeps its register allocation.
-template <typename T, bool FOLD>
+// FOLD: the kw-folded chunk layout (DwArgs::fold); RPS: output rows per stage
+// (2 only in the wide layout). Separate instantiations, so that the chunk
+// layout's issue loop keeps its register allocation.
+template <typename T, bool FOLD, int RPS>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_dw_kernel(const __grid_constant__ DwArgs a, const __grid_constant__ TaskTable tt) {
   extern __shared__ __align__(1024) uint8_t smem[];
@@ -543,8 +564,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     if (a.wide) {
       if (grp == 0 && a.dbpart != nullptr)
-        for (int s = 0; s < a.stages; ++s) {
-          uint32_t* o = reinterpret_cast<uint32_t*>(stage0 + (size_t)s * a.stage_bytes + (size_t)k2 * a.plane_bytes);
+        for (int s = 0; s < a.stages * RPS; ++s) {
+          uint32_t* o = reinterpret_cast<uint32_t*>(stage0 + (size_t)(s / RPS) * a.stage_bytes +
+                                                    (size_t)(s % RPS) * a.row_bytes + (size_t)k2 * a.plane_bytes);
           for (int i = threadIdx.x; i < a.plane_bytes / 4; i += kThreads) o[i] = OneBits<T>::v;
         }
     } else if (a.ones_group >= 0) {
@@ -617,9 +639,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int z = (int)(q % a.od);
         const int nb = (int)(q / a.od);
         const int w0 = wi * a.wt;
-        if (!wait(&empty[stage], epar)) break;
-        uint8_t* sA = stage0 + (size_t)stage * a.stage_bytes;
-        mbar_arrive_expect_tx(&full[stage], tx_bytes);
+        const int slot = RPS == 1 ? 0 : (int)((r - r_beg) % RPS);  // row slot in the stage
+        if (slot == 0) {
+          if (!wait(&empty[stage], epar)) break;
+          const uint32_t nrow = RPS == 1 ? 1u : (uint32_t)min((long long)RPS, r_end - r);
+          mbar_arrive_expect_tx(&full[stage], tx_bytes * nrow);
+        }
+        uint8_t* sA = stage0 + (size_t)stage * a.stage_bytes + (size_t)slot * a.row_bytes;
         if (a.wide) {
           // the k x k input rows of the group: planes [kd][kh] of pitch_w positions
           tma_load_5d(sA, &a.tx, &full[stage], grp * a.cw, w0 - a.pw, y - a.ph, z - a.pd, nb);
@@ -639,7 +665,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         pending[stage] = true;
         last_par[stage] = epar ^ 1;
-        if (++stage == a.stages) { stage = 0; epar ^= 1; }
+        if (slot == RPS - 1 || r + 1 == r_end) {
+          if (++stage == a.stages) { stage = 0; epar ^= 1; }
+        }
       }
       for (int s = 0; s < a.stages; ++s) {
         if (!pending[s]) continue;
@@ -659,9 +687,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                                            (uint32_t)(a.apt * a.plane_bytes / 16), (uint32_t)(2 * a.cwb)}
                                  : DwSteps{16u, 1u, (uint32_t)(16 * sbo_a) >> 4, 16u};
       for (long long r = r_beg; r < r_end; ++r) {
-        if (!wait(&full[stage], fpar)) break;
-        tc_fence_after();
-        const uint32_t sA = smem_u32(stage0 + (size_t)stage * a.stage_bytes);
+        const int slot = RPS == 1 ? 0 : (int)((r - r_beg) % RPS);
+        if (slot == 0) {
+          if (!wait(&full[stage], fpar)) break;
+          tc_fence_after();
+        }
+        const uint32_t sA = smem_u32(stage0 + (size_t)stage * a.stage_bytes + (size_t)slot * a.row_bytes);
         uint64_t a0, b0;
         if (a.wide) {
           // swizzled MN-major: LBO = MN atom stride, SBO = 8-position K group
@@ -693,8 +724,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             dw_issue_mt<1, false>(mtn, a0, b0, tmem, (uint32_t)npad, stp, ksteps, a.idesc, first);
         }
         first = false;
-        mma_commit(&empty[stage]);
-        if (++stage == a.stages) { stage = 0; fpar ^= 1; }
+        if (slot == RPS - 1 || r + 1 == r_end) {
+          mma_commit(&empty[stage]);
+          if (++stage == a.stages) { stage = 0; fpar ^= 1; }
+        }
       }
       mma_commit(done);
     }
@@ -845,7 +878,7 @@ static bool encode_ndhwc(CUtensorMap* m, const void* base, int dtype, int c, int
              CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <typename T, bool FOLD>
+template <typename T, bool FOLD, int RPS>
 static cudaError_t set_attr() {
   static bool done[64] = {false};
   static std::mutex mu;
@@ -854,7 +887,7 @@ static cudaError_t set_attr() {
   if (e != cudaSuccess) return e;
   std::lock_guard<std::mutex> lk(mu);
   if (dev >= 0 && dev < 64 && done[dev]) return cudaSuccess;
-  e = cudaFuncSetAttribute(tc_dw_kernel<T, FOLD>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
+  e = cudaFuncSetAttribute(tc_dw_kernel<T, FOLD, RPS>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
   if (e == cudaSuccess && dev >= 0 && dev < 64) done[dev] = true;
   return e;
 }
@@ -927,6 +960,7 @@ int launch_dw(int n, int d, int h, int w, int cin, int cin_real, int cout, int k
   a.mtn = P.mtn; a.nn = P.nn; a.kwn = P.kwn;
   a.ones_group = P.db_in_kernel ? P.groups : -1;
   a.stages = P.stages; a.stage_bytes = P.stage_bytes;
+  a.row_bytes = P.stage_bytes / P.rpst;
   {
     int lo, hi;
     chunk_range(0, P.mtn, ks * ks, P.c8, &lo, &hi);
@@ -960,22 +994,23 @@ int launch_dw(int n, int d, int h, int w, int cin, int cin_real, int cout, int k
   }
   const unsigned grid = (unsigned)(P.tasks.size() * P.S);
   cudaError_t e;
-  if (dtype == R4C_BF16 && P.fold) {
-    e = set_attr<__nv_bfloat16, true>();
+  // instantiations: chunk / wide (one row per stage), fold, wide with two rows per stage
+  const bool bf = dtype == R4C_BF16;
+  if (P.fold) {
+    e = bf ? set_attr<__nv_bfloat16, true, 1>() : set_attr<__half, true, 1>();
     if (e != cudaSuccess) return R4C_ERR_CUDA;
-    tc_dw_kernel<__nv_bfloat16, true><<<grid, kThreads, P.smem_bytes, st>>>(a, tt);
-  } else if (dtype == R4C_BF16) {
-    e = set_attr<__nv_bfloat16, false>();
+    if (bf) tc_dw_kernel<__nv_bfloat16, true, 1><<<grid, kThreads, P.smem_bytes, st>>>(a, tt);
+    else tc_dw_kernel<__half, true, 1><<<grid, kThreads, P.smem_bytes, st>>>(a, tt);
+  } else if (P.rpst == 2) {
+    e = bf ? set_attr<__nv_bfloat16, false, 2>() : set_attr<__half, false, 2>();
     if (e != cudaSuccess) return R4C_ERR_CUDA;
-    tc_dw_kernel<__nv_bfloat16, false><<<grid, kThreads, P.smem_bytes, st>>>(a, tt);
-  } else if (P.fold) {
-    e = set_attr<__half, true>();
-    if (e != cudaSuccess) return R4C_ERR_CUDA;
-    tc_dw_kernel<__half, true><<<grid, kThreads, P.smem_bytes, st>>>(a, tt);
+    if (bf) tc_dw_kernel<__nv_bfloat16, false, 2><<<grid, kThreads, P.smem_bytes, st>>>(a, tt);
+    else tc_dw_kernel<__half, false, 2><<<grid, kThreads, P.smem_bytes, st>>>(a, tt);
   } else {
-    e = set_attr<__half, false>();
+    e = bf ? set_attr<__nv_bfloat16, false, 1>() : set_attr<__half, false, 1>();
     if (e != cudaSuccess) return R4C_ERR_CUDA;
-    tc_dw_kernel<__half, false><<<grid, kThreads, P.smem_bytes, st>>>(a, tt);
+    if (bf) tc_dw_kernel<__nv_bfloat16, false, 1><<<grid, kThreads, P.smem_bytes, st>>>(a, tt);
+    else tc_dw_kernel<__half, false, 1><<<grid, kThreads, P.smem_bytes, st>>>(a, tt);
   }
   if (cudaGetLastError() != cudaSuccess) return R4C_ERR_CUDA;
   const long long total = (long long)cout * cin_real * T;

@@ -77,7 +77,28 @@ struct TArgs {
   int b_bytes;
   int tmem_cols;
   uint32_t idesc;
+  // forward TMA-store epilogue (stg_blk > 0): the output viewed as
+  // (2*Cout, W, 2, H, 2D*N); a tile's (a, b) block of 2*Cout columns is staged
+  // as [positions][2*Cout] (stg_blk bytes per block, two buffers) and written
+  // by one box (2*Cout, wt, 1, R, 1)
+  CUtensorMap ymap;
+  int stg_blk;
 };
+
+// Barrier 1 over the 256 epilogue threads, returning the OR of `v` over them.
+__device__ __forceinline__ int epi_bar_or(int v) {
+  int r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.s32 q, %1, 0;\n\t"
+      "bar.red.or.pred p, 1, 256, q;\n\t"
+      "selp.s32 %0, 1, 0, p;\n\t}"
+      : "=r"(r)
+      : "r"(v)
+      : "memory");
+  return r;
+}
+__device__ __forceinline__ void epi_bar_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
   // K-major, 128-byte swizzle: SBO = 8 rows x 128 B, layout code 2
@@ -112,6 +133,7 @@ __global__ void __launch_bounds__(kThreads, 1) tconv_kernel(const __grid_constan
   uint8_t* bsm = smem + kHeader;
   uint8_t* st0 = bsm + ((a.b_bytes + 1023) / 1024) * 1024;
   const int stage_bytes = a.bpst * kBoxBytes;
+  uint8_t* stg0 = st0 + (size_t)a.nstages * stage_bytes;  // forward store staging (two buffers)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -298,6 +320,65 @@ __global__ void __launch_bounds__(kThreads, 1) tconv_kernel(const __grid_constan
     __syncwarp();
   } else {
     // ---------------- epilogue (warps 2..9) ----------------
+    if (a.stg_blk > 0) {
+      // forward through staging tiles and TMA stores: each (a, b) block of the
+      // tile is one contiguous [positions][2*Cout] box (full sectors written
+      // once, instead of 16-byte stores strided by 2*Cout per position)
+      const int q = warp & 3, half = (warp - 2) >> 2;
+      const int l = q * 32 + lane;
+      const int lanes = a.R * a.wt;
+      const int c2 = 2 * a.cout;
+      const int nblk = a.ncol / c2;
+      const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
+      const bool issuer = warp == 2 && lane == 0;
+      const int ngrp = a.ncol / 16;
+      int buf = 0, sb = 0;
+      uint32_t tbits = 0u;
+      for (long long t = sub; t < a.tiles; t += cpt) {
+        int nb, z, y0, x0;
+        tile_of(t, nb, z, y0, x0);
+        int got = 1;
+        if (lane == 0) got = wait(&tfull[buf], (tbits >> buf) & 1u, 64) ? 1 : 0;
+        got = __shfl_sync(0xffffffffu, got, 0);
+        // staging buffer sb was read by the stores of two tiles ago: at most
+        // the previous tile's group may still be reading
+        if (issuer) bulk_wait_read<1>();
+        if (epi_bar_or(!got)) break;
+        tbits ^= 1u << buf;
+        tc_fence_after();
+        uint8_t* stg = stg0 + (size_t)sb * nblk * a.stg_blk;
+        for (int g = half; g < ngrp; g += 2) {
+          float v[16];
+          tmem_ld_16(lane_base + (uint32_t)(buf * a.ncol + g * 16), v);
+          if (l >= lanes) continue;
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int col = g * 16 + e * 8;
+            const int j = col / c2, eo = col - j * c2;
+            const float* vv = v + 8 * e;
+            const float* bc = bias_col + col;
+            *reinterpret_cast<uint4*>(stg + (size_t)j * a.stg_blk + ((size_t)l * c2 + eo) * 2) =
+                make_uint4(pack2<T>(vv[0] + bc[0], vv[1] + bc[1]), pack2<T>(vv[2] + bc[2], vv[3] + bc[3]),
+                           pack2<T>(vv[4] + bc[4], vv[5] + bc[5]), pack2<T>(vv[6] + bc[6], vv[7] + bc[7]));
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[buf]);
+        fence_proxy_async_smem();  // staging writes -> visible to the TMA unit
+        epi_bar_sync();
+        if (issuer) {
+          for (int j = 0; j < nblk; ++j) {
+            const int ab = task * nblk + j;
+            tma_store_5d(&a.ymap, stg + (size_t)j * a.stg_blk, 0, x0, ab & 1, y0, nb * 2 * a.d + 2 * z + (ab >> 1));
+          }
+          bulk_commit_group();
+        }
+        buf ^= 1;
+        sb ^= 1;
+      }
+      if (issuer) bulk_wait<0>();
+    } else {
     const int q = warp & 3;             // TMEM lane quarter this warp may read
     const int half = (warp - 2) >> 2;   // 16-column groups half, half + 2, ...
     const int l = q * 32 + lane;        // tile row = position of the tile
@@ -349,6 +430,7 @@ __global__ void __launch_bounds__(kThreads, 1) tconv_kernel(const __grid_constan
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[buf]);
       buf ^= 1;
+    }
     }
   }
 
@@ -612,6 +694,7 @@ struct TPlan {
   long long tiles;
   int nbox, box_c0[kMaxBoxes], box_ab[kMaxBoxes], box_ks[kMaxBoxes];
   int bpst, spt, nstages, ntask, ncol, ncol_real, b_bytes, tmem_cols, smem;
+  int stg_blk;  // forward TMA-store staging per (a, b) block (0: per-thread stores)
 };
 
 // mode 0: forward (A = x, N = 8*Cout), 1: dX (A = dY gathered per (a, b), N = Cin).
@@ -652,9 +735,20 @@ bool make_plan(int mode, int n, int d, int h, int w, int cin, int cout, TPlan* o
   p.nwt = (w + p.wt - 1) / p.wt;
   p.nyb = (h + p.R - 1) / p.R;
   p.tiles = (long long)n * d * p.nyb * p.nwt;
+  // forward: stage the output through two [blocks][positions][2*Cout] tiles
+  // stored by TMA when the task's columns are whole (a, b) blocks
+  // (R4C_TCONV_STG=0 keeps per-thread stores)
+  p.stg_blk = 0;
+  {
+    const char* ev = getenv("R4C_TCONV_STG");
+    if (mode == 0 && p.ncol % (2 * cout) == 0 && (8 * cout) % p.ncol == 0 && 2 * cout <= 256 &&
+        !(ev && ev[0] == '0'))
+      p.stg_blk = (p.R * p.wt * 2 * cout * 2 + 127) / 128 * 128;
+  }
+  const int stg_total = p.stg_blk ? 2 * (p.ncol / (2 * cout)) * p.stg_blk : 0;
   // stages of up to 4 boxes (64 KB) balanced over the tile: the largest
   // that leaves three stages (else two) beside the resident weights
-  const int avail = kSmemMax - kHeader - (p.b_bytes + 1023) / 1024 * 1024;
+  const int avail = kSmemMax - kHeader - (p.b_bytes + 1023) / 1024 * 1024 - stg_total;
   p.nstages = 0;
   for (int need = 3; need >= 2 && p.nstages == 0; --need) {
     for (int bp = std::min(4, p.nbox); bp >= 1; --bp) {
@@ -670,7 +764,7 @@ bool make_plan(int mode, int n, int d, int h, int w, int cin, int cout, TPlan* o
     }
   }
   if (p.nstages < 2) return false;
-  p.smem = kHeader + (p.b_bytes + 1023) / 1024 * 1024 + p.nstages * p.bpst * kBoxBytes;
+  p.smem = kHeader + (p.b_bytes + 1023) / 1024 * 1024 + p.nstages * p.bpst * kBoxBytes + stg_total;
   int alloc = 32;
   while (alloc < 2 * p.ncol) alloc *= 2;
   if (alloc > 512) return false;
@@ -762,9 +856,9 @@ int describe(int mode, int n, int d, int h, int w, int cin, int cout, char* buf,
   if (!make_plan(mode, n, d, h, w, cin, cout, &p)) return snprintf(buf, len, "tcgen05 tconv: no plan");
   return snprintf(buf, len,
                   "tcgen05 tconv %s (k2s2 as one GEMM over input positions): tile=%dx%d boxes=%d (%d per stage) "
-                  "stages=%d tasks=%d N/task=%d B/task=%dB smem=%dB tmem=%d tiles=%lld",
+                  "stages=%d tasks=%d N/task=%d B/task=%dB smem=%dB tmem=%d tiles=%lld%s",
                   mode == 0 ? "fwd" : "dX", p.R, p.wt, p.nbox, p.bpst, p.nstages, p.ntask, p.ncol, p.b_bytes,
-                  p.smem, p.tmem_cols, p.tiles);
+                  p.smem, p.tmem_cols, p.tiles, p.stg_blk ? " TMA-store epilogue" : "");
 }
 
 cudaError_t pack_weight(int mode, int n, int d, int h, int w, int cin, int cout, const void* w_src, int src_dtype,
@@ -839,6 +933,18 @@ int launch(int mode, int n, int d, int h, int w, int cin, int cout, const void* 
   a.ntask = p.ntask; a.ncol = p.ncol; a.ncol_real = p.ncol_real;
   a.b_bytes = p.b_bytes; a.tmem_cols = p.tmem_cols;
   a.idesc = instr_desc_f16(dtype == R4C_BF16, 128, p.ncol, 0, 0);
+  if (p.stg_blk) {
+    // output (N, 2D, 2H, 2W, Cout) as (2*Cout, W, 2, H, 2D*N), box (2*Cout, wt, 1, R, 1)
+    const cuuint64_t c2 = 2ull * cout, row = 2ull * w * cout * e;
+    cuuint64_t dd[5] = {c2, (cuuint64_t)w, 2, (cuuint64_t)h, 2ull * d * n};
+    cuuint64_t ss[4] = {c2 * e, row, 2 * row, 2 * row * h};
+    cuuint32_t bb[5] = {(cuuint32_t)c2, (cuuint32_t)p.wt, 1, (cuuint32_t)p.R, 1};
+    if (enc(&a.ymap, dtype == R4C_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5, out,
+            dd, ss, bb, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return R4C_ERR_INVALID;
+    a.stg_blk = p.stg_blk;
+  }
   // CTAs per task: the SMs shared out, at most one per tile
   const long long cpt = std::max<long long>(1, std::min<long long>(p.tiles, sm_count() / p.ntask));
   const int grid = (int)(cpt * p.ntask);

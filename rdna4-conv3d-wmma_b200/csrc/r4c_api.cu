@@ -535,8 +535,10 @@ int r4c_tconv_dw(const r4c_conv_desc* desc, const void* x, const void* go, float
     const size_t pb = tconv::dw_workspace(g.n, g.d, g.h, g.w, g.cin, g.cout);
     if (!workspace || ws_bytes < pb + L.db_bytes) return R4C_ERR_WORKSPACE;
     if (!x || !go) return R4C_ERR_INVALID;
-    int rc = tconv::launch_dw(g.n, g.d, g.h, g.w, g.cin, g.cout, x, go, dw, workspace, pb, desc->dtype, s);
-    if (rc != R4C_OK || !db) return rc;
+    bool db_done = false;
+    int rc = tconv::launch_dw(g.n, g.d, g.h, g.w, g.cin, g.cout, x, go, dw, db, workspace, pb, desc->dtype, s,
+                              &db_done);
+    if (rc != R4C_OK || !db || db_done) return rc;
     float* part = reinterpret_cast<float*>(static_cast<char*>(workspace) + pb);
     return cuda_status(generic::launch_db(go, 8 * g.in_vox(), g.cout, desc->dtype, part, db, s));
   }

@@ -153,8 +153,9 @@ int launch(int mode, int n, int d, int h, int w, int cin, int cout, const void* 
 bool dw_supported(int n, int d, int h, int w, int cin, int cout);
 size_t dw_workspace(int n, int d, int h, int w, int cin, int cout);
 int dw_describe(int n, int d, int h, int w, int cin, int cout, char* buf, size_t len);
-int launch_dw(int n, int d, int h, int w, int cin, int cout, const void* x, const void* go, float* dw, void* ws,
-              size_t ws_bytes, int dtype, cudaStream_t st);
+// db (nullable) is produced here when Cin <= 64 (*db_done set).
+int launch_dw(int n, int d, int h, int w, int cin, int cout, const void* x, const void* go, float* dw, float* db,
+              void* ws, size_t ws_bytes, int dtype, cudaStream_t st, bool* db_done);
 }  // namespace tconv
 
 }  // namespace r4c

@@ -465,6 +465,11 @@ struct DwTArgs {
   long long tiles;   // K tiles of 64 positions
   int S, ntask, nabg, nab, ngb, ncol, nmma, mma_n;
   int nbox;          // boxes per stage: 2 (x) + nab * ngb (dY)
+  // Cin <= 64 and db wanted: the second x box (channels 64..127, all zero
+  // fill) is not loaded; each stage holds instead a constant box whose
+  // channel 64 is 1 at every position, so D row 64 is the sum of dY (db)
+  int ones;
+  uint32_t one_bits;  // 1.0 in the element type
   int nstages;
   int tmem_cols;
   uint32_t idesc;
@@ -506,6 +511,17 @@ __global__ void __launch_bounds__(kThreads, 1) tconv_dw_kernel(const __grid_cons
     tmem_alloc(tmem_slot, (uint32_t)a.tmem_cols);
     tmem_relinquish();
   }
+  if (a.ones) {
+    // the constant ones box of every stage, in the 128-byte swizzled layout
+    // of a TMA box: chunk 0 (channels 64..71) of row p sits at chunk p % 8
+    for (int i = threadIdx.x; i < a.nstages * (kDwBox / 16); i += kThreads) {
+      const int s = i / (kDwBox / 16), k = i - s * (kDwBox / 16);
+      const int p = k >> 3, c = k & 7;
+      *reinterpret_cast<uint4*>(st0 + (size_t)s * stage_bytes + kDwBox + (size_t)k * 16) =
+          make_uint4(c == (p & 7) ? a.one_bits : 0u, 0u, 0u, 0u);
+    }
+    fence_proxy_async_smem();  // generic writes -> visible to the tensor core
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -537,7 +553,7 @@ __global__ void __launch_bounds__(kThreads, 1) tconv_dw_kernel(const __grid_cons
     if (lane == 0) {
       prefetch_tmap(&a.xmap);
       prefetch_tmap(&a.gmap);
-      const uint32_t tx = (uint32_t)(a.nbox * 128 * a.R * a.wt);
+      const uint32_t tx = (uint32_t)((a.nbox - (a.ones ? 1 : 0)) * 128 * a.R * a.wt);
       int s = 0;
       uint32_t epar = 1u, pending = 0u, last_par = 0u;
       for (long long t = t0; t < t1; ++t) {
@@ -551,7 +567,7 @@ __global__ void __launch_bounds__(kThreads, 1) tconv_dw_kernel(const __grid_cons
         mbar_arrive_expect_tx(&full[s], tx);
         uint8_t* dst = st0 + (size_t)s * stage_bytes;
         tma_load_5d(dst, &a.xmap, &full[s], 128 * mt, x0, y0, z, nb);
-        tma_load_5d(dst + kDwBox, &a.xmap, &full[s], 128 * mt + 64, x0, y0, z, nb);
+        if (!a.ones) tma_load_5d(dst + kDwBox, &a.xmap, &full[s], 128 * mt + 64, x0, y0, z, nb);
         int j = 2;
         for (int ab = abg * a.nab; ab < (abg + 1) * a.nab; ++ab)
           for (int g = 0; g < a.ngb; ++g, ++j)
@@ -631,6 +647,29 @@ __global__ void __launch_bounds__(kThreads, 1) tconv_dw_kernel(const __grid_cons
     tc_fence_after();
     tmem_dealloc(tmem, (uint32_t)a.tmem_cols);
   }
+}
+
+// db[co] from the ones row 64 of the partials: a block covers 32 outputs with
+// 8 lanes each; lane j adds, over (a, b, c) in order, splits j, j+8, ...; the
+// lane sums are added in a fixed tree (deterministic).
+__global__ void __launch_bounds__(256) tconv_db_reduce(const float* __restrict__ part, float* __restrict__ db,
+                                                       int cout, int S, int nab, int ngb, int ncol) {
+  __shared__ float red[8][33];
+  const int o = threadIdx.x & 31, lj = threadIdx.x >> 5;
+  const int co = blockIdx.x * 32 + o;
+  float acc = 0.f;
+  if (co < cout) {
+    for (int ab = 0; ab < 4; ++ab)
+      for (int c = 0; c < 2; ++c) {
+        const float* p = part + ((size_t)(ab / nab) * S * 128 + 64) * ncol + (ab % nab) * ngb * 64 + c * cout + co;
+#pragma unroll 4
+        for (int s = lj; s < S; s += 8) acc += p[(size_t)s * 128 * ncol];
+      }
+  }
+  red[lj][o] = acc;
+  __syncthreads();
+  if (lj == 0 && co < cout)
+    db[co] = ((red[0][o] + red[1][o]) + (red[2][o] + red[3][o])) + ((red[4][o] + red[5][o]) + (red[6][o] + red[7][o]));
 }
 
 // dw[ci][co][a][b][c] (fp32, PyTorch ConvTranspose3d layout) = sum over the
@@ -1029,8 +1068,9 @@ int dw_describe(int n, int d, int h, int w, int cin, int cout, char* buf, size_t
 }
 
 // x (NDHWC, Cin), go (NDHWC at 2x, Cout) -> dw fp32 (Cin, Cout, 2, 2, 2); ws >= dw_workspace().
-int launch_dw(int n, int d, int h, int w, int cin, int cout, const void* x, const void* go, float* dw, void* ws,
-              size_t ws_bytes, int dtype, cudaStream_t st) {
+int launch_dw(int n, int d, int h, int w, int cin, int cout, const void* x, const void* go, float* dw, float* db,
+              void* ws, size_t ws_bytes, int dtype, cudaStream_t st, bool* db_done) {
+  if (db_done) *db_done = false;
   DwTPlan p;
   if (!make_dw_plan(n, d, h, w, cin, cout, sm_count(), &p)) return R4C_ERR_UNSUPPORTED;
   if (((uintptr_t)x & 15) || ((uintptr_t)go & 15)) return R4C_ERR_ALIGN;
@@ -1071,6 +1111,8 @@ int launch_dw(int n, int d, int h, int w, int cin, int cout, const void* x, cons
   a.ncol = p.ncol; a.nmma = p.nmma; a.mma_n = p.mma_n; a.nbox = p.nbox; a.nstages = p.nstages;
   a.tmem_cols = p.tmem_cols;
   a.idesc = instr_desc_f16(dtype == R4C_BF16, 128, p.mma_n, 1, 1);
+  a.ones = (db != nullptr && cin <= 64) ? 1 : 0;
+  a.one_bits = dtype == R4C_BF16 ? 0x3F80u : 0x3C00u;
   static bool done[64] = {false};
   static std::mutex mu;
   int dev = 0;
@@ -1091,6 +1133,11 @@ int launch_dw(int n, int d, int h, int w, int cin, int cout, const void* x, cons
   tconv_dw_reduce<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(a.part, dw, cin, cout, p.S, p.nabg, p.nab, p.ngb,
                                                                    p.ncol);
   note_launches(1);
+  if (a.ones) {
+    tconv_db_reduce<<<(unsigned)((cout + 31) / 32), 256, 0, st>>>(a.part, db, cout, p.S, p.nab, p.ngb, p.ncol);
+    note_launches(1);
+    if (db_done) *db_done = true;
+  }
   return cudaGetLastError() == cudaSuccess ? R4C_OK : R4C_ERR_CUDA;
 }
 

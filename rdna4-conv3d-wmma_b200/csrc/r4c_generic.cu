@@ -364,15 +364,24 @@ __global__ void __launch_bounds__(256) db_partial_vec_kernel(const T* __restrict
   }
 }
 
-__global__ void db_reduce_kernel(const float* __restrict__ part, int S, int C, float* __restrict__ db) {
-  int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= C) return;
+// A block covers 32 channels with 8 lanes each: lane j adds splits j, j+8,
+// ... in order and the eight lane sums meet in a fixed tree (deterministic).
+// One thread per channel walking all splits was a chain of ~40 dependent L2
+// round trips even with eight loads in flight.
+__global__ void __launch_bounds__(256) db_reduce_kernel(const float* __restrict__ part, int S, int C,
+                                                        float* __restrict__ db) {
+  __shared__ float red[8][33];
+  const int o = threadIdx.x & 31, lj = threadIdx.x >> 5;
+  const int c = blockIdx.x * 32 + o;
   float sum = 0.f;
-  // in split order; the unroll keeps eight loads in flight (one at a time
-  // made this a chain of ~300 dependent L2 round trips)
-#pragma unroll 8
-  for (int s = 0; s < S; ++s) sum += part[(int64_t)s * C + c];
-  db[c] = sum;
+  if (c < C) {
+#pragma unroll 4
+    for (int s = lj; s < S; s += 8) sum += part[(int64_t)s * C + c];
+  }
+  red[lj][o] = sum;
+  __syncthreads();
+  if (lj == 0 && c < C)
+    db[c] = ((red[0][o] + red[1][o]) + (red[2][o] + red[3][o])) + ((red[4][o] + red[5][o]) + (red[6][o] + red[7][o]));
 }
 
 // ---------------------------------------------------------------------------
@@ -459,7 +468,7 @@ cudaError_t launch_db(const void* go, int64_t V, int C, int dtype, float* part, 
     db_partial_kernel<__half><<<S, NT, 0, st>>>(static_cast<const __half*>(go), V, C, chunk, part);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  db_reduce_kernel<<<cdiv(C, 256), 256, 0, st>>>(part, S, C, db);
+  db_reduce_kernel<<<cdiv(C, 32), 256, 0, st>>>(part, S, C, db);
   note_launches(2);
   return cudaGetLastError();
 }

@@ -80,6 +80,11 @@ struct alignas(64) DwArgs {
   // input rows; one MMA of N = 3 nn per (M tile, K step)
   int fold;
   int row_bytes;  // one output row's slot in a stage (stage_bytes / rows per stage)
+  // k = 1 wide layout with two atoms per M tile: the ones (db) atom is one
+  // plane shared by every stage and row slot, at this byte offset from the
+  // first stage (0: the per-row ones plane of the stage layout); each row's
+  // A descriptor reaches it through its own LBO (shared plane - x plane)
+  int ones_off;
 };
 
 struct Task {
@@ -91,7 +96,8 @@ struct DwPlan {
   bool ok;
   bool wide;
   bool fold;
-  int rpst;  // output rows per stage (wide layout: 2 when a row's boxes are under 32 KB)
+  int rpst;  // output rows per stage (wide layout: 2 or 4 when a row's boxes are under 32 KB)
+  int ones_bytes;  // the shared ones plane (k = 1 wide layout), 0 when the stages hold it
   int cw, apt, tpg, ng, plane_bytes, region_bytes, cwb, nbox, npad_w, tail_bytes;
   int n, d, h, w, od, oh, ow, cin, cout, ks, pd, ph, pw;
   int c8, groups, mtiles, pitch_w, kpad, wt, nwt;
@@ -351,14 +357,25 @@ static bool plan_dw(int n, int d, int h, int w, int cin, int cout, int ks, int p
     const int pitch_ww = round_up(kpad_w + ks - 1, 8);
     const long long rows_w = (long long)n * P.od * P.oh * nwt_w;
     const int plane = pitch_ww * cw * 2;
-    const int region = round_up(atoms * plane, 1024);
+    // k = 1, two atoms per tile: the x plane alone per row, one ones plane
+    // for the whole ring (its own LBO per row slot)
+    const bool shared = ks == 1 && apt == 2;
+    const int ones_b = shared ? round_up(plane, 1024) : 0;
+    const int region = round_up((shared ? 1 : atoms) * plane, 1024);
     const int tail = (tpg * apt - atoms) * plane + 1024;
     for (int kwn : {1}) {  // one kw per task: keeps the wide issue code (runtime steps) small
       for (int nn = cout; nn >= 8; nn -= 8) {
         if (cout % nn) continue;
         // dY boxes of cwb channels, the last padded (channels past nn are
         // computed and dropped, past Cout zero-filled); MMA N = the boxes
-        const int cwb = nn % 64 == 0 ? 64 : nn % 32 == 0 ? 32 : nn % 16 == 0 ? 16 : nn <= 16 ? 16 : nn <= 32 ? 32 : 64;
+        const int cwb0 = nn % 64 == 0 ? 64 : nn % 32 == 0 ? 32 : nn % 16 == 0 ? 16 : nn <= 16 ? 16 : nn <= 32 ? 32 : 64;
+        // k = 1: 64-channel boxes first when they mean fewer boxes (fewer,
+        // longer TMA rows, so they win ties: a TMA box row costs ~5 clk
+        // whatever its length up to 128 B, measured on the k1 dW rows of
+        // 32-96 bytes)
+       const bool fewer = ks == 1 && (nn + 63) / 64 < (nn + cwb0 - 1) / cwb0;  // 64-channel boxes save boxes
+       for (int cwb : {fewer ? 64 : cwb0, fewer ? cwb0 : 0}) {
+        if (cwb == 0) continue;
         const int nbox = (nn + cwb - 1) / cwb;
         const int npad = round_up(nbox * cwb, 16);
         if (npad > 256) continue;
@@ -371,7 +388,7 @@ static bool plan_dw(int n, int d, int h, int w, int cin, int cout, int ks, int p
           const int ntasks = ng * ((tpg + mtn - 1) / mtn) * (cout / nn) * (ks / kwn);
           if (ntasks > 128) continue;
           const int stage = region + round_up(nbox * cwb * kpad_w * 2, 1024);
-          const int stages = std::min(kMaxStages, (kSmemMax - kHeader - tail_nn) / stage);
+          const int stages = std::min(kMaxStages, (kSmemMax - kHeader - round_up(tail_nn, 1024) - ones_b) / stage);
           if (stages < 2) continue;
           const double t_mma = dw_mma_clk(npad);
           const double mma = (double)(kpad_w / 16) * kwn * mtn * t_mma;
@@ -392,7 +409,8 @@ static bool plan_dw(int n, int d, int h, int w, int cin, int cout, int ks, int p
             P.mtn = mtn; P.nn = nn; P.kwn = kwn;
             P.S = S; P.rows_per_split = rps;
             P.stages = stages; P.stage_bytes = stage;
-            P.smem_bytes = kHeader + stages * stage + tail_nn;
+            P.ones_bytes = ones_b;
+            P.smem_bytes = kHeader + stages * stage + round_up(tail_nn, 1024) + ones_b;
             int alloc = 32;
             while (alloc < cols) alloc *= 2;
             P.tmem_cols = alloc;
@@ -401,25 +419,33 @@ static bool plan_dw(int n, int d, int h, int w, int cin, int cout, int ks, int p
             P.ok = true;
           }
         }
+       }
       }
     }
   }
   if (!P.ok) return false;
-  // Two output rows per stage in the wide layout when a row's boxes move less
-  // than 32 KB: the TMA's throughput per SM is set by the bytes of each
-  // mbarrier transaction (~0.55 us per transaction below ~32 KB). k1 layers
-  // (16-24 KB per row) are the ones this reaches. R4C_DW_ROWS=1 keeps one.
+  // Two or four output rows per stage in the wide layout when a row's boxes
+  // move less than 32 KB: the TMA's throughput per SM is set by the bytes of
+  // each mbarrier transaction (~0.55 us per transaction below ~32 KB). k1
+  // layers (10-24 KB per row) are the ones this reaches: four rows while a
+  // stage stays within 64 KB and three stages fit. R4C_DW_ROWS=1 keeps one.
   P.rpst = 1;
+  if (!P.wide) P.ones_bytes = 0;
   {
     const char* re = getenv("R4C_DW_ROWS");
     if (P.wide && P.stage_bytes < 32768 && !(re && re[0] == '1')) {
       const int row = P.stage_bytes;
-      const int st2 = std::min(kMaxStages, (kSmemMax - kHeader - P.tail_bytes) / (2 * row));
-      if (st2 >= 3) {
-        P.rpst = 2;
-        P.stage_bytes = 2 * row;
-        P.stages = st2;
-        P.smem_bytes = kHeader + st2 * 2 * row + P.tail_bytes;
+      const int fixed = kHeader + round_up(P.tail_bytes, 1024) + P.ones_bytes;
+      for (int r : {4, 2}) {
+        if (r == 4 && (4 * row > 65536 || (re && re[0] == '2'))) continue;
+        const int st = std::min(kMaxStages, (kSmemMax - fixed) / (r * row));
+        if (st >= 3) {
+          P.rpst = r;
+          P.stage_bytes = r * row;
+          P.stages = st;
+          P.smem_bytes = fixed + st * r * row;
+          break;
+        }
       }
     }
   }
@@ -558,12 +584,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   // zero the whole dynamic region (finite junk rows), then the ones rows
   {
-    const int total = a.stages * a.stage_bytes + ((a.wide || FOLD) ? a.tail_bytes : 16 * mtn * sbo_a + 256);
+    const int total = a.ones_off ? a.ones_off + a.plane_bytes
+                                 : a.stages * a.stage_bytes + ((a.wide || FOLD) ? a.tail_bytes : 16 * mtn * sbo_a + 256);
     uint4 z = make_uint4(0, 0, 0, 0);
     for (int i = threadIdx.x * 16; i < total; i += kThreads * 16) *reinterpret_cast<uint4*>(stage0 + i) = z;
     __syncthreads();
     if (a.wide) {
-      if (grp == 0 && a.dbpart != nullptr)
+      if (grp == 0 && a.dbpart != nullptr && a.ones_off) {
+        uint32_t* o = reinterpret_cast<uint32_t*>(stage0 + a.ones_off);
+        for (int i = threadIdx.x; i < a.plane_bytes / 4; i += kThreads) o[i] = OneBits<T>::v;
+      } else if (grp == 0 && a.dbpart != nullptr)
         for (int s = 0; s < a.stages * RPS; ++s) {
           uint32_t* o = reinterpret_cast<uint32_t*>(stage0 + (size_t)(s / RPS) * a.stage_bytes +
                                                     (size_t)(s % RPS) * a.row_bytes + (size_t)k2 * a.plane_bytes);
@@ -696,8 +726,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint64_t a0, b0;
         if (a.wide) {
           // swizzled MN-major: LBO = MN atom stride, SBO = 8-position K group
-          a0 = desc_layout(sA + (uint32_t)(mt0 * a.apt * a.plane_bytes) + (uint32_t)(kw0 * a.cw * 2),
-                           (uint32_t)a.plane_bytes, (uint32_t)(16 * a.cw), (uint32_t)a.lay_a);
+          const uint32_t xa = sA + (uint32_t)(mt0 * a.apt * a.plane_bytes) + (uint32_t)(kw0 * a.cw * 2);
+          const uint32_t lbo = a.ones_off ? smem_u32(stage0) + (uint32_t)a.ones_off - xa : (uint32_t)a.plane_bytes;
+          a0 = desc_layout(xa, lbo, (uint32_t)(16 * a.cw), (uint32_t)a.lay_a);
           b0 = a.cwb > 8 ? desc_layout(sA + (uint32_t)a.a_bytes, (uint32_t)a.b_region, (uint32_t)(16 * a.cwb),
                                        (uint32_t)a.lay_b)
                          : smem_desc(sA + (uint32_t)a.a_bytes, 128, (uint32_t)(a.kpad * 16));
@@ -978,6 +1009,7 @@ int launch_dw(int n, int d, int h, int w, int cin, int cin_real, int cout, int k
     a.nbox = P.nbox; a.npad_w = P.npad_w;
     a.a_bytes = P.region_bytes;
     a.tail_bytes = P.tail_bytes;
+    a.ones_off = P.ones_bytes ? P.stages * P.stage_bytes + round_up(P.tail_bytes, 1024) : 0;
     a.ones_group = -1;
   }
   a.tmem_cols = P.tmem_cols;
@@ -994,13 +1026,18 @@ int launch_dw(int n, int d, int h, int w, int cin, int cin_real, int cout, int k
   }
   const unsigned grid = (unsigned)(P.tasks.size() * P.S);
   cudaError_t e;
-  // instantiations: chunk / wide (one row per stage), fold, wide with two rows per stage
+  // instantiations: chunk / wide (one row per stage), fold, wide with two or four rows per stage
   const bool bf = dtype == R4C_BF16;
   if (P.fold) {
     e = bf ? set_attr<__nv_bfloat16, true, 1>() : set_attr<__half, true, 1>();
     if (e != cudaSuccess) return R4C_ERR_CUDA;
     if (bf) tc_dw_kernel<__nv_bfloat16, true, 1><<<grid, kThreads, P.smem_bytes, st>>>(a, tt);
     else tc_dw_kernel<__half, true, 1><<<grid, kThreads, P.smem_bytes, st>>>(a, tt);
+  } else if (P.rpst == 4) {
+    e = bf ? set_attr<__nv_bfloat16, false, 4>() : set_attr<__half, false, 4>();
+    if (e != cudaSuccess) return R4C_ERR_CUDA;
+    if (bf) tc_dw_kernel<__nv_bfloat16, false, 4><<<grid, kThreads, P.smem_bytes, st>>>(a, tt);
+    else tc_dw_kernel<__half, false, 4><<<grid, kThreads, P.smem_bytes, st>>>(a, tt);
   } else if (P.rpst == 2) {
     e = bf ? set_attr<__nv_bfloat16, false, 2>() : set_attr<__half, false, 2>();
     if (e != cudaSuccess) return R4C_ERR_CUDA;

@@ -465,10 +465,11 @@ struct DwTArgs {
   long long tiles;   // K tiles of 64 positions
   int S, ntask, nabg, nab, ngb, ncol, nmma, mma_n;
   int nbox;          // boxes per stage: 2 (x) + nab * ngb (dY)
-  // Cin <= 64 and db wanted: the second x box (channels 64..127, all zero
-  // fill) is not loaded; each stage holds instead a constant box whose
-  // channel 64 is 1 at every position, so D row 64 is the sum of dY (db)
-  int ones;
+  // db wanted and the last M tile (ones_mt) holds at most 64 channels: its
+  // tasks do not load the second x box (channels 64..127 of the tile, all
+  // zero fill); each stage holds instead a constant box whose channel 64 is
+  // 1 at every position, so D row 64 of those tasks is the sum of dY (db)
+  int ones, ones_mt;
   uint32_t one_bits;  // 1.0 in the element type
   int nstages;
   int tmem_cols;
@@ -497,6 +498,7 @@ __global__ void __launch_bounds__(kThreads, 1) tconv_dw_kernel(const __grid_cons
   const int split = (int)blockIdx.x - task * a.S;
   const int mt = task / a.nabg, abg = task - mt * a.nabg;
   const long long t0 = a.tiles * split / a.S, t1 = a.tiles * (split + 1) / a.S;
+  const bool ones = a.ones && mt == a.ones_mt;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kMaxStages; ++s) {
@@ -511,7 +513,7 @@ __global__ void __launch_bounds__(kThreads, 1) tconv_dw_kernel(const __grid_cons
     tmem_alloc(tmem_slot, (uint32_t)a.tmem_cols);
     tmem_relinquish();
   }
-  if (a.ones) {
+  if (ones) {
     // the constant ones box of every stage, in the 128-byte swizzled layout
     // of a TMA box: chunk 0 (channels 64..71) of row p sits at chunk p % 8
     for (int i = threadIdx.x; i < a.nstages * (kDwBox / 16); i += kThreads) {
@@ -553,7 +555,7 @@ __global__ void __launch_bounds__(kThreads, 1) tconv_dw_kernel(const __grid_cons
     if (lane == 0) {
       prefetch_tmap(&a.xmap);
       prefetch_tmap(&a.gmap);
-      const uint32_t tx = (uint32_t)((a.nbox - (a.ones ? 1 : 0)) * 128 * a.R * a.wt);
+      const uint32_t tx = (uint32_t)((a.nbox - (ones ? 1 : 0)) * 128 * a.R * a.wt);
       int s = 0;
       uint32_t epar = 1u, pending = 0u, last_par = 0u;
       for (long long t = t0; t < t1; ++t) {
@@ -567,7 +569,7 @@ __global__ void __launch_bounds__(kThreads, 1) tconv_dw_kernel(const __grid_cons
         mbar_arrive_expect_tx(&full[s], tx);
         uint8_t* dst = st0 + (size_t)s * stage_bytes;
         tma_load_5d(dst, &a.xmap, &full[s], 128 * mt, x0, y0, z, nb);
-        if (!a.ones) tma_load_5d(dst + kDwBox, &a.xmap, &full[s], 128 * mt + 64, x0, y0, z, nb);
+        if (!ones) tma_load_5d(dst + kDwBox, &a.xmap, &full[s], 128 * mt + 64, x0, y0, z, nb);
         int j = 2;
         for (int ab = abg * a.nab; ab < (abg + 1) * a.nab; ++ab)
           for (int g = 0; g < a.ngb; ++g, ++j)
@@ -649,11 +651,12 @@ __global__ void __launch_bounds__(kThreads, 1) tconv_dw_kernel(const __grid_cons
   }
 }
 
-// db[co] from the ones row 64 of the partials: a block covers 32 outputs with
-// 8 lanes each; lane j adds, over (a, b, c) in order, splits j, j+8, ...; the
-// lane sums are added in a fixed tree (deterministic).
+// db[co] from the ones row 64 of the partials of the M tile mt: a block
+// covers 32 outputs with 8 lanes each; lane j adds, over (a, b, c) in order,
+// splits j, j+8, ...; the lane sums are added in a fixed tree (deterministic).
 __global__ void __launch_bounds__(256) tconv_db_reduce(const float* __restrict__ part, float* __restrict__ db,
-                                                       int cout, int S, int nab, int ngb, int ncol) {
+                                                       int cout, int S, int mt, int nabg, int nab, int ngb,
+                                                       int ncol) {
   __shared__ float red[8][33];
   const int o = threadIdx.x & 31, lj = threadIdx.x >> 5;
   const int co = blockIdx.x * 32 + o;
@@ -661,7 +664,7 @@ __global__ void __launch_bounds__(256) tconv_db_reduce(const float* __restrict__
   if (co < cout) {
     for (int ab = 0; ab < 4; ++ab)
       for (int c = 0; c < 2; ++c) {
-        const float* p = part + ((size_t)(ab / nab) * S * 128 + 64) * ncol + (ab % nab) * ngb * 64 + c * cout + co;
+        const float* p = part + ((size_t)(mt * nabg + ab / nab) * S * 128 + 64) * ncol + (ab % nab) * ngb * 64 + c * cout + co;
 #pragma unroll 4
         for (int s = lj; s < S; s += 8) acc += p[(size_t)s * 128 * ncol];
       }
@@ -1111,7 +1114,8 @@ int launch_dw(int n, int d, int h, int w, int cin, int cout, const void* x, cons
   a.ncol = p.ncol; a.nmma = p.nmma; a.mma_n = p.mma_n; a.nbox = p.nbox; a.nstages = p.nstages;
   a.tmem_cols = p.tmem_cols;
   a.idesc = instr_desc_f16(dtype == R4C_BF16, 128, p.mma_n, 1, 1);
-  a.ones = (db != nullptr && cin <= 64) ? 1 : 0;
+  a.ones_mt = (cin - 1) / 128;
+  a.ones = (db != nullptr && cin - 128 * a.ones_mt <= 64) ? 1 : 0;
   a.one_bits = dtype == R4C_BF16 ? 0x3F80u : 0x3C00u;
   static bool done[64] = {false};
   static std::mutex mu;
@@ -1134,7 +1138,8 @@ int launch_dw(int n, int d, int h, int w, int cin, int cout, const void* x, cons
                                                                    p.ncol);
   note_launches(1);
   if (a.ones) {
-    tconv_db_reduce<<<(unsigned)((cout + 31) / 32), 256, 0, st>>>(a.part, db, cout, p.S, p.nab, p.ngb, p.ncol);
+    tconv_db_reduce<<<(unsigned)((cout + 31) / 32), 256, 0, st>>>(a.part, db, cout, p.S, a.ones_mt, p.nabg, p.nab,
+                                                                 p.ngb, p.ncol);
     note_launches(1);
     if (db_done) *db_done = true;
   }

@@ -79,6 +79,8 @@ TCONV_CASES = [
     (1, 192, 96, 3, 8, 16),
     (1, 96, 48, 2, 4, 32),
     (1, 24, 40, 2, 3, 7),
+    # last M tile of 8 channels: db from the dW kernel's ones row there
+    (1, 136, 16, 2, 3, 8),
 ]
 
 

@@ -470,6 +470,11 @@ struct DwTArgs {
   // zero fill); each stage holds instead a constant box whose channel 64 is
   // 1 at every position, so D row 64 of those tasks is the sum of dY (db)
   int ones, ones_mt;
+  // db wanted and that tile holds 72..120 channels (a multiple of 8): the
+  // MMA warp writes, once a stage's boxes have landed, a 1 into channel
+  // ones_row of every position (the first chunk of the second x box's zero
+  // fill), so D row ones_row of those tasks is the sum of dY (db)
+  int ones_fill, ones_row;
   uint32_t one_bits;  // 1.0 in the element type
   int nstages;
   int tmem_cols;
@@ -499,6 +504,7 @@ __global__ void __launch_bounds__(kThreads, 1) tconv_dw_kernel(const __grid_cons
   const int mt = task / a.nabg, abg = task - mt * a.nabg;
   const long long t0 = a.tiles * split / a.S, t1 = a.tiles * (split + 1) / a.S;
   const bool ones = a.ones && mt == a.ones_mt;
+  const bool fill = a.ones_fill && mt == a.ones_mt;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kMaxStages; ++s) {
@@ -601,6 +607,15 @@ __global__ void __launch_bounds__(kThreads, 1) tconv_dw_kernel(const __grid_cons
       if (lane == 0) okk = wait(&full[s], fpar) ? 1 : 0;
       if (!__shfl_sync(0xffffffffu, okk, 0)) break;
       tc_fence_after();
+      if (fill) {
+        // generic stores into the zero fill, made visible to the tensor core
+        uint8_t* b2 = st0 + (size_t)s * stage_bytes + kDwBox;
+        const int ch = (a.ones_row - 64) >> 3;
+        for (int p = lane; p < 64; p += 32)
+          *reinterpret_cast<uint4*>(b2 + p * 128 + ((ch ^ (p & 7)) << 4)) = make_uint4(a.one_bits, 0u, 0u, 0u);
+        fence_proxy_async_smem();
+        __syncwarp();
+      }
       const uint32_t sa = smem_u32(st0 + (size_t)s * stage_bytes);
       const uint64_t ad = mn_desc(sa);
       const uint64_t bd = mn_desc(sa + 2u * kDwBox);
@@ -651,12 +666,12 @@ __global__ void __launch_bounds__(kThreads, 1) tconv_dw_kernel(const __grid_cons
   }
 }
 
-// db[co] from the ones row 64 of the partials of the M tile mt: a block
+// db[co] from the ones row of the partials of the M tile mt: a block
 // covers 32 outputs with 8 lanes each; lane j adds, over (a, b, c) in order,
 // splits j, j+8, ...; the lane sums are added in a fixed tree (deterministic).
 __global__ void __launch_bounds__(256) tconv_db_reduce(const float* __restrict__ part, float* __restrict__ db,
-                                                       int cout, int S, int mt, int nabg, int nab, int ngb,
-                                                       int ncol) {
+                                                       int cout, int S, int mt, int row, int nabg, int nab,
+                                                       int ngb, int ncol) {
   __shared__ float red[8][33];
   const int o = threadIdx.x & 31, lj = threadIdx.x >> 5;
   const int co = blockIdx.x * 32 + o;
@@ -664,7 +679,7 @@ __global__ void __launch_bounds__(256) tconv_db_reduce(const float* __restrict__
   if (co < cout) {
     for (int ab = 0; ab < 4; ++ab)
       for (int c = 0; c < 2; ++c) {
-        const float* p = part + ((size_t)(mt * nabg + ab / nab) * S * 128 + 64) * ncol + (ab % nab) * ngb * 64 + c * cout + co;
+        const float* p = part + ((size_t)(mt * nabg + ab / nab) * S * 128 + row) * ncol + (ab % nab) * ngb * 64 + c * cout + co;
 #pragma unroll 4
         for (int s = lj; s < S; s += 8) acc += p[(size_t)s * 128 * ncol];
       }
@@ -1115,7 +1130,12 @@ int launch_dw(int n, int d, int h, int w, int cin, int cout, const void* x, cons
   a.tmem_cols = p.tmem_cols;
   a.idesc = instr_desc_f16(dtype == R4C_BF16, 128, p.mma_n, 1, 1);
   a.ones_mt = (cin - 1) / 128;
-  a.ones = (db != nullptr && cin - 128 * a.ones_mt <= 64) ? 1 : 0;
+  const int cin_last = cin - 128 * a.ones_mt;
+  a.ones = (db != nullptr && cin_last <= 64) ? 1 : 0;
+  const char* fe = getenv("R4C_TCONV_DBFILL");
+  a.ones_fill = (db != nullptr && cin_last > 64 && cin_last <= 120 && cin_last % 8 == 0 && !(fe && fe[0] == '0'))
+                    ? 1 : 0;
+  a.ones_row = a.ones_fill ? cin_last : 64;
   a.one_bits = dtype == R4C_BF16 ? 0x3F80u : 0x3C00u;
   static bool done[64] = {false};
   static std::mutex mu;
@@ -1137,9 +1157,9 @@ int launch_dw(int n, int d, int h, int w, int cin, int cout, const void* x, cons
   tconv_dw_reduce<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(a.part, dw, cin, cout, p.S, p.nabg, p.nab, p.ngb,
                                                                    p.ncol);
   note_launches(1);
-  if (a.ones) {
-    tconv_db_reduce<<<(unsigned)((cout + 31) / 32), 256, 0, st>>>(a.part, db, cout, p.S, a.ones_mt, p.nabg, p.nab,
-                                                                 p.ngb, p.ncol);
+  if (a.ones || a.ones_fill) {
+    tconv_db_reduce<<<(unsigned)((cout + 31) / 32), 256, 0, st>>>(a.part, db, cout, p.S, a.ones_mt, a.ones_row,
+                                                                 p.nabg, p.nab, p.ngb, p.ncol);
     note_launches(1);
     if (db_done) *db_done = true;
   }

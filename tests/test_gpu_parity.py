@@ -81,6 +81,8 @@ TCONV_CASES = [
     (1, 24, 40, 2, 3, 7),
     # last M tile of 8 channels: db from the dW kernel's ones row there
     (1, 136, 16, 2, 3, 8),
+    # last M tile of 104 channels: db from a 1 written into its zero fill
+    (1, 104, 16, 2, 2, 8),
 ]
 
 

@@ -81,7 +81,7 @@ TCONV_CASES = [
     (1, 24, 40, 2, 3, 7),
     # last M tile of 8 channels: db from the dW kernel's ones row there
     (1, 136, 16, 2, 3, 8),
-    # last M tile of 104 channels: db from a 1 written into its zero fill
+    # last M tile of 104 channels: db from the db kernel by default
     (1, 104, 16, 2, 2, 8),
 ]
 
@@ -209,7 +209,25 @@ def test_tconv_legs_match_oracle(cuda_ready, case, dtype, force, monkeypatch):
     assert O.norm_rel(db, go.float().sum(dim=(0, 2, 3, 4))) <= 1e-4
 
 
-GOLDEN = sorted(glob.glob(os.path.join(GOLDEN_DIR, "*.npz")))
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16], ids=["bf16", "fp16"])
+@pytest.mark.parametrize("case", [(1, 104, 16, 2, 2, 8), (1, 96, 48, 2, 4, 32)], ids=["104x16", "96x48"])
+def test_tconv_dw_db_fill_opt_in(cuda_ready, case, dtype, monkeypatch):
+    """R4C_TCONV_DBFILL=1: db from a 1 written into the zero fill of a last
+    M tile of 72-120 channels, checked against the same oracle as the default."""
+    n, cin, cout, d, h, w = case
+    cw = _cw()
+    monkeypatch.setenv("R4C_TCONV_DBFILL", "1")
+    g = torch.Generator().manual_seed(1)
+    x = torch.randn(n, cin, d, h, w, generator=g).to(dtype)
+    wt = (torch.randn(cin, cout, 2, 2, 2, generator=g) / cin ** 0.5).to(dtype)
+    go = torch.randn(n, cout, 2 * d, 2 * h, 2 * w, generator=g).to(dtype)
+    dw, db = cw.transpose_k2s2_dw(x.cuda(), wt.shape, go.cuda(), True)
+    _, dwr = O.torch_tconv_grads(x, wt, go)
+    assert O.norm_rel(dw.cpu(), dwr) <= 1e-4
+    assert O.norm_rel(db.cpu(), go.float().sum(dim=(0, 2, 3, 4))) <= 1e-4
+
+
+GOLDEN =sorted(glob.glob(os.path.join(GOLDEN_DIR, "*.npz")))
 
 
 @pytest.mark.parametrize("path", GOLDEN, ids=[os.path.basename(p)[:-4] for p in GOLDEN])

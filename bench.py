@@ -346,6 +346,12 @@ def time_tconv(device, steps, warmup, peaks, names=None):
     for _ in range(warmup):
         step()
     torch.cuda.synchronize()
+    # a step is ~0.2 ms: keep warming up for at least 0.25 s so that a fresh
+    # process is timed after the SM clocks have ramped, not during the ramp
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < 0.25:
+        step()
+        torch.cuda.synchronize()
     evs = [[[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in layers] for _ in range(steps)]
     for s_ in range(steps):
         step(evs[s_])

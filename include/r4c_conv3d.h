@@ -18,7 +18,13 @@
  *     allocated inside the library and no state is kept between calls apart
  *     from a per-device cache of kernel attributes.
  *   - Work is enqueued on the given stream and ordered only by it; calls may
- *     come from any host thread.
+ *     come from any host thread. One exception: the first r4c_conv3d_fwd /
+ *     r4c_conv3d_dx call for a new (shape, dtype, device) times a few plan
+ *     candidates on the caller's buffers and synchronizes the stream once to
+ *     read the timings (skipped while the stream is being captured, and with
+ *     the environment variable R4C_AUTOTUNE=0, which takes the modelled plan).
+ *     Results never depend on the plan chosen. Make one call per shape before
+ *     timing or capturing if that synchronization matters.
  *   - Errors are returned as negative status codes; nothing is thrown across
  *     the ABI. r4c_strerror() turns a code into text.
  */
@@ -194,7 +200,10 @@ int r4c_tconv_dw(const r4c_conv_desc* desc, const void* x, const void* go,
  * r4c_workspace_size(desc, R4C_LEG_DW) exceeds that size are rejected with
  * R4C_ERR_TOO_LARGE. The first call on a device looks up the array's device
  * address (cudaGetSymbolAddress) with that device current; make that first
- * call before any stream capture. All calls share the one array: calls whose
+ * call before any stream capture. The address is kept for the life of the
+ * process: a cudaDeviceReset(), or anything else that destroys the device's
+ * primary context, voids it, and this entry point must not be called on that
+ * device afterwards. All calls share the one array: calls whose
  * work overlaps on the GPU (different streams, or different host threads)
  * race on it and must be serialized by the caller. The kernels write every
  * scratch element they read, so stale contents from a previous call are

@@ -205,12 +205,68 @@ def _desc(x_shape, cout: int, k: int, padding, dtype: torch.dtype) -> _native.Co
     return _native.make_desc(n, d, h, w, cin, int(cout), int(k), _t3(padding), dtype, _FORCE_KERNEL)
 
 
+# ---------------------------------------------------------------------------
+# Packed-weight cache. A packed weight is valid while the source weight is
+# unchanged; the key holds (data_ptr, autograd version counter, optimizer
+# generation). The version counter catches in-place writes made through
+# autograd-visible ops (copy_, load_state_dict, non-fused optimizers); the
+# generation, bumped by a global optimizer step hook, catches optimizers that
+# write parameters without bumping it (fused Adam). Writes made through
+# ``weight.data`` bypass both: call ``clear_packed_weight_cache()`` after them,
+# or set R4C_PACK_CACHE=0.
+# ---------------------------------------------------------------------------
+_PACK_CACHE_ON = os.environ.get("R4C_PACK_CACHE", "1") != "0"
+_OPT_GENERATION = [0]
+_PACK_CACHE_MAX = 8          # packed layouts kept per weight tensor
+
+
+def _bump_generation(*_args, **_kw):
+    _OPT_GENERATION[0] += 1
+
+
+try:
+    from torch.optim.optimizer import register_optimizer_step_post_hook as _reg_hook
+    _reg_hook(_bump_generation)
+except ImportError:  # pragma: no cover - very old PyTorch: no hook, no cache
+    _PACK_CACHE_ON = False
+
+
+def clear_packed_weight_cache() -> None:
+    """Invalidate every cached packed weight (after writes through ``.data``)."""
+    _bump_generation()
+
+
+def _packed_weight(desc: _native.ConvDesc, leg: int, weight: torch.Tensor) -> torch.Tensor:
+    if not _PACK_CACHE_ON or torch.cuda.is_current_stream_capturing():
+        return _native.pack_weight(desc, leg, weight)
+    key = (leg, bytes(desc), weight.data_ptr(), weight._version, _OPT_GENERATION[0], weight.dtype)
+    cache = getattr(weight, "_r4c_packed", None)
+    if cache is not None:
+        hit = cache.get(key)
+        if hit is not None:
+            return hit
+        # entries of an older weight state are dead: keep only the current state's
+        cache = {k: v for k, v in cache.items() if k[2:5] == key[2:5]}
+    else:
+        cache = {}
+    wp = _native.pack_weight(desc, leg, weight)
+    if len(cache) >= _PACK_CACHE_MAX:
+        cache.pop(next(iter(cache)))
+    cache[key] = wp
+    try:
+        weight._r4c_packed = cache
+    except (AttributeError, RuntimeError):  # tensors that refuse attributes: no caching
+        pass
+    return wp
+
+
 def _launch_fwd(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor], padding) -> torch.Tensor:
-    """y (NDHWC) = conv3d(x, weight) + bias on the B200 kernels."""
+    """y (NDHWC) = conv3d(x, weight) + bias on the B200 kernels. The weight
+    may be fp32 (packing rounds it to x's dtype) or x's dtype."""
     k = int(weight.shape[2])
     cout = int(weight.shape[0])
     desc = _desc(x.shape, cout, k, padding, x.dtype)
-    wp = _native.pack_weight(desc, _native.LEG_FWD, weight)
+    wp = _packed_weight(desc, _native.LEG_FWD, weight)
     pd, ph, pw = _t3(padding)
     out = (_out_size(x.shape[2], k, 1, pd, 1), _out_size(x.shape[3], k, 1, ph, 1),
            _out_size(x.shape[4], k, 1, pw, 1))
@@ -222,7 +278,7 @@ def _launch_dgrad(go: torch.Tensor, weight: torch.Tensor, x_shape, padding) -> t
     """dX (NDHWC) of a stride-1 conv: conv of dY with the flipped weight, pad k-1-p."""
     k = int(weight.shape[2])
     desc = _desc(x_shape, int(weight.shape[0]), k, padding, go.dtype)
-    wp = _native.pack_weight(desc, _native.LEG_DX, weight)
+    wp = _packed_weight(desc, _native.LEG_DX, weight)
     return _native.conv_dx(desc, _as_ndhwc(go), wp)
 
 
@@ -258,7 +314,9 @@ class Conv3dWmmaFn(torch.autograd.Function):
         cin, cout = int(x.shape[1]), int(weight.shape[0])
         ks = tuple(int(s) for s in weight.shape[2:])
         if not wmma_ok_fwd(cin, cout, ks, stride, dilation, 1):
-            return F.conv3d(x, weight, bias, stride, padding, dilation)
+            w_c = weight if weight.dtype == x.dtype else weight.to(x.dtype)
+            b_c = bias if bias is None or bias.dtype == x.dtype else bias.to(x.dtype)
+            return F.conv3d(x, w_c, b_c, stride, padding, dilation)
         compute_dtype = x.dtype
         xc = x if compute_dtype in _HALF else x.to(torch.float16)
         y = _launch_fwd(xc, weight, bias, padding)
@@ -347,11 +405,20 @@ def _autocast_dtype():
 
 
 def _autocast_args(x, weight, bias):
+    """Cast the activation to the autocast dtype here, outside the Function,
+    so the output comes out in that dtype as autocast would make it.
+
+    The weight and bias go in uncast: packing rounds the weight to the
+    compute dtype (the same values ``weight.to(dt)`` would hold) and dW / db
+    come back in fp32 straight into the fp32 master parameters, without the
+    half-precision rounding that a cast's backward would add (the reference
+    rounds dW to the compute dtype, conv3d_wmma.py:1213-1214; keeping fp32 is
+    the more accurate side of the same result).
+    """
     dt = _autocast_dtype()
     if dt is None or not x.is_cuda:
         return x, weight, bias
-    cast = lambda t: t if (t is None or t.dtype == dt) else t.to(dt)  # noqa: E731
-    return cast(x), cast(weight), cast(bias)
+    return (x if x.dtype == dt else x.to(dt)), weight, bias
 
 
 def conv3d_wmma(x, weight, bias=None, stride=1, padding=0, dilation=1, groups=1):
@@ -453,14 +520,14 @@ def _tdesc(x_shape, cout: int, dtype) -> _native.ConvDesc:
 def transpose_k2s2_fwd(x, weight, bias=None):
     """weight in PyTorch ConvTranspose3d layout (Cin, Cout, 2, 2, 2); NDHWC out."""
     desc = _tdesc(x.shape, int(weight.shape[1]), x.dtype)
-    wp = _native.pack_weight(desc, _native.LEG_TFWD, weight)
+    wp = _packed_weight(desc, _native.LEG_TFWD, weight)
     b = None if bias is None else bias.to(x.dtype).contiguous()
     return _native.tconv_fwd(desc, _as_ndhwc(x), wp, b)
 
 
 def transpose_k2s2_dx(x_shape, weight, go):
     desc = _tdesc(x_shape, int(weight.shape[1]), go.dtype)
-    wp = _native.pack_weight(desc, _native.LEG_TDX, weight)
+    wp = _packed_weight(desc, _native.LEG_TDX, weight)
     return _native.tconv_dx(desc, _as_ndhwc(go), wp)
 
 

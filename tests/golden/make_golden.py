@@ -8,7 +8,7 @@ the C oracle (tests/test_oracle_golden.py) and the B200 kernels
 (tests/test_gpu_parity.py).
 
 Usage (needs the reference checkout, which only exists on the build host):
-    python tests/golden/make_golden.py [/path/to/reference]
+    python tests/golden/make_golden.py /path/to/reference
 
 Cases follow the reference's own GPU test (tests/test_conv3d.py:47-75 of the
 reference: seed 0, fp16 randn x/w/b, randn grad_out), plus pad 0 / pad 2 k3
@@ -81,4 +81,6 @@ def main(ref_root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_golden.py <path of the reference checkout>")
+    main(sys.argv[1])

@@ -36,16 +36,31 @@ def _cl(t):
     return t.contiguous(memory_format=torch.channels_last_3d)
 
 
-@pytest.mark.parametrize("case", [(2, 24, 24, 16, 32, 32, 3, 1), (2, 5, 7, 9, 11, 13, 3, 1),
-                                  (1, 48, 24, 8, 16, 16, 1, 0)], ids=["cfg1", "odd", "k1"])
-def test_noalloc_matches_workspace_entry(cuda_ready, case):
+# (n, cin, cout, d, h, w, k, pad), dtype, kernel family forced (0 = automatic,
+# 1 = the SIMT weight-gradient kernel): every dW path that uses the scratch
+NOALLOC_CASES = [
+    ((2, 24, 24, 16, 32, 32, 3, 1), torch.bfloat16, 0),   # tcgen05 dW
+    ((2, 24, 24, 16, 32, 32, 3, 1), torch.float16, 0),
+    ((1, 12, 24, 4, 6, 8, 3, 1), torch.bfloat16, 0),      # tcgen05 dW after channel padding into the scratch
+    ((1, 48, 24, 8, 16, 16, 1, 0), torch.bfloat16, 0),    # k1
+    ((1, 1, 24, 8, 16, 16, 3, 1), torch.bfloat16, 0),     # stem dW (one input channel)
+    ((1, 3, 16, 6, 8, 16, 3, 1), torch.float16, 0),       # stem dW, three input channels
+    ((1, 5, 7, 4, 5, 6, 3, 1), torch.bfloat16, 1),        # SIMT dW (split-K partials in the scratch)
+    ((1, 16, 8, 4, 6, 8, 3, 1), torch.float16, 1),
+]
+
+
+@pytest.mark.parametrize("case,dtype,force", NOALLOC_CASES,
+                         ids=["cfg1", "cfg1-fp16", "cpad", "k1", "stem", "stem3-fp16", "simt", "simt-fp16"])
+def test_noalloc_matches_workspace_entry(cuda_ready, case, dtype, force):
     fn = _bind()
     n, cin, cout, d, h, w, k, pad = case
     g = torch.Generator().manual_seed(7)
-    x = _cl(torch.randn(n, cin, d, h, w, generator=g).to(torch.bfloat16).cuda())
+    x = _cl(torch.randn(n, cin, d, h, w, generator=g).to(dtype).cuda())
     od, oh, ow = (s + 2 * pad - (k - 1) for s in (d, h, w))
-    go = _cl(torch.randn(n, cout, od, oh, ow, generator=g).to(torch.bfloat16).cuda())
-    desc = _native.make_desc(n, d, h, w, cin, cout, k, (pad, pad, pad), torch.bfloat16)
+    go = _cl(torch.randn(n, cout, od, oh, ow, generator=g).to(dtype).cuda())
+    desc = _native.make_desc(n, d, h, w, cin, cout, k, (pad, pad, pad), dtype, force)
+    assert 0 < _native.workspace_bytes(desc, _native.LEG_DW) <= 32 << 20
 
     ref_dw, ref_db = _native.conv_dw(desc, x, go, True)     # existing entry point, torch workspace
     stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)

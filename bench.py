@@ -477,6 +477,168 @@ def pcie_floor_ms(h2d, d2h, probe_bytes=512 << 20):
     return max(h2d / best_u, d2h / best_d) * 1e3, best_u / 1e9, best_d / 1e9
 
 
+# ---------------------------------------------------------------------------
+# UNet3D training step
+# ---------------------------------------------------------------------------
+UNET_SPATIAL = (64, 128, 128)
+DEPTH_SHARD_SPATIAL = (128, 256, 256)
+
+
+def _unet_step_fn(net, opt):
+    import torch.nn.functional as F
+
+    def step(x, tgt, loss_scale=1.0):
+        opt.zero_grad(set_to_none=True)
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            loss = F.cross_entropy(net(x), tgt) * loss_scale
+        loss.backward()
+        opt.step()
+        return loss.detach()
+    return step
+
+
+def time_unet(dev, base, batch, steps, warmup, world, rank):
+    """fwd + bwd + Adam of UNet3D (AMP bf16) at `batch` samples per GPU,
+    batch-sharded data parallel over the ranks (GradSync: bucketed gradient
+    all-reduce overlapped with the backward pass). Device time with CUDA
+    events (max over ranks), then the same steps end to end: input and labels
+    copied from pinned host memory and the loss read back every step."""
+    from rdna4_conv3d import _native
+    from rdna4_conv3d.distributed import GradSync
+    from rdna4_conv3d.unet3d import conv_flops_per_sample, unet3d
+    cl = torch.channels_last_3d
+    torch.manual_seed(0)
+    net = unet3d(base, wmma=True, device=dev)
+    sync = GradSync(net) if world > 1 else None
+    opt = torch.optim.Adam(net.parameters(), lr=1e-3, fused=True)
+    step = _unet_step_fn(net, opt)
+    g = torch.Generator(device=dev).manual_seed(100 + rank)
+    x = torch.randn(batch, 1, *UNET_SPATIAL, device=dev, generator=g).contiguous(memory_format=cl)
+    tgt = torch.randint(0, 4, (batch,) + UNET_SPATIAL, device=dev, generator=g)
+    for _ in range(max(warmup, 3)):
+        step(x, tgt)
+    torch.cuda.synchronize()
+    barrier(world)
+    n0 = _native.launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        loss = step(x, tgt)
+    e1.record()
+    torch.cuda.synchronize()
+    launches = (_native.launch_count() - n0) // steps
+    ms = max_over_ranks(e0.elapsed_time(e1), world) / steps
+    barrier(world)
+
+    # end to end: pinned host input/labels in, loss out, every step
+    hx = torch.empty(x.shape, dtype=x.dtype, pin_memory=True, memory_format=cl)
+    ht = torch.empty(tgt.shape, dtype=tgt.dtype, pin_memory=True)
+    hx.copy_(x)
+    ht.copy_(tgt)
+    hl = torch.empty(steps, dtype=torch.float32, pin_memory=True)
+    torch.cuda.synchronize()
+    barrier(world)
+    e0.record()
+    for i in range(steps):
+        xd = hx.to(dev, non_blocking=True)
+        td = ht.to(dev, non_blocking=True)
+        hl[i:i + 1].copy_(step(xd, td).float().reshape(1), non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    ms_e2e = max_over_ranks(e0.elapsed_time(e1), world) / steps
+    barrier(world)
+    flops = 3.0 * conv_flops_per_sample(net, UNET_SPATIAL) * batch * world
+    res = {"base": base, "input": [batch, 1, *UNET_SPATIAL], "batch_per_gpu": batch, "global_batch": batch * world,
+           "ms_per_step": round(ms, 3), "ms_per_sample": round(ms / (batch * world), 3),
+           "conv_tflops": round(flops / (ms / 1e3) / 1e12, 2),
+           "e2e_ms_per_step": round(ms_e2e, 3), "e2e_ms_per_sample": round(ms_e2e / (batch * world), 3),
+           "h2d_bytes_per_step": int(hx.numel() * hx.element_size() + ht.numel() * ht.element_size()),
+           "d2h_bytes_per_step": 4, "native_launches_per_step": int(launches),
+           "loss_last": round(float(hl[-1]), 5)}
+    if sync is not None:
+        sync.remove()
+    del net, opt, x, tgt
+    torch.cuda.empty_cache()
+    return res
+
+
+def time_depth_shard(dev, base, steps, warmup, world, rank):
+    """One 1x1x128x256x256 volume per step, D-sharded over the ranks (halo
+    exchange per k3 conv, whole-volume BatchNorm statistics); on one GPU the
+    plain unsharded model. ms per sample = per step."""
+    import torch.distributed as dist
+
+    from rdna4_conv3d.distributed import GradSync, depth_shard_model
+    from rdna4_conv3d.unet3d import unet3d
+    cl = torch.channels_last_3d
+    torch.manual_seed(0)
+    net = unet3d(base, wmma=True, device=dev)
+    sync = None
+    if world > 1:
+        sync = GradSync(depth_shard_model(net), average=False)
+    opt = torch.optim.Adam(net.parameters(), lr=1e-3, fused=True)
+    step = _unet_step_fn(net, opt)
+    d, h, w = DEPTH_SHARD_SPATIAL
+    dl = d // world
+    g = torch.Generator(device=dev).manual_seed(7)
+    x = torch.randn(1, 1, d, h, w, device=dev, generator=g)[:, :, rank * dl:(rank + 1) * dl]
+    x = x.contiguous(memory_format=cl)
+    tgt = torch.randint(0, 4, (1, d, h, w), device=dev, generator=g)[:, rank * dl:(rank + 1) * dl].contiguous()
+    for _ in range(max(warmup, 3)):
+        step(x, tgt, 1.0 / world)
+    torch.cuda.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        loss = step(x, tgt, 1.0 / world)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1), world) / steps
+    if world > 1:
+        dist.all_reduce(loss)
+    barrier(world)
+    res = {"base": base, "volume": [1, 1, d, h, w], "planes_per_gpu": dl, "ms_per_sample": round(ms, 3),
+           "loss_last": round(float(loss), 5)}
+    if sync is not None:
+        sync.remove()
+    del net, opt, x, tgt
+    torch.cuda.empty_cache()
+    return res
+
+
+def cpu_unet_baseline(base=24, spatial=(16, 32, 32), budget_s=10.0):
+    """Stock fp32 UNet3D fwd + bwd + Adam on the host cores (the reference's
+    CPU path: nn.Conv3d on CPU tensors), batch 1 on a reduced volume; the
+    per-sample time is scaled to the full 64x128x128 volume by the ratio of
+    conv FLOPs."""
+    import torch.nn.functional as F
+
+    from rdna4_conv3d.unet3d import conv_flops_per_sample, unet3d
+    torch.manual_seed(0)
+    net = unet3d(base, wmma=False)
+    opt = torch.optim.Adam(net.parameters(), lr=1e-3)
+    x = torch.randn(1, 1, *spatial).contiguous(memory_format=torch.channels_last_3d)
+    tgt = torch.randint(0, 4, (1,) + spatial)
+
+    def step():
+        opt.zero_grad(set_to_none=True)
+        F.cross_entropy(net(x), tgt).backward()
+        opt.step()
+    step()
+    times, t_start = [], time.perf_counter()
+    while len(times) < 5 or (time.perf_counter() - t_start < budget_s and len(times) < 30):
+        t0 = time.perf_counter()
+        step()
+        times.append(time.perf_counter() - t0)
+    med = statistics.median(times)
+    scale = conv_flops_per_sample(net, UNET_SPATIAL) / conv_flops_per_sample(net, spatial)
+    return {"ms_per_sample": round(med * scale * 1e3, 1), "cores": torch.get_num_threads(), "kind": "port",
+            "sample": (f"stock torch fp32 UNet3D base {base} fwd+bwd+Adam on CPU, batch 1 at "
+                       f"{'x'.join(map(str, spatial))}, median of {len(times)} steps, scaled to 64x128x128 by "
+                       f"conv FLOPs (x{scale:.0f})")}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -489,6 +651,9 @@ def main():
     ap.add_argument("--only", default=None, help="run one trunk layer, e.g. 'k3 24->24', or one transpose-conv "
                                                  "layer, e.g. 'T k2s2 48->24' (profiling)")
     ap.add_argument("--legs", default="fwd,dw,dx", help="comma list of legs to run (profiling)")
+    ap.add_argument("--no-unet", action="store_true", help="skip the UNet3D training steps (configs[3]/[4])")
+    ap.add_argument("--no-depth-shard", action="store_true", help="skip the depth-sharded volume")
+    ap.add_argument("--unet-only", action="store_true", help="only the UNet3D steps (one JSON line)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -500,6 +665,20 @@ def main():
     from rdna4_conv3d import _native
     from rdna4_conv3d.conv3d_wmma import conv3d_kernels
     _native.lib()
+
+    if args.unet_only:
+        u_steps = max(3, args.steps)
+        res = {"base24": time_unet(dev, 24, BATCH, u_steps, args.warmup, world, rank)}
+        if not args.no_depth_shard:
+            res["base32"] = time_unet(dev, 32, BATCH, u_steps, args.warmup, world, rank)
+            res["depth_shard_base32"] = time_depth_shard(dev, 32, max(2, min(args.steps, 5)), 3, world, rank)
+        if rank == 0:
+            print(json.dumps({"impl": "ours", "n_gpus": world, "unet": res}), flush=True)
+        if world > 1:
+            import torch.distributed as dist
+            barrier(world)
+            dist.destroy_process_group()
+        return 0
 
     if args.only in [t[0] for t in TCONV]:
         # one transpose-conv layer (profiling): its legs only, one JSON line of per-leg times
@@ -619,9 +798,22 @@ def main():
     if args.only is None and len(legs) == 3 and not args.no_tconv:
         tconv = time_tconv(dev, min(args.steps, 5), 2, peaks)
 
+    unet = None
+    if args.only is None and len(legs) == 3 and not args.no_unet:
+        # BASELINE configs[3] (base 24, 4 samples per GPU) at every N, and
+        # configs[4] (base 32, 4 per GPU = global batch 32 at N = 8; and the
+        # depth-sharded 1x1x128x256x256 volume)
+        u_steps = max(3, min(args.steps, 10))
+        unet = {"base24": time_unet(dev, 24, BATCH, u_steps, 3, world, rank),
+                "base32": time_unet(dev, 32, BATCH, u_steps, 3, world, rank)}
+        if not args.no_depth_shard:
+            unet["depth_shard_base32"] = time_depth_shard(dev, 32, max(2, min(args.steps, 5)), 3, world, rank)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and args.only is None:
         cpu = cpu_baseline(TRUNK)
+        if unet is not None:
+            unet["cpu_baseline_base24"] = cpu_unet_baseline(24)
 
     if rank == 0:
         line = {
@@ -641,6 +833,11 @@ def main():
             "tconv_note": "BASELINE configs[2] (ConvTranspose3d k2s2, batch 4, bf16), timed after the trunk "
                           "with CUDA events per leg; not part of value; hbm_frac against the measured copy "
                           "bandwidth for the minimum bytes of each leg",
+            "unet": unet,
+            "unet_note": "BASELINE configs[3]/[4]: UNet3D fwd+bwd+Adam (AMP bf16, fused Adam), seeded synthetic "
+                         "N(0,1) input and uniform labels, random init; ms_per_sample = device step time (max "
+                         "over ranks) / global batch; e2e_* copies input and labels from pinned host memory and "
+                         "reads the loss back every step; not part of value",
         }
         print(json.dumps(line), flush=True)
     if world > 1:

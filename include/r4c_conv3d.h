@@ -186,6 +186,44 @@ int r4c_tconv_dw(const r4c_conv_desc* desc, const void* x, const void* go,
                  r4c_stream_t stream);
 
 /*
+ * Conv3d of any geometry: per-axis kernel size, stride, zero padding,
+ * dilation and groups. The reference runs these geometries on the vendor
+ * library (src/rdna4_conv3d/conv3d_wmma.py:1241-1242; its generic Triton
+ * kernels, conv3d_wmma.py:246-541, hold the same index arithmetic).
+ *   - k = 2, stride 2, pad 0, dilation 1, groups 1 with even input extents,
+ *     bf16/fp16, channels multiples of 8 (the downsampling conv) runs on the
+ *     tcgen05 ConvTranspose3d kernels with the roles swapped (its forward is
+ *     the transpose conv's dX, its dX the transpose conv's forward);
+ *   - everything else on SIMT implicit GEMMs with fp32 accumulation
+ *     (bf16, fp16 or fp32 tensors).
+ * n/d/h/w are the input sizes; output o = (i + 2p - dil*(k-1) - 1) / s + 1
+ * per axis. Weights are in PyTorch's layout (Cout, Cin/groups, kd, kh, kw)
+ * and desc->dtype, unpacked; bias (Cout) in desc->dtype or NULL; dW / db
+ * fp32. Workspace: r4c_convex_workspace_size(desc, leg) bytes (leg =
+ * R4C_LEG_FWD / R4C_LEG_DX / R4C_LEG_DW), caller-owned.
+ */
+typedef struct r4c_convex_desc {
+  int32_t n, d, h, w;
+  int32_t cin, cout, groups;
+  int32_t kd, kh, kw;
+  int32_t sd, sh, sw;        /* stride */
+  int32_t pd, ph, pw;        /* zero padding */
+  int32_t dd, dh, dw;        /* dilation */
+  int32_t dtype;             /* R4C_BF16, R4C_F16 or R4C_F32 */
+} r4c_convex_desc;
+
+/* R4C_KERNEL_TC (k2s2 on the transpose-conv kernels), R4C_KERNEL_GENERIC, or
+ * a negative status for an invalid descriptor. Pure host logic. */
+int r4c_convex_plan(const r4c_convex_desc* desc);
+size_t r4c_convex_workspace_size(const r4c_convex_desc* desc, int leg);
+int r4c_convex_fwd(const r4c_convex_desc* desc, const void* x, const void* w, const void* bias, void* y,
+                   void* workspace, size_t ws_bytes, r4c_stream_t stream);
+int r4c_convex_dx(const r4c_convex_desc* desc, const void* go, const void* w, void* dx, void* workspace,
+                  size_t ws_bytes, r4c_stream_t stream);
+int r4c_convex_dw(const r4c_convex_desc* desc, const void* x, const void* go, float* dw, float* db,
+                  void* workspace, size_t ws_bytes, r4c_stream_t stream);
+
+/*
  * Conv3d weight and bias gradient without any allocation. No counterpart in
  * the reference: it exists for callers that cannot allocate device memory,
  * e.g. a plugin or custom op running inside another framework that owns the

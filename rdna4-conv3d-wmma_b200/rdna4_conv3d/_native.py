@@ -40,6 +40,13 @@ class ConvDesc(ctypes.Structure):
     ]
 
 
+class ConvexDesc(ctypes.Structure):
+    """r4c_convex_desc: Conv3d of any geometry (include/r4c_conv3d.h)."""
+    _fields_ = [(name, ctypes.c_int32) for name in (
+        "n", "d", "h", "w", "cin", "cout", "groups", "kd", "kh", "kw", "sd", "sh", "sw",
+        "pd", "ph", "pw", "dd", "dh", "dw", "dtype")]
+
+
 class NativeError(RuntimeError):
     """A C-ABI entry point returned a non-zero status."""
 
@@ -51,6 +58,7 @@ def library_path() -> str:
 def _bind(lib) -> None:
     P = ctypes.c_void_p
     D = ctypes.POINTER(ConvDesc)
+    X = ctypes.POINTER(ConvexDesc)
     sz = ctypes.c_size_t
     i = ctypes.c_int
     sig = {
@@ -69,6 +77,11 @@ def _bind(lib) -> None:
         "r4c_tconv_fwd": ([D, P, P, P, P, P, sz, P], i),
         "r4c_tconv_dx": ([D, P, P, P, P, sz, P], i),
         "r4c_tconv_dw": ([D, P, P, P, P, P, sz, P], i),
+        "r4c_convex_plan": ([X], i),
+        "r4c_convex_workspace_size": ([X, i], sz),
+        "r4c_convex_fwd": ([X, P, P, P, P, P, sz, P], i),
+        "r4c_convex_dx": ([X, P, P, P, P, sz, P], i),
+        "r4c_convex_dw": ([X, P, P, P, P, P, sz, P], i),
     }
     for name, (args, res) in sig.items():
         fn = getattr(lib, name)
@@ -190,11 +203,22 @@ def _ndhwc_empty(n, c, d, h, w, device, dtype) -> torch.Tensor:
     return torch.empty((n, c, d, h, w), device=device, dtype=dtype, memory_format=torch.channels_last_3d)
 
 
+def _check_out(out: torch.Tensor, shape, dtype) -> torch.Tensor:
+    """A caller-given output must be a dense NDHWC buffer of the right size."""
+    if (tuple(out.shape) != tuple(shape) or out.dtype != dtype or not out.is_cuda
+            or not out.is_contiguous(memory_format=torch.channels_last_3d) or out.data_ptr() % 16):
+        raise NativeError(f"out must be a 16-byte aligned channels_last_3d {dtype} tensor of shape {tuple(shape)}")
+    return out
+
+
 def conv_fwd(desc: ConvDesc, x_cl: torch.Tensor, w_packed: torch.Tensor, bias: Optional[torch.Tensor],
-             out_shape) -> torch.Tensor:
+             out_shape, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     dev = _require_cuda(x_cl, w_packed, bias)
     od, oh, ow = out_shape
-    y = _ndhwc_empty(desc.n, desc.cout, od, oh, ow, dev, x_cl.dtype)
+    if out is None:
+        y = _ndhwc_empty(desc.n, desc.cout, od, oh, ow, dev, x_cl.dtype)
+    else:
+        y = _check_out(out, (desc.n, desc.cout, od, oh, ow), x_cl.dtype)
     ws, nb = _workspace(desc, LEG_FWD, dev)
     with torch.cuda.device(dev):
         st = lib().r4c_conv3d_fwd(ctypes.byref(desc), _ptr(x_cl), _ptr(w_packed), _ptr(bias), _ptr(y),
@@ -203,9 +227,13 @@ def conv_fwd(desc: ConvDesc, x_cl: torch.Tensor, w_packed: torch.Tensor, bias: O
     return y
 
 
-def conv_dx(desc: ConvDesc, go_cl: torch.Tensor, w_packed: torch.Tensor) -> torch.Tensor:
+def conv_dx(desc: ConvDesc, go_cl: torch.Tensor, w_packed: torch.Tensor,
+            out: Optional[torch.Tensor] = None) -> torch.Tensor:
     dev = _require_cuda(go_cl, w_packed)
-    dx = _ndhwc_empty(desc.n, desc.cin, desc.d, desc.h, desc.w, dev, go_cl.dtype)
+    if out is None:
+        dx = _ndhwc_empty(desc.n, desc.cin, desc.d, desc.h, desc.w, dev, go_cl.dtype)
+    else:
+        dx = _check_out(out, (desc.n, desc.cin, desc.d, desc.h, desc.w), go_cl.dtype)
     ws, nb = _workspace(desc, LEG_DX, dev)
     with torch.cuda.device(dev):
         st = lib().r4c_conv3d_dx(ctypes.byref(desc), _ptr(go_cl), _ptr(w_packed), _ptr(dx), _ptr(ws), nb,
@@ -260,6 +288,67 @@ def tconv_dw(desc: ConvDesc, x_cl: torch.Tensor, go_cl: torch.Tensor, want_db: b
         st = lib().r4c_tconv_dw(ctypes.byref(desc), _ptr(x_cl), _ptr(go_cl), _ptr(dw), _ptr(db), _ptr(ws), nb,
                                 _stream(dev))
     _check(st, "r4c_tconv_dw")
+    return dw, db
+
+
+# ---------------------------------------------------------------------------
+# Conv3d of any geometry (r4c_convex_*)
+# ---------------------------------------------------------------------------
+def make_convex_desc(x_shape, w_shape, stride, padding, dilation, groups, dtype: torch.dtype) -> ConvexDesc:
+    n, cin, d, h, w = (int(v) for v in x_shape)
+    cout, _, kd, kh, kw = (int(v) for v in w_shape)
+    return ConvexDesc(n, d, h, w, cin, cout, int(groups), kd, kh, kw, *(int(v) for v in stride),
+                      *(int(v) for v in padding), *(int(v) for v in dilation), dtype_code(dtype))
+
+
+def convex_out_shape(desc: ConvexDesc):
+    o = lambda i, k, s, p, dl: (i + 2 * p - dl * (k - 1) - 1) // s + 1  # noqa: E731
+    return (desc.n, desc.cout, o(desc.d, desc.kd, desc.sd, desc.pd, desc.dd), o(desc.h, desc.kh, desc.sh, desc.ph, desc.dh),
+            o(desc.w, desc.kw, desc.sw, desc.pw, desc.dw))
+
+
+def convex_plan(desc: ConvexDesc) -> int:
+    return int(lib().r4c_convex_plan(ctypes.byref(desc)))
+
+
+def _convex_ws(desc: ConvexDesc, leg: int, device):
+    nb = int(lib().r4c_convex_workspace_size(ctypes.byref(desc), leg))
+    if nb == 0:
+        return None, 0
+    return torch.empty(nb, dtype=torch.uint8, device=device), nb
+
+
+def convex_fwd(desc: ConvexDesc, x_cl: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor]) -> torch.Tensor:
+    dev = _require_cuda(x_cl, w, bias)
+    shp = convex_out_shape(desc)
+    y = _ndhwc_empty(*shp, dev, x_cl.dtype)
+    ws, nb = _convex_ws(desc, LEG_FWD, dev)
+    with torch.cuda.device(dev):
+        st = lib().r4c_convex_fwd(ctypes.byref(desc), _ptr(x_cl), _ptr(w), _ptr(bias), _ptr(y), _ptr(ws), nb,
+                                  _stream(dev))
+    _check(st, "r4c_convex_fwd")
+    return y
+
+
+def convex_dx(desc: ConvexDesc, go_cl: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    dev = _require_cuda(go_cl, w)
+    dx = _ndhwc_empty(desc.n, desc.cin, desc.d, desc.h, desc.w, dev, go_cl.dtype)
+    ws, nb = _convex_ws(desc, LEG_DX, dev)
+    with torch.cuda.device(dev):
+        st = lib().r4c_convex_dx(ctypes.byref(desc), _ptr(go_cl), _ptr(w), _ptr(dx), _ptr(ws), nb, _stream(dev))
+    _check(st, "r4c_convex_dx")
+    return dx
+
+
+def convex_dw(desc: ConvexDesc, x_cl: torch.Tensor, go_cl: torch.Tensor, want_db: bool):
+    dev = _require_cuda(x_cl, go_cl)
+    dw = torch.empty((desc.cout, desc.cin // desc.groups, desc.kd, desc.kh, desc.kw), dtype=torch.float32, device=dev)
+    db = torch.empty((desc.cout,), dtype=torch.float32, device=dev) if want_db else None
+    ws, nb = _convex_ws(desc, LEG_DW, dev)
+    with torch.cuda.device(dev):
+        st = lib().r4c_convex_dw(ctypes.byref(desc), _ptr(x_cl), _ptr(go_cl), _ptr(dw), _ptr(db), _ptr(ws), nb,
+                                 _stream(dev))
+    _check(st, "r4c_convex_dw")
     return dw, db
 
 

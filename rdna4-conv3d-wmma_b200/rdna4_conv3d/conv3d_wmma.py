@@ -260,26 +260,29 @@ def _packed_weight(desc: _native.ConvDesc, leg: int, weight: torch.Tensor) -> to
     return wp
 
 
-def _launch_fwd(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor], padding) -> torch.Tensor:
+def _launch_fwd(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor], padding,
+                out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """y (NDHWC) = conv3d(x, weight) + bias on the B200 kernels. The weight
-    may be fp32 (packing rounds it to x's dtype) or x's dtype."""
+    may be fp32 (packing rounds it to x's dtype) or x's dtype. ``out``, when
+    given, is a dense NDHWC buffer the result is written into."""
     k = int(weight.shape[2])
     cout = int(weight.shape[0])
     desc = _desc(x.shape, cout, k, padding, x.dtype)
     wp = _packed_weight(desc, _native.LEG_FWD, weight)
     pd, ph, pw = _t3(padding)
-    out = (_out_size(x.shape[2], k, 1, pd, 1), _out_size(x.shape[3], k, 1, ph, 1),
+    osz = (_out_size(x.shape[2], k, 1, pd, 1), _out_size(x.shape[3], k, 1, ph, 1),
            _out_size(x.shape[4], k, 1, pw, 1))
     b = None if bias is None else bias.to(x.dtype).contiguous()
-    return _native.conv_fwd(desc, _as_ndhwc(x), wp, b, out)
+    return _native.conv_fwd(desc, _as_ndhwc(x), wp, b, osz, out)
 
 
-def _launch_dgrad(go: torch.Tensor, weight: torch.Tensor, x_shape, padding) -> torch.Tensor:
+def _launch_dgrad(go: torch.Tensor, weight: torch.Tensor, x_shape, padding,
+                  out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """dX (NDHWC) of a stride-1 conv: conv of dY with the flipped weight, pad k-1-p."""
     k = int(weight.shape[2])
     desc = _desc(x_shape, int(weight.shape[0]), k, padding, go.dtype)
     wp = _packed_weight(desc, _native.LEG_DX, weight)
-    return _native.conv_dx(desc, _as_ndhwc(go), wp)
+    return _native.conv_dx(desc, _as_ndhwc(go), wp, out)
 
 
 def _launch_wgrad(x: torch.Tensor, go: torch.Tensor, weight_shape, padding, want_db: bool):
@@ -423,6 +426,11 @@ def _autocast_args(x, weight, bias):
 
 def conv3d_wmma(x, weight, bias=None, stride=1, padding=0, dilation=1, groups=1):
     """Functional Conv3d; same arguments as F.conv3d (integer/tuple padding)."""
+    if x.is_cuda and _wmma_hw() and not isinstance(padding, str):
+        cin, cout = int(x.shape[1]), int(weight.shape[0])
+        if _k2s2_ok(x, cin, cout, weight.shape[2:], stride, padding, dilation, groups) or (
+                _GENERAL and not _geom_ok(tuple(weight.shape[2:]), stride, dilation, groups)):
+            return conv3d_general(x, weight, bias, stride, padding, dilation, groups)
     if groups != 1:
         return F.conv3d(x, weight, bias, stride, padding, dilation, groups)
     x, weight, bias = _autocast_args(x, weight, bias)
@@ -467,6 +475,98 @@ def wmma_dx(x, weight, go, stride=1, padding=0, dilation=1):
     return gx if cl else gx.contiguous()
 
 
+# ---------------------------------------------------------------------------
+# Any other geometry (per-axis kernel size, stride, padding, dilation,
+# groups): the r4c_convex_* entry points. k=2 stride-2 pad-0 convs with
+# channels that are multiples of 8 run on the tcgen05 transpose-conv kernels
+# (the downsampling conv is the transpose of the k2s2 up-conv); the rest on
+# SIMT kernels. The reference sends all of these to the vendor library
+# (conv3d_wmma.py:1241-1242), and so does Conv3dWmma by default, except the
+# k2s2 form; RDNA4_CONV3D_GENERAL=1 routes the rest here too.
+# ---------------------------------------------------------------------------
+_GENERAL = os.environ.get("RDNA4_CONV3D_GENERAL", "0").lower() in ("1", "simt", "on", "true")
+
+
+def _k2s2_ok(x, cin, cout, kernel_size, stride, padding, dilation, groups) -> bool:
+    """k=2, stride 2, pad 0 conv on the tcgen05 transpose-conv kernels (bf16 /
+    fp16 activations, or autocast on; fp32 stays with the vendor library)."""
+    if x.dtype not in _HALF and _autocast_dtype() is None:
+        return False
+    x_shape = x.shape
+    if _t3(kernel_size) != (2, 2, 2) or _t3(stride) != (2, 2, 2) or _t3(padding) != (0, 0, 0):
+        return False
+    if _t3(dilation) != (1, 1, 1) or int(groups) != 1 or cin % 8 or cout % 8:
+        return False
+    return all(int(v) % 2 == 0 for v in x_shape[2:])
+
+
+def _convex_desc(x_shape, w_shape, stride, padding, dilation, groups, dtype):
+    return _native.make_convex_desc(x_shape, w_shape, _t3(stride), _t3(padding), _t3(dilation), groups, dtype)
+
+
+class Conv3dGeneralFn(torch.autograd.Function):
+    """Conv3d of any geometry on the r4c_convex_* kernels. Computes in x's
+    dtype (bf16 / fp16 / fp32); dW and db in fp32."""
+
+    @staticmethod
+    def forward(x, weight, bias, stride, padding, dilation, groups):
+        xc = _as_ndhwc(x)
+        w = weight.to(x.dtype).contiguous()
+        b = None if bias is None else bias.to(x.dtype).contiguous()
+        desc = _convex_desc(x.shape, weight.shape, stride, padding, dilation, groups, x.dtype)
+        y = _native.convex_fwd(desc, xc, w, b)
+        if not x.is_contiguous(memory_format=torch.channels_last_3d):
+            y = y.contiguous()
+        return y
+
+    @staticmethod
+    def setup_context(ctx, inputs, output):
+        x, weight, bias, stride, padding, dilation, groups = inputs
+        ctx.save_for_backward(x, weight)
+        ctx.has_bias = bias is not None
+        ctx.bias_dtype = None if bias is None else bias.dtype
+        ctx.geom = (stride, padding, dilation, groups)
+        ctx.x_layout = (torch.channels_last_3d if x.is_contiguous(memory_format=torch.channels_last_3d)
+                        else torch.contiguous_format)
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        x, weight = ctx.saved_tensors
+        stride, padding, dilation, groups = ctx.geom
+        go = _as_ndhwc(grad_out.to(x.dtype))
+        desc = _convex_desc(x.shape, weight.shape, stride, padding, dilation, groups, x.dtype)
+        need_x, need_w, need_b = ctx.needs_input_grad[:3]
+        dw = db = None
+        if need_w or (need_b and ctx.has_bias):
+            dw, db = _native.convex_dw(desc, _as_ndhwc(x), go, bool(ctx.has_bias and need_b))
+        handle = _reduce_async([dw, db])
+        gx = None
+        if need_x:
+            gx = _native.convex_dx(desc, go, weight.to(x.dtype).contiguous())
+            if ctx.x_layout == torch.contiguous_format:
+                gx = gx.contiguous()
+        if handle is not None:
+            handle.wait()
+        if dw is not None:
+            dw = dw.to(weight.dtype) if need_w else None
+        if db is not None and ctx.bias_dtype is not None:
+            db = db.to(ctx.bias_dtype)
+        return gx, dw, db, None, None, None, None
+
+
+def conv3d_general(x, weight, bias=None, stride=1, padding=0, dilation=1, groups=1):
+    """Conv3d of any geometry (integer or per-axis stride / padding /
+    dilation, groups) on this library's kernels, CUDA tensors only. Under
+    autocast the activation and weight are cast to the autocast dtype here,
+    outside the Function, as for conv3d_wmma."""
+    if not x.is_cuda:
+        raise ValueError("conv3d_general runs on CUDA tensors")
+    dt = _autocast_dtype()
+    if dt is not None and x.dtype != dt:
+        x = x.to(dt)
+    return Conv3dGeneralFn.apply(x, weight, bias, _t3(stride), _t3(padding), _t3(dilation), int(groups))
+
+
 def swap_conv3d(module: nn.Module) -> int:
     """Replace every plain ``nn.Conv3d`` under ``module`` with ``Conv3dWmma``.
 
@@ -499,10 +599,15 @@ class Conv3dWmma(nn.Conv3d):
     """Drop-in ``nn.Conv3d``: B200 kernels for in-scope geometry on CUDA tensors."""
 
     def forward(self, x):
-        if (self.groups != 1 or not x.is_cuda or self.padding_mode != "zeros"
-                or isinstance(self.padding, str)):
+        if not x.is_cuda or self.padding_mode != "zeros" or isinstance(self.padding, str):
             return super().forward(x)
         cin, cout = int(x.shape[1]), int(self.weight.shape[0])
+        if _wmma_hw() and (_k2s2_ok(x, cin, cout, self.kernel_size, self.stride, self.padding,
+                                    self.dilation, self.groups)
+                           or (_GENERAL and not _geom_ok(self.kernel_size, self.stride, self.dilation, self.groups))):
+            return conv3d_general(x, self.weight, self.bias, self.stride, self.padding, self.dilation, self.groups)
+        if self.groups != 1:
+            return super().forward(x)
         plan = conv3d_plan(cin, cout, self.kernel_size, self.stride, self.dilation, self.groups)
         if all(v == "miopen" for v in plan.values()):
             return super().forward(x)

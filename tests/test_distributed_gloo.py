@@ -139,3 +139,85 @@ def test_grad_allreducer_average_and_sum():
         torch.testing.assert_close(r["a"], torch.full((4, 3), 1.5))
         torch.testing.assert_close(r["b"], torch.arange(5, dtype=torch.float32) * 1.5)
         torch.testing.assert_close(r["c"], torch.ones(2) * 3.0)
+
+
+def _worker_gradsync(rank, port, outdir):
+    import rdna4_conv3d  # noqa: F401
+    from rdna4_conv3d.distributed import GradSync
+    _init(rank, port)
+    try:
+        torch.manual_seed(0)
+        net = torch.nn.Sequential(torch.nn.Linear(4, 3), torch.nn.Tanh(), torch.nn.Linear(3, 2)).double()
+        sync = GradSync(net, bucket_bytes=40)       # small buckets: several flushes per backward
+        g = torch.Generator().manual_seed(100 + rank)
+        x = torch.randn(5, 4, generator=g, dtype=torch.float64)
+        for _ in range(2):                          # the hooks re-arm for every backward pass
+            net.zero_grad(set_to_none=True)
+            net(x).pow(2).sum().backward()
+        torch.save({"grads": [p.grad.clone() for p in net.parameters()], "flushed": sync.buckets_flushed},
+                   os.path.join(outdir, f"r{rank}.pt"))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gradsync_averages_bucketed_grads():
+    res = _run(_worker_gradsync)
+    torch.manual_seed(0)
+    net = torch.nn.Sequential(torch.nn.Linear(4, 3), torch.nn.Tanh(), torch.nn.Linear(3, 2)).double()
+    per_rank = []
+    for rank in range(WORLD):
+        g = torch.Generator().manual_seed(100 + rank)
+        x = torch.randn(5, 4, generator=g, dtype=torch.float64)
+        net.zero_grad(set_to_none=True)
+        net(x).pow(2).sum().backward()
+        per_rank.append([p.grad.clone() for p in net.parameters()])
+    want = [(a + b) / 2 for a, b in zip(*per_rank)]
+    for r in res:
+        assert r["flushed"] >= 4
+        for got, ref in zip(r["grads"], want):
+            torch.testing.assert_close(got, ref, rtol=1e-12, atol=1e-12)
+
+
+def _small_unet():
+    from rdna4_conv3d.unet3d import UNet3D
+    torch.manual_seed(3)
+    return UNet3D(in_channels=1, n_classes=2, base=4, levels=3).double()
+
+
+def _worker_depth_unet(rank, port, outdir):
+    import rdna4_conv3d  # noqa: F401
+    from rdna4_conv3d.distributed import GradSync, depth_shard_model
+    _init(rank, port)
+    try:
+        net = _small_unet()
+        partial = depth_shard_model(net)
+        GradSync(partial, average=False)
+        g = torch.Generator().manual_seed(9)
+        x = torch.randn(1, 1, 16, 8, 8, generator=g, dtype=torch.float64)
+        gy = torch.randn(1, 2, 16, 8, 8, generator=g, dtype=torch.float64)
+        y = net(_slab(x, rank))
+        (y * _slab(gy, rank)).sum().backward()
+        torch.save({"y": y.detach(), "grads": {n: p.grad.clone() for n, p in net.named_parameters()},
+                    "bufs": {n: b.clone() for n, b in net.named_buffers()}}, os.path.join(outdir, f"r{rank}.pt"))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_depth_sharded_unet_matches_full_volume():
+    """A whole UNet (k3 convs with halos, whole-volume BatchNorm statistics,
+    pooling, k2s2 transpose convs, skip concatenation, k1 head) over two D
+    slabs against the same UNet on the full volume, fp64."""
+    res = _run(_worker_depth_unet)
+    net = _small_unet()
+    g = torch.Generator().manual_seed(9)
+    x = torch.randn(1, 1, 16, 8, 8, generator=g, dtype=torch.float64)
+    gy = torch.randn(1, 2, 16, 8, 8, generator=g, dtype=torch.float64)
+    y = net(x)
+    (y * gy).sum().backward()
+    torch.testing.assert_close(torch.cat([r["y"] for r in res], dim=2), y.detach(), rtol=1e-9, atol=1e-9)
+    for r in res:
+        for n, p in net.named_parameters():
+            torch.testing.assert_close(r["grads"][n], p.grad, rtol=1e-8, atol=1e-9, msg=n)
+        for n, b in net.named_buffers():
+            if b.dtype.is_floating_point:
+                torch.testing.assert_close(r["bufs"][n], b, rtol=1e-9, atol=1e-9, msg=n)

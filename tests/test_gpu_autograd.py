@@ -154,7 +154,7 @@ def test_unet_amp_loss_parity(cuda_ready):
                 loss = F.cross_entropy(net(x), tgt)
             loss.backward()
             opt.step()
-            hist.append(float(loss))
+            hist.append(float(loss.detach()))
         losses.append(hist)
     diffs = [abs(a - b) for a, b in zip(*losses)]
-    assert max(diffs) <= 1e-3 * max(1.0, max(losses[0])), (max(diffs), losses[0][-1], losses[1][-1])
+    assert max(diffs) <= 1e-3, (max(diffs), losses[0][-1], losses[1][-1])   # absolute

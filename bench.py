@@ -497,12 +497,40 @@ def _unet_step_fn(net, opt):
     return step
 
 
-def time_unet(dev, base, batch, steps, warmup, world, rank):
+def _graph_step(net, opt, x, tgt, warmup):
+    """Capture one whole training step (forward, backward, Adam) in a CUDA
+    graph over static input / label buffers; returns (replay, loss buffer).
+    Warm-up runs eagerly on a side stream first (plan tuning, NCCL set-up)."""
+    import torch.nn.functional as F
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(max(warmup, 3)):
+            opt.zero_grad(set_to_none=True)
+            with torch.autocast("cuda", dtype=torch.bfloat16):
+                loss = F.cross_entropy(net(x), tgt)
+            loss.backward()
+            opt.step()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    opt.zero_grad(set_to_none=True)
+    with torch.cuda.graph(g):
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            static_loss = F.cross_entropy(net(x), tgt)
+        static_loss.backward()
+        opt.step()
+    return g, static_loss
+
+
+def time_unet(dev, base, batch, steps, warmup, world, rank, graph=False):
     """fwd + bwd + Adam of UNet3D (AMP bf16) at `batch` samples per GPU,
     batch-sharded data parallel over the ranks (GradSync: bucketed gradient
     all-reduce overlapped with the backward pass). Device time with CUDA
     events (max over ranks), then the same steps end to end: input and labels
-    copied from pinned host memory and the loss read back every step."""
+    copied from pinned host memory and the loss read back every step.
+    ``graph``: the step is captured once in a CUDA graph and replayed (the
+    host then only launches the graph)."""
     from rdna4_conv3d import _native
     from rdna4_conv3d.distributed import GradSync
     from rdna4_conv3d.unet3d import conv_flops_per_sample, unet3d
@@ -510,21 +538,32 @@ def time_unet(dev, base, batch, steps, warmup, world, rank):
     torch.manual_seed(0)
     net = unet3d(base, wmma=True, device=dev)
     sync = GradSync(net) if world > 1 else None
-    opt = torch.optim.Adam(net.parameters(), lr=1e-3, fused=True)
+    opt = torch.optim.Adam(net.parameters(), lr=1e-3, fused=True, capturable=graph)
     step = _unet_step_fn(net, opt)
     g = torch.Generator(device=dev).manual_seed(100 + rank)
     x = torch.randn(batch, 1, *UNET_SPATIAL, device=dev, generator=g).contiguous(memory_format=cl)
     tgt = torch.randint(0, 4, (batch,) + UNET_SPATIAL, device=dev, generator=g)
+    if graph:
+        cg, static_loss = _graph_step(net, opt, x, tgt, warmup)
+
+        def step(xx, tt, loss_scale=1.0):  # noqa: F811  (graphed step: refill the static inputs, replay)
+            if xx is not x:
+                x.copy_(xx, non_blocking=True)
+                tgt.copy_(tt, non_blocking=True)
+            cg.replay()
+            return static_loss.detach()
     for _ in range(max(warmup, 3)):
         step(x, tgt)
     torch.cuda.synchronize()
     barrier(world)
     n0 = _native.launch_count()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    h0 = time.perf_counter()
     e0.record()
     for _ in range(steps):
         loss = step(x, tgt)
     e1.record()
+    host_ms = (time.perf_counter() - h0) * 1e3 / steps
     torch.cuda.synchronize()
     launches = (_native.launch_count() - n0) // steps
     ms = max_over_ranks(e0.elapsed_time(e1), world) / steps
@@ -549,12 +588,16 @@ def time_unet(dev, base, batch, steps, warmup, world, rank):
     barrier(world)
     flops = 3.0 * conv_flops_per_sample(net, UNET_SPATIAL) * batch * world
     res = {"base": base, "input": [batch, 1, *UNET_SPATIAL], "batch_per_gpu": batch, "global_batch": batch * world,
+           "cuda_graph": bool(graph),
            "ms_per_step": round(ms, 3), "ms_per_sample": round(ms / (batch * world), 3),
-           "conv_tflops": round(flops / (ms / 1e3) / 1e12, 2),
+           "conv_tflops": round(flops / (ms / 1e3) / 1e12, 2), "host_issue_ms_per_step": round(host_ms, 3),
            "e2e_ms_per_step": round(ms_e2e, 3), "e2e_ms_per_sample": round(ms_e2e / (batch * world), 3),
            "h2d_bytes_per_step": int(hx.numel() * hx.element_size() + ht.numel() * ht.element_size()),
-           "d2h_bytes_per_step": 4, "native_launches_per_step": int(launches),
+           "d2h_bytes_per_step": 4,
+           "native_launches_per_step": None if graph else int(launches),
            "loss_last": round(float(hl[-1]), 5)}
+    if graph:
+        del cg
     if sync is not None:
         sync.remove()
     del net, opt, x, tgt
@@ -654,6 +697,7 @@ def main():
     ap.add_argument("--no-unet", action="store_true", help="skip the UNet3D training steps (configs[3]/[4])")
     ap.add_argument("--no-depth-shard", action="store_true", help="skip the depth-sharded volume")
     ap.add_argument("--unet-only", action="store_true", help="only the UNet3D steps (one JSON line)")
+    ap.add_argument("--no-graph", action="store_true", help="skip the CUDA-graph UNet step (N = 1)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -669,6 +713,8 @@ def main():
     if args.unet_only:
         u_steps = max(3, args.steps)
         res = {"base24": time_unet(dev, 24, BATCH, u_steps, args.warmup, world, rank)}
+        if world == 1 and not args.no_graph:
+            res["base24_graph"] = time_unet(dev, 24, BATCH, u_steps, args.warmup, world, rank, graph=True)
         if not args.no_depth_shard:
             res["base32"] = time_unet(dev, 32, BATCH, u_steps, args.warmup, world, rank)
             res["depth_shard_base32"] = time_depth_shard(dev, 32, max(2, min(args.steps, 5)), 3, world, rank)
@@ -806,6 +852,8 @@ def main():
         u_steps = max(3, min(args.steps, 10))
         unet = {"base24": time_unet(dev, 24, BATCH, u_steps, 3, world, rank),
                 "base32": time_unet(dev, 32, BATCH, u_steps, 3, world, rank)}
+        if world == 1 and not args.no_graph:
+            unet["base24_graph"] = time_unet(dev, 24, BATCH, u_steps, 3, world, rank, graph=True)
         if not args.no_depth_shard:
             unet["depth_shard_base32"] = time_depth_shard(dev, 32, max(2, min(args.steps, 5)), 3, world, rank)
 

@@ -103,6 +103,15 @@ int r4c_version(void);
  */
 int r4c_device_error(r4c_stream_t stream, int clear);
 
+/*
+ * Self-test of those bounded waits: launches one block that waits, through
+ * the kernels' own bounded-wait routine, on a barrier nothing arrives at, for
+ * `limit_ns` nanoseconds (at most 2 s). The wait runs out, the block records
+ * code 3 in the device error flag and returns; read it with
+ * r4c_device_error(). No reference counterpart.
+ */
+int r4c_watchdog_selftest(uint64_t limit_ns, r4c_stream_t stream);
+
 /* Total number of CUDA kernels this library has launched in this process
  * (all devices, all threads). Lets a caller count the kernels behind a timed
  * region. No reference counterpart. */
@@ -222,6 +231,48 @@ int r4c_convex_dx(const r4c_convex_desc* desc, const void* go, const void* w, vo
                   size_t ws_bytes, r4c_stream_t stream);
 int r4c_convex_dw(const r4c_convex_desc* desc, const void* x, const void* go, float* dw, float* db,
                   void* workspace, size_t ws_bytes, r4c_stream_t stream);
+
+/*
+ * BatchNorm3d with batch statistics, fused with ReLU, on NDHWC activations
+ * of `vox` voxels x C channels (bf16 / fp16, C a multiple of 8, 16-byte
+ * aligned). No reference kernel: the reference's model blocks are Conv3d ->
+ * BatchNorm3d -> ReLU on the vendor library (benches/unet_e2e.py:13-20).
+ * Training forward:  r4c_bn_stats -> r4c_bn_finalize -> r4c_bn_relu_fwd.
+ * Backward:          r4c_bn_relu_bwd_sums -> r4c_bn_relu_bwd_dx.
+ * Every reduction is deterministic (fixed block ranges and orders). All
+ * per-channel arrays are fp32; `ws` is r4c_bn_workspace_size(vox, C) bytes.
+ * A caller that shards one volume across processes all-reduces `sums`
+ * (element-wise sum) between the first and second call of each direction.
+ */
+size_t r4c_bn_workspace_size(int64_t vox, int C);
+/* sums (3*C floats): [0:C) = sum (x - p), [C:2C) = sum (x - p)^2, [2C:3C) =
+ * the pivot p used: `pivot` (C floats) when given, else the first voxel of x.
+ * Deviations from a value inside the distribution keep the variance free of
+ * the cancellation E[x^2] - E[x]^2 suffers when |mean| >> std. Shards of one
+ * volume whose sums are all-reduced must pass the same pivot. */
+int r4c_bn_stats(const void* x, int64_t vox, int C, int dtype, const float* pivot, float* sums, void* ws,
+                 size_t ws_bytes, r4c_stream_t stream);
+/* From sums over `count` voxels: mean_invstd = (mean, 1/sqrt(var + eps)),
+ * affine = (gamma, beta), 1 and 0 where gamma / beta are NULL. Running
+ * statistics (both or neither) get the momentum update with the unbiased
+ * variance, as torch.nn.BatchNorm3d does. */
+int r4c_bn_finalize(const float* sums, double count, int C, const float* gamma, const float* beta, float eps,
+                    float momentum, float* running_mean, float* running_var, float* mean_invstd,
+                    float* affine, r4c_stream_t stream);
+/* y = relu(gamma * (x - mean) * invstd + beta) (no ReLU when relu == 0), the
+ * expression and order of PyTorch's BatchNorm kernels; y may alias x. */
+int r4c_bn_relu_fwd(const void* x, void* y, const float* mean_invstd, const float* affine, int64_t vox, int C,
+                    int dtype, int relu, r4c_stream_t stream);
+/* sums[0:C) = sum g, sums[C:2C) = sum g*(x - mean) with g = dy masked by the
+ * forward's ReLU (recomputed from x with the forward's expression). */
+int r4c_bn_relu_bwd_sums(const void* dy, const void* x, const float* mean_invstd, const float* affine,
+                         int64_t vox, int C, int dtype, int relu, float* sums, void* ws, size_t ws_bytes,
+                         r4c_stream_t stream);
+/* dgamma, dbeta (nullable) and dx (nullable) from the backward sums over
+ * `count` voxels; coef is 3*C floats of scratch. */
+int r4c_bn_relu_bwd_dx(const void* dy, const void* x, void* dx, const float* mean_invstd, const float* affine,
+                       const float* sums, double count, int64_t vox, int C, int dtype, int relu, float* dgamma,
+                       float* dbeta, float* coef, r4c_stream_t stream);
 
 /*
  * Conv3d weight and bias gradient without any allocation. No counterpart in

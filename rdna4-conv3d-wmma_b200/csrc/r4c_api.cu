@@ -129,19 +129,38 @@ __global__ void cpad_kernel(const T* __restrict__ x, T* __restrict__ xp, int64_t
   *reinterpret_cast<uint4*>(xp + v * cinp + c0) = *reinterpret_cast<const uint4*>(tmp);
 }
 
-cudaError_t launch_cpad(const void* x, void* xp, const Geom& g, int dtype, cudaStream_t st) {
-  const int cinp = cin_eff(g);
-  const int64_t n = g.in_vox() * (cinp / 8);
+cudaError_t launch_cpad_n(const void* x, void* xp, int64_t vox, int c, int cp, int dtype, cudaStream_t st) {
+  const int64_t n = vox * (cp / 8);
   const unsigned blocks = (unsigned)((n + 255) / 256);
   if (n == 0) return cudaSuccess;
   if (dtype == R4C_BF16)
     cpad_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x),
-                                                       static_cast<__nv_bfloat16*>(xp), g.in_vox(), g.cin, cinp);
+                                                       static_cast<__nv_bfloat16*>(xp), vox, c, cp);
   else
-    cpad_kernel<__half><<<blocks, 256, 0, st>>>(static_cast<const __half*>(x), static_cast<__half*>(xp), g.in_vox(),
-                                                g.cin, cinp);
+    cpad_kernel<__half><<<blocks, 256, 0, st>>>(static_cast<const __half*>(x), static_cast<__half*>(xp), vox, c, cp);
   note_launches(1);
   return cudaGetLastError();
+}
+
+cudaError_t launch_cpad(const void* x, void* xp, const Geom& g, int dtype, cudaStream_t st) {
+  return launch_cpad_n(x, xp, g.in_vox(), g.cin, cin_eff(g), dtype, st);
+}
+
+// The same for dY when Cout is not a multiple of 8 (dX and dW legs: dY is the
+// source the TMA reads): dY copied with Cout rounded up to 8, zeros past
+// Cout; the dX weights of the padded channels are packed as zeros and the dW
+// rows of the padded channels (zero) are dropped.
+int cout_eff(const Geom& g) { return g.cout % 8 ? (g.cout + 7) / 8 * 8 : g.cout; }
+bool needs_gpad(const Geom& g) { return g.cout % 8 != 0; }
+size_t gpad_bytes(const Geom& g) {
+  return needs_gpad(g) ? align_up((size_t)g.out_vox() * cout_eff(g) * 2, 256) : 0;
+}
+// dW / db of the padded Cout, of which the first Cout rows are the result
+// (OIDHW: a prefix), when dY is padded.
+size_t gpad_dw_bytes(const Geom& g) {
+  if (!needs_gpad(g)) return 0;
+  return align_up((size_t)cout_eff(g) * g.cin * g.k * g.k * g.k * sizeof(float), 256) +
+         align_up((size_t)cout_eff(g) * sizeof(float), 256);
 }
 
 // Forward of a k=3 layer with 1..4 input channels: the stem kernel.
@@ -179,17 +198,17 @@ bool use_tc(const r4c_conv_desc* ds, int leg, const Geom& g, tc::ConvPlan* pl) {
   if (leg == R4C_LEG_FWD)
     return tc::plan_conv(g.n, g.d, g.h, g.w, cin_eff(g), g.cout, g.k, g.pd, g.ph, g.pw, pl);
   if (leg == R4C_LEG_DX)
-    return tc::plan_conv(g.n, g.od, g.oh, g.ow, g.cout, g.cin, g.k, g.k - 1 - g.pd,
+    return tc::plan_conv(g.n, g.od, g.oh, g.ow, cout_eff(g), g.cin, g.k, g.k - 1 - g.pd,
                          g.k - 1 - g.ph, g.k - 1 - g.pw, pl);
   if (leg == R4C_LEG_DW)
-    return tc::dw_supported(g.n, g.d, g.h, g.w, cin_eff(g), g.cout, g.k, g.pd, g.ph, g.pw);
+    return tc::dw_supported(g.n, g.d, g.h, g.w, cin_eff(g), cout_eff(g), g.k, g.pd, g.ph, g.pw);
   return false;
 }
 
 // Workspace of the tcgen05 dW: its split partials plus the generic db
 // partials (used when the kernel cannot fold db into its spare rows).
 size_t tc_dw_ws(const Geom& g, size_t* part_bytes) {
-  size_t a = align_up(tc::dw_workspace(g.n, g.d, g.h, g.w, cin_eff(g), g.cout, g.k, g.pd, g.ph, g.pw), 256);
+  size_t a = align_up(tc::dw_workspace(g.n, g.d, g.h, g.w, cin_eff(g), cout_eff(g), g.k, g.pd, g.ph, g.pw), 256);
   int Sdb; int64_t ch;
   generic::db_split(g.out_vox(), &Sdb, &ch);
   if (part_bytes) *part_bytes = a;
@@ -253,7 +272,7 @@ int r4c_describe_plan(const r4c_conv_desc* desc, int leg, char* buf, size_t len)
       tconv::dw_describe(g.n, g.d, g.h, g.w, g.cin, g.cout, tmp, sizeof(tmp));
       st = R4C_KERNEL_TC;
     } else if (leg == R4C_LEG_DW && use_tc(desc, leg, g, &pl)) {
-      tc::dw_describe(g.n, g.d, g.h, g.w, cin_eff(g), g.cout, g.k, g.pd, g.ph, g.pw, tmp, sizeof(tmp));
+      tc::dw_describe(g.n, g.d, g.h, g.w, cin_eff(g), cout_eff(g), g.k, g.pd, g.ph, g.pw, tmp, sizeof(tmp));
       if (needs_cpad(g)) strncat(tmp, " (input channels padded to a multiple of 8)", sizeof(tmp) - strlen(tmp) - 1);
       st = R4C_KERNEL_TC;
     } else if (use_tc(desc, leg, g, &pl)) {
@@ -305,7 +324,11 @@ size_t r4c_workspace_size(const r4c_conv_desc* desc, int leg) {
   if (leg == R4C_LEG_DW) {
     if (use_stem_dw(desc, leg, g)) return stem::dw_workspace(g.n, g.d, g.h, g.w, g.cin, g.cout, g.pd, g.ph, g.pw);
     tc::ConvPlan pl;
-    if (use_tc(desc, leg, g, &pl)) return cpad_bytes(g) + tc_dw_ws(g, nullptr);
+    if (use_tc(desc, leg, g, &pl)) return cpad_bytes(g) + gpad_bytes(g) + gpad_dw_bytes(g) + tc_dw_ws(g, nullptr);
+  }
+  if (leg == R4C_LEG_DX) {
+    tc::ConvPlan pl;
+    if (!use_stem_dx(desc, leg, g) && use_tc(desc, leg, g, &pl)) return gpad_bytes(g);
   }
   if (leg == R4C_LEG_FWD) {
     if (use_stem(desc, leg, g)) return 0;
@@ -349,7 +372,9 @@ int r4c_pack_weight(const r4c_conv_desc* desc, int leg, const void* w_src, int s
   tc::ConvPlan pl;
   if (use_tc(desc, leg, g, &pl)) {
     if ((reinterpret_cast<uintptr_t>(w_packed) & 15) != 0) return R4C_ERR_ALIGN;
-    return cuda_status(tc::pack_weight(pl, leg == R4C_LEG_DX, leg == R4C_LEG_DX ? pl.cin : g.cin, w_src,
+    // dX: the conv runs over dY's channels (padded to a multiple of 8); the
+    // padded channels get zero weights
+    return cuda_status(tc::pack_weight(pl, leg == R4C_LEG_DX, leg == R4C_LEG_DX ? g.cout : g.cin, w_src,
                                        src_dtype, w_packed, desc->dtype, s));
   }
   int taps = (leg == R4C_LEG_TFWD || leg == R4C_LEG_TDX) ? 8 : g.k * g.k * g.k;
@@ -398,7 +423,6 @@ int r4c_conv3d_fwd(const r4c_conv_desc* desc, const void* x, const void* w_packe
 
 int r4c_conv3d_dx(const r4c_conv_desc* desc, const void* go, const void* w_packed, void* dx,
                   void* workspace, size_t ws_bytes, r4c_stream_t stream) {
-  (void)workspace; (void)ws_bytes;
   Geom g;
   int st = check_desc(desc, R4C_LEG_DX, &g);
   if (st != R4C_OK) return st;
@@ -408,8 +432,16 @@ int r4c_conv3d_dx(const r4c_conv_desc* desc, const void* go, const void* w_packe
   if (use_stem_dx(desc, R4C_LEG_DX, g))
     return stem::launch_dx(g.n, g.d, g.h, g.w, g.cout, go, w_packed, dx, desc->dtype, s);
   tc::ConvPlan pl;
-  if (use_tc(desc, R4C_LEG_DX, g, &pl))
-    return tc::launch_conv_tuned(pl, go, w_packed, nullptr, dx, desc->dtype, s);
+  if (use_tc(desc, R4C_LEG_DX, g, &pl)) {
+    const void* src = go;
+    if (needs_gpad(g)) {
+      if (!workspace || ws_bytes < gpad_bytes(g)) return R4C_ERR_WORKSPACE;
+      if (launch_cpad_n(go, workspace, g.out_vox(), g.cout, cout_eff(g), desc->dtype, s) != cudaSuccess)
+        return R4C_ERR_CUDA;
+      src = workspace;
+    }
+    return tc::launch_conv_tuned(pl, src, w_packed, nullptr, dx, desc->dtype, s);
+  }
   // dX of a stride-1 conv is a conv of dY with the flipped, transposed kernel
   // and padding k-1-p (negative padding crops).
   generic::FwdParams p{};
@@ -437,21 +469,40 @@ int r4c_conv3d_dw(const r4c_conv_desc* desc, const void* x, const void* go, floa
   tc::ConvPlan tcp;
   if (g.out_vox() > 0 && use_tc(desc, R4C_LEG_DW, g, &tcp)) {
     size_t part_bytes = 0;
-    const size_t xpad = cpad_bytes(g);
-    const size_t need = xpad + tc_dw_ws(g, &part_bytes);
+    const size_t xpad = cpad_bytes(g), gpad = gpad_bytes(g), dwtmp = gpad_dw_bytes(g);
+    const size_t need = xpad + gpad + dwtmp + tc_dw_ws(g, &part_bytes);
     if (ws_bytes < need || !workspace) return R4C_ERR_WORKSPACE;
     if (!x || !go) return R4C_ERR_INVALID;
     const void* xin = x;
+    const void* gin = go;
     char* wsb = static_cast<char*>(workspace);
     if (xpad) {
-      if (launch_cpad(x, workspace, g, desc->dtype, s) != cudaSuccess) return R4C_ERR_CUDA;
-      xin = workspace;
+      if (launch_cpad(x, wsb, g, desc->dtype, s) != cudaSuccess) return R4C_ERR_CUDA;
+      xin = wsb;
       wsb += xpad;
     }
+    float* dw_k = dw;
+    float* db_k = db;
+    if (gpad) {
+      if (launch_cpad_n(go, wsb, g.out_vox(), g.cout, cout_eff(g), desc->dtype, s) != cudaSuccess)
+        return R4C_ERR_CUDA;
+      gin = wsb;
+      wsb += gpad;
+      dw_k = reinterpret_cast<float*>(wsb);
+      db_k = db ? reinterpret_cast<float*>(wsb + align_up((size_t)cout_eff(g) * g.cin * taps * sizeof(float), 256))
+                : nullptr;
+      wsb += dwtmp;
+    }
     bool db_done = false;
-    int rc = tc::launch_dw(g.n, g.d, g.h, g.w, cin_eff(g), g.cin, g.cout, g.k, g.pd, g.ph, g.pw, xin, go, dw, db,
-                           wsb, part_bytes, desc->dtype, s, &db_done);
+    int rc = tc::launch_dw(g.n, g.d, g.h, g.w, cin_eff(g), g.cin, cout_eff(g), g.k, g.pd, g.ph, g.pw, xin, gin, dw_k,
+                           db_k, wsb, part_bytes, desc->dtype, s, &db_done);
     if (rc != R4C_OK) return rc;
+    if (gpad) {  // OIDHW: the real Cout rows are a prefix of the padded result
+      cudaError_t e = cudaMemcpyAsync(dw, dw_k, sizeof(float) * g.cout * g.cin * taps, cudaMemcpyDeviceToDevice, s);
+      if (e == cudaSuccess && db && db_done)
+        e = cudaMemcpyAsync(db, db_k, sizeof(float) * g.cout, cudaMemcpyDeviceToDevice, s);
+      if (e != cudaSuccess) return R4C_ERR_CUDA;
+    }
     if (db && !db_done) {
       float* part = reinterpret_cast<float*>(wsb + part_bytes);
       return cuda_status(generic::launch_db(go, g.out_vox(), g.cout, desc->dtype, part, db, s));

@@ -1,0 +1,432 @@
+// r4c_bn.cu — BatchNorm3d (training statistics) fused with ReLU, NDHWC.
+//
+// The reference's model blocks are Conv3d -> BatchNorm3d -> ReLU
+// (benches/unet_e2e.py:13-20 of the reference), and its design notes put
+// BatchNorm at ~11 ms of its step (docs/DESIGN.md:66). Stock PyTorch runs BN
+// and ReLU as separate kernels: statistics, normalise, ReLU forward; ReLU
+// backward, BN reduction, BN dX — about 13 full passes over the activation.
+// Here the pair takes 5 + 3:
+//   forward   stats (read x)  ->  finalize (C threads)  ->  y = relu(w*(x-mean)*invstd + b) (read x, write y)
+//   backward  sums of g and g*(x-mean), g = dy * [pre-activation > 0] (read dy, x)
+//             -> finalize -> dx = (g - mean(g) - (x-mean)*invstd^2*mean(g*(x-mean))) * w*invstd
+//                           (read dy, x, write dx)
+// These are the normalisation and gradient expressions of PyTorch's own
+// BatchNorm kernels, so the fused pair rounds like the stock one. The ReLU
+// mask is recomputed from x with the forward's own expression, so it is
+// bit-identical to the forward's.
+//
+// Reductions are deterministic: each block owns a fixed voxel range and sums
+// it in a fixed thread order, block partials are summed in block order in
+// double. Elements: bf16 / fp16 storage, fp32 arithmetic; C a multiple of 8
+// (16-byte vectors of 8 channels of one voxel).
+#include <algorithm>
+
+#include "r4c_internal.h"
+
+namespace r4c {
+namespace bn {
+
+constexpr int kMaxThreads = 256;
+
+// Threads per block for C channels: (C/8) vector lanes x R voxel rows.
+static int rows_for(int C) { return std::max(1, kMaxThreads / (C / 8)); }
+
+template <typename T>
+struct Vec8 {
+  uint4 raw;
+  __device__ __forceinline__ void to_f(float* f) const {
+    const T* p = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) f[i] = Elem<T>::to_f(p[i]);
+  }
+  __device__ __forceinline__ void from_f(const float* f) {
+    T* p = reinterpret_cast<T*>(&raw);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) p[i] = Elem<T>::from_f(f[i]);
+  }
+};
+
+// MODE 0: part[b] = (sum u, sum u^2) per channel over the block's voxels,
+//         u = x - pivot (pivot = the first voxel's value: sums of deviations
+//         from a value inside the distribution keep E[u^2] - E[u]^2 free of
+//         the cancellation that E[x^2] - E[x]^2 suffers when |mean| >> std).
+// MODE 1: part[b] = (sum g, sum g*(x - mean)), g = dy * [pre-activation > 0]
+//         (g = dy when relu is 0).
+// Layout: part[b][0..C) first sum, part[b][C..2C) second.
+// Pre-activation of the normalisation, in PyTorch's order of operations.
+__device__ __forceinline__ float bn_pre(float x, float mean, float invstd, float w, float b) {
+  return w * (x - mean) * invstd + b;
+}
+template <typename T, int MODE>
+__global__ void __launch_bounds__(kMaxThreads) sums_kernel(const T* __restrict__ x, const T* __restrict__ dy,
+                                                           const float* __restrict__ af, const float* __restrict__ mi,
+                                                           int64_t vox, int C, int64_t chunk, int relu,
+                                                           float* __restrict__ part) {
+  extern __shared__ float red[];  // [R][2*C]
+  const int nv = C / 8;
+  const int lane = threadIdx.x % nv, row = threadIdx.x / nv;
+  const int R = blockDim.x / nv;
+  const int c0 = lane * 8;
+  float s1[8], s2[8], sc[8], sh[8], mu[8], is[8];
+  {
+    float pv[8];
+    if (MODE == 0) {
+      if (mi) {  // the caller's pivot
+#pragma unroll
+        for (int i = 0; i < 8; ++i) pv[i] = mi[c0 + i];
+      } else {   // voxel 0
+        Vec8<T> p0;
+        p0.raw = *reinterpret_cast<const uint4*>(x + c0);
+        p0.to_f(pv);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      s1[i] = 0.f;
+      s2[i] = 0.f;
+      sc[i] = MODE == 1 ? af[c0 + i] : 0.f;       // gamma
+      sh[i] = MODE == 1 ? af[C + c0 + i] : 0.f;   // beta
+      mu[i] = MODE == 1 ? mi[c0 + i] : pv[i];
+      is[i] = MODE == 1 ? mi[C + c0 + i] : 1.f;
+    }
+  }
+  const int64_t v0 = (int64_t)blockIdx.x * chunk, v1 = min(v0 + chunk, vox);
+  if (row < R) {
+    // four voxels per iteration, loads first (four 16-byte loads in flight)
+    for (int64_t vb = v0 + row; vb < v1; vb += 4 * (int64_t)R) {
+      Vec8<T> a[4], b[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int64_t v = vb + (int64_t)u * R;
+        if (v < v1) {
+          a[u].raw = *reinterpret_cast<const uint4*>(x + v * C + c0);
+          if (MODE == 1) b[u].raw = *reinterpret_cast<const uint4*>(dy + v * C + c0);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int64_t v = vb + (int64_t)u * R;
+        if (v >= v1) break;
+        float xf[8];
+        a[u].to_f(xf);
+        if (MODE == 0) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float u = xf[i] - mu[i];
+            s1[i] += u;
+            s2[i] = fmaf(u, u, s2[i]);
+          }
+        } else {
+          float gf[8];
+          b[u].to_f(gf);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float g = (!relu || bn_pre(xf[i], mu[i], is[i], sc[i], sh[i]) > 0.f) ? gf[i] : 0.f;
+            s1[i] += g;
+            s2[i] = fmaf(g, xf[i] - mu[i], s2[i]);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      red[row * 2 * C + c0 + i] = s1[i];
+      red[row * 2 * C + C + c0 + i] = s2[i];
+    }
+  }
+  __syncthreads();
+  // fixed-order sum over the rows, one thread per output
+  for (int o = threadIdx.x; o < 2 * C; o += blockDim.x) {
+    float acc = 0.f;
+    for (int r = 0; r < R; ++r) acc += red[r * 2 * C + o];
+    part[(int64_t)blockIdx.x * 2 * C + o] = acc;
+  }
+}
+
+// Forward finalize: mean, invstd, and the affine pair (gamma, beta; 1 and 0
+// when absent); running statistics updated with the unbiased variance.
+__global__ void fwd_finalize_kernel(const float* __restrict__ sums_in, int C, double count,
+                                    const float* __restrict__ gamma, const float* __restrict__ beta, float eps,
+                                    float momentum, float* running_mean, float* running_var, float* mean_invstd,
+                                    float* affine) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= C) return;
+  const double s1 = sums_in[c], s2 = sums_in[C + c];
+  const double pivot = sums_in[2 * C + c];             // the stats pass's pivot
+  const double du = s1 / count;                       // mean of x - pivot
+  const double mean = pivot + du;
+  double var = s2 / count - du * du;
+  if (var < 0.0) var = 0.0;
+  const float invstd = (float)(1.0 / sqrt(var + (double)eps));
+  const float g = gamma ? gamma[c] : 1.f, b = beta ? beta[c] : 0.f;
+  mean_invstd[c] = (float)mean;
+  mean_invstd[C + c] = invstd;
+  affine[c] = g;
+  affine[C + c] = b;
+  if (running_mean) {
+    const double unbiased = count > 1.0 ? var * count / (count - 1.0) : var;
+    running_mean[c] = (1.f - momentum) * running_mean[c] + momentum * (float)mean;
+    running_var[c] = (1.f - momentum) * running_var[c] + momentum * (float)unbiased;
+  }
+}
+
+// Sum of the block partials (fixed order, double) into sums[2C]; with
+// `pivots`, also the pivot the statistics pass used into sums[2C:3C) (the
+// caller's, or voxel 0 of x).
+template <typename T>
+__global__ void sum_parts_kernel(const float* __restrict__ part, int S, int C, float* __restrict__ sums, int pivots,
+                                 const float* __restrict__ pivot, const T* __restrict__ x) {
+  // one warp per output: lane l sums partials l, l+32, ... in order, then a
+  // fixed butterfly over the lanes (same result on every run)
+  const int o = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (o < 2 * C) {
+    double a = 0.0;
+    for (int s = lane; s < S; s += 32) a += part[(int64_t)s * 2 * C + o];
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) a += __shfl_xor_sync(0xffffffffu, a, off);
+    if (lane == 0) sums[o] = (float)a;
+  }
+  if (pivots && lane == 0 && o < C) sums[2 * C + o] = pivot ? pivot[o] : Elem<T>::to_f(x[o]);
+}
+
+// Backward finalize from (sum g, sum g*(x - mean)): dgamma = sum g*(x-mean) *
+// invstd, dbeta = sum g, and the dX coefficients (mean(g), invstd^2 *
+// mean(g*(x-mean)), gamma * invstd).
+__global__ void bwd_finalize_kernel(const float* __restrict__ sums, const float* __restrict__ mean_invstd,
+                                    const float* __restrict__ affine, int C, double count, float* dgamma,
+                                    float* dbeta, float* coef) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= C) return;
+  const float sg = sums[c], sgx = sums[C + c];
+  const float invstd = mean_invstd[C + c];
+  if (dgamma) dgamma[c] = sgx * invstd;
+  if (dbeta) dbeta[c] = sg;
+  const float norm = (float)(1.0 / count);
+  coef[c] = sg * norm;
+  coef[C + c] = invstd * invstd * (sgx * norm);
+  coef[2 * C + c] = affine[c] * invstd;
+}
+
+// Elementwise passes: each thread takes U = 4 vectors of 8 channels per
+// iteration (all loads issued before any use, so four 16-byte loads per
+// thread are in flight), then grid-strides.
+constexpr int kU = 4;
+
+// y = relu(w*(x-mean)*invstd + b) (relu optional).
+template <typename T>
+__global__ void __launch_bounds__(256) apply_kernel(const T* __restrict__ x, T* __restrict__ y,
+                                                    const float* __restrict__ mi, const float* __restrict__ af,
+                                                    int64_t nvec, int C, int relu) {
+  const int nv = C / 8;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t base = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; base < nvec; base += stride * kU) {
+    Vec8<T> a[kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int64_t i = base + u * stride;
+      if (i < nvec) a[u].raw = __ldcs(reinterpret_cast<const uint4*>(x) + i);
+    }
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int64_t i = base + u * stride;
+      if (i >= nvec) break;
+      const int c0 = (int)(i % nv) * 8;
+      float f[8];
+      a[u].to_f(f);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int c = c0 + k;
+        const float v = bn_pre(f[k], __ldg(mi + c), __ldg(mi + C + c), __ldg(af + c), __ldg(af + C + c));
+        f[k] = relu ? (v > 0.f ? v : 0.f) : v;
+      }
+      a[u].from_f(f);
+      reinterpret_cast<uint4*>(y)[i] = a[u].raw;
+    }
+  }
+}
+
+// dx = (g - mean(g) - (x-mean) * f1) * f2, g = dy * [pre-activation > 0] (relu) or dy.
+template <typename T>
+__global__ void __launch_bounds__(256) dx_kernel(const T* __restrict__ dy, const T* __restrict__ x, T* __restrict__ dx,
+                                                 const float* __restrict__ mi, const float* __restrict__ af,
+                                                 const float* __restrict__ coef, int64_t nvec, int C, int relu) {
+  const int nv = C / 8;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t base = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; base < nvec; base += stride * kU) {
+    Vec8<T> a[kU], b[kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int64_t i = base + u * stride;
+      if (i < nvec) {
+        a[u].raw = __ldcs(reinterpret_cast<const uint4*>(x) + i);
+        b[u].raw = __ldcs(reinterpret_cast<const uint4*>(dy) + i);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int64_t i = base + u * stride;
+      if (i >= nvec) break;
+      const int c0 = (int)(i % nv) * 8;
+      float xf[8], gf[8];
+      a[u].to_f(xf);
+      b[u].to_f(gf);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int c = c0 + k;
+        float g = gf[k];
+        const float m = __ldg(mi + c);
+        if (relu && !(bn_pre(xf[k], m, __ldg(mi + C + c), __ldg(af + c), __ldg(af + C + c)) > 0.f)) g = 0.f;
+        xf[k] = (g - __ldg(coef + c) - (xf[k] - m) * __ldg(coef + C + c)) * __ldg(coef + 2 * C + c);
+      }
+      a[u].from_f(xf);
+      reinterpret_cast<uint4*>(dx)[i] = a[u].raw;
+    }
+  }
+}
+
+struct Split {
+  int S;
+  int64_t chunk;
+};
+
+static Split split_for(int64_t vox) {
+  // about two blocks per SM, at least 512 voxels each
+  Split s;
+  s.chunk = std::max<int64_t>(512, (vox + 295) / 296);
+  s.S = (int)std::max<int64_t>(1, (vox + s.chunk - 1) / s.chunk);
+  return s;
+}
+
+// One resident wave (the elementwise kernels hold 45-64 registers a thread:
+// four 256-thread blocks per SM).
+static int grid_for(int64_t nvec) {
+  return (int)std::max<int64_t>(1, std::min<int64_t>((nvec + 255) / 256, 148 * 4));
+}
+
+static bool ok_args(const void* p, int64_t vox, int C, int dtype) {
+  return p && vox >= 0 && C > 0 && C % 8 == 0 && C <= 2048 && (dtype == R4C_BF16 || dtype == R4C_F16) &&
+         (reinterpret_cast<uintptr_t>(p) & 15) == 0;
+}
+
+}  // namespace bn
+}  // namespace r4c
+
+using namespace r4c::bn;
+
+extern "C" {
+
+size_t r4c_bn_workspace_size(int64_t vox, int C) {
+  if (C <= 0) return 0;
+  const Split s = split_for(vox);
+  return r4c::align_up((size_t)s.S * 2 * C * sizeof(float), 256);
+}
+
+static int launch_sums(int mode, const void* x, const void* dy, const float* ss, const float* mi, int64_t vox, int C,
+                       int dtype, int relu, float* sums, void* ws, size_t ws_bytes, cudaStream_t s) {
+  const Split sp = split_for(vox);
+  if (!ws || ws_bytes < r4c_bn_workspace_size(vox, C)) return R4C_ERR_WORKSPACE;
+  float* part = static_cast<float*>(ws);
+  const int R = rows_for(C);
+  const int threads = R * (C / 8);
+  const size_t smem = (size_t)R * 2 * C * sizeof(float);
+  if (smem > 48 * 1024) return R4C_ERR_UNSUPPORTED;
+  if (dtype == R4C_BF16) {
+    const auto* xb = static_cast<const __nv_bfloat16*>(x);
+    const auto* gb = static_cast<const __nv_bfloat16*>(dy);
+    if (mode == 0) sums_kernel<__nv_bfloat16, 0><<<sp.S, threads, smem, s>>>(xb, gb, ss, mi, vox, C, sp.chunk, relu, part);
+    else sums_kernel<__nv_bfloat16, 1><<<sp.S, threads, smem, s>>>(xb, gb, ss, mi, vox, C, sp.chunk, relu, part);
+  } else {
+    const auto* xh = static_cast<const __half*>(x);
+    const auto* gh = static_cast<const __half*>(dy);
+    if (mode == 0) sums_kernel<__half, 0><<<sp.S, threads, smem, s>>>(xh, gh, ss, mi, vox, C, sp.chunk, relu, part);
+    else sums_kernel<__half, 1><<<sp.S, threads, smem, s>>>(xh, gh, ss, mi, vox, C, sp.chunk, relu, part);
+  }
+  if (dtype == R4C_BF16)
+    sum_parts_kernel<__nv_bfloat16><<<(2 * C + 7) / 8, 256, 0, s>>>(part, sp.S, C, sums, mode == 0, mi,
+                                                                     static_cast<const __nv_bfloat16*>(x));
+  else
+    sum_parts_kernel<__half><<<(2 * C + 7) / 8, 256, 0, s>>>(part, sp.S, C, sums, mode == 0, mi,
+                                                              static_cast<const __half*>(x));
+  r4c::note_launches(2);
+  return cudaGetLastError() == cudaSuccess ? R4C_OK : R4C_ERR_CUDA;
+}
+
+int r4c_bn_stats(const void* x, int64_t vox, int C, int dtype, const float* pivot, float* sums, void* ws,
+                 size_t ws_bytes, r4c_stream_t stream) {
+  if (!ok_args(x, vox, C, dtype) || !sums) return R4C_ERR_INVALID;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (vox == 0) {
+    if (cudaMemsetAsync(sums, 0, 2 * C * sizeof(float), s) != cudaSuccess) return R4C_ERR_CUDA;
+    if (pivot) return cudaMemcpyAsync(sums + 2 * C, pivot, C * sizeof(float), cudaMemcpyDeviceToDevice, s) ==
+                              cudaSuccess ? R4C_OK : R4C_ERR_CUDA;
+    return cudaMemsetAsync(sums + 2 * C, 0, C * sizeof(float), s) == cudaSuccess ? R4C_OK : R4C_ERR_CUDA;
+  }
+  return launch_sums(0, x, nullptr, nullptr, pivot, vox, C, dtype, 0, sums, ws, ws_bytes, s);
+}
+
+int r4c_bn_finalize(const float* sums, double count, int C, const float* gamma, const float* beta, float eps,
+                    float momentum, float* running_mean, float* running_var, float* mean_invstd,
+                    float* affine, r4c_stream_t stream) {
+  if (!sums || !mean_invstd || !affine || C <= 0 || count <= 0.0) return R4C_ERR_INVALID;
+  if ((running_mean == nullptr) != (running_var == nullptr)) return R4C_ERR_INVALID;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  fwd_finalize_kernel<<<(C + 127) / 128, 128, 0, s>>>(sums, C, count, gamma, beta, eps, momentum, running_mean,
+                                                       running_var, mean_invstd, affine);
+  r4c::note_launches(1);
+  return cudaGetLastError() == cudaSuccess ? R4C_OK : R4C_ERR_CUDA;
+}
+
+int r4c_bn_relu_fwd(const void* x, void* y, const float* mean_invstd, const float* affine, int64_t vox, int C,
+                    int dtype, int relu, r4c_stream_t stream) {
+  if (!ok_args(x, vox, C, dtype) || !ok_args(y, vox, C, dtype) || !mean_invstd || !affine) return R4C_ERR_INVALID;
+  if (vox == 0) return R4C_OK;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int64_t nvec = vox * (C / 8);
+  if (dtype == R4C_BF16)
+    apply_kernel<__nv_bfloat16><<<grid_for(nvec), 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x),
+                                                               static_cast<__nv_bfloat16*>(y), mean_invstd, affine, nvec,
+                                                               C, relu);
+  else
+    apply_kernel<__half><<<grid_for(nvec), 256, 0, s>>>(static_cast<const __half*>(x), static_cast<__half*>(y),
+                                                        mean_invstd, affine, nvec, C, relu);
+  r4c::note_launches(1);
+  return cudaGetLastError() == cudaSuccess ? R4C_OK : R4C_ERR_CUDA;
+}
+
+int r4c_bn_relu_bwd_sums(const void* dy, const void* x, const float* mean_invstd, const float* affine,
+                         int64_t vox, int C, int dtype, int relu, float* sums, void* ws, size_t ws_bytes,
+                         r4c_stream_t stream) {
+  if (!ok_args(x, vox, C, dtype) || !ok_args(dy, vox, C, dtype) || !affine || !mean_invstd || !sums)
+    return R4C_ERR_INVALID;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (vox == 0) return cudaMemsetAsync(sums, 0, 2 * C * sizeof(float), s) == cudaSuccess ? R4C_OK : R4C_ERR_CUDA;
+  return launch_sums(1, x, dy, affine, mean_invstd, vox, C, dtype, relu, sums, ws, ws_bytes, s);
+}
+
+int r4c_bn_relu_bwd_dx(const void* dy, const void* x, void* dx, const float* mean_invstd, const float* affine,
+                       const float* sums, double count, int64_t vox, int C, int dtype, int relu, float* dgamma,
+                       float* dbeta, float* coef, r4c_stream_t stream) {
+  if (!ok_args(x, vox, C, dtype) || !ok_args(dy, vox, C, dtype) || !affine || !mean_invstd || !sums || !coef)
+    return R4C_ERR_INVALID;
+  if (dx && !ok_args(dx, vox, C, dtype)) return R4C_ERR_INVALID;
+  if (count <= 0.0) return R4C_ERR_INVALID;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  bwd_finalize_kernel<<<(C + 127) / 128, 128, 0, s>>>(sums, mean_invstd, affine, C, count, dgamma, dbeta, coef);
+  r4c::note_launches(1);
+  if (dx && vox > 0) {
+    const int64_t nvec = vox * (C / 8);
+    if (dtype == R4C_BF16)
+      dx_kernel<__nv_bfloat16><<<grid_for(nvec), 256, 0, s>>>(
+          static_cast<const __nv_bfloat16*>(dy), static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(dx),
+          mean_invstd, affine, coef, nvec, C, relu);
+    else
+      dx_kernel<__half><<<grid_for(nvec), 256, 0, s>>>(static_cast<const __half*>(dy), static_cast<const __half*>(x),
+                                                       static_cast<__half*>(dx), mean_invstd, affine, coef, nvec, C,
+                                                       relu);
+    r4c::note_launches(1);
+  }
+  return cudaGetLastError() == cudaSuccess ? R4C_OK : R4C_ERR_CUDA;
+}
+
+}  // extern "C"

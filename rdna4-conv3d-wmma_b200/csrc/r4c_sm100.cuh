@@ -63,6 +63,33 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   return true;
 }
 
+// Bounded wait with an abort flag, shared by the kernels' pipeline roles:
+// returns true once the barrier phase completes; false when `*abort` is set
+// by another role, or when the wait has lasted `limit_ns` (globaltimer),
+// in which case it sets `*abort`, stores `code` into `*err` and returns.
+// The clock is read only every 64 polls and only once a wait has lasted a
+// while; `nap` > 0 sleeps between polls (leaves issue slots to other warps).
+__device__ __forceinline__ bool bounded_wait(uint64_t* bar, uint32_t parity, uint64_t limit_ns, volatile int* abort,
+                                             int* err, int code, uint32_t nap) {
+  uint64_t deadline = 0;
+  uint32_t spins = 0;
+  while (!mbar_try_wait(bar, parity)) {
+    if (nap) __nanosleep(nap);
+    if (((++spins) & 63u) == 0) {
+      if (*abort) return false;
+      const uint64_t now = global_timer_ns();
+      if (deadline == 0) {
+        deadline = now + limit_ns;
+      } else if (now > deadline) {
+        *abort = 1;
+        atomicExch(err, code);
+        return false;
+      }
+    }
+  }
+  return true;
+}
+
 // ---- TMA ----------------------------------------------------------------
 __device__ __forceinline__ void tma_load_5d(void* dst, const void* tmap, uint64_t* bar, int c0, int c1,
                                             int c2, int c3, int c4) {

@@ -776,23 +776,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_conv_kernel(const __grid_const
   // Bounded wait. `nap` > 0 makes the polling thread sleep between polls so
   // that warps which only wait leave issue slots to the MMA thread.
   auto wait = [&](uint64_t* bar, uint32_t par, uint32_t nap = 0) -> bool {
-    uint64_t deadline = 0;  // the clock is read only once a wait has lasted a while
-    uint32_t spins = 0;
-    while (!mbar_try_wait(bar, par)) {
-      if (nap) __nanosleep(nap);
-      if (((++spins) & 63u) == 0) {
-        if (*abort_flag) return false;
-        const uint64_t now = global_timer_ns();
-        if (deadline == 0) {
-          deadline = now + kWaitNs;
-        } else if (now > deadline) {
-          *abort_flag = 1;
-          atomicExch(&g_r4c_dev_error, 1);
-          return false;
-        }
-      }
-    }
-    return true;
+    return bounded_wait(bar, par, kWaitNs, abort_flag, &g_r4c_dev_error, 1, nap);
   };
   const int set_cols = a.P * a.slot_w * a.mtiles;
 
@@ -918,8 +902,10 @@ __global__ void __launch_bounds__(kThreads, 1) tc_conv_kernel(const __grid_const
         mma_commit(&tfull[set]);
         if (a.nsets == 2) set ^= 1;
       }
+      // every MMA issued must have completed before TMEM is released, abort
+      // or not: this wait ignores the abort flag (bounded by time only)
       mma_commit(mdone);
-      wait(mdone, 0);
+      mbar_wait_bounded(mdone, 0, global_timer_ns() + kWaitNs);
     }
   } else {
     // ---------------- epilogue (warps 2..9) ----------------

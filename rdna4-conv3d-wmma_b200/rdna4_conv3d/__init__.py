@@ -24,6 +24,8 @@ from rdna4_conv3d.conv3d_wmma import (
     wmma_ok_fwd,
 )
 
+from rdna4_conv3d import ops as _ops  # noqa: E402,F401  (registers torch.ops.r4c.*)
+
 __version__ = "0.1.0"
 __all__ = [
     "Conv3dWmma",

@@ -61,10 +61,14 @@ def _bind(lib) -> None:
     X = ctypes.POINTER(ConvexDesc)
     sz = ctypes.c_size_t
     i = ctypes.c_int
+    i64 = ctypes.c_int64
+    dbl = ctypes.c_double
+    flt = ctypes.c_float
     sig = {
         "r4c_strerror": ([i], ctypes.c_char_p),
         "r4c_version": ([], i),
         "r4c_device_error": ([P, i], i),
+        "r4c_watchdog_selftest": ([ctypes.c_uint64, P], i),
         "r4c_launch_count": ([], ctypes.c_uint64),
         "r4c_plan_kernel": ([D, i], i),
         "r4c_describe_plan": ([D, i, ctypes.c_char_p, sz], i),
@@ -77,6 +81,12 @@ def _bind(lib) -> None:
         "r4c_tconv_fwd": ([D, P, P, P, P, P, sz, P], i),
         "r4c_tconv_dx": ([D, P, P, P, P, sz, P], i),
         "r4c_tconv_dw": ([D, P, P, P, P, P, sz, P], i),
+        "r4c_bn_workspace_size": ([i64, i], sz),
+        "r4c_bn_stats": ([P, i64, i, i, P, P, P, sz, P], i),
+        "r4c_bn_finalize": ([P, dbl, i, P, P, flt, flt, P, P, P, P, P], i),
+        "r4c_bn_relu_fwd": ([P, P, P, P, i64, i, i, i, P], i),
+        "r4c_bn_relu_bwd_sums": ([P, P, P, P, i64, i, i, i, P, P, sz, P], i),
+        "r4c_bn_relu_bwd_dx": ([P, P, P, P, P, P, dbl, i64, i, i, i, P, P, P, P], i),
         "r4c_convex_plan": ([X], i),
         "r4c_convex_workspace_size": ([X, i], sz),
         "r4c_convex_fwd": ([X, P, P, P, P, P, sz, P], i),
@@ -352,9 +362,78 @@ def convex_dw(desc: ConvexDesc, x_cl: torch.Tensor, go_cl: torch.Tensor, want_db
     return dw, db
 
 
+# ---------------------------------------------------------------------------
+# BatchNorm3d + ReLU (r4c_bn_*)
+# ---------------------------------------------------------------------------
+def bn_relu_forward(x_cl: torch.Tensor, gamma, beta, running_mean, running_var, momentum: float, eps: float,
+                    relu: bool, sums_hook=None, pivot=None):
+    """Training forward. Returns (y, mean_invstd, affine, count).
+    ``sums_hook(sums, count)``, when given, may all-reduce the per-channel
+    sums in place before they are finalised and returns the total count (a
+    volume sharded over ranks: every rank then passes the same ``pivot``)."""
+    dev = _require_cuda(x_cl)
+    C = int(x_cl.shape[1])
+    vox = x_cl.numel() // C
+    L = lib()
+    f32 = dict(dtype=torch.float32, device=dev)
+    ws = torch.empty(int(L.r4c_bn_workspace_size(vox, C)), dtype=torch.uint8, device=dev)
+    sums = torch.empty(3 * C, **f32)
+    mi = torch.empty(2 * C, **f32)
+    ss = torch.empty(2 * C, **f32)
+    y = torch.empty_like(x_cl, memory_format=torch.channels_last_3d)
+    dt = dtype_code(x_cl.dtype)
+    with torch.cuda.device(dev):
+        st = L.r4c_bn_stats(_ptr(x_cl), vox, C, dt, _ptr(pivot), _ptr(sums), _ptr(ws), ws.numel(), _stream(dev))
+        _check(st, "r4c_bn_stats")
+        count = float(vox)
+        if sums_hook is not None:
+            count = float(sums_hook(sums, count))
+        st = L.r4c_bn_finalize(_ptr(sums), count, C, _ptr(gamma), _ptr(beta), float(eps), float(momentum),
+                               _ptr(running_mean), _ptr(running_var), _ptr(mi), _ptr(ss), _stream(dev))
+        _check(st, "r4c_bn_finalize")
+        st = L.r4c_bn_relu_fwd(_ptr(x_cl), _ptr(y), _ptr(mi), _ptr(ss), vox, C, dt, 1 if relu else 0, _stream(dev))
+        _check(st, "r4c_bn_relu_fwd")
+    return y, mi, ss, count
+
+
+def bn_relu_backward(dy_cl: torch.Tensor, x_cl: torch.Tensor, mean_invstd, affine, count: float, relu: bool,
+                     need_dx: bool = True, sums_hook=None):
+    """(dx or None, dgamma, dbeta), fp32 parameter gradients."""
+    dev = _require_cuda(dy_cl, x_cl)
+    C = int(x_cl.shape[1])
+    vox = x_cl.numel() // C
+    L = lib()
+    f32 = dict(dtype=torch.float32, device=dev)
+    ws = torch.empty(int(L.r4c_bn_workspace_size(vox, C)), dtype=torch.uint8, device=dev)
+    sums = torch.empty(2 * C, **f32)
+    dg = torch.empty(C, **f32)
+    db = torch.empty(C, **f32)
+    coef = torch.empty(3 * C, **f32)
+    dx = torch.empty_like(x_cl, memory_format=torch.channels_last_3d) if need_dx else None
+    dt = dtype_code(x_cl.dtype)
+    with torch.cuda.device(dev):
+        st = L.r4c_bn_relu_bwd_sums(_ptr(dy_cl), _ptr(x_cl), _ptr(mean_invstd), _ptr(affine), vox, C, dt,
+                                    1 if relu else 0, _ptr(sums), _ptr(ws), ws.numel(), _stream(dev))
+        _check(st, "r4c_bn_relu_bwd_sums")
+        if sums_hook is not None:
+            sums_hook(sums, None)
+        st = L.r4c_bn_relu_bwd_dx(_ptr(dy_cl), _ptr(x_cl), _ptr(dx), _ptr(mean_invstd), _ptr(affine),
+                                  _ptr(sums), float(count), vox, C, dt, 1 if relu else 0, _ptr(dg), _ptr(db),
+                                  _ptr(coef), _stream(dev))
+        _check(st, "r4c_bn_relu_bwd_dx")
+    return dx, dg, db
+
+
 def launch_count() -> int:
     """Kernels launched by the native library so far in this process."""
     return int(lib().r4c_launch_count())
+
+
+def watchdog_selftest(limit_ns: int, device=None) -> None:
+    """Launch the bounded-wait self-test (a wait that runs out after limit_ns)."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    with torch.cuda.device(dev):
+        _check(lib().r4c_watchdog_selftest(int(limit_ns), _stream(dev)), "r4c_watchdog_selftest")
 
 
 def device_error(device=None, clear: bool = True) -> int:

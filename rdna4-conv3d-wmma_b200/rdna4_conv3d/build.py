@@ -15,7 +15,7 @@ PKG_DIR = os.path.dirname(os.path.abspath(__file__))
 SRC_DIR = os.path.join(os.path.dirname(PKG_DIR), "csrc")
 INC_DIR = os.path.join(os.path.dirname(os.path.dirname(PKG_DIR)), "include")
 OUT = os.path.join(PKG_DIR, "libr4c_conv3d.so")
-SOURCES = ["r4c_api.cu", "r4c_generic.cu", "r4c_tc.cu", "r4c_tc_dw.cu", "r4c_tc_stem.cu", "r4c_tc_stem_dx.cu", "r4c_tc_tconv.cu", "r4c_noalloc.cu", "r4c_general.cu"]
+SOURCES = ["r4c_api.cu", "r4c_generic.cu", "r4c_tc.cu", "r4c_tc_dw.cu", "r4c_tc_stem.cu", "r4c_tc_stem_dx.cu", "r4c_tc_tconv.cu", "r4c_noalloc.cu", "r4c_general.cu", "r4c_bn.cu", "r4c_watchdog.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -57,11 +57,16 @@ class UNet3D(nn.Module):
 
 
 def unet3d(base: int = 24, levels: int = 4, in_channels: int = 1, n_classes: int = 4, wmma: bool = True,
-           device=None) -> UNet3D:
+           device=None, fuse_bn: bool = None) -> UNet3D:
     """The UNet3D on this package's kernels (``wmma=True``) or on stock PyTorch,
-    channels_last_3d parameters on ``device``."""
+    channels_last_3d parameters on ``device``. ``fuse_bn`` (default: same as
+    ``wmma``) runs each BatchNorm3d + ReLU pair on the fused kernels; the
+    state_dict keys are those of the stock model either way."""
     conv, tconv = (Conv3dWmma, ConvTranspose3dWmma) if wmma else (nn.Conv3d, nn.ConvTranspose3d)
     net = UNet3D(in_channels, n_classes, base, levels, conv, tconv)
+    if wmma if fuse_bn is None else fuse_bn:
+        from .bn_relu import fuse_bn_relu
+        fuse_bn_relu(net)
     if device is not None:
         net = net.to(device)
     return net.to(memory_format=torch.channels_last_3d)

@@ -107,3 +107,51 @@ def test_in_scope_cuda_call_without_gpu_raises():
     with pytest.raises(_native.NativeError):
         _native.pack_weight(_native.make_desc(1, 4, 4, 4, 8, 8, 3, (1, 1, 1), torch.bfloat16), 0,
                             torch.randn(8, 8, 3, 3, 3))
+
+
+def test_fuse_bn_relu_structure_and_cpu_fallback():
+    """(BatchNorm3d, ReLU) pairs become (BatchNormReLU3d, Identity) with the
+    same state_dict; on CPU the module runs stock BatchNorm3d + ReLU."""
+    from rdna4_conv3d.bn_relu import BatchNormReLU3d, fuse_bn_relu
+    from rdna4_conv3d.unet3d import unet3d
+    torch.manual_seed(0)
+    stock = unet3d(8, levels=2, wmma=False)
+    fused = unet3d(8, levels=2, wmma=False, fuse_bn=True)
+    assert sum(isinstance(m, BatchNormReLU3d) for m in fused.modules()) == 6   # 3 blocks x 2
+    assert set(stock.state_dict()) == set(fused.state_dict())
+    fused.load_state_dict(stock.state_dict())
+    x = torch.randn(2, 1, 8, 8, 8).contiguous(memory_format=torch.channels_last_3d)
+    torch.testing.assert_close(fused(x), stock(x))
+    for a, b in zip(stock.buffers(), fused.buffers()):    # running statistics updated alike
+        torch.testing.assert_close(a, b)
+    seq = torch.nn.Sequential(torch.nn.BatchNorm3d(4), torch.nn.ReLU(), torch.nn.BatchNorm3d(4))
+    assert fuse_bn_relu(seq) == 1 and isinstance(seq[1], torch.nn.Identity)
+    assert type(seq[2]) is torch.nn.BatchNorm3d
+
+
+def test_torch_ops_registered_with_fake_kernels():
+    """torch.ops.r4c.* exist and their fake kernels give shapes, dtypes and the
+    NDHWC layout without running anything (FakeTensor on a CPU-only host)."""
+    from torch._subclasses.fake_tensor import FakeTensorMode
+    import rdna4_conv3d  # noqa: F401
+    cl = torch.channels_last_3d
+    with FakeTensorMode():
+        x = torch.empty(2, 24, 8, 16, 16, dtype=torch.bfloat16).contiguous(memory_format=cl)
+        w = torch.empty(48, 24, 3, 3, 3)
+        y = torch.ops.r4c.conv3d_fwd(x, w, None, [1, 1, 1])
+        assert y.shape == (2, 48, 8, 16, 16) and y.dtype == torch.bfloat16
+        assert y.is_contiguous(memory_format=cl)
+        y0 = torch.ops.r4c.conv3d_fwd(x, w, None, [0, 1, 1])
+        assert y0.shape == (2, 48, 6, 16, 16)
+        dx = torch.ops.r4c.conv3d_dx(y, w, list(x.shape), [1, 1, 1])
+        assert dx.shape == x.shape and dx.is_contiguous(memory_format=cl)
+        dw, db = torch.ops.r4c.conv3d_dw(x, y, list(w.shape), [1, 1, 1], True)
+        assert dw.shape == w.shape and dw.dtype == torch.float32 and db.shape == (48,)
+        _, db0 = torch.ops.r4c.conv3d_dw(x, y, list(w.shape), [1, 1, 1], False)
+        assert db0.shape == (0,)
+        wt = torch.empty(24, 12, 2, 2, 2)
+        t = torch.ops.r4c.tconv_fwd(x, wt, None)
+        assert t.shape == (2, 12, 16, 32, 32)
+        assert torch.ops.r4c.tconv_dx(t, wt, list(x.shape)).shape == x.shape
+        tdw, tdb = torch.ops.r4c.tconv_dw(x, t, list(wt.shape), True)
+        assert tdw.shape == wt.shape and tdb.shape == (12,)

@@ -1,0 +1,91 @@
+"""Fused BatchNorm3d + ReLU kernels (r4c_bn_*) on a B200.
+
+Against stock BatchNorm3d + ReLU in fp32 on the same bf16/fp16-rounded
+NDHWC activations: forward output (max-rel 2e-2, the output is rounded to
+the activation dtype), running statistics, and the gradients dX (max-rel
+2e-2), dgamma and dbeta (norm-rel 3e-2). The statistics are fp32 sums, so
+they match far inside that.
+"""
+import pytest
+import torch
+import torch.nn.functional as F
+
+import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("relu", [True, False], ids=["relu", "bn"])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16], ids=["bf16", "fp16"])
+@pytest.mark.parametrize("shape", [(4, 24, 16, 32, 32), (2, 48, 8, 16, 16), (1, 192, 4, 8, 8), (3, 8, 5, 7, 9),
+                                   (4, 24, 64, 128, 128)], ids=lambda s: "x".join(map(str, s)))
+def test_bn_relu_matches_stock(cuda_ready, shape, dtype, relu):
+    from rdna4_conv3d import _native
+    from rdna4_conv3d.bn_relu import BatchNormReLU3d
+    C = shape[1]
+    g = torch.Generator().manual_seed(C)
+    x = (torch.randn(shape, generator=g) * 2.0 + 3.0).to(dtype)        # |mean| > std: tests the pivot
+    gy = torch.randn(shape, generator=g).to(dtype)
+    ref = torch.nn.BatchNorm3d(C)
+    with torch.no_grad():
+        ref.weight.copy_(torch.rand(C, generator=g) + 0.5)
+        ref.bias.copy_(torch.randn(C, generator=g) * 0.1)
+    mod = BatchNormReLU3d(C, relu=relu).cuda()
+    mod.load_state_dict(ref.state_dict())
+    xg = x.cuda().contiguous(memory_format=torch.channels_last_3d).requires_grad_(True)
+    n0 = _native.launch_count()
+    y = mod(xg)
+    y.backward(gy.cuda().contiguous(memory_format=torch.channels_last_3d))
+    torch.cuda.synchronize()
+    assert _native.launch_count() - n0 >= 6          # stats, finalize, apply, bwd sums, finalize, dX
+    assert y.dtype == dtype and y.is_contiguous(memory_format=torch.channels_last_3d)
+
+    xr = x.float().requires_grad_(True)
+    yr = ref(xr)
+    if relu:
+        yr = F.relu(yr)
+    yr.backward(gy.float())
+    assert O.max_rel(y.float().cpu(), yr) <= 2e-2
+    assert O.max_rel(xg.grad.float().cpu(), xr.grad) <= 2e-2
+    assert O.norm_rel(mod.weight.grad.cpu(), ref.weight.grad) <= 3e-2
+    assert O.norm_rel(mod.bias.grad.cpu(), ref.bias.grad) <= 3e-2
+    # fp32 sums of the same inputs: far inside the stated bound
+    assert O.norm_rel(mod.weight.grad.cpu(), ref.weight.grad) <= 1e-3
+    assert O.norm_rel(mod.bias.grad.cpu(), ref.bias.grad) <= 1e-3
+    torch.testing.assert_close(mod.running_mean.cpu(), ref.running_mean, rtol=1e-4, atol=1e-5)
+    torch.testing.assert_close(mod.running_var.cpu(), ref.running_var, rtol=1e-4, atol=1e-5)
+    assert int(mod.num_batches_tracked) == 1
+
+
+def test_bn_relu_deterministic(cuda_ready):
+    from rdna4_conv3d.bn_relu import BatchNormReLU3d
+    mod = BatchNormReLU3d(48).cuda()
+    x = torch.randn(2, 48, 8, 16, 16, device="cuda", dtype=torch.bfloat16).contiguous(
+        memory_format=torch.channels_last_3d).requires_grad_(True)
+    gy = torch.randn_like(x)
+    outs = []
+    for _ in range(2):
+        x.grad = None
+        mod.weight.grad = None
+        y = mod(x)
+        y.backward(gy)
+        outs.append((y.detach().clone(), x.grad.clone(), mod.weight.grad.clone()))
+    for a, b in zip(*outs):
+        assert torch.equal(a, b)
+
+
+def test_bn_relu_eval_and_fallbacks(cuda_ready):
+    """Eval mode (running statistics) and NCDHW inputs take the stock path."""
+    from rdna4_conv3d import _native
+    from rdna4_conv3d.bn_relu import BatchNormReLU3d
+    mod = BatchNormReLU3d(16).cuda()
+    ref = torch.nn.BatchNorm3d(16).cuda()
+    x = torch.randn(2, 16, 4, 6, 8, device="cuda", dtype=torch.bfloat16)
+    mod.eval()
+    ref.eval()
+    n0 = _native.launch_count()
+    torch.testing.assert_close(mod(x.contiguous(memory_format=torch.channels_last_3d)), F.relu(ref(x)))
+    mod.train()
+    ref.train()
+    torch.testing.assert_close(mod(x), F.relu(ref(x)))           # NCDHW: stock
+    assert _native.launch_count() == n0

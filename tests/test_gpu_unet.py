@@ -48,7 +48,8 @@ def test_unet3d_base24_amp_loss_parity(cuda_ready):
     assert _native.launch_count() - n0 > 40 * 50, "the UNet did not run on the native kernels"
     assert _native.device_error() == 0
     diffs = [abs(a - b) for a, b in zip(ref, got)]
-    assert max(diffs) <= LOSS_TOL, (max(diffs), ref[0], ref[-1], got[-1])
+    print("per-step |loss_ours - loss_stock|:", [f"{d:.2e}" for d in diffs])
+    assert max(diffs) <= LOSS_TOL, (max(diffs), ref[0], ref[-1], got[-1], [round(d, 5) for d in diffs])
     assert ref[-1] < ref[0]          # the run trains at all
 
 

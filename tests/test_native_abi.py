@@ -52,10 +52,12 @@ def test_plan_families():
     assert _native.plan_kernel(_d(), _native.LEG_FWD) == _native.KERNEL_TC
     assert _native.plan_kernel(_d(), _native.LEG_DX) == _native.KERNEL_TC
     # odd input channels: the forward pads them to 8 in workspace and stays on
-    # tcgen05; dX of that layer (input channels = Cout = 7) uses the SIMT kernels
+    # tcgen05; dX and dW of that layer pad dY's 7 channels to 8 the same way
     assert _native.plan_kernel(_d(cin=5, cout=7), _native.LEG_FWD) == _native.KERNEL_TC
     assert _native.workspace_bytes(_d(cin=5, cout=7), _native.LEG_FWD) >= 2 * 16 * 32 * 32 * 8 * 2
-    assert _native.plan_kernel(_d(cin=5, cout=7), _native.LEG_DX) == _native.KERNEL_GENERIC
+    assert _native.plan_kernel(_d(cin=5, cout=7), _native.LEG_DX) == _native.KERNEL_TC
+    assert _native.workspace_bytes(_d(cin=5, cout=7), _native.LEG_DX) >= 2 * 16 * 32 * 32 * 8 * 2
+    assert _native.plan_kernel(_d(cin=24, cout=4, k=1, p=0), _native.LEG_DW) == _native.KERNEL_TC
     # the generic family can be forced
     assert _native.plan_kernel(_d(force=1), _native.LEG_FWD) == _native.KERNEL_GENERIC
     assert "tcgen05" in _native.describe_plan(_d(), _native.LEG_FWD)
@@ -147,7 +149,9 @@ def test_workspace_sizes():
 
 
 def test_packed_sizes():
-    assert _native.packed_weight_bytes(_d(cin=5, cout=7), _native.LEG_DX) == 5 * 7 * 27 * 2
+    # SIMT layout: plain [tap][Cout][Cin]; tcgen05 layouts hold at least the padded weight
+    assert _native.packed_weight_bytes(_d(cin=5, cout=7, force=1), _native.LEG_DX) == 5 * 7 * 27 * 2
+    assert _native.packed_weight_bytes(_d(cin=5, cout=7), _native.LEG_DX) >= 8 * 5 * 27 * 2
     assert _native.packed_weight_bytes(_d(), _native.LEG_FWD) >= 24 * 24 * 27 * 2
 
 
@@ -155,3 +159,30 @@ def test_null_descriptor_rejected():
     lib = _native.lib()
     assert lib.r4c_plan_kernel(None, 0) == -1
     assert lib.r4c_conv3d_fwd(None, None, None, None, None, None, 0, None) == -1
+
+
+def _x(xs, ws, s, p, dl, g, dt=torch.bfloat16):
+    return _native.make_convex_desc(xs, ws, (s,) * 3, (p,) * 3, (dl,) * 3, g, dt)
+
+
+def test_convex_plan_and_sizes():
+    # k2s2 downsampling conv: the tcgen05 transpose-conv kernels (packed weight in the workspace)
+    d = _x((2, 16, 8, 12, 16), (32, 16, 2, 2, 2), 2, 0, 1, 1)
+    assert _native.convex_plan(d) == _native.KERNEL_TC
+    assert _native.convex_out_shape(d) == (2, 32, 4, 6, 8)
+    lib = _native.lib()
+    assert lib.r4c_convex_workspace_size(d, _native.LEG_FWD) > 0
+    assert lib.r4c_convex_workspace_size(d, _native.LEG_DW) > 0
+    # odd extents, fp32 or odd channels: SIMT
+    assert _native.convex_plan(_x((2, 16, 7, 12, 16), (32, 16, 2, 2, 2), 2, 0, 1, 1)) == _native.KERNEL_GENERIC
+    assert _native.convex_plan(_x((2, 16, 8, 12, 16), (32, 16, 2, 2, 2), 2, 0, 1, 1, torch.float32)) == \
+        _native.KERNEL_GENERIC
+    # strided, dilated, grouped: SIMT, dW split-K partials in the workspace only
+    g = _x((1, 8, 10, 11, 12), (16, 4, 3, 3, 3), 2, 2, 2, 2)
+    assert _native.convex_plan(g) == _native.KERNEL_GENERIC
+    assert _native.convex_out_shape(g) == (1, 16, 5, 6, 6)   # (i + 4 - 4 - 1) // 2 + 1
+    assert lib.r4c_convex_workspace_size(g, _native.LEG_FWD) == 0
+    assert lib.r4c_convex_workspace_size(g, _native.LEG_DW) >= 16 * 4 * 27 * 4
+    # invalid: channels not divisible by groups, zero stride
+    assert _native.convex_plan(_x((1, 6, 4, 4, 4), (4, 2, 3, 3, 3), 1, 1, 1, 4)) == -1
+    assert _native.convex_plan(_x((1, 8, 4, 4, 4), (8, 8, 3, 3, 3), 0, 1, 1, 1)) == -2

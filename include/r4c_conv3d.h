@@ -275,6 +275,28 @@ int r4c_bn_relu_bwd_dx(const void* dy, const void* x, void* dx, const float* mea
                        float* dbeta, float* coef, r4c_stream_t stream);
 
 /*
+ * BatchNorm + ReLU + MaxPool3d(2) in one pass, NDHWC, even D/H/W (n/d/h/w are
+ * the unpooled sizes). Forward writes y = relu(bn(x)) with a channel pitch
+ * `y_pitch` >= C (y may be a channel slice of a wider NDHWC buffer, e.g. the
+ * decoder's concatenation) and p = maxpool(y) dense. Backward routes dP to
+ * each window's argmax, recomputed from x with PyTorch's max_pool3d rule
+ * (scan in (d, h, w) order, first maximum, a NaN wins), adds dY (read with
+ * pitch `gy_pitch`) and runs the fused BN backward: r4c_bn_relu_pool_bwd_sums
+ * then r4c_bn_relu_pool_bwd_dx, workspace r4c_bn_pool_workspace_size().
+ * Statistics come from r4c_bn_stats / r4c_bn_finalize over x as above.
+ */
+int r4c_bn_relu_pool_fwd(const void* x, void* y, int y_pitch, void* p, const float* mean_invstd, const float* affine,
+                         int n, int d, int h, int w, int C, int dtype, r4c_stream_t stream);
+size_t r4c_bn_pool_workspace_size(int n, int d, int h, int w, int C);
+int r4c_bn_relu_pool_bwd_sums(const void* gy, int gy_pitch, const void* gp, const void* x, const float* mean_invstd,
+                              const float* affine, int n, int d, int h, int w, int C, int dtype, float* sums, void* ws,
+                              size_t ws_bytes, r4c_stream_t stream);
+int r4c_bn_relu_pool_bwd_dx(const void* gy, int gy_pitch, const void* gp, const void* x, void* dx,
+                            const float* mean_invstd, const float* affine, const float* sums, double count, int n,
+                            int d, int h, int w, int C, int dtype, float* dgamma, float* dbeta, float* coef,
+                            r4c_stream_t stream);
+
+/*
  * Conv3d weight and bias gradient without any allocation. No counterpart in
  * the reference: it exists for callers that cannot allocate device memory,
  * e.g. a plugin or custom op running inside another framework that owns the

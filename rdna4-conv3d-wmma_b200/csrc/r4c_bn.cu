@@ -285,6 +285,196 @@ __global__ void __launch_bounds__(256) dx_kernel(const T* __restrict__ dy, const
   }
 }
 
+// ---------------------------------------------------------------------------
+// BatchNorm + ReLU + MaxPool3d(2), NDHWC, even extents. One thread per
+// (pooled voxel, 8-channel vector): it normalises the 2x2x2 window, writes
+// the eight outputs y (with a channel pitch, so y can be a channel slice of a
+// wider buffer: the decoder's concatenation) and their maximum p. Backward
+// recomputes the window's outputs from x, takes the argmax the way PyTorch's
+// max_pool3d does (scan in (d, h, w) order, first maximum; a NaN wins), and
+// routes dP there: g = [pre > 0] * (dY + [argmax] * dP).
+// ---------------------------------------------------------------------------
+struct PoolGeo {
+  int n, d, h, w, C;
+  int ypitch;          // channels between consecutive voxels of y / dY
+  int64_t pvox;        // pooled voxels n * d/2 * h/2 * w/2
+};
+
+__device__ __forceinline__ int64_t window_voxel(const PoolGeo& g, int64_t pv, int k) {
+  const int pw = g.w >> 1, ph = g.h >> 1, pd = g.d >> 1;
+  int64_t t = pv;
+  const int px = (int)(t % pw); t /= pw;
+  const int py = (int)(t % ph); t /= ph;
+  const int pz = (int)(t % pd);
+  const int nb = (int)(t / pd);
+  const int a = k >> 2, b = (k >> 1) & 1, c = k & 1;
+  return (((int64_t)nb * g.d + 2 * pz + a) * g.h + 2 * py + b) * g.w + 2 * px + c;
+}
+
+template <typename T>
+__device__ __forceinline__ float round_to(float v) { return Elem<T>::to_f(Elem<T>::from_f(v)); }
+
+// Window pass shared by the three kernels: loads x for the 8 voxels and
+// returns, per channel, the argmax voxel of the rounded outputs.
+template <typename T>
+__device__ __forceinline__ void window_argmax(const T* __restrict__ x, const PoolGeo& g, int64_t pv, int c0,
+                                              const float* mi, const float* af, float (&xf)[8][8], int (&am)[8],
+                                              float (&mx)[8], int64_t (&vox)[8]) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) { am[i] = 0; mx[i] = 0.f; }
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    vox[k] = window_voxel(g, pv, k);
+    Vec8<T> a;
+    a.raw = *reinterpret_cast<const uint4*>(x + vox[k] * g.C + c0);
+    a.to_f(xf[k]);
+  }
+#pragma unroll
+  for (int k = 0; k < 8; ++k)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int c = c0 + i;
+      const float pre = bn_pre(xf[k][i], __ldg(mi + c), __ldg(mi + g.C + c), __ldg(af + c), __ldg(af + g.C + c));
+      const float y = round_to<T>(pre > 0.f ? pre : 0.f);
+      if (k == 0 || y > mx[i] || isnan(y)) {   // PyTorch's max_pool3d rule
+        mx[i] = y;
+        am[i] = k;
+      }
+    }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(128) pool_fwd_kernel(const T* __restrict__ x, T* __restrict__ y, T* __restrict__ p,
+                                                       const float* __restrict__ mi, const float* __restrict__ af,
+                                                       PoolGeo g) {
+  const int nv = g.C / 8;
+  const int64_t total = g.pvox * nv;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t pv = i / nv;
+    const int c0 = (int)(i - pv * nv) * 8;
+    float xf[8][8], mx[8];
+    int am[8];
+    int64_t vox[8];
+    window_argmax<T>(x, g, pv, c0, mi, af, xf, am, mx, vox);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      float f[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int c = c0 + j;
+        const float pre = bn_pre(xf[k][j], __ldg(mi + c), __ldg(mi + g.C + c), __ldg(af + c), __ldg(af + g.C + c));
+        f[j] = pre > 0.f ? pre : 0.f;
+      }
+      Vec8<T> o;
+      o.from_f(f);
+      *reinterpret_cast<uint4*>(y + vox[k] * g.ypitch + c0) = o.raw;
+    }
+    Vec8<T> o;
+    o.from_f(mx);
+    reinterpret_cast<uint4*>(p)[i] = o.raw;
+  }
+}
+
+// g per voxel k and channel j of the window.
+template <typename T>
+__device__ __forceinline__ void window_grad(const T* __restrict__ gy, const T* __restrict__ gp, const PoolGeo& g,
+                                            int64_t i, int c0, const float* mi, const float* af,
+                                            const float (&xf)[8][8], const int (&am)[8], const int64_t (&vox)[8],
+                                            float (&gf)[8][8]) {
+  Vec8<T> pb;
+  pb.raw = reinterpret_cast<const uint4*>(gp)[i];
+  float gpf[8];
+  pb.to_f(gpf);
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    Vec8<T> b;
+    b.raw = *reinterpret_cast<const uint4*>(gy + vox[k] * g.ypitch + c0);
+    b.to_f(gf[k]);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int c = c0 + j;
+      const float pre = bn_pre(xf[k][j], __ldg(mi + c), __ldg(mi + g.C + c), __ldg(af + c), __ldg(af + g.C + c));
+      float v = gf[k][j] + (am[j] == k ? gpf[j] : 0.f);
+      gf[k][j] = pre > 0.f ? v : 0.f;
+    }
+  }
+}
+
+// part[b] = (sum g, sum g*(x - mean)) over the block's pooled voxels.
+template <typename T>
+__global__ void __launch_bounds__(128) pool_sums_kernel(const T* __restrict__ x, const T* __restrict__ gy,
+                                                        const T* __restrict__ gp, const float* __restrict__ mi,
+                                                        const float* __restrict__ af, PoolGeo g, int64_t chunk,
+                                                        float* __restrict__ part) {
+  extern __shared__ float red[];  // [R][2*C]
+  const int nv = g.C / 8;
+  const int lane = threadIdx.x % nv, row = threadIdx.x / nv;
+  const int R = blockDim.x / nv;
+  const int c0 = lane * 8;
+  float s1[8], s2[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) { s1[j] = 0.f; s2[j] = 0.f; }
+  const int64_t v0 = (int64_t)blockIdx.x * chunk, v1 = min(v0 + chunk, g.pvox);
+  if (row < R) {
+    for (int64_t pv = v0 + row; pv < v1; pv += R) {
+      float xf[8][8], mx[8], gf[8][8];
+      int am[8];
+      int64_t vox[8];
+      window_argmax<T>(x, g, pv, c0, mi, af, xf, am, mx, vox);
+      window_grad<T>(gy, gp, g, pv * nv + lane, c0, mi, af, xf, am, vox, gf);
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          s1[j] += gf[k][j];
+          s2[j] = fmaf(gf[k][j], xf[k][j] - __ldg(mi + c0 + j), s2[j]);
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      red[row * 2 * g.C + c0 + j] = s1[j];
+      red[row * 2 * g.C + g.C + c0 + j] = s2[j];
+    }
+  }
+  __syncthreads();
+  for (int o = threadIdx.x; o < 2 * g.C; o += blockDim.x) {
+    float acc = 0.f;
+    for (int r = 0; r < R; ++r) acc += red[r * 2 * g.C + o];
+    part[(int64_t)blockIdx.x * 2 * g.C + o] = acc;
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(128) pool_dx_kernel(const T* __restrict__ x, const T* __restrict__ gy,
+                                                      const T* __restrict__ gp, T* __restrict__ dx,
+                                                      const float* __restrict__ mi, const float* __restrict__ af,
+                                                      const float* __restrict__ coef, PoolGeo g) {
+  const int nv = g.C / 8;
+  const int64_t total = g.pvox * nv;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t pv = i / nv;
+    const int c0 = (int)(i - pv * nv) * 8;
+    float xf[8][8], mx[8], gf[8][8];
+    int am[8];
+    int64_t vox[8];
+    window_argmax<T>(x, g, pv, c0, mi, af, xf, am, mx, vox);
+    window_grad<T>(gy, gp, g, i, c0, mi, af, xf, am, vox, gf);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      float f[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int c = c0 + j;
+        f[j] = (gf[k][j] - __ldg(coef + c) - (xf[k][j] - __ldg(mi + c)) * __ldg(coef + g.C + c)) *
+               __ldg(coef + 2 * g.C + c);
+      }
+      Vec8<T> o;
+      o.from_f(f);
+      *reinterpret_cast<uint4*>(dx + vox[k] * g.C + c0) = o.raw;
+    }
+  }
+}
+
 struct Split {
   int S;
   int64_t chunk;
@@ -424,6 +614,105 @@ int r4c_bn_relu_bwd_dx(const void* dy, const void* x, void* dx, const float* mea
       dx_kernel<__half><<<grid_for(nvec), 256, 0, s>>>(static_cast<const __half*>(dy), static_cast<const __half*>(x),
                                                        static_cast<__half*>(dx), mean_invstd, affine, coef, nvec, C,
                                                        relu);
+    r4c::note_launches(1);
+  }
+  return cudaGetLastError() == cudaSuccess ? R4C_OK : R4C_ERR_CUDA;
+}
+
+static bool pool_args(const void* x, int n, int d, int h, int w, int C, int pitch, int dtype) {
+  return x && n >= 0 && d > 0 && h > 0 && w > 0 && !(d & 1) && !(h & 1) && !(w & 1) && C > 0 && C % 8 == 0 &&
+         C <= 2048 && pitch >= C && pitch % 8 == 0 && (dtype == R4C_BF16 || dtype == R4C_F16) &&
+         (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+}
+
+static PoolGeo pool_geo(int n, int d, int h, int w, int C, int pitch) {
+  PoolGeo g;
+  g.n = n; g.d = d; g.h = h; g.w = w; g.C = C; g.ypitch = pitch;
+  g.pvox = (int64_t)n * (d / 2) * (h / 2) * (w / 2);
+  return g;
+}
+
+int r4c_bn_relu_pool_fwd(const void* x, void* y, int y_pitch, void* p, const float* mean_invstd, const float* affine,
+                         int n, int d, int h, int w, int C, int dtype, r4c_stream_t stream) {
+  if (!pool_args(x, n, d, h, w, C, C, dtype) || !pool_args(y, n, d, h, w, C, y_pitch, dtype) ||
+      !pool_args(p, n, d, h, w, C, C, dtype) || !mean_invstd || !affine)
+    return R4C_ERR_INVALID;
+  const PoolGeo g = pool_geo(n, d, h, w, C, y_pitch);
+  if (g.pvox == 0) return R4C_OK;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int64_t total = g.pvox * (C / 8);
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((total + 127) / 128, 148 * 8));
+  if (dtype == R4C_BF16)
+    pool_fwd_kernel<__nv_bfloat16><<<grid, 128, 0, s>>>(static_cast<const __nv_bfloat16*>(x),
+                                                        static_cast<__nv_bfloat16*>(y), static_cast<__nv_bfloat16*>(p),
+                                                        mean_invstd, affine, g);
+  else
+    pool_fwd_kernel<__half><<<grid, 128, 0, s>>>(static_cast<const __half*>(x), static_cast<__half*>(y),
+                                                 static_cast<__half*>(p), mean_invstd, affine, g);
+  r4c::note_launches(1);
+  return cudaGetLastError() == cudaSuccess ? R4C_OK : R4C_ERR_CUDA;
+}
+
+size_t r4c_bn_pool_workspace_size(int n, int d, int h, int w, int C) {
+  if (C <= 0 || n < 0) return 0;
+  return r4c_bn_workspace_size((int64_t)n * (d / 2) * (h / 2) * (w / 2), C);
+}
+
+int r4c_bn_relu_pool_bwd_sums(const void* gy, int gy_pitch, const void* gp, const void* x, const float* mean_invstd,
+                              const float* affine, int n, int d, int h, int w, int C, int dtype, float* sums, void* ws,
+                              size_t ws_bytes, r4c_stream_t stream) {
+  if (!pool_args(x, n, d, h, w, C, C, dtype) || !pool_args(gy, n, d, h, w, C, gy_pitch, dtype) ||
+      !pool_args(gp, n, d, h, w, C, C, dtype) || !mean_invstd || !affine || !sums)
+    return R4C_ERR_INVALID;
+  const PoolGeo g = pool_geo(n, d, h, w, C, gy_pitch);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (g.pvox == 0) return cudaMemsetAsync(sums, 0, 2 * C * sizeof(float), s) == cudaSuccess ? R4C_OK : R4C_ERR_CUDA;
+  const Split sp = split_for(g.pvox);
+  if (!ws || ws_bytes < r4c_bn_workspace_size(g.pvox, C)) return R4C_ERR_WORKSPACE;
+  float* part = static_cast<float*>(ws);
+  const int R = std::max(1, 128 / (C / 8));
+  const int threads = R * (C / 8);
+  const size_t smem = (size_t)R * 2 * C * sizeof(float);
+  if (smem > 48 * 1024) return R4C_ERR_UNSUPPORTED;
+  if (dtype == R4C_BF16)
+    pool_sums_kernel<__nv_bfloat16><<<sp.S, threads, smem, s>>>(
+        static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(gy),
+        static_cast<const __nv_bfloat16*>(gp), mean_invstd, affine, g, sp.chunk, part);
+  else
+    pool_sums_kernel<__half><<<sp.S, threads, smem, s>>>(static_cast<const __half*>(x), static_cast<const __half*>(gy),
+                                                         static_cast<const __half*>(gp), mean_invstd, affine, g,
+                                                         sp.chunk, part);
+  if (dtype == R4C_BF16)
+    sum_parts_kernel<__nv_bfloat16><<<(2 * C + 7) / 8, 256, 0, s>>>(part, sp.S, C, sums, 0, nullptr, nullptr);
+  else
+    sum_parts_kernel<__half><<<(2 * C + 7) / 8, 256, 0, s>>>(part, sp.S, C, sums, 0, nullptr, nullptr);
+  r4c::note_launches(2);
+  return cudaGetLastError() == cudaSuccess ? R4C_OK : R4C_ERR_CUDA;
+}
+
+int r4c_bn_relu_pool_bwd_dx(const void* gy, int gy_pitch, const void* gp, const void* x, void* dx,
+                            const float* mean_invstd, const float* affine, const float* sums, double count, int n,
+                            int d, int h, int w, int C, int dtype, float* dgamma, float* dbeta, float* coef,
+                            r4c_stream_t stream) {
+  if (!pool_args(x, n, d, h, w, C, C, dtype) || !pool_args(gy, n, d, h, w, C, gy_pitch, dtype) ||
+      !pool_args(gp, n, d, h, w, C, C, dtype) || !mean_invstd || !affine || !sums || !coef || count <= 0.0)
+    return R4C_ERR_INVALID;
+  if (dx && !pool_args(dx, n, d, h, w, C, C, dtype)) return R4C_ERR_INVALID;
+  const PoolGeo g = pool_geo(n, d, h, w, C, gy_pitch);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  bwd_finalize_kernel<<<(C + 127) / 128, 128, 0, s>>>(sums, mean_invstd, affine, C, count, dgamma, dbeta, coef);
+  r4c::note_launches(1);
+  if (dx && g.pvox > 0) {
+    const int64_t total = g.pvox * (C / 8);
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((total + 127) / 128, 148 * 8));
+    if (dtype == R4C_BF16)
+      pool_dx_kernel<__nv_bfloat16><<<grid, 128, 0, s>>>(
+          static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(gy),
+          static_cast<const __nv_bfloat16*>(gp), static_cast<__nv_bfloat16*>(dx), mean_invstd, affine, coef, g);
+    else
+      pool_dx_kernel<__half><<<grid, 128, 0, s>>>(static_cast<const __half*>(x), static_cast<const __half*>(gy),
+                                                  static_cast<const __half*>(gp), static_cast<__half*>(dx), mean_invstd,
+                                                  affine, coef, g);
     r4c::note_launches(1);
   }
   return cudaGetLastError() == cudaSuccess ? R4C_OK : R4C_ERR_CUDA;

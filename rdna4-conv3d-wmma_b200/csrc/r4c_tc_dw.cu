@@ -923,16 +923,369 @@ static cudaError_t set_attr() {
   return e;
 }
 
+// ---------------------------------------------------------------------------
+// Row-stage layout (k = 3, padding 1): one pipeline stage per INPUT row.
+//
+// For output plane z and input row yi the products that row takes part in
+// are, for each kw,
+//   D[(kd, ci), (kh, co)] += sum_x X[z+kd-1][yi][x+kw-1][ci] * dY[z][yi+1-kh][x][co]
+// so a stage holds two TMA boxes: the input row yi of the three planes
+// z-1..z+1 (M atoms kd, cw channels each, swizzled MN-major: LBO = one plane
+// slot) and the three dY rows yi-1..yi+1 of plane z (N atoms kh' = 2 - kh,
+// cwb channels each: LBO = one dY row slot). kw is a start-address shift of
+// A by kw positions, as in the wide layout. Per 16 positions: one MMA per
+// (kw, M tile) with N = 3 * cwb — 24 MMAs of N = 96 per row at 24 -> 24
+// against 48 of N = 32 in the chunk layout, and ~50 KB of boxes per row
+// against ~65 KB. Summing over every (z, yi) covers each (output row, tap)
+// pair exactly once: dY rows outside the volume are TMA zero fill.
+// Plane slot 3 holds bf16 ones, so its D rows (junk otherwise) are
+// sum_x dY: taken from kh' = 1 (dY row yi) and kw = 0, each dY row once: db.
+// Tasks: (input channel group g of cw, dY channel chunk n0 of cwb, kw range).
+// ---------------------------------------------------------------------------
+struct alignas(64) DwsArgs {
+  CUtensorMap tx;   // x:  box (cw, pitch, 1, 3, 1)
+  CUtensorMap tg;   // dy: box (cwb, kpad, 3, 1, 1)
+  float* part;      // [S][cout][cin][27]
+  float* dbpart;    // [S][cout] or nullptr
+  int* err;
+  int d, h, w, cin, cout;
+  int cw, cwb, apt, mtiles, nslots, kwn;
+  int pitch, kpad, wt, nwt;
+  int plane_bytes, brow_bytes, a_bytes, stage_bytes, stages;
+  int tmem_cols, npad;
+  long long rows, rows_per_split;
+  int ntasks;
+  uint32_t idesc;
+  int lay_a, lay_b;
+};
+
+struct DwsTasks {
+  int g[128], n0[128], kw0[128];
+};
+
+template <int MT, int KWN>
+__device__ __forceinline__ void dws_issue(uint64_t a0, uint64_t b0, uint32_t tmem, uint32_t npad, uint32_t tile_a,
+                                          uint32_t row_a, uint32_t ks_a, uint32_t ks_b, int ksteps, uint32_t idesc,
+                                          bool first) {
+#pragma unroll 1
+  for (int ks = 0; ks < ksteps; ++ks) {
+    const uint32_t acc = (first && ks == 0) ? 0u : 1u;
+    const uint64_t b = b0 + (uint64_t)(ks * ks_b);
+#pragma unroll
+    for (int kw = 0; kw < KWN; ++kw)
+#pragma unroll
+      for (int t = 0; t < MT; ++t)
+        mma_f16_ss(tmem + (uint32_t)(kw * MT + t) * npad,
+                   a0 + (uint64_t)(ks * ks_a + kw * row_a) + (uint64_t)t * tile_a, b, idesc, acc);
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 1)
+    tc_dws_kernel(const __grid_constant__ DwsArgs a, const __grid_constant__ DwsTasks tt) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* empty = full + kMaxStages;
+  uint64_t* done = empty + kMaxStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint8_t* stage0 = smem + kHeader;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  if ((smem_u32(smem) & 1023u) != 0u) {
+    if (threadIdx.x == 0) atomicExch(a.err, 2);
+    return;
+  }
+  const int task = blockIdx.x % a.ntasks;
+  const int split = blockIdx.x / a.ntasks;
+  const int grp = tt.g[task], n0 = tt.n0[task], kw0 = tt.kw0[task];
+
+  // zero every stage and tail (junk atoms read finite data), then fill plane
+  // slot 3 of every stage with ones (never written by TMA)
+  {
+    const int total = a.stages * a.stage_bytes;
+    const uint4 z = make_uint4(0, 0, 0, 0);
+    for (int i = threadIdx.x * 16; i < total; i += kThreads * 16) *reinterpret_cast<uint4*>(stage0 + i) = z;
+    __syncthreads();
+    for (int s = 0; s < a.stages; ++s) {
+      uint32_t* o = reinterpret_cast<uint32_t*>(stage0 + (size_t)s * a.stage_bytes + (size_t)3 * a.plane_bytes);
+      for (int i = threadIdx.x; i < a.plane_bytes / 4; i += kThreads) o[i] = OneBits<T>::v;
+    }
+  }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < a.stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, (uint32_t)a.tmem_cols);
+    tmem_relinquish();
+  }
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  const long long r_beg = (long long)split * a.rows_per_split;
+  const long long r_end = min(r_beg + a.rows_per_split, a.rows);
+  const uint64_t kWaitNs = 1000000000ull;
+  auto wait = [&](uint64_t* bar, uint32_t par, uint32_t nap = 0) -> bool {
+    return bounded_wait(bar, par, kWaitNs, abort_flag, a.err, 1, nap);
+  };
+  const uint32_t tx_bytes = (uint32_t)(3 * a.plane_bytes + 3 * a.brow_bytes);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tmap(&a.tx);
+      prefetch_tmap(&a.tg);
+      int stage = 0;
+      uint32_t epar = 1;
+      bool pending[kMaxStages];
+      uint32_t last_par[kMaxStages];
+      for (int s = 0; s < kMaxStages; ++s) { pending[s] = false; last_par[s] = 0; }
+      for (long long r = r_beg; r < r_end; ++r) {
+        const int wi = (int)(r % a.nwt);
+        long long q = r / a.nwt;
+        const int yi = (int)(q % a.h); q /= a.h;
+        const int z = (int)(q % a.d);
+        const int nb = (int)(q / a.d);
+        const int x0 = wi * a.wt;
+        if (!wait(&empty[stage], epar)) break;
+        mbar_arrive_expect_tx(&full[stage], tx_bytes);
+        uint8_t* sA = stage0 + (size_t)stage * a.stage_bytes;
+        // input row yi of planes z-1, z, z+1 (positions x0-1 ..), then dY rows yi-1..yi+1 of plane z
+        tma_load_5d(sA, &a.tx, &full[stage], grp * a.cw, x0 - 1, yi, z - 1, nb);
+        tma_load_5d(sA + a.a_bytes, &a.tg, &full[stage], n0, x0, yi - 1, z, nb);
+        pending[stage] = true;
+        last_par[stage] = epar ^ 1;
+        if (++stage == a.stages) { stage = 0; epar ^= 1; }
+      }
+      for (int s = 0; s < a.stages; ++s) {
+        if (!pending[s]) continue;
+        uint64_t dl = global_timer_ns() + kWaitNs;
+        while (!mbar_try_wait(&full[s], last_par[s]) && global_timer_ns() < dl) {
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t fpar = 0;
+      bool first = true;
+      const int ksteps = a.kpad / 16;
+      // descriptor steps in 16-byte units: A row (one position), 16 rows (K
+      // step), M tile (apt plane slots); B 16 rows
+      const uint32_t row_a = (uint32_t)(a.cw / 8), ks_a = (uint32_t)(2 * a.cw);
+      const uint32_t tile_a = (uint32_t)(a.apt * a.plane_bytes / 16), ks_b = (uint32_t)(2 * a.cwb);
+      for (long long r = r_beg; r < r_end; ++r) {
+        if (!wait(&full[stage], fpar)) break;
+        tc_fence_after();
+        const uint32_t sA = smem_u32(stage0 + (size_t)stage * a.stage_bytes);
+        const uint64_t a0 = desc_layout(sA + (uint32_t)(kw0 * a.cw * 2), (uint32_t)a.plane_bytes,
+                                        (uint32_t)(16 * a.cw), (uint32_t)a.lay_a);
+        const uint64_t b0 = desc_layout(sA + (uint32_t)a.a_bytes, (uint32_t)a.brow_bytes, (uint32_t)(16 * a.cwb),
+                                        (uint32_t)a.lay_b);
+        const uint32_t np = (uint32_t)a.npad;
+        if (a.kwn == 3) {
+          if (a.mtiles == 1) dws_issue<1, 3>(a0, b0, tmem, np, tile_a, row_a, ks_a, ks_b, ksteps, a.idesc, first);
+          else dws_issue<2, 3>(a0, b0, tmem, np, tile_a, row_a, ks_a, ks_b, ksteps, a.idesc, first);
+        } else {
+          if (a.mtiles == 1) dws_issue<1, 1>(a0, b0, tmem, np, tile_a, row_a, ks_a, ks_b, ksteps, a.idesc, first);
+          else dws_issue<2, 1>(a0, b0, tmem, np, tile_a, row_a, ks_a, ks_b, ksteps, a.idesc, first);
+        }
+        first = false;
+        mma_commit(&empty[stage]);
+        if (++stage == a.stages) { stage = 0; fpar ^= 1; }
+      }
+      mma_commit(done);
+    }
+  } else {
+    // epilogue: the task's fp32 partials (and db from the ones atom)
+    int got = 1;
+    if (lane == 0) got = wait(done, 0, 256) ? 1 : 0;
+    got = __shfl_sync(0xffffffffu, got, 0);
+    if (got && r_beg < r_end) {
+      tc_fence_after();
+      const int q = warp & 3;
+      const int row = q * 32 + lane;
+      float* dst = a.part + (size_t)split * a.cout * a.cin * 27;
+      for (int kw = 0; kw < a.kwn; ++kw)
+        for (int t = 0; t < a.mtiles; ++t) {
+          const int atom = t * a.apt + row / a.cw;
+          const int ci = grp * a.cw + row % a.cw;
+          const bool real = atom < 3 && ci < a.cin;
+          const bool dbrow = atom == 3 && grp == 0 && row % a.cw == 0 && kw0 + kw == 0 && a.dbpart != nullptr;
+          const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)((kw * a.mtiles + t) * a.npad);
+          for (int cc = 0; cc < a.npad; cc += 16) {
+            float v[16];
+            tmem_ld_16(tb + (uint32_t)cc, v);
+            if (real) {
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                const int col = cc + i, khp = col / a.cwb, co = n0 + col % a.cwb;
+                if (khp < 3 && co < a.cout)
+                  dst[((size_t)co * a.cin + ci) * 27 + (atom * 3 + (2 - khp)) * 3 + kw0 + kw] = v[i];
+              }
+            } else if (dbrow) {
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                const int col = cc + i, khp = col / a.cwb, co = n0 + col % a.cwb;
+                if (khp == 1 && co < a.cout) a.dbpart[(size_t)split * a.cout + co] = v[i];
+              }
+            }
+          }
+        }
+    } else if (got) {
+      // an empty split: its partials are zero
+      const int q = warp & 3;
+      const int row = q * 32 + lane;
+      float* dst = a.part + (size_t)split * a.cout * a.cin * 27;
+      for (int t = 0; t < a.mtiles; ++t) {
+        const int atom = t * a.apt + row / a.cw, ci = grp * a.cw + row % a.cw;
+        if (atom < 3 && ci < a.cin)
+          for (int kw = 0; kw < a.kwn; ++kw)
+            for (int col = 0; col < 3 * a.cwb; ++col) {
+              const int khp = col / a.cwb, co = n0 + col % a.cwb;
+              if (co < a.cout) dst[((size_t)co * a.cin + ci) * 27 + (atom * 3 + (2 - khp)) * 3 + kw0 + kw] = 0.f;
+            }
+        if (atom == 3 && grp == 0 && row % a.cw == 0 && kw0 == 0 && a.dbpart != nullptr)
+          for (int c = 0; c < a.cwb; ++c)
+            if (n0 + c < a.cout) a.dbpart[(size_t)split * a.cout + n0 + c] = 0.f;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, (uint32_t)a.tmem_cols);
+  }
+}
+
+struct DwsPlan {
+  bool ok;
+  int cw, cwb, ng, nco, apt, mtiles, nslots, kwn;
+  int pitch, kpad, wt, nwt;
+  int plane_bytes, brow_bytes, a_bytes, stage_bytes, stages, smem_bytes, tmem_cols, npad;
+  long long rows, rows_per_split;
+  int S;
+  std::vector<Task> tasks;  // g, n0, kw0 used
+  double est;
+};
+
+// Row-stage plan: k = 3, padding (1, 1, 1), Cin and Cout multiples of 8.
+// R4C_DW_STRIP=0 disables it (the chunk / wide layouts then run).
+static bool plan_dws(int n, int d, int h, int w, int cin, int cout, int ks, int pd, int ph, int pw, DwsPlan* out) {
+  // automatic for input and output channel counts up to 64 (the layers whose
+  // chunk-layout dW moves the most bytes per FLOP); R4C_DW_STRIP=1 takes it
+  // for any eligible layer, =0 never
+  const char* env = getenv("R4C_DW_STRIP");
+  if (env && env[0] == '0') return false;
+  if (!(env && env[0] == '1') && (cin > 64 || cout > 64)) return false;
+  if (ks != 3 || pd != 1 || ph != 1 || pw != 1) return false;
+  if (cin % 8 || cout % 8 || cin <= 0 || cout <= 0 || n <= 0 || d <= 0 || h <= 0 || w <= 0) return false;
+  DwsPlan P{};
+  P.cw = cin <= 16 ? 16 : cin <= 32 ? 32 : 64;
+  P.ng = (cin + P.cw - 1) / P.cw;
+  P.cwb = cout <= 16 ? 16 : cout <= 32 ? 32 : 64;
+  P.nco = (cout + P.cwb - 1) / P.cwb;
+  P.apt = 128 / P.cw;
+  P.mtiles = (4 + P.apt - 1) / P.apt;          // atoms kd = 0..2 and the ones atom
+  P.nslots = P.mtiles * P.apt;                 // plane slots an M tile may read
+  P.npad = 3 * P.cwb;
+  // W tiles: multiples of 16 except the last (whose tail reads dY zero fill)
+  int wt = w;
+  while (wt > 16 && (round_up(wt, 16) + 8 > 256)) wt = round_up((wt + 1) / 2, 16);
+  auto stage_of = [&](int t) {
+    const int kpad = round_up(t, 16), pitch = round_up(kpad + 2, 8);
+    return round_up(P.nslots * pitch * P.cw * 2, 1024) + round_up(3 * kpad * P.cwb * 2, 1024);
+  };
+  while (wt > 16 && kHeader + 3 * stage_of(wt) > kSmemMax) wt = round_up((wt + 1) / 2, 16);
+  P.wt = wt;
+  P.nwt = (w + wt - 1) / wt;
+  P.kpad = round_up(wt, 16);
+  P.pitch = round_up(P.kpad + 2, 8);
+  if (P.pitch > 256 || P.kpad > 256) return false;
+  P.plane_bytes = P.pitch * P.cw * 2;
+  P.brow_bytes = P.kpad * P.cwb * 2;
+  P.a_bytes = round_up(P.nslots * P.plane_bytes, 1024);
+  P.stage_bytes = P.a_bytes + round_up(3 * P.brow_bytes, 1024);
+  P.stages = std::min(kMaxStages, (kSmemMax - kHeader) / P.stage_bytes);
+  if (P.stages < 2) return false;
+  P.smem_bytes = kHeader + P.stages * P.stage_bytes;
+  P.kwn = 3 * P.mtiles * P.npad <= 512 ? 3 : 1;
+  const int cols = P.kwn * P.mtiles * P.npad;
+  if (cols > 512) return false;
+  int alloc = 32;
+  while (alloc < cols) alloc *= 2;
+  P.tmem_cols = alloc;
+  for (int g = 0; g < P.ng; ++g)
+    for (int c = 0; c < P.nco; ++c)
+      for (int kw0 = 0; kw0 < 3; kw0 += P.kwn) P.tasks.push_back(Task{0, P.mtiles, c * P.cwb, P.cwb, kw0, P.kwn, g});
+  if ((int)P.tasks.size() > 128) return false;
+  P.rows = (long long)n * d * h * P.nwt;
+  // cost per row: the MMAs (measured ~45 clk at N <= 32, N/2 above) or the
+  // boxes' bytes (~30 B/clk per SM), plus the stage hand-off
+  const double t_mma = std::max(45.0, P.npad / 2.0 + 8.0) * (P.kpad / 16) * P.kwn * P.mtiles;
+  const double t_load = (3.0 * P.plane_bytes + 3.0 * P.brow_bytes) / 30.0;
+  const double per_row = std::max(t_mma, t_load) + 80.0;
+  const int sms = num_sms();
+  const int ntasks = (int)P.tasks.size();
+  double best = 1e300;
+  for (int k = 1; k <= 4; ++k) {
+    int S = (int)std::max<long long>(1, std::min<long long>(P.rows, (long long)k * sms / ntasks));
+    const long long rps = (P.rows + S - 1) / S;
+    S = (int)((P.rows + rps - 1) / rps);
+    const long long waves = ((long long)ntasks * S + sms - 1) / sms;
+    const double c = waves * (rps * per_row + 3000.0);
+    if (c < best) {
+      best = c;
+      P.S = S;
+      P.rows_per_split = rps;
+    }
+  }
+  P.est = best;
+  P.ok = true;
+  if (out) *out = P;
+  return true;
+}
+
+template <typename T>
+static cudaError_t set_attr_dws() {
+  static bool done[64] = {false};
+  static std::mutex mu;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lk(mu);
+  if (dev >= 0 && dev < 64 && done[dev]) return cudaSuccess;
+  e = cudaFuncSetAttribute(tc_dws_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
+  if (e == cudaSuccess && dev >= 0 && dev < 64) done[dev] = true;
+  return e;
+}
+
 }  // namespace tcdw
 
 namespace tc {
 
 bool dw_supported(int n, int d, int h, int w, int cin, int cout, int ks, int pd, int ph, int pw) {
+  if (tcdw::plan_dws(n, d, h, w, cin, cout, ks, pd, ph, pw, nullptr)) return true;
   tcdw::DwPlan P;
   return tcdw::plan_dw(n, d, h, w, cin, cout, ks, pd, ph, pw, &P) && (int)P.tasks.size() <= 128;
 }
 
 size_t dw_workspace(int n, int d, int h, int w, int cin, int cout, int ks, int pd, int ph, int pw) {
+  tcdw::DwsPlan R;
+  if (tcdw::plan_dws(n, d, h, w, cin, cout, ks, pd, ph, pw, &R)) {
+    size_t part = (size_t)R.S * cout * cin * 27 * sizeof(float);
+    part = (part + 255) / 256 * 256;
+    return part + ((size_t)R.S * cout * sizeof(float) + 255) / 256 * 256;
+  }
   tcdw::DwPlan P;
   if (!tcdw::plan_dw(n, d, h, w, cin, cout, ks, pd, ph, pw, &P)) return 0;
   size_t T = (size_t)ks * ks * ks;
@@ -944,6 +1297,16 @@ size_t dw_workspace(int n, int d, int h, int w, int cin, int cout, int ks, int p
 
 int dw_describe(int n, int d, int h, int w, int cin, int cout, int ks, int pd, int ph, int pw, char* buf,
                 size_t len) {
+  tcdw::DwsPlan R;
+  if (tcdw::plan_dws(n, d, h, w, cin, cout, ks, pd, ph, pw, &R)) {
+    snprintf(buf, len,
+             "tcgen05 dW (row stages: input row x 3 planes as A, 3 dY rows as B): cw=%d cwb=%d groups=%d "
+             "co_chunks=%d M tiles=%d kw/task=%d N=%d tasks=%d splits=%d rows/split=%lld wt=%d kpad=%d pitch=%d "
+             "stages=%d stage=%dB smem=%dB tmem=%d est=%.0fus",
+             R.cw, R.cwb, R.ng, R.nco, R.mtiles, R.kwn, R.npad, (int)R.tasks.size(), R.S, R.rows_per_split, R.wt,
+             R.kpad, R.pitch, R.stages, R.stage_bytes, R.smem_bytes, R.tmem_cols, R.est / 1.9e3);
+    return 1;
+  }
   tcdw::DwPlan P;
   if (!tcdw::plan_dw(n, d, h, w, cin, cout, ks, pd, ph, pw, &P)) return 0;
   if (P.wide)
@@ -967,6 +1330,57 @@ int launch_dw(int n, int d, int h, int w, int cin, int cin_real, int cout, int k
               const void* x, const void* go, float* dw, float* db, void* ws, size_t ws_bytes, int dtype,
               cudaStream_t st, bool* db_done) {
   using namespace tcdw;
+  {
+    DwsPlan R;
+    if (plan_dws(n, d, h, w, cin, cout, ks, pd, ph, pw, &R)) {
+      if (((uintptr_t)x & 15) || ((uintptr_t)go & 15)) return R4C_ERR_ALIGN;
+      const size_t part_bytes = ((size_t)R.S * cout * cin * 27 * sizeof(float) + 255) / 256 * 256;
+      const size_t need = part_bytes + ((size_t)R.S * cout * sizeof(float) + 255) / 256 * 256;
+      if (ws_bytes < need || ws == nullptr) return R4C_ERR_WORKSPACE;
+      DwsArgs a;
+      memset(&a, 0, sizeof(a));
+      if (!encode_ndhwc(&a.tx, x, dtype, cin, w, h, d, n, R.pitch, 1, 3, R.cw)) return R4C_ERR_INVALID;
+      if (!encode_ndhwc(&a.tg, go, dtype, cout, w, h, d, n, R.kpad, 3, 1, R.cwb)) return R4C_ERR_INVALID;
+      a.part = static_cast<float*>(ws);
+      a.dbpart = db ? reinterpret_cast<float*>(static_cast<char*>(ws) + part_bytes) : nullptr;
+      a.err = device_error_flag();
+      if (!a.err) return R4C_ERR_CUDA;
+      a.d = d; a.h = h; a.w = w; a.cin = cin; a.cout = cout;
+      a.cw = R.cw; a.cwb = R.cwb; a.apt = R.apt; a.mtiles = R.mtiles; a.nslots = R.nslots; a.kwn = R.kwn;
+      a.pitch = R.pitch; a.kpad = R.kpad; a.wt = R.wt; a.nwt = R.nwt;
+      a.plane_bytes = R.plane_bytes; a.brow_bytes = R.brow_bytes; a.a_bytes = R.a_bytes;
+      a.stage_bytes = R.stage_bytes; a.stages = R.stages; a.tmem_cols = R.tmem_cols; a.npad = R.npad;
+      a.rows = R.rows; a.rows_per_split = R.rows_per_split; a.ntasks = (int)R.tasks.size();
+      a.idesc = sm100::instr_desc_f16(dtype == R4C_BF16, 128, R.npad, 1, 1);
+      auto lay = [](int c) { return c == 64 ? 2 : c == 32 ? 4 : c == 16 ? 6 : 0; };
+      a.lay_a = lay(R.cw);
+      a.lay_b = lay(R.cwb);
+      DwsTasks tt;
+      memset(&tt, 0, sizeof(tt));
+      for (size_t i = 0; i < R.tasks.size(); ++i) {
+        tt.g[i] = R.tasks[i].g; tt.n0[i] = R.tasks[i].n0; tt.kw0[i] = R.tasks[i].kw0;
+      }
+      const unsigned grid = (unsigned)(R.tasks.size() * R.S);
+      const bool bf = dtype == R4C_BF16;
+      cudaError_t e = bf ? set_attr_dws<__nv_bfloat16>() : set_attr_dws<__half>();
+      if (e != cudaSuccess) return R4C_ERR_CUDA;
+      if (bf) tc_dws_kernel<__nv_bfloat16><<<grid, kThreads, R.smem_bytes, st>>>(a, tt);
+      else tc_dws_kernel<__half><<<grid, kThreads, R.smem_bytes, st>>>(a, tt);
+      if (cudaGetLastError() != cudaSuccess) return R4C_ERR_CUDA;
+      const long long total = (long long)cout * cin_real * 27;
+      const long long nout = total + (a.dbpart ? cout : 0);
+      if (R.S >= 48)
+        dw_reduce_kernel<8><<<(unsigned)((nout + 31) / 32), 256, 0, st>>>(a.part, R.S, cout, cin, cin_real, 27, dw,
+                                                                          a.dbpart, a.dbpart ? db : nullptr);
+      else
+        dw_reduce_kernel<1><<<(unsigned)((nout + 255) / 256), 256, 0, st>>>(a.part, R.S, cout, cin, cin_real, 27,
+                                                                            dw, a.dbpart, a.dbpart ? db : nullptr);
+      note_launches(2);
+      if (cudaGetLastError() != cudaSuccess) return R4C_ERR_CUDA;
+      if (db_done) *db_done = (a.dbpart != nullptr);
+      return R4C_OK;
+    }
+  }
   DwPlan P;
   if (!plan_dw(n, d, h, w, cin, cout, ks, pd, ph, pw, &P)) return R4C_ERR_UNSUPPORTED;
   if ((int)P.tasks.size() > 128) return R4C_ERR_UNSUPPORTED;

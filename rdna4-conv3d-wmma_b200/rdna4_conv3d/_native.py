@@ -87,6 +87,10 @@ def _bind(lib) -> None:
         "r4c_bn_relu_fwd": ([P, P, P, P, i64, i, i, i, P], i),
         "r4c_bn_relu_bwd_sums": ([P, P, P, P, i64, i, i, i, P, P, sz, P], i),
         "r4c_bn_relu_bwd_dx": ([P, P, P, P, P, P, dbl, i64, i, i, i, P, P, P, P], i),
+        "r4c_bn_relu_pool_fwd": ([P, P, i, P, P, P, i, i, i, i, i, i, P], i),
+        "r4c_bn_pool_workspace_size": ([i, i, i, i, i], sz),
+        "r4c_bn_relu_pool_bwd_sums": ([P, i, P, P, P, P, i, i, i, i, i, i, P, P, sz, P], i),
+        "r4c_bn_relu_pool_bwd_dx": ([P, i, P, P, P, P, P, P, dbl, i, i, i, i, i, i, P, P, P, P], i),
         "r4c_convex_plan": ([X], i),
         "r4c_convex_workspace_size": ([X, i], sz),
         "r4c_convex_fwd": ([X, P, P, P, P, P, sz, P], i),
@@ -366,7 +370,7 @@ def convex_dw(desc: ConvexDesc, x_cl: torch.Tensor, go_cl: torch.Tensor, want_db
 # BatchNorm3d + ReLU (r4c_bn_*)
 # ---------------------------------------------------------------------------
 def bn_relu_forward(x_cl: torch.Tensor, gamma, beta, running_mean, running_var, momentum: float, eps: float,
-                    relu: bool, sums_hook=None, pivot=None):
+                    relu: bool, sums_hook=None, pivot=None, apply: bool = True):
     """Training forward. Returns (y, mean_invstd, affine, count).
     ``sums_hook(sums, count)``, when given, may all-reduce the per-channel
     sums in place before they are finalised and returns the total count (a
@@ -380,7 +384,7 @@ def bn_relu_forward(x_cl: torch.Tensor, gamma, beta, running_mean, running_var, 
     sums = torch.empty(3 * C, **f32)
     mi = torch.empty(2 * C, **f32)
     ss = torch.empty(2 * C, **f32)
-    y = torch.empty_like(x_cl, memory_format=torch.channels_last_3d)
+    y = torch.empty_like(x_cl, memory_format=torch.channels_last_3d) if apply else None
     dt = dtype_code(x_cl.dtype)
     with torch.cuda.device(dev):
         st = L.r4c_bn_stats(_ptr(x_cl), vox, C, dt, _ptr(pivot), _ptr(sums), _ptr(ws), ws.numel(), _stream(dev))
@@ -391,9 +395,11 @@ def bn_relu_forward(x_cl: torch.Tensor, gamma, beta, running_mean, running_var, 
         st = L.r4c_bn_finalize(_ptr(sums), count, C, _ptr(gamma), _ptr(beta), float(eps), float(momentum),
                                _ptr(running_mean), _ptr(running_var), _ptr(mi), _ptr(ss), _stream(dev))
         _check(st, "r4c_bn_finalize")
-        st = L.r4c_bn_relu_fwd(_ptr(x_cl), _ptr(y), _ptr(mi), _ptr(ss), vox, C, dt, 1 if relu else 0, _stream(dev))
-        _check(st, "r4c_bn_relu_fwd")
-    return y, mi, ss, count
+        if apply:
+            st = L.r4c_bn_relu_fwd(_ptr(x_cl), _ptr(y), _ptr(mi), _ptr(ss), vox, C, dt, 1 if relu else 0,
+                                   _stream(dev))
+            _check(st, "r4c_bn_relu_fwd")
+    return (y if apply else None), mi, ss, count
 
 
 def bn_relu_backward(dy_cl: torch.Tensor, x_cl: torch.Tensor, mean_invstd, affine, count: float, relu: bool,
@@ -421,6 +427,52 @@ def bn_relu_backward(dy_cl: torch.Tensor, x_cl: torch.Tensor, mean_invstd, affin
                                   _ptr(sums), float(count), vox, C, dt, 1 if relu else 0, _ptr(dg), _ptr(db),
                                   _ptr(coef), _stream(dev))
         _check(st, "r4c_bn_relu_bwd_dx")
+    return dx, dg, db
+
+
+def bn_relu_pool_forward(x_cl: torch.Tensor, mean_invstd, affine, lead: int):
+    """(buf, p): buf is a new NDHWC tensor of lead + C channels whose channels
+    [lead, lead + C) hold relu(bn(x)) (the rest left for the caller), p the
+    2x2x2 max-pool of those channels."""
+    dev = _require_cuda(x_cl)
+    n, C, d, h, w = (int(v) for v in x_cl.shape)
+    buf = _ndhwc_empty(n, lead + C, d, h, w, dev, x_cl.dtype)
+    p = _ndhwc_empty(n, C, d // 2, h // 2, w // 2, dev, x_cl.dtype)
+    yptr = ctypes.c_void_p(buf.data_ptr() + lead * buf.element_size())
+    with torch.cuda.device(dev):
+        st = lib().r4c_bn_relu_pool_fwd(_ptr(x_cl), yptr, lead + C, _ptr(p), _ptr(mean_invstd), _ptr(affine),
+                                        n, d, h, w, C, dtype_code(x_cl.dtype), _stream(dev))
+    _check(st, "r4c_bn_relu_pool_fwd")
+    return buf, p
+
+
+def bn_relu_pool_backward(gbuf_cl: torch.Tensor, lead: int, gp_cl: torch.Tensor, x_cl: torch.Tensor, mean_invstd,
+                          affine, count: float, need_dx: bool = True, sums_hook=None):
+    """(dx or None, dgamma, dbeta) from dY = channels [lead, lead + C) of gbuf
+    and dP = gp."""
+    dev = _require_cuda(gbuf_cl, gp_cl, x_cl)
+    n, C, d, h, w = (int(v) for v in x_cl.shape)
+    L = lib()
+    f32 = dict(dtype=torch.float32, device=dev)
+    ws = torch.empty(int(L.r4c_bn_pool_workspace_size(n, d, h, w, C)), dtype=torch.uint8, device=dev)
+    sums = torch.empty(2 * C, **f32)
+    dg = torch.empty(C, **f32)
+    db = torch.empty(C, **f32)
+    coef = torch.empty(3 * C, **f32)
+    dx = _ndhwc_empty(n, C, d, h, w, dev, x_cl.dtype) if need_dx else None
+    dt = dtype_code(x_cl.dtype)
+    pitch = int(gbuf_cl.shape[1])
+    gyptr = ctypes.c_void_p(gbuf_cl.data_ptr() + lead * gbuf_cl.element_size())
+    with torch.cuda.device(dev):
+        st = L.r4c_bn_relu_pool_bwd_sums(gyptr, pitch, _ptr(gp_cl), _ptr(x_cl), _ptr(mean_invstd), _ptr(affine),
+                                         n, d, h, w, C, dt, _ptr(sums), _ptr(ws), ws.numel(), _stream(dev))
+        _check(st, "r4c_bn_relu_pool_bwd_sums")
+        if sums_hook is not None:
+            sums_hook(sums, None)
+        st = L.r4c_bn_relu_pool_bwd_dx(gyptr, pitch, _ptr(gp_cl), _ptr(x_cl), _ptr(dx), _ptr(mean_invstd),
+                                       _ptr(affine), _ptr(sums), float(count), n, d, h, w, C, dt, _ptr(dg), _ptr(db),
+                                       _ptr(coef), _stream(dev))
+        _check(st, "r4c_bn_relu_pool_bwd_dx")
     return dx, dg, db
 
 

@@ -28,11 +28,11 @@ _HALF = (torch.float16, torch.bfloat16)
 
 class BNReLUFn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x, weight, bias, running_mean, running_var, momentum, eps, relu, sums_hook):
+    def forward(ctx, x, weight, bias, running_mean, running_var, momentum, eps, relu, sums_hook, pivot=None):
         gamma = None if weight is None else weight.detach().float().contiguous()
         beta = None if bias is None else bias.detach().float().contiguous()
         y, mi, ss, count = _native.bn_relu_forward(x, gamma, beta, running_mean, running_var, momentum, eps, relu,
-                                                   sums_hook)
+                                                   sums_hook, pivot)
         ctx.save_for_backward(x, mi, ss)
         ctx.count, ctx.relu, ctx.sums_hook = count, relu, sums_hook
         ctx.wdtype = None if weight is None else weight.dtype
@@ -49,7 +49,63 @@ class BNReLUFn(torch.autograd.Function):
                                               ctx.sums_hook)
         dg = dg.to(ctx.wdtype) if ctx.wdtype is not None and ctx.needs_input_grad[1] else None
         db = db.to(ctx.bdtype) if ctx.bdtype is not None and ctx.needs_input_grad[2] else None
-        return dx, dg, db, None, None, None, None, None, None
+        return dx, dg, db, None, None, None, None, None, None, None
+
+
+class BNReLUPoolFn(torch.autograd.Function):
+    """(buf, p) = (lead empty channels + relu(bn(x)), maxpool2(relu(bn(x))))."""
+
+    @staticmethod
+    def forward(ctx, x, weight, bias, running_mean, running_var, momentum, eps, lead, sums_hook=None, pivot=None):
+        gamma = None if weight is None else weight.detach().float().contiguous()
+        beta = None if bias is None else bias.detach().float().contiguous()
+        _, mi, af, count = _native.bn_relu_forward(x, gamma, beta, running_mean, running_var, momentum, eps, True,
+                                                   sums_hook, pivot, apply=False)
+        buf, p = _native.bn_relu_pool_forward(x, mi, af, lead)
+        ctx.save_for_backward(x, mi, af)
+        ctx.count, ctx.lead, ctx.sums_hook = count, lead, sums_hook
+        ctx.wdtype = None if weight is None else weight.dtype
+        ctx.bdtype = None if bias is None else bias.dtype
+        return buf, p
+
+    @staticmethod
+    def backward(ctx, gbuf, gp):
+        x, mi, af = ctx.saved_tensors
+        cl = torch.channels_last_3d
+        if gbuf is None:
+            gbuf = torch.zeros((x.shape[0], ctx.lead + x.shape[1]) + tuple(x.shape[2:]), dtype=x.dtype,
+                               device=x.device, memory_format=cl)
+        if gp is None:
+            gp = torch.zeros((x.shape[0], x.shape[1]) + tuple(s // 2 for s in x.shape[2:]), dtype=x.dtype,
+                             device=x.device, memory_format=cl)
+        gbuf = gbuf.to(x.dtype).contiguous(memory_format=cl)
+        gp = gp.to(x.dtype).contiguous(memory_format=cl)
+        dx, dg, db = _native.bn_relu_pool_backward(gbuf, ctx.lead, gp, x, mi, af, ctx.count, ctx.needs_input_grad[0],
+                                                   ctx.sums_hook)
+        dg = dg.to(ctx.wdtype) if ctx.wdtype is not None and ctx.needs_input_grad[1] else None
+        db = db.to(ctx.bdtype) if ctx.bdtype is not None and ctx.needs_input_grad[2] else None
+        return dx, dg, db, None, None, None, None, None, None, None
+
+
+class SkipCatFn(torch.autograd.Function):
+    """Write `up` into channels [0, lead) of `buf` in place (the rest of buf
+    already holds the skip connection): torch.cat([up, skip], 1) without
+    copying the skip."""
+
+    @staticmethod
+    def forward(ctx, up, buf, lead):
+        buf[:, :lead].copy_(up)
+        ctx.mark_dirty(buf)
+        ctx.lead = lead
+        return buf
+
+    @staticmethod
+    def backward(ctx, g):
+        return g[:, :ctx.lead], g, None
+
+
+def skip_cat(up: torch.Tensor, buf: torch.Tensor, lead: int) -> torch.Tensor:
+    return SkipCatFn.apply(up, buf, lead)
 
 
 class BatchNormReLU3d(nn.BatchNorm3d):
@@ -62,6 +118,10 @@ class BatchNormReLU3d(nn.BatchNorm3d):
 
     def _sums_hook(self):
         """Per-channel sums reduction across ranks (None: this process's data only)."""
+        return None
+
+    def _pivot(self):
+        """Statistics pivot shared by every rank (None: the first voxel)."""
         return None
 
     def _fused_ok(self, x) -> bool:
@@ -88,7 +148,23 @@ class BatchNormReLU3d(nn.BatchNorm3d):
         rm = self.running_mean if (self.training and self.track_running_stats) else None
         rv = self.running_var if (self.training and self.track_running_stats) else None
         return BNReLUFn.apply(x, self.weight, self.bias, rm, rv, float(mom), float(self.eps), bool(self.relu),
-                              self._sums_hook())
+                              self._sums_hook(), self._pivot())
+
+    def forward_pool(self, x, lead: int):
+        """(buf, p): buf an NDHWC tensor of ``lead`` + C channels whose last C
+        hold relu(bn(x)) — the skip connection, placed where the decoder's
+        concatenation wants it — and p = max_pool3d(relu(bn(x)), 2). One
+        fused kernel set on the supported path, stock ops otherwise."""
+        even = x.dim() == 5 and all(int(s) % 2 == 0 for s in x.shape[2:])
+        if not (self.relu and even and self._fused_ok(x) and self.training and self.track_running_stats):
+            y = self.forward(x)
+            head = torch.empty((x.shape[0], lead) + tuple(x.shape[2:]), dtype=y.dtype, device=y.device)
+            buf = torch.cat([head, y], dim=1).contiguous(memory_format=torch.channels_last_3d)
+            return buf, F.max_pool3d(y, 2)
+        self.num_batches_tracked.add_(1)
+        mom = 1.0 / float(self.num_batches_tracked) if self.momentum is None else self.momentum
+        return BNReLUPoolFn.apply(x, self.weight, self.bias, self.running_mean, self.running_var, float(mom),
+                                  float(self.eps), int(lead), self._sums_hook(), self._pivot())
 
 
 def fuse_bn_relu(model: nn.Module) -> int:

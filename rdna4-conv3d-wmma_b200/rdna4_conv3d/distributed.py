@@ -21,6 +21,8 @@ from typing import List, Optional
 import torch
 import torch.distributed as dist
 
+from .bn_relu import BatchNormReLU3d
+
 
 def _cw():
     return sys.modules["rdna4_conv3d.conv3d_wmma"]
@@ -517,6 +519,38 @@ class DepthShardedBatchNorm3d(torch.nn.BatchNorm3d):
                                training)
 
 
+class DepthShardedBatchNormReLU3d(BatchNormReLU3d):
+    """BatchNormReLU3d (fused kernels) over a D-sharded volume: the
+    per-channel sums are all-reduced over ``group`` between the statistics
+    pass and the finalize (and between the backward sums and the dX pass),
+    with the running mean as the pivot every rank shares (the running
+    statistics are updated identically on every rank). dgamma / dbeta come
+    out as whole-volume sums."""
+
+    def __init__(self, *args, group=None, **kw):
+        super().__init__(*args, **kw)
+        self.group = group
+
+    def _sums_hook(self):
+        if not (dist.is_available() and dist.is_initialized()):
+            return None
+        group, C = self.group, self.num_features
+
+        def hook(sums, count):
+            dist.all_reduce(sums[:2 * C], group=group)
+            if count is None:
+                return None
+            t = torch.tensor([count], dtype=torch.float64, device=sums.device)
+            dist.all_reduce(t, group=group)
+            return float(t.item())
+        return hook
+
+    def _pivot(self):
+        if self.running_mean is None or not (dist.is_available() and dist.is_initialized()):
+            return None
+        return self.running_mean.detach().float().contiguous()
+
+
 class DepthShardedConv3d(torch.nn.Conv3d):
     """Conv3d (k=3, pad=1) over a D-sharded volume; other geometries run
     locally (k=1 convs need no halo)."""
@@ -538,7 +572,8 @@ class DepthShardedConv3d(torch.nn.Conv3d):
 def depth_shard_model(model: torch.nn.Module, group=None) -> List[torch.nn.Parameter]:
     """Convert a model in place for depth sharding over ``group``: every k3
     pad-1 Conv3d becomes a DepthShardedConv3d (halo exchange), every
-    BatchNorm3d a DepthShardedBatchNorm3d (statistics over the whole volume).
+    BatchNorm3d a DepthShardedBatchNorm3d and every fused BatchNormReLU3d a
+    DepthShardedBatchNormReLU3d (statistics over the whole volume).
     Pooling, k2s2 transpose convs, concatenation and k1 convs need no
     exchange. Returns the parameters whose gradients are still per-slab
     partial sums (the transpose convs and k1 convs): reduce them with
@@ -557,7 +592,16 @@ def depth_shard_model(model: torch.nn.Module, group=None) -> List[torch.nn.Param
                     if child.bias is not None:
                         new.bias.copy_(child.bias)
                 setattr(mod, name, new)
-            elif isinstance(child, torch.nn.BatchNorm3d) and not isinstance(child, DepthShardedBatchNorm3d):
+            elif isinstance(child, BatchNormReLU3d) and not isinstance(child, DepthShardedBatchNormReLU3d):
+                ref = child.weight if child.affine else child.running_mean
+                new = DepthShardedBatchNormReLU3d(child.num_features, child.eps, child.momentum, child.affine,
+                                                  child.track_running_stats, relu=child.relu, group=group,
+                                                  device=None if ref is None else ref.device,
+                                                  dtype=None if ref is None else ref.dtype)
+                new.load_state_dict(child.state_dict())
+                setattr(mod, name, new)
+            elif isinstance(child, torch.nn.BatchNorm3d) and not isinstance(child, DepthShardedBatchNorm3d) \
+                    and not isinstance(child, BatchNormReLU3d):
                 ref = child.weight if child.affine else child.running_mean
                 new = DepthShardedBatchNorm3d(child.num_features, child.eps, child.momentum, child.affine,
                                               child.track_running_stats, group=group,

@@ -45,7 +45,13 @@ class UNet3D(nn.Module):
         self.dec = nn.ModuleList([conv_block(2 * ch[i], ch[i], conv) for i in reversed(range(levels - 1))])
         self.head = conv(ch[0], n_classes, 1)
 
+    def _fused_skips(self) -> bool:
+        from .bn_relu import BatchNormReLU3d
+        return all(isinstance(b[-2], BatchNormReLU3d) and isinstance(b[-1], nn.Identity) for b in self.enc)
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if self._fused_skips():
+            return self._forward_fused(x)
         skips: List[torch.Tensor] = []
         for i, block in enumerate(self.enc):
             x = block(x if i == 0 else self.pool(x))
@@ -53,6 +59,29 @@ class UNet3D(nn.Module):
         x = skips.pop()
         for up, dec in zip(self.up, self.dec):
             x = dec(torch.cat([up(x), skips.pop()], dim=1))
+        return self.head(x)
+
+
+    def _forward_fused(self, x: torch.Tensor) -> torch.Tensor:
+        """Same network, with each encoder level's last BatchNorm+ReLU also
+        doing the MaxPool3d(2) and writing its output (the skip connection)
+        straight into the channels of the decoder's concatenation buffer; the
+        decoder then only writes the up-conv's output in front of it."""
+        from .bn_relu import skip_cat
+        bufs = []
+        last = len(self.enc) - 1
+        for i, block in enumerate(self.enc):
+            for m in list(block)[:-2]:
+                x = m(x)
+            if i == last:
+                x = block[-2](x)
+            else:
+                lead = self.channels[i]           # the up-conv at this level outputs ch[i] channels
+                buf, x = block[-2].forward_pool(x, lead)
+                bufs.append((buf, lead))
+        for up, dec in zip(self.up, self.dec):
+            buf, lead = bufs.pop()
+            x = dec(skip_cat(up(x), buf, lead))
         return self.head(x)
 
 

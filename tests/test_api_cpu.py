@@ -155,3 +155,22 @@ def test_torch_ops_registered_with_fake_kernels():
         assert torch.ops.r4c.tconv_dx(t, wt, list(x.shape)).shape == x.shape
         tdw, tdb = torch.ops.r4c.tconv_dw(x, t, list(wt.shape), True)
         assert tdw.shape == wt.shape and tdb.shape == (12,)
+
+
+def test_unet_fused_skip_path_on_cpu_matches_stock():
+    """The fused-skip forward (forward_pool + skip_cat) falls back to stock ops
+    on CPU and computes the same network, gradients included."""
+    from rdna4_conv3d.unet3d import unet3d
+    torch.manual_seed(0)
+    stock = unet3d(4, levels=3, wmma=False).double()
+    fused = unet3d(4, levels=3, wmma=False, fuse_bn=True).double()
+    fused.load_state_dict(stock.state_dict())
+    assert fused._fused_skips() and not stock._fused_skips()
+    x = torch.randn(2, 1, 8, 8, 8, dtype=torch.float64)
+    ys, yf = stock(x), fused(x)
+    torch.testing.assert_close(yf, ys)
+    gy = torch.randn_like(ys)
+    ys.backward(gy)
+    yf.backward(gy)
+    for (n, a), b in zip(stock.named_parameters(), fused.parameters()):
+        torch.testing.assert_close(b.grad, a.grad, msg=n)

@@ -89,3 +89,54 @@ def test_bn_relu_eval_and_fallbacks(cuda_ready):
     ref.train()
     torch.testing.assert_close(mod(x), F.relu(ref(x)))           # NCDHW: stock
     assert _native.launch_count() == n0
+
+
+@pytest.mark.parametrize("quantised", [False, True], ids=["random", "ties"])
+@pytest.mark.parametrize("shape,lead", [((2, 24, 8, 16, 16), 24), ((1, 48, 4, 8, 8), 48), ((2, 8, 6, 4, 10), 0),
+                                        ((4, 24, 64, 128, 128), 24)], ids=["24", "48", "lead0", "full"])
+def test_bn_relu_pool_and_skip_buffer(cuda_ready, shape, lead, quantised):
+    """forward_pool (BN + ReLU + MaxPool3d(2), skip written after `lead`
+    channels of the concatenation buffer) and skip_cat against stock
+    BatchNorm3d + ReLU + max_pool3d + cat, values and gradients. Quantised
+    inputs put ties into the pooling windows: the argmax must follow
+    max_pool3d's first-maximum rule for the gradients to agree."""
+    from rdna4_conv3d.bn_relu import BatchNormReLU3d, skip_cat
+    C = shape[1]
+    g = torch.Generator().manual_seed(C + lead)
+    x = torch.randn(shape, generator=g) * 2.0 + 0.3
+    if quantised:
+        x = torch.round(x * 2) / 2
+    x = x.to(torch.bfloat16)
+    up = torch.randn((shape[0], lead) + shape[2:], generator=g).to(torch.bfloat16)
+    gcat = torch.randn((shape[0], lead + C) + shape[2:], generator=g).to(torch.bfloat16)
+    gp = torch.randn((shape[0], C) + tuple(s // 2 for s in shape[2:]), generator=g).to(torch.bfloat16)
+    ref = torch.nn.BatchNorm3d(C)
+    mod = BatchNormReLU3d(C).cuda()
+    mod.load_state_dict(ref.state_dict())
+    cl = torch.channels_last_3d
+    xg = x.cuda().contiguous(memory_format=cl).requires_grad_(True)
+    upg = up.cuda().contiguous(memory_format=cl).requires_grad_(True)
+    buf, p = mod.forward_pool(xg, lead)
+    cat = skip_cat(upg, buf, lead)
+    torch.autograd.backward([cat, p], [gcat.cuda().contiguous(memory_format=cl), gp.cuda().contiguous(memory_format=cl)])
+    torch.cuda.synchronize()
+
+    # the stock path on the GPU in bf16 (same rounding points as the model's stock run)
+    refg = ref.cuda()
+    xr = x.cuda().contiguous(memory_format=cl).requires_grad_(True)
+    upr = up.cuda().contiguous(memory_format=cl).requires_grad_(True)
+    yr = F.relu(refg(xr))
+    pr = F.max_pool3d(yr, 2)
+    catr = torch.cat([upr, yr], dim=1)
+    torch.autograd.backward([catr, pr], [gcat.cuda(), gp.cuda()])
+    assert p.shape == pr.shape and cat.shape == catr.shape
+    assert O.max_rel(cat.float().cpu(), catr.float().cpu()) <= 2e-2
+    assert O.max_rel(p.float().cpu(), pr.float().cpu()) <= 2e-2
+    assert O.max_rel(xg.grad.float().cpu(), xr.grad.float().cpu()) <= 2e-2
+    if lead:
+        assert torch.equal(upg.grad.cpu(), upr.grad.cpu())
+    # the stock path rounds the sum of the skip and pool gradients to bf16
+    # before BatchNorm's backward; the fused kernels add them in fp32
+    assert O.norm_rel(mod.weight.grad.cpu(), refg.weight.grad.cpu()) <= 3e-2
+    assert O.norm_rel(mod.bias.grad.cpu(), refg.bias.grad.cpu()) <= 3e-2
+    torch.testing.assert_close(mod.running_mean, refg.running_mean, rtol=1e-4, atol=1e-5)

@@ -158,21 +158,27 @@ DW_CASES = [
     (1, 40, 40, 3, 5, 16, 1, 0),       # padded channel group (40 of 64) and dY box (40 of 64)
     (1, 24, 24, 3, 5, 16, 3, 1),       # padded 32-channel group and dY box (24 real)
     (2, 24, 24, 3, 4, 128, 3, 1),      # fold: K = 144 positions, two M tiles (trunk 24->24 row)
+    (1, 16, 8, 4, 5, 6, 3, 1),         # rows: 16-channel atoms (8 per M tile), 16-channel dY atoms
+    (1, 64, 64, 3, 5, 24, 3, 1),       # rows: two M tiles, N = 192, one kw per task
+    (2, 48, 24, 4, 6, 300, 3, 1),      # rows: W split into tiles, Cin padded to 64
     (1, 8, 16, 4, 5, 6, 3, 2),         # pad 2
     (1, 16, 8, 3, 4, 200, 3, 0),       # pad 0, K = 208 positions
 ]
 
 
-@pytest.mark.parametrize("layout", ["chunks", "fold", "wide"])
+@pytest.mark.parametrize("layout", ["chunks", "fold", "wide", "rows"])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16], ids=["bf16", "fp16"])
 @pytest.mark.parametrize("case", DW_CASES, ids=_ids(DW_CASES))
 def test_dw_layouts_match_oracle(cuda_ready, case, dtype, layout, monkeypatch):
     # chunks: 8-channel chunks, one MMA per kw; fold: the same with kw folded
     # into N (three kw-shifted dY copies; k3 rows that fit one W tile);
-    # wide: swizzled channel groups
+    # wide: swizzled channel groups; rows: one stage per input row (three
+    # input planes as A, three dY rows as B; k3 pad 1, forced for every
+    # channel count here — other geometries fall back to the default plan)
     n, cin, cout, d, h, w, k, pad = case
     monkeypatch.setenv("R4C_DW_WIDE", "1" if layout == "wide" else "0")
     monkeypatch.setenv("R4C_DW_FOLD", "1" if layout == "fold" else "0")
+    monkeypatch.setenv("R4C_DW_STRIP", "1" if layout == "rows" else "0")
     cw = _cw()
     x, wt, b, go = _inputs(*case, dtype)
     dw, db = cw._launch_wgrad(x.cuda(), go.cuda(), wt.shape, (pad,) * 3, True)

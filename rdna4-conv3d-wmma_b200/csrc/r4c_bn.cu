@@ -480,16 +480,16 @@ struct Split {
   int64_t chunk;
 };
 
-static Split split_for(int64_t vox) {
-  // about two blocks per SM, at least 512 voxels each
+static Split split_for(int64_t vox, int64_t min_chunk = 64) {
+  // about four blocks per SM (small levels of a UNet need the blocks: each
+  // thread's voxel loop is a chain of dependent loads), at least min_chunk
+  // voxels each
   Split s;
-  s.chunk = std::max<int64_t>(512, (vox + 295) / 296);
+  s.chunk = std::max<int64_t>(min_chunk, (vox + 591) / 592);
   s.S = (int)std::max<int64_t>(1, (vox + s.chunk - 1) / s.chunk);
   return s;
 }
 
-// One resident wave (the elementwise kernels hold 45-64 registers a thread:
-// four 256-thread blocks per SM).
 static int grid_for(int64_t nvec) {
   return (int)std::max<int64_t>(1, std::min<int64_t>((nvec + 255) / 256, 148 * 4));
 }
@@ -655,7 +655,8 @@ int r4c_bn_relu_pool_fwd(const void* x, void* y, int y_pitch, void* p, const flo
 
 size_t r4c_bn_pool_workspace_size(int n, int d, int h, int w, int C) {
   if (C <= 0 || n < 0) return 0;
-  return r4c_bn_workspace_size((int64_t)n * (d / 2) * (h / 2) * (w / 2), C);
+  const Split s = split_for((int64_t)n * (d / 2) * (h / 2) * (w / 2), 8);
+  return r4c::align_up((size_t)s.S * 2 * C * sizeof(float), 256);
 }
 
 int r4c_bn_relu_pool_bwd_sums(const void* gy, int gy_pitch, const void* gp, const void* x, const float* mean_invstd,
@@ -667,8 +668,8 @@ int r4c_bn_relu_pool_bwd_sums(const void* gy, int gy_pitch, const void* gp, cons
   const PoolGeo g = pool_geo(n, d, h, w, C, gy_pitch);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (g.pvox == 0) return cudaMemsetAsync(sums, 0, 2 * C * sizeof(float), s) == cudaSuccess ? R4C_OK : R4C_ERR_CUDA;
-  const Split sp = split_for(g.pvox);
-  if (!ws || ws_bytes < r4c_bn_workspace_size(g.pvox, C)) return R4C_ERR_WORKSPACE;
+  const Split sp = split_for(g.pvox, 8);   // a pooled voxel is 8 voxels of work
+  if (!ws || ws_bytes < r4c_bn_pool_workspace_size(n, d, h, w, C)) return R4C_ERR_WORKSPACE;
   float* part = static_cast<float*>(ws);
   const int R = std::max(1, 128 / (C / 8));
   const int threads = R * (C / 8);

@@ -1213,13 +1213,14 @@ int launch_conv_tuned(const ConvPlan& model, const void* x, const void* w_packed
   cudaGetDevice(&dev);
   const PlanKey key{{model.n, model.d, model.h, model.w, model.cin, model.cout, model.ks, model.pd, model.ph,
                      model.pw, dev, dtype}};
+  if (getenv("R4C_TC_PLAN")) return launch_conv(model, x, w_packed, bias, y, dtype, st);  // explicit override wins
   {
     std::lock_guard<std::mutex> lk(mu);
     auto it = tuned.find(key);
     if (it != tuned.end()) return launch_conv(it->second, x, w_packed, bias, y, dtype, st);
   }
   const char* at = getenv("R4C_AUTOTUNE");
-  if (getenv("R4C_TC_PLAN") || (at && at[0] == '0')) return launch_conv(model, x, w_packed, bias, y, dtype, st);
+  if (at && at[0] == '0') return launch_conv(model, x, w_packed, bias, y, dtype, st);
   cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
   if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone)
     return launch_conv(model, x, w_packed, bias, y, dtype, st);

@@ -951,6 +951,7 @@ struct alignas(64) DwsArgs {
   int d, h, w, cin, cout;
   int cw, cwb, apt, mtiles, nslots, kwn;
   int pitch, kpad, wt, nwt;
+  int bz;                            // planes walked innermost at each input row (a divisor of d)
   int plane_bytes, brow_bytes, a_bytes, stage_bytes, stages;
   int tmem_cols, npad;
   long long rows, rows_per_split;
@@ -1049,11 +1050,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t last_par[kMaxStages];
       for (int s = 0; s < kMaxStages; ++s) { pending[s] = false; last_par[s] = 0; }
       for (long long r = r_beg; r < r_end; ++r) {
+        // row order (n, z block, yi, z in block, w tile): an input row is
+        // reused by the next planes of its block and a dY row by the next
+        // rows while both are still in L2
         const int wi = (int)(r % a.nwt);
         long long q = r / a.nwt;
+        const int zi = (int)(q % a.bz); q /= a.bz;
         const int yi = (int)(q % a.h); q /= a.h;
-        const int z = (int)(q % a.d);
-        const int nb = (int)(q / a.d);
+        const int nzb = a.d / a.bz;
+        const int z = (int)(q % nzb) * a.bz + zi;
+        const int nb = (int)(q / nzb);
         const int x0 = wi * a.wt;
         if (!wait(&empty[stage], epar)) break;
         mbar_arrive_expect_tx(&full[stage], tx_bytes);
@@ -1170,7 +1176,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 struct DwsPlan {
   bool ok;
   int cw, cwb, ng, nco, apt, mtiles, nslots, kwn;
-  int pitch, kpad, wt, nwt;
+  int pitch, kpad, wt, nwt, bz;
   int plane_bytes, brow_bytes, a_bytes, stage_bytes, stages, smem_bytes, tmem_cols, npad;
   long long rows, rows_per_split;
   int S;
@@ -1229,6 +1235,11 @@ static bool plan_dws(int n, int d, int h, int w, int cin, int cout, int ks, int 
       for (int kw0 = 0; kw0 < 3; kw0 += P.kwn) P.tasks.push_back(Task{0, P.mtiles, c * P.cwb, P.cwb, kw0, P.kwn, g});
   if ((int)P.tasks.size() > 128) return false;
   P.rows = (long long)n * d * h * P.nwt;
+  P.bz = d % 4 == 0 ? 4 : d % 2 == 0 ? 2 : 1;
+  {
+    const char* bze = getenv("R4C_DW_BZ");   // tuning: planes per block (must divide d)
+    if (bze && atoi(bze) > 0 && d % atoi(bze) == 0) P.bz = atoi(bze);
+  }
   // cost per row: the MMAs (measured ~45 clk at N <= 32, N/2 above) or the
   // boxes' bytes (~30 B/clk per SM), plus the stage hand-off
   const double t_mma = std::max(45.0, P.npad / 2.0 + 8.0) * (P.kpad / 16) * P.kwn * P.mtiles;
@@ -1347,7 +1358,7 @@ int launch_dw(int n, int d, int h, int w, int cin, int cin_real, int cout, int k
       if (!a.err) return R4C_ERR_CUDA;
       a.d = d; a.h = h; a.w = w; a.cin = cin; a.cout = cout;
       a.cw = R.cw; a.cwb = R.cwb; a.apt = R.apt; a.mtiles = R.mtiles; a.nslots = R.nslots; a.kwn = R.kwn;
-      a.pitch = R.pitch; a.kpad = R.kpad; a.wt = R.wt; a.nwt = R.nwt;
+      a.pitch = R.pitch; a.kpad = R.kpad; a.wt = R.wt; a.nwt = R.nwt; a.bz = R.bz;
       a.plane_bytes = R.plane_bytes; a.brow_bytes = R.brow_bytes; a.a_bytes = R.a_bytes;
       a.stage_bytes = R.stage_bytes; a.stages = R.stages; a.tmem_cols = R.tmem_cols; a.npad = R.npad;
       a.rows = R.rows; a.rows_per_split = R.rows_per_split; a.ntasks = (int)R.tasks.size();

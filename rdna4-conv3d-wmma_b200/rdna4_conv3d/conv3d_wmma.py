@@ -349,6 +349,8 @@ class Conv3dWmmaFn(torch.autograd.Function):
         x_c = x if x.dtype in _HALF else x.to(torch.float16)
         if go.dtype != x_c.dtype:
             go = go.to(x_c.dtype)
+        if x.is_cuda and wmma_ok_dw(cin, cout, ks, stride, dilation, 1):
+            go = _as_ndhwc(go)        # one dense NDHWC copy for both kernel legs
         need_x, need_w, need_b = ctx.needs_input_grad[:3]
         want_db = ctx.has_bias and need_b
         dx_leg = need_x and wmma_ok_dx(cin, cout, ks, stride, dilation, 1)
@@ -669,6 +671,9 @@ class ConvTranspose3dWmmaFn(torch.autograd.Function):
         need_x, need_w, need_b = ctx.needs_input_grad[:3]
         x_c = x if x.dtype in _HALF else x.to(torch.float16)
         go = grad_out.to(x_c.dtype) if grad_out.dtype != x_c.dtype else grad_out
+        # one dense NDHWC copy shared by both legs when dY arrives as a view
+        # (e.g. the channel slice of a concatenation's gradient)
+        go = _as_ndhwc(go)
         want_db = ctx.has_bias and need_b
         dw = db = None
         if need_w:

@@ -72,6 +72,7 @@ struct ConvPlan {
   int a_bytes, b_bytes, stage_bytes, stages, smem_bytes;
   int wres;              // 1: the whole packed weight stays resident in smem
   int wres_bytes;        // its size (ks * ngroups * b_bytes) when resident
+  int warp_issue;        // 1: the whole MMA warp runs the issue loop (elect.sync); 0: lane 0 alone
   int tmem_cols;
   int stg_bytes;         // output staging buffer (one of two) for TMA stores; 0: per-thread stores
   double est_cycles;     // planner's cost-model estimate for the whole launch

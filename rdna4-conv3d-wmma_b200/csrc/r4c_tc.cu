@@ -44,6 +44,7 @@
 #include <cuda.h>
 
 #include <algorithm>
+#include <utility>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -91,6 +92,7 @@ struct alignas(64) TcConvArgs {
   int mtiles, nsets;
   int a_bytes, a_tx, b_bytes, stage_bytes, stages;
   int wres, wres_bytes;
+  int warp_issue;  // 1: the whole MMA warp runs the issue loop; 0: lane 0 alone
   int tmem_cols;
   int stg_bytes;  // one output staging buffer (two follow the weights); 0: per-thread stores
   long long units;
@@ -251,7 +253,7 @@ static double mma_clk(int n) { return std::max({n / 2.0, 40.0 + n / 6.0, 45.0});
 // G = 8-channel chunks per stage, stages caps the stage count). Unset keys
 // are searched as usual.
 struct PlanForce {
-  int ht = 0, nw = 0, P = 0, G = 0, wres = -1, stages = 0, stg = -1, pad = -1;
+  int ht = 0, nw = 0, P = 0, G = 0, wres = -1, stages = 0, stg = -1, pad = -1, wi = -1;
 };
 static PlanForce plan_force() {
   PlanForce f;
@@ -268,6 +270,7 @@ static PlanForce plan_force() {
     else if (!strcmp(key, "stages")) f.stages = val;
     else if (!strcmp(key, "stg")) f.stg = val;
     else if (!strcmp(key, "pad")) f.pad = val;
+    else if (!strcmp(key, "wi")) f.wi = val;
     e += used;
     while (*e == ',' || *e == ' ') ++e;
   }
@@ -400,6 +403,7 @@ static void enumerate_plans(int n, int d, int h, int w, int cin, int cout, int k
             P.P = Pb; P.nin = nin;
             P.a_bytes = L.a_bytes; P.b_bytes = b_bytes; P.stage_bytes = stage; P.stages = stages;
             P.wres = wres; P.wres_bytes = wres_bytes;
+            P.warp_issue = force.wi >= 0 ? force.wi : wres;  // the measured better default (tuned per shape)
             P.smem_bytes = kHeader + wres_bytes + 2 * stg + stages * stage;
             P.stg_bytes = stg;
             const int cols = nsets * Pb * P.npad * mtiles;
@@ -617,7 +621,8 @@ __device__ __forceinline__ void store_row(T* dst, const float (&v)[NV], const fl
   }
 }
 
-// MMA issue for the nsteps K steps of one stage (one thread). MT tiles x NS
+// MMA issue for the nsteps K steps of one stage. WARP: the whole warp runs
+// it and elect.sync issues each MMA; otherwise one thread does. MT tiles x NS
 // slot segments per step are fully unrolled and K steps are unrolled so that
 // a loop iteration carries at least four MMAs: a loop iteration costs the
 // issuing thread a ~40-clock bubble (branch resolution after an MMA), which
@@ -629,7 +634,13 @@ __device__ __forceinline__ void store_row(T* dst, const float (&v)[NV], const fl
 //   dk, bk, ik    : TMEM column offset, B offset (16-byte units) and
 //                   instruction descriptor of slot segment k
 // Every MMA accumulates: the epilogue zeroes the accumulators it drains.
-template <int MT, int NS>
+template <bool WARP>
+__device__ __forceinline__ void mma_issue(uint32_t d, uint64_t a, uint64_t b, uint32_t i) {
+  if (WARP) mma_f16_ss_warp(d, a, b, i, 1u);
+  else mma_f16_ss(d, a, b, i, 1u);
+}
+
+template <bool WARP, int MT, int NS>
 __device__ __forceinline__ void issue_steps(const uint32_t* __restrict__ tlo, const uint32_t* __restrict__ thi,
                                             const uint32_t* __restrict__ tts, int nsteps, uint32_t sA4,
                                             uint64_t bd0, uint64_t bstep, uint32_t dbase, uint32_t tile_cols,
@@ -651,7 +662,7 @@ __device__ __forceinline__ void issue_steps(const uint32_t* __restrict__ tlo, co
       for (int t = 0; t < MT; ++t)
 #pragma unroll
         for (int k = 0; k < NS; ++k)
-          mma_f16_ss(dk[k] + (uint32_t)t * tile_cols, ad + (uint64_t)t * ts, bd + bk[k], ik[k], 1u);
+          mma_issue<WARP>(dk[k] + (uint32_t)t * tile_cols, ad + (uint64_t)t * ts, bd + bk[k], ik[k]);
     }
   }
 #pragma unroll 1
@@ -663,7 +674,7 @@ __device__ __forceinline__ void issue_steps(const uint32_t* __restrict__ tlo, co
     for (int t = 0; t < MT; ++t)
 #pragma unroll
       for (int k = 0; k < NS; ++k)
-        mma_f16_ss(dk[k] + (uint32_t)t * tile_cols, ad + (uint64_t)t * ts, bd + bk[k], ik[k], 1u);
+        mma_issue<WARP>(dk[k] + (uint32_t)t * tile_cols, ad + (uint64_t)t * ts, bd + bk[k], ik[k]);
   }
 }
 
@@ -673,25 +684,26 @@ __device__ __forceinline__ void issue_steps(const uint32_t* __restrict__ tlo, co
       uint64_t bstep, uint32_t dbase, uint32_t tile_cols, uint32_t d0, uint32_t d1, uint32_t d2, uint32_t b0, \
       uint32_t b1, uint32_t b2, uint32_t i0, uint32_t i1, uint32_t i2
 
-template <int MT>
+template <bool WARP, int MT>
 __device__ __forceinline__ void issue_ns(int ns, R4C_ISSUE_PARAMS) {
   switch (ns) {
-    case 1: issue_steps<MT, 1>(R4C_ISSUE_ARGS); break;
-    case 2: issue_steps<MT, 2>(R4C_ISSUE_ARGS); break;
-    default: issue_steps<MT, 3>(R4C_ISSUE_ARGS); break;
+    case 1: issue_steps<WARP, MT, 1>(R4C_ISSUE_ARGS); break;
+    case 2: issue_steps<WARP, MT, 2>(R4C_ISSUE_ARGS); break;
+    default: issue_steps<WARP, MT, 3>(R4C_ISSUE_ARGS); break;
   }
 }
 
+template <bool WARP>
 __device__ __forceinline__ void issue(int mt, int ns, R4C_ISSUE_PARAMS) {
   switch (mt) {
-    case 1: issue_ns<1>(ns, R4C_ISSUE_ARGS); break;
-    case 2: issue_ns<2>(ns, R4C_ISSUE_ARGS); break;
-    case 3: issue_ns<3>(ns, R4C_ISSUE_ARGS); break;
-    case 4: issue_ns<4>(ns, R4C_ISSUE_ARGS); break;
-    case 5: issue_ns<5>(ns, R4C_ISSUE_ARGS); break;
-    case 6: issue_ns<6>(ns, R4C_ISSUE_ARGS); break;
-    case 7: issue_ns<7>(ns, R4C_ISSUE_ARGS); break;
-    default: issue_ns<8>(ns, R4C_ISSUE_ARGS); break;
+    case 1: issue_ns<WARP, 1>(ns, R4C_ISSUE_ARGS); break;
+    case 2: issue_ns<WARP, 2>(ns, R4C_ISSUE_ARGS); break;
+    case 3: issue_ns<WARP, 3>(ns, R4C_ISSUE_ARGS); break;
+    case 4: issue_ns<WARP, 4>(ns, R4C_ISSUE_ARGS); break;
+    case 5: issue_ns<WARP, 5>(ns, R4C_ISSUE_ARGS); break;
+    case 6: issue_ns<WARP, 6>(ns, R4C_ISSUE_ARGS); break;
+    case 7: issue_ns<WARP, 7>(ns, R4C_ISSUE_ARGS); break;
+    default: issue_ns<WARP, 8>(ns, R4C_ISSUE_ARGS); break;
   }
 }
 #undef R4C_ISSUE_ARGS
@@ -713,9 +725,6 @@ __global__ void __launch_bounds__(kThreads, 1) tc_conv_kernel(const __grid_const
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* epi_ok = reinterpret_cast<volatile int*>(smem + 256);  // one flag per epilogue warp
   float* sbias = reinterpret_cast<float*>(smem + 1024);        // 256 floats
-  uint32_t* s_lo = reinterpret_cast<uint32_t*>(smem + 2048);   // kMaxSteps each
-  uint32_t* s_hi = s_lo + kMaxSteps;
-  uint32_t* s_ts = s_hi + kMaxSteps;
   uint8_t* wres_smem = smem + kHeader;
   uint8_t* stg0 = smem + kHeader + a.wres_bytes;  // two output staging tiles when stg_bytes > 0
   uint8_t* stage0 = stg0 + 2 * a.stg_bytes;
@@ -732,8 +741,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_conv_kernel(const __grid_const
   }
 
   // One-time set-up: zero the stage buffers (rows past the TMA boxes are
-  // read by junk GEMM rows only, but must be finite), stage the bias as fp32
-  // and the descriptor tables, init barriers, allocate TMEM.
+  // read by junk GEMM rows only, but must be finite), stage the bias as fp32,
+  // init barriers, allocate TMEM.
   {
     const uint4 z = make_uint4(0, 0, 0, 0);
     const int total = a.stages * a.stage_bytes;
@@ -741,11 +750,6 @@ __global__ void __launch_bounds__(kThreads, 1) tc_conv_kernel(const __grid_const
     const T* bias = static_cast<const T*>(a.bias);
     for (int i = threadIdx.x; i < a.slot_w; i += kThreads)
       sbias[i] = (bias != nullptr && i < a.cout) ? Elem<T>::to_f(bias[i]) : 0.f;
-    for (int i = threadIdx.x; i < a.nsteps; i += kThreads) {
-      s_lo[i] = a.dlo[i];
-      s_hi[i] = a.dhi[i];
-      s_ts[i] = a.dts[i];
-    }
   }
   if (threadIdx.x == 0) {
     for (int s = 0; s < a.stages; ++s) {
@@ -844,23 +848,40 @@ __global__ void __launch_bounds__(kThreads, 1) tc_conv_kernel(const __grid_const
       }
     }
   } else if (warp == kMmaWarp) {
-    // ---------------- MMA issuer (lane 0) ----------------
-    // One thread issues. A warp-wide issuer (elected lane, uniform
-    // descriptors) issues each MMA slightly faster in isolation but measured
-    // slower inside the pipelined kernel.
-    if (lane == 0) {
+    // ---------------- MMA issuer (warp 1) ----------------
+    // The per-step descriptor words are read from the kernel parameter
+    // (constant bank) with a uniform index. With the weights resident the
+    // whole warp runs the issue loop (warp-uniform control flow, descriptors
+    // in uniform registers, elect.sync issues each MMA; lane 0 polls the
+    // barriers and broadcasts the outcome): measured 15-20% fewer clocks per
+    // MMA than one thread. With the weights staged per stage the single-
+    // thread loop mostly measured equal or faster (up to 2x for 48 -> 48), so
+    // the form is a plan parameter (default: warp iff resident weights) that
+    // the on-device tuner also tries flipped.
+    const bool wi = a.warp_issue != 0;
+    auto wait_w = [&](uint64_t* bar, uint32_t par) -> bool {
+      if (!wi) return wait(bar, par);
+      int got = 0;
+      if (lane == 0) got = wait(bar, par) ? 1 : 0;
+      return __shfl_sync(0xffffffffu, got, 0) != 0;
+    };
+    auto commit = [&](uint64_t* bar) {
+      if (wi) mma_commit_warp(bar);
+      else mma_commit(bar);
+    };
+    if (wi || lane == 0) {
       int stage = 0;
       uint32_t fpar = 0;
       uint32_t tpar[2] = {0, 0};  // phase 0 of tempty = the epilogue's initial zeroing
       int set = 0;
       bool ok = true;
-      if (a.wres && !wait(wbar, 0)) ok = false;
+      if (a.wres && !wait_w(wbar, 0)) ok = false;
       const uint32_t bslot = (uint32_t)(a.slot_w * 16);  // bytes of one slot's B rows
       const int ks = a.ks, Pb = a.P, slot_w = a.slot_w, mtiles = a.mtiles, nsteps = a.nsteps;
       const int fold = a.fold, ngroups = a.ngroups, nin = a.nin;
       const uint32_t tile_cols = (uint32_t)(Pb * slot_w);
       for (long long u = blockIdx.x; u < units && ok; u += gridDim.x) {
-        if (!wait(&tempty[set], tpar[set])) { ok = false; break; }
+        if (!wait_w(&tempty[set], tpar[set])) { ok = false; break; }
         tpar[set] ^= 1;
         tc_fence_after();
         const uint32_t dset = tmem + (uint32_t)(set * set_cols);
@@ -871,41 +892,45 @@ __global__ void __launch_bounds__(kThreads, 1) tc_conv_kernel(const __grid_const
           const int lo = max(0, j - ks + 1), hi = min(Pb - 1, j);
           const int b0 = (ks - 1) - (j - lo);
           const int nsl = hi - lo + 1;
-          uint32_t dd[3] = {0, 0, 0}, bb[3] = {0, 0, 0}, ii[3] = {0, 0, 0};
-          int ns = 0;
-          for (int o = lo; o <= hi && ns < 3; ++ns) {
-            const int n = min(fold, hi - o + 1);
-            dd[ns] = (uint32_t)(o * slot_w);
-            bb[ns] = (uint32_t)(((o - lo) * bslot) >> 4);
-            ii[ns] = a.idesc[n];
-            o += n;
-          }
+          // runs of at most `fold` slots, as scalars (a runtime-indexed
+          // array would live in local memory, outside the uniform registers)
+          const int n0 = min(fold, nsl), n1 = min(fold, nsl - n0), n2 = min(fold, nsl - n0 - n1);
+          const int ns = 1 + (n1 > 0) + (n2 > 0);
+          const uint32_t d0 = (uint32_t)(lo * slot_w), d1 = (uint32_t)((lo + n0) * slot_w),
+                         d2 = (uint32_t)((lo + n0 + n1) * slot_w);
+          const uint32_t bb0 = 0u, bb1 = (uint32_t)((n0 * bslot) >> 4), bb2 = (uint32_t)(((n0 + n1) * bslot) >> 4);
+          const uint32_t i0 = a.idesc[n0], i1 = a.idesc[n1], i2 = a.idesc[n2];
           // resident weights keep all ks slots per (step, half); staged ones
           // only the nsl slots of this input plane
           const int bslots = a.wres ? ks : nsl;
           const uint64_t bstep = (uint64_t)((2 * bslots * bslot) >> 4);
           const uint32_t blbo = (uint32_t)(bslots * bslot);
           for (int g = 0; g < ngroups; ++g) {
-            if (!wait(&full[stage], fpar)) { ok = false; break; }
+            if (!wait_w(&full[stage], fpar)) { ok = false; break; }
             tc_fence_after();
             const uint32_t sA4 = smem_u32(stage0 + (size_t)stage * a.stage_bytes) >> 4;
             const uint32_t sB = a.wres ? smem_u32(wres_smem + (size_t)g * a.b_bytes) + (uint32_t)b0 * bslot
                                        : smem_u32(stage0 + (size_t)stage * a.stage_bytes + a.a_bytes);
             const uint64_t bdesc = smem_desc(sB, blbo, 128);
-            issue(mtiles, ns, s_lo, s_hi, s_ts, nsteps, sA4, bdesc, bstep, dset, tile_cols, dd[0], dd[1], dd[2],
-                  bb[0], bb[1], bb[2], ii[0], ii[1], ii[2]);
-            mma_commit(&empty[stage]);
+            if (wi)
+              issue<true>(mtiles, ns, a.dlo, a.dhi, a.dts, nsteps, sA4, bdesc, bstep, dset, tile_cols, d0, d1, d2, bb0,
+                          bb1, bb2, i0, i1, i2);
+            else
+              issue<false>(mtiles, ns, a.dlo, a.dhi, a.dts, nsteps, sA4, bdesc, bstep, dset, tile_cols, d0, d1, d2,
+                           bb0, bb1, bb2, i0, i1, i2);
+            commit(&empty[stage]);
             if (++stage == a.stages) { stage = 0; fpar ^= 1; }
           }
         }
         if (!ok) break;
-        mma_commit(&tfull[set]);
+        commit(&tfull[set]);
         if (a.nsets == 2) set ^= 1;
       }
       // every MMA issued must have completed before TMEM is released, abort
       // or not: this wait ignores the abort flag (bounded by time only)
-      mma_commit(mdone);
-      mbar_wait_bounded(mdone, 0, global_timer_ns() + kWaitNs);
+      commit(mdone);
+      if (lane == 0) mbar_wait_bounded(mdone, 0, global_timer_ns() + kWaitNs);
+      if (wi) __syncwarp();
     }
   } else {
     // ---------------- epilogue (warps 2..9) ----------------
@@ -1146,6 +1171,7 @@ int launch_conv(const ConvPlan& P, const void* x, const void* w_packed, const vo
   a.a_bytes = L.a_bytes; a.a_tx = L.a_tx;
   a.b_bytes = P.b_bytes; a.stage_bytes = P.stage_bytes; a.stages = P.stages;
   a.wres = P.wres; a.wres_bytes = P.wres_bytes;
+  a.warp_issue = P.warp_issue;
   a.tmem_cols = P.tmem_cols;
   a.units = P.work_units;
   // Output map for the TMA-store epilogue: box (cout, wt, ht, 1, 1) over the
@@ -1235,6 +1261,7 @@ int launch_conv_tuned(const ConvPlan& model, const void* x, const void* w_packed
   ConvPlan best = model;
   float best_ms = 1e30f;
   int rc = R4C_OK;
+  std::vector<std::pair<float, ConvPlan>> timed;
   for (const ConvPlan& c : cands) {
     rc = launch_conv(c, x, w_packed, bias, y, dtype, st);  // warm-up (and module load)
     if (rc != R4C_OK) break;
@@ -1248,9 +1275,34 @@ int launch_conv_tuned(const ConvPlan& model, const void* x, const void* w_packed
       if (rc == R4C_OK && cudaEventElapsedTime(&t, e0, e1) == cudaSuccess) ms = std::min(ms, t);
     }
     if (rc != R4C_OK) break;
+    timed.emplace_back(ms, c);
     if (ms < best_ms) {
       best_ms = ms;
       best = c;
+    }
+  }
+  // the issue form: the fastest three plans again with it flipped
+  if (rc == R4C_OK) {
+    std::vector<std::pair<float, ConvPlan>> timed_sorted = timed;
+    std::sort(timed_sorted.begin(), timed_sorted.end(),
+              [](const std::pair<float, ConvPlan>& x, const std::pair<float, ConvPlan>& y) { return x.first < y.first; });
+    for (size_t i = 0; i < timed_sorted.size() && i < 3 && rc == R4C_OK; ++i) {
+      ConvPlan c = timed_sorted[i].second;
+      c.warp_issue ^= 1;
+      rc = launch_conv(c, x, w_packed, bias, y, dtype, st);
+      float ms = 1e30f;
+      for (int rep = 0; rep < 2 && rc == R4C_OK; ++rep) {
+        cudaEventRecord(e0, st);
+        rc = launch_conv(c, x, w_packed, bias, y, dtype, st);
+        cudaEventRecord(e1, st);
+        if (cudaEventSynchronize(e1) != cudaSuccess) rc = R4C_ERR_CUDA;
+        float t = 0.f;
+        if (rc == R4C_OK && cudaEventElapsedTime(&t, e0, e1) == cudaSuccess) ms = std::min(ms, t);
+      }
+      if (rc == R4C_OK && ms < best_ms) {
+        best_ms = ms;
+        best = c;
+      }
     }
   }
   cudaEventDestroy(e0);

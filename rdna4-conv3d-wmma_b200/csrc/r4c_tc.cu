@@ -343,7 +343,11 @@ static void enumerate_plans(int n, int d, int h, int w, int cin, int cout, int k
         const int ngroups = L.ngroups;
         const int b_bytes = nsteps * 2 * ks * P.npad * 16;
         const int wbytes = ngroups * b_bytes;
-        if (wres && wbytes > 96 * 1024) continue;
+        // resident weights up to 160 KB (the stage ring must still fit beside
+        // them, checked below): at 48 -> 48 (124 KB) they let a unit hold
+        // several output planes without streaming the weights per stage
+        // (B200, batch 4: forward 177 -> 135 us)
+        if (wres && wbytes > 160 * 1024) continue;
         const int wres_bytes = wres ? round_up(wbytes, 1024) : 0;
         const int stg = so ? round_up(ht * wt * cout * 2, 1024) : 0;
         const int avail = kSmemMax - kHeader - wres_bytes - 2 * stg;

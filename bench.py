@@ -282,6 +282,7 @@ def run_step(layers, reducer, ev=None, legs=("fwd", "dw", "dx")):
     cw = sys.modules["rdna4_conv3d.conv3d_wmma"]
     p3 = lambda p: (p, p, p)  # noqa: E731
     outs = []
+    pending = []
     for i, L in enumerate(layers):
         y = dw = db = dx = handle = None
         if ev is not None:
@@ -300,8 +301,12 @@ def run_step(layers, reducer, ev=None, legs=("fwd", "dw", "dx")):
         if ev is not None:
             ev[i][3].record()
         if handle is not None:
-            handle.wait()
+            pending.append(handle)
         outs.append((y, dw, db, dx))
+    # the reductions ran on a side stream under the later legs; the step
+    # waits for them once, at its end
+    for handle in pending:
+        handle.wait()
     return outs
 
 
@@ -497,7 +502,7 @@ def _unet_step_fn(net, opt):
     return step
 
 
-def _graph_step(net, opt, x, tgt, warmup):
+def _graph_step(net, opt, x, tgt, warmup, loss_scale=1.0):
     """Capture one whole training step (forward, backward, Adam) in a CUDA
     graph over static input / label buffers; returns (replay, loss buffer).
     Warm-up runs eagerly on a side stream first (plan tuning, NCCL set-up)."""
@@ -508,16 +513,19 @@ def _graph_step(net, opt, x, tgt, warmup):
         for _ in range(max(warmup, 3)):
             opt.zero_grad(set_to_none=True)
             with torch.autocast("cuda", dtype=torch.bfloat16):
-                loss = F.cross_entropy(net(x), tgt)
+                loss = F.cross_entropy(net(x), tgt) * loss_scale
             loss.backward()
             opt.step()
+    # the last warm-up loss holds its autograd graph, whose gradient
+    # accumulators would keep the side stream as their stream during capture
+    del loss
     torch.cuda.current_stream().wait_stream(side)
     torch.cuda.synchronize()
     g = torch.cuda.CUDAGraph()
     opt.zero_grad(set_to_none=True)
     with torch.cuda.graph(g):
         with torch.autocast("cuda", dtype=torch.bfloat16):
-            static_loss = F.cross_entropy(net(x), tgt)
+            static_loss = F.cross_entropy(net(x), tgt) * loss_scale
         static_loss.backward()
         opt.step()
     return g, static_loss
@@ -605,10 +613,12 @@ def time_unet(dev, base, batch, steps, warmup, world, rank, graph=False):
     return res
 
 
-def time_depth_shard(dev, base, steps, warmup, world, rank):
+def time_depth_shard(dev, base, steps, warmup, world, rank, graph=False):
     """One 1x1x128x256x256 volume per step, D-sharded over the ranks (halo
     exchange per k3 conv, whole-volume BatchNorm statistics); on one GPU the
-    plain unsharded model. ms per sample = per step."""
+    plain unsharded model. ms per sample = per step. ``graph``: the step
+    (halo exchanges and gradient all-reduces included) is captured once in a
+    CUDA graph and replayed."""
     import torch.distributed as dist
 
     from rdna4_conv3d.distributed import GradSync, depth_shard_model
@@ -619,7 +629,7 @@ def time_depth_shard(dev, base, steps, warmup, world, rank):
     sync = None
     if world > 1:
         sync = GradSync(depth_shard_model(net), average=False)
-    opt = torch.optim.Adam(net.parameters(), lr=1e-3, fused=True)
+    opt = torch.optim.Adam(net.parameters(), lr=1e-3, fused=True, capturable=graph)
     step = _unet_step_fn(net, opt)
     d, h, w = DEPTH_SHARD_SPATIAL
     dl = d // world
@@ -627,22 +637,35 @@ def time_depth_shard(dev, base, steps, warmup, world, rank):
     x = torch.randn(1, 1, d, h, w, device=dev, generator=g)[:, :, rank * dl:(rank + 1) * dl]
     x = x.contiguous(memory_format=cl)
     tgt = torch.randint(0, 4, (1, d, h, w), device=dev, generator=g)[:, rank * dl:(rank + 1) * dl].contiguous()
+    cg = None
+    if graph:
+        cg, static_loss = _graph_step(net, opt, x, tgt, warmup, 1.0 / world)
+
+        def step(xx, tt, loss_scale=1.0):  # noqa: F811  (graphed step)
+            cg.replay()
+            return static_loss.detach()
     for _ in range(max(warmup, 3)):
         step(x, tgt, 1.0 / world)
     torch.cuda.synchronize()
     barrier(world)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    h0 = time.perf_counter()
     e0.record()
     for _ in range(steps):
         loss = step(x, tgt, 1.0 / world)
     e1.record()
+    host_ms = (time.perf_counter() - h0) * 1e3 / steps
     torch.cuda.synchronize()
     ms = max_over_ranks(e0.elapsed_time(e1), world) / steps
+    loss = loss.clone()
     if world > 1:
         dist.all_reduce(loss)
     barrier(world)
-    res = {"base": base, "volume": [1, 1, d, h, w], "planes_per_gpu": dl, "ms_per_sample": round(ms, 3),
+    res = {"base": base, "volume": [1, 1, d, h, w], "planes_per_gpu": dl, "cuda_graph": bool(graph),
+           "ms_per_sample": round(ms, 3), "host_issue_ms_per_step": round(host_ms, 3),
            "loss_last": round(float(loss), 5)}
+    if cg is not None:
+        del cg
     if sync is not None:
         sync.remove()
     del net, opt, x, tgt
@@ -697,7 +720,7 @@ def main():
     ap.add_argument("--no-unet", action="store_true", help="skip the UNet3D training steps (configs[3]/[4])")
     ap.add_argument("--no-depth-shard", action="store_true", help="skip the depth-sharded volume")
     ap.add_argument("--unet-only", action="store_true", help="only the UNet3D steps (one JSON line)")
-    ap.add_argument("--no-graph", action="store_true", help="skip the CUDA-graph UNet step (N = 1)")
+    ap.add_argument("--no-graph", action="store_true", help="skip the CUDA-graph UNet steps (eager depth shard)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -713,11 +736,12 @@ def main():
     if args.unet_only:
         u_steps = max(3, args.steps)
         res = {"base24": time_unet(dev, 24, BATCH, u_steps, args.warmup, world, rank)}
-        if world == 1 and not args.no_graph:
+        if not args.no_graph:
             res["base24_graph"] = time_unet(dev, 24, BATCH, u_steps, args.warmup, world, rank, graph=True)
         if not args.no_depth_shard:
             res["base32"] = time_unet(dev, 32, BATCH, u_steps, args.warmup, world, rank)
-            res["depth_shard_base32"] = time_depth_shard(dev, 32, max(2, min(args.steps, 5)), 3, world, rank)
+            res["depth_shard_base32"] = time_depth_shard(dev, 32, max(2, min(args.steps, 5)), 3, world, rank,
+                                                         graph=not args.no_graph)
         if rank == 0:
             print(json.dumps({"impl": "ours", "n_gpus": world, "unet": res}), flush=True)
         if world > 1:
@@ -852,10 +876,14 @@ def main():
         u_steps = max(3, min(args.steps, 10))
         unet = {"base24": time_unet(dev, 24, BATCH, u_steps, 3, world, rank),
                 "base32": time_unet(dev, 32, BATCH, u_steps, 3, world, rank)}
-        if world == 1 and not args.no_graph:
+        if not args.no_graph:
+            # the whole step (gradient all-reduces included at N > 1) in one
+            # CUDA graph: the eager step is bound by the host's issue rate
             unet["base24_graph"] = time_unet(dev, 24, BATCH, u_steps, 3, world, rank, graph=True)
+            unet["base32_graph"] = time_unet(dev, 32, BATCH, u_steps, 3, world, rank, graph=True)
         if not args.no_depth_shard:
-            unet["depth_shard_base32"] = time_depth_shard(dev, 32, max(2, min(args.steps, 5)), 3, world, rank)
+            unet["depth_shard_base32"] = time_depth_shard(dev, 32, max(2, min(args.steps, 5)), 3, world, rank,
+                                                          graph=not args.no_graph)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and args.only is None:

@@ -29,11 +29,12 @@ def _cw():
 
 
 class _Pending:
-    def __init__(self, works, tensors, stream, scale):
+    def __init__(self, works, tensors, stream, scale, flat=None):
         self.works = works
         self.tensors = tensors
         self.stream = stream
         self.scale = scale
+        self.flat = flat  # reduced (and already scaled) copy of the tensors, one buffer
 
     def wait(self):
         for w in self.works:
@@ -42,7 +43,15 @@ class _Pending:
             torch.cuda.current_stream().wait_stream(self.stream)
             for t in self.tensors:
                 t.record_stream(self.stream)
-        if self.scale != 1.0:
+            if self.flat is not None:
+                self.flat.record_stream(torch.cuda.current_stream())
+        if self.flat is not None:
+            off = 0
+            for t in self.tensors:
+                n = t.numel()
+                t.copy_(self.flat[off:off + n].view_as(t))
+                off += n
+        elif self.scale != 1.0:
             for t in self.tensors:
                 t.mul_(self.scale)
 
@@ -66,8 +75,16 @@ class GradAllReducer:
             return _Pending(works, tensors, None, scale)
         self.stream.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(self.stream):
-            works = [dist.all_reduce(t, group=self.group, async_op=True) for t in tensors]
-        return _Pending(works, tensors, self.stream, scale)
+            if len(tensors) == 1 or any(t.dtype != tensors[0].dtype for t in tensors):
+                works = [dist.all_reduce(t, group=self.group, async_op=True) for t in tensors]
+                return _Pending(works, tensors, self.stream, scale)
+            # one collective per call: the tensors (e.g. a layer's dW and db)
+            # packed into one buffer, reduced and scaled on the side stream
+            flat = torch.cat([t.reshape(-1) for t in tensors])
+            dist.all_reduce(flat, group=self.group)
+            if scale != 1.0:
+                flat.mul_(scale)
+        return _Pending([], tensors, self.stream, scale, flat)
 
 
 class GradSync:
@@ -530,19 +547,28 @@ class DepthShardedBatchNormReLU3d(BatchNormReLU3d):
     def __init__(self, *args, group=None, **kw):
         super().__init__(*args, **kw)
         self.group = group
+        # whole-volume voxel count per local count: the finalize kernels take
+        # the count from the host, and reading an all-reduced count back each
+        # call would stall the host once per layer and step
+        self._totals = {}
 
     def _sums_hook(self):
         if not (dist.is_available() and dist.is_initialized()):
             return None
-        group, C = self.group, self.num_features
+        group, C, totals = self.group, self.num_features, self._totals
 
         def hook(sums, count):
             dist.all_reduce(sums[:2 * C], group=group)
             if count is None:
                 return None
-            t = torch.tensor([count], dtype=torch.float64, device=sums.device)
-            dist.all_reduce(t, group=group)
-            return float(t.item())
+            # Every rank calls this in the same order with its own slab, so
+            # all ranks meet a new slab shape (and run this collective) at the
+            # same call; later calls with the same shapes reuse the total.
+            if count not in totals:
+                t = torch.tensor([count], dtype=torch.float64, device=sums.device)
+                dist.all_reduce(t, group=group)
+                totals[count] = float(t.item())
+            return totals[count]
         return hook
 
     def _pivot(self):

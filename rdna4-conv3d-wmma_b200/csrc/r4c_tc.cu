@@ -65,6 +65,7 @@ namespace tc {
 
 constexpr int kMaxSteps = 128;
 constexpr int kMaxStages = 8;
+constexpr int kMaxPlanes = 16;  // output planes per unit (per-plane accumulator hand-off barriers)
 constexpr int kMaxMt = 8;    // M tiles per unit (the issue loop is unrolled over them)
 constexpr int kMaxChg = 16;  // channel groups per stage
 constexpr int kEpiWarps = 8;  // two per TMEM lane quarter (alternate (tile, plane) slots)
@@ -396,7 +397,10 @@ static void enumerate_plans(int n, int d, int h, int w, int cin, int cout, int k
                                  150.0)
                  : (double)Pb * mtiles * (((P.npad + 31) / 32) * 100.0 + ((cout + 7) / 8) * 12.0 + 40.0);
           double t_unit = std::max(mma, load) + 100.0 * nin * ngroups;
-          t_unit = nsets == 2 ? std::max(t_unit, epi) : t_unit + epi;
+          // two sets: the epilogue of a unit overlaps the next unit; one set:
+          // planes are handed over one at a time, so only about one plane's
+          // drain is not overlapped
+          t_unit = nsets == 2 ? std::max(t_unit, epi) : std::max(t_unit, epi) + epi / Pb;
           const long long units = (long long)n * ((P.od + Pb - 1) / Pb) * tiles_h * nw;
           const long long waves = (units + sms - 1) / sms;
           const double est = (double)waves * t_unit;
@@ -728,6 +732,14 @@ __global__ void __launch_bounds__(kThreads, 1) tc_conv_kernel(const __grid_const
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(wbar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* epi_ok = reinterpret_cast<volatile int*>(smem + 256);  // one flag per epilogue warp
+  // One accumulator set (nsets == 1): output planes are handed over one by
+  // one. sfull[o]: the MMAs of plane o's last input plane completed; sempty[o]:
+  // the epilogue drained and re-zeroed plane o, so the next unit may write it.
+  // The epilogue of a unit thus overlaps the MMAs of its later input planes
+  // and of the next unit's first ones.
+  uint64_t* sfull = reinterpret_cast<uint64_t*>(smem + 512);
+  uint64_t* sempty = sfull + kMaxPlanes;
+  const bool by_plane = a.nsets == 1;
   float* sbias = reinterpret_cast<float*>(smem + 1024);        // 256 floats
   uint8_t* wres_smem = smem + kHeader;
   uint8_t* stg0 = smem + kHeader + a.wres_bytes;  // two output staging tiles when stg_bytes > 0
@@ -739,7 +751,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_conv_kernel(const __grid_const
   // Swizzled TMA boxes and the MMA's address-based swizzle need the stage
   // regions on 1024-byte boundaries: the layout is built on a 1024-aligned
   // base.
-  if ((smem_u32(smem) & 1023u) != 0u || a.tmem_cols > 512) {
+  if ((smem_u32(smem) & 1023u) != 0u || a.tmem_cols > 512 || a.P > kMaxPlanes) {
     if (threadIdx.x == 0) atomicExch(&g_r4c_dev_error, 2);
     return;
   }
@@ -766,6 +778,10 @@ __global__ void __launch_bounds__(kThreads, 1) tc_conv_kernel(const __grid_const
     }
     mbar_init(mdone, 1);
     mbar_init(wbar, 1);
+    for (int o = 0; o < kMaxPlanes; ++o) {
+      mbar_init(&sfull[o], 1);
+      mbar_init(&sempty[o], kEpiWarps);
+    }
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -877,6 +893,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_conv_kernel(const __grid_const
       int stage = 0;
       uint32_t fpar = 0;
       uint32_t tpar[2] = {0, 0};  // phase 0 of tempty = the epilogue's initial zeroing
+      uint32_t separ = 0;         // by_plane: parity bit per output plane of sempty
       int set = 0;
       bool ok = true;
       if (a.wres && !wait_w(wbar, 0)) ok = false;
@@ -885,11 +902,20 @@ __global__ void __launch_bounds__(kThreads, 1) tc_conv_kernel(const __grid_const
       const int fold = a.fold, ngroups = a.ngroups, nin = a.nin;
       const uint32_t tile_cols = (uint32_t)(Pb * slot_w);
       for (long long u = blockIdx.x; u < units && ok; u += gridDim.x) {
-        if (!wait_w(&tempty[set], tpar[set])) { ok = false; break; }
-        tpar[set] ^= 1;
-        tc_fence_after();
+        if (!by_plane) {
+          if (!wait_w(&tempty[set], tpar[set])) { ok = false; break; }
+          tpar[set] ^= 1;
+          tc_fence_after();
+        }
         const uint32_t dset = tmem + (uint32_t)(set * set_cols);
         for (int j = 0; j < nin && ok; ++j) {
+          // by_plane: input plane j is the first to write output plane j,
+          // which must have been drained from the previous unit
+          if (by_plane && j < Pb) {
+            if (!wait_w(&sempty[j], (separ >> j) & 1u)) { ok = false; break; }
+            separ ^= 1u << j;
+            tc_fence_after();
+          }
           // input plane j feeds output slots lo..hi; one MMA per run of at
           // most `fold` slots (their B rows are adjacent: slot o uses the
           // weights of kd = j - o, stored in reverse kd order)
@@ -925,9 +951,11 @@ __global__ void __launch_bounds__(kThreads, 1) tc_conv_kernel(const __grid_const
             commit(&empty[stage]);
             if (++stage == a.stages) { stage = 0; fpar ^= 1; }
           }
+          // by_plane: output plane j - ks + 1 has had its last input plane
+          if (ok && by_plane && j >= ks - 1) commit(&sfull[j - ks + 1]);
         }
         if (!ok) break;
-        commit(&tfull[set]);
+        if (!by_plane) commit(&tfull[set]);
         if (a.nsets == 2) set ^= 1;
       }
       // every MMA issued must have completed before TMEM is released, abort
@@ -957,8 +985,101 @@ __global__ void __launch_bounds__(kThreads, 1) tc_conv_kernel(const __grid_const
     if (lane == 0) {
       mbar_arrive(&tempty[0]);
       mbar_arrive(&tempty[1]);
+      if (by_plane)
+        for (int o = 0; o < a.P; ++o) mbar_arrive(&sempty[o]);
     }
-    for (long long u = blockIdx.x; u < units; u += gridDim.x) {
+    uint32_t sfpar = 0;  // by_plane: parity bit per output plane of sfull
+    // Waits on `bar` (lane 0 polls) and returns whether it completed; with
+    // the TMA-store epilogue the warps meet on a named barrier afterwards,
+    // so they agree on the outcome first and leave the loops together.
+    auto epi_wait = [&](uint64_t* bar, uint32_t par) -> bool {
+      int got = 1;
+      if (lane == 0) got = wait(bar, par, 128) ? 1 : 0;
+      got = __shfl_sync(0xffffffffu, got, 0);
+      if (a.stg_bytes) {
+        if (lane == 0) epi_ok[warp - 2] = got;
+        epi_bar_sync();
+        got = 1;
+#pragma unroll
+        for (int i = 0; i < kEpiWarps; ++i) got &= epi_ok[i];
+        epi_bar_sync();  // every warp has read the flags before they are rewritten
+      }
+      return got != 0;
+    };
+    for (long long u = blockIdx.x; by_plane && u < units; u += gridDim.x) {
+      const int wi = (int)(u % a.nwt);
+      long long r = u / a.nwt;
+      const int hi = (int)(r % a.nht); r /= a.nht;
+      const int zb = (int)(r % a.nzb);
+      const int nb = (int)(r / a.nzb);
+      const int h0 = hi * a.ht, w0 = wi * a.wt, z0 = zb * a.P;
+      const int nz = min(a.P, a.od - z0);
+      const long long plane = (long long)a.oh * a.ow * a.cout;  // elements per output plane
+      T* const yu = y + ((((long long)nb * a.od + z0) * a.oh + h0) * a.ow + w0) * a.cout;
+      bool ok = true;
+      for (int o = 0; o < a.P; ++o) {
+        if (!epi_wait(&sfull[o], (sfpar >> o) & 1u)) { ok = false; break; }
+        sfpar ^= 1u << o;
+        tc_fence_after();
+        const bool live = o < nz;  // planes past the volume's depth are only zeroed
+        if (a.stg_bytes) {
+          // TMEM -> bias, rounding -> staging tile [ht][wt][cout] -> one TMA
+          // store (clips positions outside the volume); two staging tiles
+          // alternate as in the per-unit form below
+          if (live) {
+            if (threadIdx.x == 64) bulk_wait_read<1>();
+            epi_bar_sync();
+          }
+          T* sb = reinterpret_cast<T*>(stg0 + (size_t)sbuf * a.stg_bytes);
+          for (int t = half; t < a.mtiles; t += 2) {
+            const int p = t * 128 + row;
+            const int hh = p / a.pitch_w;
+            const int ww = p - hh * a.pitch_w;
+            const bool valid = live && hh < a.ht && ww < a.wt;
+            T* dst = sb + ((size_t)hh * a.wt + ww) * a.cout;
+            const uint32_t tb = tq + (uint32_t)(t * a.P * a.slot_w + o * a.slot_w);
+            for (int cc = 0; cc < a.slot_w; cc += 16) {
+              float v[16];
+              tmem_ld_16(tb + (uint32_t)cc, v);
+              tmem_zero_16(tb + (uint32_t)cc);
+              if (valid) store_row<T, 16>(dst, v, sbias, cc, a.cout, true);
+            }
+          }
+          if (live) {
+            fence_proxy_async_smem();
+            epi_bar_sync();
+            if (threadIdx.x == 64) {
+              tma_store_5d(&a.ymap, sb, 0, w0, h0, z0 + o, nb);
+              bulk_commit_group();
+            }
+            sbuf ^= 1;
+          }
+        } else {
+          // every tile of the plane; the two warps of a lane quarter take
+          // alternate 16-column groups of each tile
+          for (int t = 0; t < a.mtiles; ++t) {
+            const int p = t * 128 + row;
+            const int hh = p / a.pitch_w;
+            const int ww = p - hh * a.pitch_w;
+            const bool valid = live && hh < a.ht && ww < a.wt && (h0 + hh) < a.oh && (w0 + ww) < a.ow;
+            T* dst = yu + (long long)o * plane + ((long long)hh * a.ow + ww) * a.cout;
+            const uint32_t tb = tq + (uint32_t)(t * a.P * a.slot_w + o * a.slot_w);
+            for (int cc = 16 * half; cc < a.slot_w; cc += 32) {
+              float v[16];
+              tmem_ld_16(tb + (uint32_t)cc, v);
+              tmem_zero_16(tb + (uint32_t)cc);
+              if (valid) store_row<T, 16>(dst, v, sbias, cc, a.cout, vec_ok);
+            }
+          }
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sempty[o]);
+      }
+      if (!ok) break;
+    }
+    for (long long u = blockIdx.x; !by_plane && u < units; u += gridDim.x) {
       const int wi = (int)(u % a.nwt);
       long long r = u / a.nwt;
       const int hi = (int)(r % a.nht); r /= a.nht;

@@ -490,12 +490,12 @@ DEPTH_SHARD_SPATIAL = (128, 256, 256)
 
 
 def _unet_step_fn(net, opt):
-    import torch.nn.functional as F
+    from rdna4_conv3d.losses import cross_entropy
 
     def step(x, tgt, loss_scale=1.0):
         opt.zero_grad(set_to_none=True)
         with torch.autocast("cuda", dtype=torch.bfloat16):
-            loss = F.cross_entropy(net(x), tgt) * loss_scale
+            loss = cross_entropy(net(x), tgt) * loss_scale
         loss.backward()
         opt.step()
         return loss.detach()
@@ -506,14 +506,14 @@ def _graph_step(net, opt, x, tgt, warmup, loss_scale=1.0):
     """Capture one whole training step (forward, backward, Adam) in a CUDA
     graph over static input / label buffers; returns (replay, loss buffer).
     Warm-up runs eagerly on a side stream first (plan tuning, NCCL set-up)."""
-    import torch.nn.functional as F
+    from rdna4_conv3d.losses import cross_entropy
     side = torch.cuda.Stream()
     side.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(side):
         for _ in range(max(warmup, 3)):
             opt.zero_grad(set_to_none=True)
             with torch.autocast("cuda", dtype=torch.bfloat16):
-                loss = F.cross_entropy(net(x), tgt) * loss_scale
+                loss = cross_entropy(net(x), tgt) * loss_scale
             loss.backward()
             opt.step()
     # the last warm-up loss holds its autograd graph, whose gradient
@@ -525,7 +525,7 @@ def _graph_step(net, opt, x, tgt, warmup, loss_scale=1.0):
     opt.zero_grad(set_to_none=True)
     with torch.cuda.graph(g):
         with torch.autocast("cuda", dtype=torch.bfloat16):
-            static_loss = F.cross_entropy(net(x), tgt) * loss_scale
+            static_loss = cross_entropy(net(x), tgt) * loss_scale
         static_loss.backward()
         opt.step()
     return g, static_loss

@@ -297,6 +297,28 @@ int r4c_bn_relu_pool_bwd_dx(const void* gy, int gy_pitch, const void* gp, const 
                             r4c_stream_t stream);
 
 /*
+ * Cross-entropy over the channel dimension of NDHWC (channels-last) logits,
+ * mean over the voxels whose label is not `ignore_index` — F.cross_entropy
+ * with reduction='mean' and no class weights, the loss of the UNet training
+ * step measured here (four classes). No reference kernel: the reference's
+ * training step computes its loss with stock PyTorch (benches/unet_e2e.py:
+ * 41-52). Logits bf16 or
+ * fp16 (fp32 arithmetic), `vox` voxels x C classes, int64 labels.
+ * r4c_ce_fwd writes loss_count[0] = mean loss, loss_count[1] = the number of
+ * counted voxels (device memory, 2 floats); `ws` holds
+ * r4c_ce_workspace_size(vox) bytes; the sum is deterministic (fixed blocks,
+ * fixed order). r4c_ce_bwd writes dlogits = grad_loss[0] * (softmax - onehot)
+ * / count (zero for ignored voxels) in the logits' dtype and layout,
+ * grad_loss a device scalar. A label outside [0, C) that is not ignore_index
+ * is skipped and sets code 6 in the device error flag.
+ */
+size_t r4c_ce_workspace_size(int64_t vox);
+int r4c_ce_fwd(const void* logits, const int64_t* target, int64_t vox, int C, int dtype, int64_t ignore_index,
+               float* loss_count, void* ws, size_t ws_bytes, r4c_stream_t stream);
+int r4c_ce_bwd(const void* logits, const int64_t* target, int64_t vox, int C, int dtype, int64_t ignore_index,
+               const float* loss_count, const float* grad_loss, void* dlogits, r4c_stream_t stream);
+
+/*
  * Conv3d weight and bias gradient without any allocation. No counterpart in
  * the reference: it exists for callers that cannot allocate device memory,
  * e.g. a plugin or custom op running inside another framework that owns the

@@ -91,6 +91,9 @@ def _bind(lib) -> None:
         "r4c_bn_pool_workspace_size": ([i, i, i, i, i], sz),
         "r4c_bn_relu_pool_bwd_sums": ([P, i, P, P, P, P, i, i, i, i, i, i, P, P, sz, P], i),
         "r4c_bn_relu_pool_bwd_dx": ([P, i, P, P, P, P, P, P, dbl, i, i, i, i, i, i, P, P, P, P], i),
+        "r4c_ce_workspace_size": ([i64], sz),
+        "r4c_ce_fwd": ([P, P, i64, i, i, i64, P, P, sz, P], i),
+        "r4c_ce_bwd": ([P, P, i64, i, i, i64, P, P, P, P], i),
         "r4c_convex_plan": ([X], i),
         "r4c_convex_workspace_size": ([X, i], sz),
         "r4c_convex_fwd": ([X, P, P, P, P, P, sz, P], i),
@@ -493,3 +496,36 @@ def device_error(device=None, clear: bool = True) -> int:
     dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
     with torch.cuda.device(dev):
         return int(lib().r4c_device_error(_stream(dev), 1 if clear else 0))
+
+
+# ---------------------------------------------------------------------------
+# Cross-entropy over NDHWC logits (r4c_ce_*)
+# ---------------------------------------------------------------------------
+def ce_forward(logits_cl: torch.Tensor, target: torch.Tensor, ignore_index: int) -> torch.Tensor:
+    """(mean loss, counted voxels) as a 2-float device tensor."""
+    dev = _require_cuda(logits_cl, target)
+    C = int(logits_cl.shape[1])
+    vox = logits_cl.numel() // C
+    L = lib()
+    ws = torch.empty(int(L.r4c_ce_workspace_size(vox)), dtype=torch.uint8, device=dev)
+    out = torch.empty(2, dtype=torch.float32, device=dev)
+    with torch.cuda.device(dev):
+        st = L.r4c_ce_fwd(_ptr(logits_cl), _ptr(target), vox, C, dtype_code(logits_cl.dtype), int(ignore_index),
+                          _ptr(out), _ptr(ws), ws.numel(), _stream(dev))
+    _check(st, "r4c_ce_fwd")
+    return out
+
+
+def ce_backward(logits_cl: torch.Tensor, target: torch.Tensor, ignore_index: int, loss_count: torch.Tensor,
+                grad: torch.Tensor) -> torch.Tensor:
+    """d(loss)/d(logits), NDHWC in the logits' dtype; ``grad`` a device scalar."""
+    dev = _require_cuda(logits_cl, target)
+    C = int(logits_cl.shape[1])
+    vox = logits_cl.numel() // C
+    g = grad.detach().to(torch.float32).reshape(1).contiguous()
+    dz = torch.empty_like(logits_cl, memory_format=torch.channels_last_3d)
+    with torch.cuda.device(dev):
+        st = lib().r4c_ce_bwd(_ptr(logits_cl), _ptr(target), vox, C, dtype_code(logits_cl.dtype), int(ignore_index),
+                              _ptr(loss_count), _ptr(g), _ptr(dz), _stream(dev))
+    _check(st, "r4c_ce_bwd")
+    return dz

@@ -17,7 +17,7 @@ SRC_DIR = os.path.join(os.path.dirname(PKG_DIR), "csrc")
 INC_DIR = os.path.join(os.path.dirname(os.path.dirname(PKG_DIR)), "include")
 OUT = os.path.join(PKG_DIR, "libr4c_conv3d.so")
 OBJ_DIR = os.path.join(os.path.dirname(PKG_DIR), "_build")  # objects (git-ignored)
-SOURCES = ["r4c_api.cu", "r4c_generic.cu", "r4c_tc.cu", "r4c_tc_dw.cu", "r4c_tc_stem.cu", "r4c_tc_stem_dx.cu", "r4c_tc_tconv.cu", "r4c_noalloc.cu", "r4c_general.cu", "r4c_bn.cu", "r4c_watchdog.cu"]
+SOURCES = ["r4c_api.cu", "r4c_generic.cu", "r4c_tc.cu", "r4c_tc_dw.cu", "r4c_tc_stem.cu", "r4c_tc_stem_dx.cu", "r4c_tc_tconv.cu", "r4c_noalloc.cu", "r4c_general.cu", "r4c_bn.cu", "r4c_watchdog.cu", "r4c_ce.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -98,7 +98,16 @@ def unet3d(base: int = 24, levels: int = 4, in_channels: int = 1, n_classes: int
         fuse_bn_relu(net)
     if device is not None:
         net = net.to(device)
-    return net.to(memory_format=torch.channels_last_3d)
+    net = net.to(memory_format=torch.channels_last_3d)
+    if wmma:
+        # activations are NDHWC, but conv weights stay in PyTorch's OIDHW
+        # order: the packing kernels read that order and the weight
+        # gradients come back in it, so neither the packing nor the gradient
+        # accumulation needs a layout copy
+        for m in net.modules():
+            if isinstance(m, (nn.Conv3d, nn.ConvTranspose3d)):
+                m.weight.data = m.weight.data.contiguous()
+    return net
 
 
 def conv_flops_per_sample(net: UNet3D, spatial, in_channels: int = 1) -> float:

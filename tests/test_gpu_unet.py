@@ -27,13 +27,13 @@ pytestmark = pytest.mark.gpu
 LOSS_TOL = 1e-3
 
 
-def _train(net, x, tgt, steps):
+def _train(net, x, tgt, steps, loss_fn=F.cross_entropy):
     opt = torch.optim.Adam(net.parameters(), lr=1e-3)
     hist = []
     for _ in range(steps):
         opt.zero_grad(set_to_none=True)
         with torch.autocast("cuda", dtype=torch.bfloat16):
-            loss = F.cross_entropy(net(x), tgt)
+            loss = loss_fn(net(x), tgt)
         loss.backward()
         opt.step()
         hist.append(loss.detach())
@@ -42,6 +42,7 @@ def _train(net, x, tgt, steps):
 
 def test_unet3d_base24_amp_loss_parity(cuda_ready):
     from rdna4_conv3d import _native
+    from rdna4_conv3d.losses import cross_entropy
     from rdna4_conv3d.unet3d import unet3d
     dev = torch.device("cuda")
     torch.manual_seed(0)
@@ -61,7 +62,7 @@ def test_unet3d_base24_amp_loss_parity(cuda_ready):
     ours = unet3d(24, wmma=True, device=dev)
     ours.load_state_dict(state)
     n0 = _native.launch_count()
-    got = _train(ours, x, tgt, 40)
+    got = _train(ours, x, tgt, 40, cross_entropy)   # the whole step on the library: convs, BN, loss
     assert _native.launch_count() - n0 > 40 * 50, "the UNet did not run on the native kernels"
     assert _native.device_error() == 0
     diffs = [abs(a - b) for a, b in zip(ref, got)]

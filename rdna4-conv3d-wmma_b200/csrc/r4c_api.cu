@@ -279,17 +279,17 @@ int r4c_describe_plan(const r4c_conv_desc* desc, int leg, char* buf, size_t len)
       snprintf(tmp, sizeof(tmp),
                "tcgen05 conv: cin=%d cout=%d(npad %d) k=%d planes/unit=%d fold=%d tile=%dx%d pitch=%dx%d G=%d groups=%d "
                "padg=%d steps=%d mtiles=%d sets=%d stages=%d stage=%dB wres=%d stg=%d smem=%dB tmem=%d units=%lld "
-               "grid=%d est=%.0fus wi=%d",
+               "grid=%d est=%.0fus wi=%d pps=%d",
                pl.cin, pl.cout, pl.npad, pl.ks, pl.P, pl.fold, pl.ht, pl.wt, pl.pitch_h, pl.pitch_w, pl.G, pl.ngroups,
                pl.padg, pl.nsteps, pl.mtiles, pl.nsets, pl.stages, pl.stage_bytes, pl.wres_bytes, pl.stg_bytes,
                pl.smem_bytes,
-               pl.tmem_cols, (long long)pl.work_units, pl.grid, pl.est_cycles / 1.9e3, pl.warp_issue);
+               pl.tmem_cols, (long long)pl.work_units, pl.grid, pl.est_cycles / 1.9e3, pl.warp_issue, pl.pps);
       tc::ConvPlan tp;
       if (tc::tuned_plan(pl, desc->dtype, &tp)) {
         char t2[160];
         snprintf(t2, sizeof(t2),
-                 " | tuned on device: planes/unit=%d tile=%dx%d mtiles=%d sets=%d stages=%d wres=%d stg=%d wi=%d",
-                 tp.P, tp.ht, tp.wt, tp.mtiles, tp.nsets, tp.stages, tp.wres_bytes, tp.stg_bytes, tp.warp_issue);
+                 " | tuned on device: planes/unit=%d tile=%dx%d mtiles=%d sets=%d stages=%d wres=%d stg=%d wi=%d pps=%d",
+                 tp.P, tp.ht, tp.wt, tp.mtiles, tp.nsets, tp.stages, tp.wres_bytes, tp.stg_bytes, tp.warp_issue, tp.pps);
         strncat(tmp, t2, sizeof(tmp) - strlen(tmp) - 1);
       }
       st = R4C_KERNEL_TC;

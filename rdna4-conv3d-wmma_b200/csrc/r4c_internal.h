@@ -75,6 +75,7 @@ struct ConvPlan {
   int warp_issue;        // 1: the whole MMA warp runs the issue loop (elect.sync); 0: lane 0 alone
   int tmem_cols;
   int stg_bytes;         // output staging buffer (one of two) for TMA stores; 0: per-thread stores
+  int pps;               // input planes per pipeline stage (1, or 2 with resident weights)
   double est_cycles;     // planner's cost-model estimate for the whole launch
   int64_t work_units;    // n * ceil(od / P) * tiles_h * tiles_w
   int grid;

@@ -94,6 +94,7 @@ struct alignas(64) TcConvArgs {
   int a_bytes, a_tx, b_bytes, stage_bytes, stages;
   int wres, wres_bytes;
   int warp_issue;  // 1: the whole MMA warp runs the issue loop; 0: lane 0 alone
+  int pps;         // input planes per pipeline stage (2: resident weights, one channel stage per plane)
   int tmem_cols;
   int stg_bytes;  // one output staging buffer (two follow the weights); 0: per-thread stores
   long long units;
@@ -254,7 +255,7 @@ static double mma_clk(int n) { return std::max({n / 2.0, 40.0 + n / 6.0, 45.0});
 // G = 8-channel chunks per stage, stages caps the stage count). Unset keys
 // are searched as usual.
 struct PlanForce {
-  int ht = 0, nw = 0, P = 0, G = 0, wres = -1, stages = 0, stg = -1, pad = -1, wi = -1;
+  int ht = 0, nw = 0, P = 0, G = 0, wres = -1, stages = 0, stg = -1, pad = -1, wi = -1, pps = 0;
 };
 static PlanForce plan_force() {
   PlanForce f;
@@ -272,6 +273,7 @@ static PlanForce plan_force() {
     else if (!strcmp(key, "stg")) f.stg = val;
     else if (!strcmp(key, "pad")) f.pad = val;
     else if (!strcmp(key, "wi")) f.wi = val;
+    else if (!strcmp(key, "pps")) f.pps = val;
     e += used;
     while (*e == ',' || *e == ' ') ++e;
   }
@@ -314,6 +316,15 @@ static void enumerate_plans(int n, int d, int h, int w, int cin, int cout, int k
       if (n2 <= 0 || n2 == n1) continue;
     }
     if (force.pad >= 0 && (int)padg != force.pad) continue;
+    // k = 3: a padded last group that is a quarter or more zero channels
+    // loses to the exact groups (48 -> 48: 64-channel rows, best tuned plan
+    // 100 us, against 90 us for 32 + 16 on B200); the model cannot see it
+    // and the tuner only compares plans of one packed layout
+    if (padg && ks == 3 && force.pad != 1) {
+      Chg pg[kMaxChg];
+      const int npg = channel_groups(cin, pg, true);
+      if (npg > 0 && 4 * (pg[npg - 1].cw - pg[npg - 1].creal) >= pg[npg - 1].creal) continue;
+    }
     const int G = split > 0 ? split / 8 : P.c8;
     if (force.G && G != force.G) continue;
     if (G_only > 0 && G != G_only) continue;
@@ -361,10 +372,15 @@ static void enumerate_plans(int n, int d, int h, int w, int cin, int cout, int k
           rows_clk += (double)pitch_h * pitch_w * std::max(1.0, L.g[gi].cw * 2 / 105.0);
         for (int Pb = 1; Pb <= std::min(P.od, 16); ++Pb) {
           if (force.P && Pb != force.P) continue;
+          // pps = 2: two input planes per pipeline stage (one barrier wait and
+          // one release per two planes); resident weights, one channel stage
+         for (int pps = 1; pps <= 2; ++pps) {
+          if (pps == 2 && !(wres && ngroups == 1 && Pb + ks - 1 >= 2)) continue;
+          if (force.pps && pps != force.pps) continue;
           // a stage holds the A regions and, unless resident, the weight
           // slots of the output planes its input plane feeds (<= min(ks, Pb))
           const int sb = std::min(ks, Pb) * nsteps * 2 * P.npad * 16;
-          const int stage = round_up(L.a_bytes + (wres ? 0 : sb), 1024);
+          const int stage = round_up(pps * L.a_bytes + (wres ? 0 : sb), 1024);
           const int stages =
               std::min(force.stages ? force.stages : kMaxStages, std::min(kMaxStages, avail / stage));
           if (stages < 2) break;
@@ -396,7 +412,10 @@ static void enumerate_plans(int n, int d, int h, int w, int cin, int cout, int k
               so ? (double)Pb * (mtiles * (((P.npad + 31) / 32) * 100.0 + ((cout + 7) / 8) * 4.0 * conflict + 40.0) +
                                  150.0)
                  : (double)Pb * mtiles * (((P.npad + 31) / 32) * 100.0 + ((cout + 7) / 8) * 12.0 + 40.0);
-          double t_unit = std::max(mma, load) + 100.0 * nin * ngroups;
+          // per pipeline stage: the barrier wait, the release commit and the
+          // MMA pipe's turnaround (~600 clk, fitted to B200 timings)
+          const int unit_stages = pps > 1 ? (nin + 1) / 2 : nin * ngroups;
+          double t_unit = std::max(mma, load) + 600.0 * unit_stages;
           // two sets: the epilogue of a unit overlaps the next unit; one set:
           // planes are handed over one at a time, so only about one plane's
           // drain is not overlapped
@@ -412,6 +431,7 @@ static void enumerate_plans(int n, int d, int h, int w, int cin, int cout, int k
             P.a_bytes = L.a_bytes; P.b_bytes = b_bytes; P.stage_bytes = stage; P.stages = stages;
             P.wres = wres; P.wres_bytes = wres_bytes;
             P.warp_issue = force.wi >= 0 ? force.wi : wres;  // the measured better default (tuned per shape)
+            P.pps = pps;
             P.smem_bytes = kHeader + wres_bytes + 2 * stg + stages * stage;
             P.stg_bytes = stg;
             const int cols = nsets * Pb * P.npad * mtiles;
@@ -424,6 +444,7 @@ static void enumerate_plans(int n, int d, int h, int w, int cin, int cout, int k
             P.ok = true;
             visit(static_cast<const ConvPlan&>(P));
           }
+         }
         }
       }
       }
@@ -488,7 +509,7 @@ static std::vector<ConvPlan> plan_candidates(const ConvPlan& m, int k_top) {
   std::vector<ConvPlan> out;
   auto same = [](const ConvPlan& a, const ConvPlan& b) {
     return a.ht == b.ht && a.wt == b.wt && a.P == b.P && a.wres == b.wres && a.stages == b.stages &&
-           a.stg_bytes == b.stg_bytes;
+           a.stg_bytes == b.stg_bytes && a.pps == b.pps;
   };
   auto add = [&](const ConvPlan& c) {
     for (const ConvPlan& o : out)
@@ -496,6 +517,11 @@ static std::vector<ConvPlan> plan_candidates(const ConvPlan& m, int k_top) {
     out.push_back(c);
   };
   for (size_t i = 0; i < all.size() && (int)out.size() < k_top; ++i) add(all[i]);
+  // the cheapest plan of each stage form (planes per stage x accumulator sets)
+  for (int pps = 1; pps <= 2; ++pps)
+    for (int ns = 1; ns <= 2; ++ns)
+      for (const ConvPlan& c : all)
+        if (c.pps == pps && c.nsets == ns) { add(c); break; }
   for (int so = 0; so <= 1; ++so) {
     for (int Pb : {1, 2, 3, 4, 5, 6, 8, 12, 16})
       for (const ConvPlan& c : all)
@@ -831,14 +857,21 @@ __global__ void __launch_bounds__(kThreads, 1) tc_conv_kernel(const __grid_const
           const int iz = zb * a.P - a.pd + j;  // outside [0, d): TMA fills zeros
           const int lo = max(0, j - a.ks + 1), hs = min(a.P - 1, j);
           const int nsl = hs - lo + 1, b0 = (a.ks - 1) - (j - lo);
+          // pps = 2: planes j (even) and j + 1 share a stage, at A-region
+          // offsets 0 and a_bytes (one channel stage per plane)
+          const int q = a.pps > 1 ? (j & 1) : 0;
+          const bool last_q = q == a.pps - 1 || j == a.nin - 1;
           for (int g = 0; g < a.ngroups; ++g) {
-            if (!wait(&empty[stage], epar)) { ok = false; break; }
             uint8_t* sbase = stage0 + (size_t)stage * a.stage_bytes;
             const uint32_t wtx = a.wres ? 0u : (uint32_t)(a.nsteps * 2 * nsl) * slot_bytes;
-            mbar_arrive_expect_tx(&full[stage], (uint32_t)a.a_tx + wtx);
+            if (q == 0) {
+              if (!wait(&empty[stage], epar)) { ok = false; break; }
+              const uint32_t np = (uint32_t)min(a.pps, a.nin - j);
+              mbar_arrive_expect_tx(&full[stage], np * (uint32_t)a.a_tx + wtx);
+            }
             for (int gi = 0; gi < a.nchg; ++gi)
-              tma_load_5d(sbase + a.chg_roff[gi], &a.maps[a.chg_map[gi]], &full[stage], a.chg_c0[gi] + g * a.stage_c0,
-                          w0, h0, iz, nb);
+              tma_load_5d(sbase + (size_t)q * a.a_bytes + a.chg_roff[gi], &a.maps[a.chg_map[gi]], &full[stage],
+                          a.chg_c0[gi] + g * a.stage_c0, w0, h0, iz, nb);
             if (!a.wres) {
               // weight rows of slots [lo, hs] for every K step and half:
               // global [g][step][half][ks slots][rows] -> smem [step][half][nsl slots][rows]
@@ -848,6 +881,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_conv_kernel(const __grid_const
                 bulk_load(sdst + (size_t)sh * nsl * slot_bytes, gsrc + (size_t)sh * a.ks * slot_bytes,
                           (uint32_t)nsl * slot_bytes, &full[stage]);
             }
+            if (!last_q) continue;
             pending[stage] = true;
             last_par[stage] = epar ^ 1;
             if (++stage == a.stages) { stage = 0; epar ^= 1; }
@@ -935,10 +969,14 @@ __global__ void __launch_bounds__(kThreads, 1) tc_conv_kernel(const __grid_const
           const int bslots = a.wres ? ks : nsl;
           const uint64_t bstep = (uint64_t)((2 * bslots * bslot) >> 4);
           const uint32_t blbo = (uint32_t)(bslots * bslot);
+          const int q = a.pps > 1 ? (j & 1) : 0;  // plane slot in the stage (pps = 2)
+          const bool last_q = q == a.pps - 1 || j == nin - 1;
           for (int g = 0; g < ngroups; ++g) {
-            if (!wait_w(&full[stage], fpar)) { ok = false; break; }
-            tc_fence_after();
-            const uint32_t sA4 = smem_u32(stage0 + (size_t)stage * a.stage_bytes) >> 4;
+            if (q == 0) {
+              if (!wait_w(&full[stage], fpar)) { ok = false; break; }
+              tc_fence_after();
+            }
+            const uint32_t sA4 = (smem_u32(stage0 + (size_t)stage * a.stage_bytes) + (uint32_t)(q * a.a_bytes)) >> 4;
             const uint32_t sB = a.wres ? smem_u32(wres_smem + (size_t)g * a.b_bytes) + (uint32_t)b0 * bslot
                                        : smem_u32(stage0 + (size_t)stage * a.stage_bytes + a.a_bytes);
             const uint64_t bdesc = smem_desc(sB, blbo, 128);
@@ -948,6 +986,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_conv_kernel(const __grid_const
             else
               issue<false>(mtiles, ns, a.dlo, a.dhi, a.dts, nsteps, sA4, bdesc, bstep, dset, tile_cols, d0, d1, d2,
                            bb0, bb1, bb2, i0, i1, i2);
+            if (!last_q) continue;
             commit(&empty[stage]);
             if (++stage == a.stages) { stage = 0; fpar ^= 1; }
           }
@@ -1297,6 +1336,8 @@ int launch_conv(const ConvPlan& P, const void* x, const void* w_packed, const vo
   a.b_bytes = P.b_bytes; a.stage_bytes = P.stage_bytes; a.stages = P.stages;
   a.wres = P.wres; a.wres_bytes = P.wres_bytes;
   a.warp_issue = P.warp_issue;
+  a.pps = P.pps > 1 ? 2 : 1;
+  if (a.pps == 2 && (!P.wres || P.ngroups != 1)) return R4C_ERR_INVALID;
   a.tmem_cols = P.tmem_cols;
   a.units = P.work_units;
   // Output map for the TMA-store epilogue: box (cout, wt, ht, 1, 1) over the
@@ -1376,7 +1417,7 @@ int launch_conv_tuned(const ConvPlan& model, const void* x, const void* w_packed
   if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone)
     return launch_conv(model, x, w_packed, bias, y, dtype, st);
 
-  std::vector<ConvPlan> cands = plan_candidates(model, 8);
+  std::vector<ConvPlan> cands = plan_candidates(model, 12);
   if (cands.empty()) cands.push_back(model);
   cudaEvent_t e0 = nullptr, e1 = nullptr;
   if (cudaEventCreate(&e0) != cudaSuccess || cudaEventCreate(&e1) != cudaSuccess) {

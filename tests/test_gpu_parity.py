@@ -292,3 +292,33 @@ def test_kernel_families_used(cuda_ready):
 def test_no_device_error_flag(cuda_ready):
     from rdna4_conv3d import _native
     assert _native.device_error() == 0
+
+
+# Two input planes per pipeline stage (pps=2) forced on and off through the
+# plan override, with odd and even plane counts per unit, k1 and k3.
+PPS_CASES = [
+    (2, 24, 24, 16, 32, 32, 3, 1),
+    (2, 24, 24, 5, 9, 11, 3, 0),
+    (2, 24, 24, 5, 9, 11, 3, 2),
+    (1, 48, 48, 8, 16, 16, 3, 1),
+    (1, 16, 8, 6, 7, 9, 3, 1),
+    (1, 40, 16, 4, 6, 10, 3, 1),
+    (2, 24, 48, 3, 5, 130, 3, 1),
+    (1, 48, 24, 8, 16, 16, 1, 0),
+]
+
+
+@pytest.mark.parametrize("plan", ["pps=2", "pps=2,P=3", "pps=2,P=2,stg=0", "pps=1"])
+@pytest.mark.parametrize("case", PPS_CASES, ids=_ids(PPS_CASES))
+def test_conv_planes_per_stage(cuda_ready, case, plan, monkeypatch):
+    from rdna4_conv3d import _native
+    n, cin, cout, d, h, w, k, pad = case
+    monkeypatch.setenv("R4C_TC_PLAN", plan)
+    x, wt, b, go = _inputs(*case, torch.bfloat16, seed=5)
+    desc = _native.make_desc(n, d, h, w, cin, cout, k, (pad,) * 3, torch.bfloat16)
+    if "tcgen05 conv" not in _native.describe_plan(desc, _native.LEG_FWD):
+        pytest.skip("no plan of this form for the shape")
+    y, dx, dw, db = _run_conv(x, wt, b, go, pad)
+    assert O.max_rel(y, O.torch_conv_fwd(x, wt, b, pad)) <= FWD_TOL
+    assert O.max_rel(dx, O.torch_conv_dx(x.shape, wt, go, pad)) <= FWD_TOL
+    assert _native.device_error() == 0

@@ -333,10 +333,11 @@ int r4c_ce_bwd(const void* logits, const int64_t* target, int64_t vox, int C, in
  * r4c_workspace_size(desc, R4C_LEG_DW) exceeds that size are rejected with
  * R4C_ERR_TOO_LARGE. The first call on a device looks up the array's device
  * address (cudaGetSymbolAddress) with that device current; make that first
- * call before any stream capture. The address is kept for the life of the
- * process: a cudaDeviceReset(), or anything else that destroys the device's
- * primary context, voids it, and this entry point must not be called on that
- * device afterwards. All calls share the one array: calls whose
+ * call before any stream capture. The address is kept per device and looked
+ * up again when the device's current context has changed (after a
+ * cudaDeviceReset the library's module is loaded anew and the array may
+ * move); the first call after such a change should likewise come before any
+ * stream capture. All calls share the one array: calls whose
  * work overlaps on the GPU (different streams, or different host threads)
  * race on it and must be serialized by the caller. The kernels write every
  * scratch element they read, so stale contents from a previous call are

@@ -183,6 +183,18 @@ int r4c_tconv_fwd(const r4c_conv_desc* desc, const void* x, const void* w_packed
                   const void* bias, void* y, void* workspace, size_t ws_bytes,
                   r4c_stream_t stream);
 
+/* r4c_tconv_fwd into a channel slice of a wider NDHWC buffer: consecutive
+ * output voxels are y_pitch elements apart (y_pitch >= Cout, a multiple of 8,
+ * y 16-byte aligned), so the up-convolution of a UNet decoder writes its
+ * output straight into the first channels of the skip concatenation
+ * (torch.cat([up, skip], 1) of the reference's UNet, benches/unet_e2e.py:38)
+ * instead of into a tensor that is then copied there. y_pitch == Cout is
+ * r4c_tconv_fwd; other pitches need the tcgen05 path (R4C_ERR_UNSUPPORTED
+ * otherwise). */
+int r4c_tconv_fwd_pitched(const r4c_conv_desc* desc, const void* x, const void* w_packed,
+                          const void* bias, void* y, int y_pitch, void* workspace, size_t ws_bytes,
+                          r4c_stream_t stream);
+
 /* ConvTranspose3d k2s2 input gradient. Replaces transpose_k2s2_dx
  * (conv3d_wmma.py:1491-1514). */
 int r4c_tconv_dx(const r4c_conv_desc* desc, const void* go, const void* w_packed,

@@ -554,6 +554,20 @@ int r4c_tconv_fwd(const r4c_conv_desc* desc, const void* x, const void* w_packed
   return cuda_status(generic::launch_fwd(p, MODE_TFWD, desc->dtype, s));
 }
 
+int r4c_tconv_fwd_pitched(const r4c_conv_desc* desc, const void* x, const void* w_packed, const void* bias,
+                          void* y, int y_pitch, void* workspace, size_t ws_bytes, r4c_stream_t stream) {
+  Geom g;
+  int st = check_desc(desc, R4C_LEG_TFWD, &g);
+  if (st != R4C_OK) return st;
+  if (y_pitch == g.cout) return r4c_tconv_fwd(desc, x, w_packed, bias, y, workspace, ws_bytes, stream);
+  if (y_pitch < g.cout || y_pitch % 8) return R4C_ERR_INVALID;
+  if (g.in_vox() == 0) return R4C_OK;
+  if (!x || !w_packed || !y) return R4C_ERR_INVALID;
+  if (!use_tc_tconv(desc, R4C_LEG_TFWD, g)) return R4C_ERR_UNSUPPORTED;
+  return tconv::launch(0, g.n, g.d, g.h, g.w, g.cin, g.cout, x, w_packed, bias, y, desc->dtype,
+                       reinterpret_cast<cudaStream_t>(stream), y_pitch);
+}
+
 int r4c_tconv_dx(const r4c_conv_desc* desc, const void* go, const void* w_packed, void* dx,
                  void* workspace, size_t ws_bytes, r4c_stream_t stream) {
   (void)workspace; (void)ws_bytes;

@@ -148,8 +148,11 @@ size_t packed_bytes(int mode, int n, int d, int h, int w, int cin, int cout);
 int describe(int mode, int n, int d, int h, int w, int cin, int cout, char* buf, size_t len);
 cudaError_t pack_weight(int mode, int n, int d, int h, int w, int cin, int cout, const void* w_src, int src_dtype,
                         void* w_packed, int dtype, cudaStream_t st);
+// ypitch (forward only): elements between consecutive output voxels, >= cout
+// and a multiple of 8 (0: cout) — the output may be a channel slice of a
+// wider NDHWC buffer.
 int launch(int mode, int n, int d, int h, int w, int cin, int cout, const void* in, const void* w_packed,
-           const void* bias, void* out, int dtype, cudaStream_t st);
+           const void* bias, void* out, int dtype, cudaStream_t st, int ypitch = 0);
 // dW (fp32, PyTorch ConvTranspose3d layout) from x and dY; `ws` holds the
 // split partials (dw_workspace() bytes).
 bool dw_supported(int n, int d, int h, int w, int cin, int cout);

@@ -78,11 +78,12 @@ struct TArgs {
   int tmem_cols;
   uint32_t idesc;
   // forward TMA-store epilogue (stg_blk > 0): the output viewed as
-  // (2*Cout, W, 2, H, 2D*N); a tile's (a, b) block of 2*Cout columns is staged
-  // as [positions][2*Cout] (stg_blk bytes per block, two buffers) and written
-  // by one box (2*Cout, wt, 1, R, 1)
+  // (Cout, 2W, 2, H, 2D*N) with the voxel pitch ypitch; a tile's (a, b) block
+  // of 2*Cout columns is staged as [positions][2*Cout] (stg_blk bytes per
+  // block, two buffers) and written by one box (Cout, 2*wt, 1, R, 1)
   CUtensorMap ymap;
   int stg_blk;
+  int ypitch;  // forward: elements between consecutive output voxels (>= cout)
 };
 
 // Barrier 1 over the 256 epilogue threads, returning the OR of `v` over them.
@@ -163,14 +164,14 @@ __global__ void __launch_bounds__(kThreads, 1) tconv_kernel(const __grid_constan
   if (a.mode == 0) {
     // column tables of this task: output offset of each 8-column group from
     // the position (2z, 2y, 2x), and the bias of each column
-    const long long sa = 4ll * a.h * a.w * a.cout, sb = 2ll * a.w * a.cout;
+    const long long sa = 4ll * a.h * a.w * a.ypitch, sb = 2ll * a.w * a.ypitch;
     for (int i = threadIdx.x; i < a.ncol; i += kThreads) {
       const int gcol = task * a.ncol + i;
       float bv = 0.f;
       long long off = 0;
       if (gcol < a.ncol_real) {
         const int abc = gcol / a.cout, co = gcol - abc * a.cout;
-        off = (abc >> 2) * sa + ((abc >> 1) & 1) * sb + (long long)(abc & 1) * a.cout + co;
+        off = (abc >> 2) * sa + ((abc >> 1) & 1) * sb + (long long)(abc & 1) * a.ypitch + co;
         if (a.bias) bv = Elem<T>::to_f(static_cast<const T*>(a.bias)[co]);
       }
       bias_col[i] = bv;
@@ -370,7 +371,8 @@ __global__ void __launch_bounds__(kThreads, 1) tconv_kernel(const __grid_constan
         if (issuer) {
           for (int j = 0; j < nblk; ++j) {
             const int ab = task * nblk + j;
-            tma_store_5d(&a.ymap, stg + (size_t)j * a.stg_blk, 0, x0, ab & 1, y0, nb * 2 * a.d + 2 * z + (ab >> 1));
+            tma_store_5d(&a.ymap, stg + (size_t)j * a.stg_blk, 0, 2 * x0, ab & 1, y0,
+                         nb * 2 * a.d + 2 * z + (ab >> 1));
           }
           bulk_commit_group();
         }
@@ -401,7 +403,7 @@ __global__ void __launch_bounds__(kThreads, 1) tconv_kernel(const __grid_constan
       // output base of this position (elements)
       long long base;
       if (a.mode == 0)
-        base = ((((long long)nb * 2 * a.d + 2 * z) * 2 * a.h + 2 * y) * 2 * a.w + 2 * x) * a.cout;
+        base = ((((long long)nb * 2 * a.d + 2 * z) * 2 * a.h + 2 * y) * 2 * a.w + 2 * x) * a.ypitch;
       else
         base = ((((long long)nb * a.d + z) * a.h + y) * a.w + x) * a.cin + (long long)task * a.ncol;
       for (int g = half; g < ngrp; g += 2) {
@@ -938,7 +940,10 @@ cudaError_t pack_weight(int mode, int n, int d, int h, int w, int cin, int cout,
 
 // x: forward input (NDHWC, Cin) or dY (NDHWC at 2x, Cout); out: y (2x, Cout) or dX (Cin).
 int launch(int mode, int n, int d, int h, int w, int cin, int cout, const void* in, const void* w_packed,
-           const void* bias, void* out, int dtype, cudaStream_t st) {
+           const void* bias, void* out, int dtype, cudaStream_t st, int ypitch) {
+  if (ypitch == 0) ypitch = cout;
+  if (mode != 0 && ypitch != cout) return R4C_ERR_UNSUPPORTED;
+  if (ypitch < cout || ypitch % 8) return R4C_ERR_INVALID;
   TPlan p;
   if (!make_plan(mode, n, d, h, w, cin, cout, &p)) return R4C_ERR_UNSUPPORTED;
   if (((uintptr_t)in & 15) || ((uintptr_t)w_packed & 15) || ((uintptr_t)out & 15)) return R4C_ERR_ALIGN;
@@ -978,6 +983,7 @@ int launch(int mode, int n, int d, int h, int w, int cin, int cout, const void* 
   a.err = tc::device_error_flag();
   if (!a.err) return R4C_ERR_CUDA;
   a.mode = mode;
+  a.ypitch = ypitch;
   a.n = n; a.d = d; a.h = h; a.w = w; a.cin = cin; a.cout = cout;
   a.wt = p.wt; a.R = p.R; a.nwt = p.nwt; a.nyb = p.nyb; a.tiles = p.tiles;
   a.nbox = p.nbox;
@@ -991,11 +997,12 @@ int launch(int mode, int n, int d, int h, int w, int cin, int cout, const void* 
   a.b_bytes = p.b_bytes; a.tmem_cols = p.tmem_cols;
   a.idesc = instr_desc_f16(dtype == R4C_BF16, 128, p.ncol, 0, 0);
   if (p.stg_blk) {
-    // output (N, 2D, 2H, 2W, Cout) as (2*Cout, W, 2, H, 2D*N), box (2*Cout, wt, 1, R, 1)
-    const cuuint64_t c2 = 2ull * cout, row = 2ull * w * cout * e;
-    cuuint64_t dd[5] = {c2, (cuuint64_t)w, 2, (cuuint64_t)h, 2ull * d * n};
-    cuuint64_t ss[4] = {c2 * e, row, 2 * row, 2 * row * h};
-    cuuint32_t bb[5] = {(cuuint32_t)c2, (cuuint32_t)p.wt, 1, (cuuint32_t)p.R, 1};
+    // output (N, 2D, 2H, 2W, ypitch) as (Cout, 2W, 2, H, 2D*N), box (Cout, 2*wt, 1, R, 1):
+    // the staged [positions][2*Cout] block is [2*wt][Cout] per row
+    const cuuint64_t yp = (cuuint64_t)ypitch, row = 2ull * w * yp * e;
+    cuuint64_t dd[5] = {(cuuint64_t)cout, 2ull * w, 2, (cuuint64_t)h, 2ull * d * n};
+    cuuint64_t ss[4] = {yp * e, row, 2 * row, 2 * row * h};
+    cuuint32_t bb[5] = {(cuuint32_t)cout, 2u * (cuuint32_t)p.wt, 1, (cuuint32_t)p.R, 1};
     if (enc(&a.ymap, dtype == R4C_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5, out,
             dd, ss, bb, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
             CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)

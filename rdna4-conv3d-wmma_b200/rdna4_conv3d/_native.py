@@ -79,6 +79,7 @@ def _bind(lib) -> None:
         "r4c_conv3d_dx": ([D, P, P, P, P, sz, P], i),
         "r4c_conv3d_dw": ([D, P, P, P, P, P, sz, P], i),
         "r4c_tconv_fwd": ([D, P, P, P, P, P, sz, P], i),
+        "r4c_tconv_fwd_pitched": ([D, P, P, P, P, i, P, sz, P], i),
         "r4c_tconv_dx": ([D, P, P, P, P, sz, P], i),
         "r4c_tconv_dw": ([D, P, P, P, P, P, sz, P], i),
         "r4c_bn_workspace_size": ([i64, i], sz),
@@ -283,6 +284,22 @@ def tconv_fwd(desc: ConvDesc, x_cl: torch.Tensor, w_packed: torch.Tensor,
                                  _ptr(ws), nb, _stream(dev))
     _check(st, "r4c_tconv_fwd")
     return y
+
+
+def tconv_fwd_into(desc: ConvDesc, x_cl: torch.Tensor, w_packed: torch.Tensor, bias: Optional[torch.Tensor],
+                   buf: torch.Tensor) -> None:
+    """The transpose conv's output written into channels [0, Cout) of ``buf``,
+    a dense NDHWC buffer with more channels (r4c_tconv_fwd_pitched)."""
+    dev = _require_cuda(x_cl, w_packed, bias, buf)
+    pitch = int(buf.shape[1])
+    if (tuple(buf.shape) != (desc.n, pitch, 2 * desc.d, 2 * desc.h, 2 * desc.w) or buf.dtype != x_cl.dtype
+            or not buf.is_contiguous(memory_format=torch.channels_last_3d) or buf.data_ptr() % 16 or pitch < desc.cout):
+        raise NativeError("buf must be a 16-byte aligned channels_last_3d tensor (N, >= Cout, 2D, 2H, 2W) of x's dtype")
+    ws, nb = _workspace(desc, LEG_TFWD, dev)
+    with torch.cuda.device(dev):
+        st = lib().r4c_tconv_fwd_pitched(ctypes.byref(desc), _ptr(x_cl), _ptr(w_packed), _ptr(bias), _ptr(buf),
+                                         pitch, _ptr(ws), nb, _stream(dev))
+    _check(st, "r4c_tconv_fwd_pitched")
 
 
 def tconv_dx(desc: ConvDesc, go_cl: torch.Tensor, w_packed: torch.Tensor) -> torch.Tensor:

@@ -667,34 +667,68 @@ class ConvTranspose3dWmmaFn(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, grad_out):
-        x, weight = ctx.saved_tensors
-        need_x, need_w, need_b = ctx.needs_input_grad[:3]
-        x_c = x if x.dtype in _HALF else x.to(torch.float16)
-        go = grad_out.to(x_c.dtype) if grad_out.dtype != x_c.dtype else grad_out
-        # one dense NDHWC copy shared by both legs when dY arrives as a view
-        # (e.g. the channel slice of a concatenation's gradient)
-        go = _as_ndhwc(go)
-        want_db = ctx.has_bias and need_b
-        dw = db = None
-        if need_w:
-            dw, db = transpose_k2s2_dw(x_c, weight.shape, go, want_db)
-        if want_db and db is None:
-            db = go.float().sum(dim=(0, 2, 3, 4))
-        handle = _reduce_async([dw, db])
-        gx = None
-        if need_x:
-            gx = transpose_k2s2_dx(x.shape, weight, go)
-            if gx.dtype != x.dtype:
-                gx = gx.to(x.dtype)
-            if ctx.x_layout == torch.contiguous_format:
-                gx = gx.contiguous()
-        if handle is not None:
-            handle.wait()
-        if dw is not None and dw.dtype != weight.dtype:
-            dw = dw.to(weight.dtype)
-        if db is not None and ctx.bias_dtype is not None and db.dtype != ctx.bias_dtype:
-            db = db.to(ctx.bias_dtype)
-        return gx, dw, db
+        return _tconv_backward(ctx, grad_out)
+
+
+def _tconv_backward(ctx, grad_out):
+    """(dX, dW, db) of the k2s2 transpose conv saved in ctx (x, weight)."""
+    x, weight = ctx.saved_tensors
+    need_x, need_w, need_b = ctx.needs_input_grad[:3]
+    x_c = x if x.dtype in _HALF else x.to(torch.float16)
+    go = grad_out.to(x_c.dtype) if grad_out.dtype != x_c.dtype else grad_out
+    # one dense NDHWC copy shared by both legs when dY arrives as a view
+    # (e.g. the channel slice of a concatenation's gradient)
+    go = _as_ndhwc(go)
+    want_db = ctx.has_bias and need_b
+    dw = db = None
+    if need_w:
+        dw, db = transpose_k2s2_dw(x_c, weight.shape, go, want_db)
+    if want_db and db is None:
+        db = go.float().sum(dim=(0, 2, 3, 4))
+    handle = _reduce_async([dw, db])
+    gx = None
+    if need_x:
+        gx = transpose_k2s2_dx(x.shape, weight, go)
+        if gx.dtype != x.dtype:
+            gx = gx.to(x.dtype)
+        if ctx.x_layout == torch.contiguous_format:
+            gx = gx.contiguous()
+    if handle is not None:
+        handle.wait()
+    if dw is not None and dw.dtype != weight.dtype:
+        dw = dw.to(weight.dtype)
+    if db is not None and ctx.bias_dtype is not None and db.dtype != ctx.bias_dtype:
+        db = db.to(ctx.bias_dtype)
+    return gx, dw, db
+
+
+class UpConcatFn(torch.autograd.Function):
+    """ConvTranspose3d k2s2 of x written straight into channels [0, lead) of
+    ``buf``, whose channels [lead, ...) already hold the skip connection:
+    torch.cat([up(x), skip], 1) of a UNet decoder (the reference's UNet,
+    benches/unet_e2e.py:38) without materialising up(x) and copying it. The
+    gradient of buf's first ``lead`` channels drives the transpose conv's
+    backward; buf's gradient passes on whole (its skip part)."""
+
+    @staticmethod
+    def forward(ctx, x, weight, bias, buf, lead):
+        desc = _tdesc(x.shape, int(weight.shape[1]), x.dtype)
+        wp = _packed_weight(desc, _native.LEG_TFWD, weight)
+        b = None if bias is None else bias.to(x.dtype).contiguous()
+        _native.tconv_fwd_into(desc, _as_ndhwc(x), wp, b, buf)
+        ctx.mark_dirty(buf)
+        ctx.save_for_backward(x, weight)
+        ctx.has_bias = bias is not None
+        ctx.bias_dtype = None if bias is None else bias.dtype
+        ctx.x_layout = (torch.channels_last_3d if x.is_contiguous(memory_format=torch.channels_last_3d)
+                        else torch.contiguous_format)
+        ctx.lead = int(lead)
+        return buf
+
+    @staticmethod
+    def backward(ctx, g):
+        gx, dw, db = _tconv_backward(ctx, g[:, :ctx.lead])
+        return gx, dw, db, g, None
 
 
 class ConvTranspose3dWmma(nn.ConvTranspose3d):
@@ -713,3 +747,25 @@ class ConvTranspose3dWmma(nn.ConvTranspose3d):
             return super().forward(x, output_size)
         x, weight, bias = _autocast_args(x, self.weight, self.bias)
         return ConvTranspose3dWmmaFn.apply(x, weight, bias)
+
+    def forward_into(self, x, buf, lead: int):
+        """``buf`` with self(x) written into its channels [0, lead): the
+        decoder concatenation torch.cat([self(x), buf[:, lead:]], 1) built in
+        place. On the native path the transpose conv stores into buf directly
+        (r4c_tconv_fwd_pitched); otherwise self(x) is copied there."""
+        direct = (
+            self.kernel_size == (2, 2, 2) and self.stride == (2, 2, 2) and self.padding == (0, 0, 0)
+            and self.output_padding == (0, 0, 0) and self.dilation == (1, 1, 1) and self.groups == 1
+            and self.padding_mode == "zeros" and x.is_cuda and x.dim() == 5 and _wmma_hw()
+            and int(lead) == self.out_channels and buf.dim() == 5 and buf.shape[1] % 8 == 0
+            and self.out_channels % 8 == 0 and self.in_channels % 8 == 0
+            and tuple(buf.shape[2:]) == tuple(2 * int(v) for v in x.shape[2:])
+            and buf.is_contiguous(memory_format=torch.channels_last_3d) and buf.data_ptr() % 16 == 0
+        )
+        if direct:
+            xa, weight, bias = _autocast_args(x, self.weight, self.bias)
+            direct = xa.dtype in _HALF and buf.dtype == xa.dtype
+        if not direct:
+            from .bn_relu import skip_cat
+            return skip_cat(self(x), buf, lead)
+        return UpConcatFn.apply(xa, weight, bias, buf, int(lead))

@@ -66,7 +66,7 @@ class UNet3D(nn.Module):
         """Same network, with each encoder level's last BatchNorm+ReLU also
         doing the MaxPool3d(2) and writing its output (the skip connection)
         straight into the channels of the decoder's concatenation buffer; the
-        decoder then only writes the up-conv's output in front of it."""
+        up-conv then writes its output into the buffer's first channels."""
         from .bn_relu import skip_cat
         bufs = []
         last = len(self.enc) - 1
@@ -81,7 +81,8 @@ class UNet3D(nn.Module):
                 bufs.append((buf, lead))
         for up, dec in zip(self.up, self.dec):
             buf, lead = bufs.pop()
-            x = dec(skip_cat(up(x), buf, lead))
+            # the up-conv writes into the buffer's first channels when it can
+            x = dec(up.forward_into(x, buf, lead) if hasattr(up, "forward_into") else skip_cat(up(x), buf, lead))
         return self.head(x)
 
 

@@ -140,3 +140,39 @@ def test_bn_relu_pool_and_skip_buffer(cuda_ready, shape, lead, quantised):
     assert O.norm_rel(mod.weight.grad.cpu(), refg.weight.grad.cpu()) <= 3e-2
     assert O.norm_rel(mod.bias.grad.cpu(), refg.bias.grad.cpu()) <= 3e-2
     torch.testing.assert_close(mod.running_mean, refg.running_mean, rtol=1e-4, atol=1e-5)
+
+
+@pytest.mark.parametrize("amp", [False, True], ids=["bf16", "autocast-fp32-in"])
+@pytest.mark.parametrize("cin,cout,pitch", [(48, 24, 48), (96, 48, 96), (64, 32, 96)])
+def test_up_conv_writes_into_concat_buffer(cuda_ready, cin, cout, pitch, amp, monkeypatch):
+    """ConvTranspose3dWmma.forward_into: the up-conv stores straight into the
+    first channels of the decoder's concatenation buffer (pitched output);
+    forward and every gradient equal the up-conv-then-copy path bit for bit."""
+    import sys
+    from rdna4_conv3d import ConvTranspose3dWmma
+    from rdna4_conv3d.bn_relu import skip_cat
+    cw = sys.modules["rdna4_conv3d.conv3d_wmma"]
+    calls = []
+    orig = cw.UpConcatFn.apply
+    monkeypatch.setattr(cw.UpConcatFn, "apply", lambda *a: calls.append(1) or orig(*a))
+    torch.manual_seed(0)
+    up = ConvTranspose3dWmma(cin, cout, 2, stride=2).cuda()
+    cl = torch.channels_last_3d
+    x0 = torch.randn(2, cin, 4, 6, 8, device="cuda")
+    skip = torch.randn(2, pitch - cout, 8, 12, 16, device="cuda").to(torch.bfloat16)
+    g = torch.randn(2, pitch, 8, 12, 16, device="cuda").to(torch.bfloat16).contiguous(memory_format=cl)
+    outs = []
+    for direct in (True, False):
+        up.zero_grad(set_to_none=True)
+        x = (x0 if amp else x0.to(torch.bfloat16)).contiguous(memory_format=cl).requires_grad_(True)
+        s = skip.clone().requires_grad_(True)
+        head = torch.zeros(2, cout, 8, 12, 16, device="cuda", dtype=torch.bfloat16)
+        buf = torch.cat([head, s], 1).contiguous(memory_format=cl)  # skip channels from a graph input
+        with torch.autocast("cuda", dtype=torch.bfloat16, enabled=amp):
+            y = up.forward_into(x, buf, cout) if direct else skip_cat(up(x), buf, cout)
+        y.backward(g)
+        outs.append((y.detach().clone(), x.grad.clone(), up.weight.grad.clone(), up.bias.grad.clone(), s.grad.clone()))
+    assert len(calls) == 1                                  # the direct path ran once (first pass)
+    for a, b in zip(*outs):
+        assert torch.equal(a, b)
+    assert torch.equal(outs[0][0][:, cout:], skip)          # the skip channels are untouched

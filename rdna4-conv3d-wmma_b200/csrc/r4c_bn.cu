@@ -218,7 +218,18 @@ template <typename T>
 __global__ void __launch_bounds__(256) apply_kernel(const T* __restrict__ x, T* __restrict__ y,
                                                     const float* __restrict__ mi, const float* __restrict__ af,
                                                     int64_t nvec, int C, int relu) {
+  // blockDim is a multiple of C/8 (vec_threads), so every vector a thread
+  // touches holds the same 8 channels: their parameters stay in registers
   const int nv = C / 8;
+  const int c0 = (int)(threadIdx.x % nv) * 8;
+  float pm[8], pi[8], pw[8], pb[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    pm[k] = __ldg(mi + c0 + k);
+    pi[k] = __ldg(mi + C + c0 + k);
+    pw[k] = __ldg(af + c0 + k);
+    pb[k] = __ldg(af + C + c0 + k);
+  }
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t base = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; base < nvec; base += stride * kU) {
     Vec8<T> a[kU];
@@ -231,13 +242,11 @@ __global__ void __launch_bounds__(256) apply_kernel(const T* __restrict__ x, T* 
     for (int u = 0; u < kU; ++u) {
       const int64_t i = base + u * stride;
       if (i >= nvec) break;
-      const int c0 = (int)(i % nv) * 8;
       float f[8];
       a[u].to_f(f);
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
-        const int c = c0 + k;
-        const float v = bn_pre(f[k], __ldg(mi + c), __ldg(mi + C + c), __ldg(af + c), __ldg(af + C + c));
+        const float v = bn_pre(f[k], pm[k], pi[k], pw[k], pb[k]);
         f[k] = relu ? (v > 0.f ? v : 0.f) : v;
       }
       a[u].from_f(f);
@@ -251,7 +260,20 @@ template <typename T>
 __global__ void __launch_bounds__(256) dx_kernel(const T* __restrict__ dy, const T* __restrict__ x, T* __restrict__ dx,
                                                  const float* __restrict__ mi, const float* __restrict__ af,
                                                  const float* __restrict__ coef, int64_t nvec, int C, int relu) {
+  // blockDim is a multiple of C/8: fixed channels per thread, parameters in registers
   const int nv = C / 8;
+  const int c0 = (int)(threadIdx.x % nv) * 8;
+  float pm[8], pi[8], pw[8], pb[8], q0[8], q1[8], q2[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    pm[k] = __ldg(mi + c0 + k);
+    pi[k] = __ldg(mi + C + c0 + k);
+    pw[k] = __ldg(af + c0 + k);
+    pb[k] = __ldg(af + C + c0 + k);
+    q0[k] = __ldg(coef + c0 + k);
+    q1[k] = __ldg(coef + C + c0 + k);
+    q2[k] = __ldg(coef + 2 * C + c0 + k);
+  }
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t base = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; base < nvec; base += stride * kU) {
     Vec8<T> a[kU], b[kU];
@@ -267,17 +289,14 @@ __global__ void __launch_bounds__(256) dx_kernel(const T* __restrict__ dy, const
     for (int u = 0; u < kU; ++u) {
       const int64_t i = base + u * stride;
       if (i >= nvec) break;
-      const int c0 = (int)(i % nv) * 8;
       float xf[8], gf[8];
       a[u].to_f(xf);
       b[u].to_f(gf);
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
-        const int c = c0 + k;
         float g = gf[k];
-        const float m = __ldg(mi + c);
-        if (relu && !(bn_pre(xf[k], m, __ldg(mi + C + c), __ldg(af + c), __ldg(af + C + c)) > 0.f)) g = 0.f;
-        xf[k] = (g - __ldg(coef + c) - (xf[k] - m) * __ldg(coef + C + c)) * __ldg(coef + 2 * C + c);
+        if (relu && !(bn_pre(xf[k], pm[k], pi[k], pw[k], pb[k]) > 0.f)) g = 0.f;
+        xf[k] = (g - q0[k] - (xf[k] - pm[k]) * q1[k]) * q2[k];
       }
       a[u].from_f(xf);
       reinterpret_cast<uint4*>(dx)[i] = a[u].raw;
@@ -493,6 +512,9 @@ static Split split_for(int64_t vox, int64_t min_chunk = 64) {
 static int grid_for(int64_t nvec) {
   return (int)std::max<int64_t>(1, std::min<int64_t>((nvec + 255) / 256, 148 * 4));
 }
+// Threads per block of the element-wise kernels: a multiple of C/8 (the 16-byte
+// vectors of one voxel), so each thread keeps the same 8 channels.
+static int vec_threads(int C) { return (256 / (C / 8)) * (C / 8); }
 
 static bool ok_args(const void* p, int64_t vox, int C, int dtype) {
   return p && vox >= 0 && C > 0 && C % 8 == 0 && C <= 2048 && (dtype == R4C_BF16 || dtype == R4C_F16) &&
@@ -574,11 +596,11 @@ int r4c_bn_relu_fwd(const void* x, void* y, const float* mean_invstd, const floa
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const int64_t nvec = vox * (C / 8);
   if (dtype == R4C_BF16)
-    apply_kernel<__nv_bfloat16><<<grid_for(nvec), 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x),
+    apply_kernel<__nv_bfloat16><<<grid_for(nvec), vec_threads(C), 0, s>>>(static_cast<const __nv_bfloat16*>(x),
                                                                static_cast<__nv_bfloat16*>(y), mean_invstd, affine, nvec,
                                                                C, relu);
   else
-    apply_kernel<__half><<<grid_for(nvec), 256, 0, s>>>(static_cast<const __half*>(x), static_cast<__half*>(y),
+    apply_kernel<__half><<<grid_for(nvec), vec_threads(C), 0, s>>>(static_cast<const __half*>(x), static_cast<__half*>(y),
                                                         mean_invstd, affine, nvec, C, relu);
   r4c::note_launches(1);
   return cudaGetLastError() == cudaSuccess ? R4C_OK : R4C_ERR_CUDA;
@@ -607,11 +629,11 @@ int r4c_bn_relu_bwd_dx(const void* dy, const void* x, void* dx, const float* mea
   if (dx && vox > 0) {
     const int64_t nvec = vox * (C / 8);
     if (dtype == R4C_BF16)
-      dx_kernel<__nv_bfloat16><<<grid_for(nvec), 256, 0, s>>>(
+      dx_kernel<__nv_bfloat16><<<grid_for(nvec), vec_threads(C), 0, s>>>(
           static_cast<const __nv_bfloat16*>(dy), static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(dx),
           mean_invstd, affine, coef, nvec, C, relu);
     else
-      dx_kernel<__half><<<grid_for(nvec), 256, 0, s>>>(static_cast<const __half*>(dy), static_cast<const __half*>(x),
+      dx_kernel<__half><<<grid_for(nvec), vec_threads(C), 0, s>>>(static_cast<const __half*>(dy), static_cast<const __half*>(x),
                                                        static_cast<__half*>(dx), mean_invstd, affine, coef, nvec, C,
                                                        relu);
     r4c::note_launches(1);

@@ -335,9 +335,24 @@ __device__ __forceinline__ float round_to(float v) { return Elem<T>::to_f(Elem<T
 
 // Window pass shared by the three kernels: loads x for the 8 voxels and
 // returns, per channel, the argmax voxel of the rounded outputs.
+// The normalisation parameters of the 8 channels c0..c0+7, loaded once per
+// thread instead of per element.
+struct BnPar8 {
+  float m[8], is[8], w[8], b[8];
+};
+__device__ __forceinline__ void load_par8(BnPar8& P, const float* mi, const float* af, int C, int c0) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    P.m[j] = __ldg(mi + c0 + j);
+    P.is[j] = __ldg(mi + C + c0 + j);
+    P.w[j] = __ldg(af + c0 + j);
+    P.b[j] = __ldg(af + C + c0 + j);
+  }
+}
+
 template <typename T>
 __device__ __forceinline__ void window_argmax(const T* __restrict__ x, const PoolGeo& g, int64_t pv, int c0,
-                                              const float* mi, const float* af, float (&xf)[8][8], int (&am)[8],
+                                              const BnPar8& P, float (&xf)[8][8], int (&am)[8],
                                               float (&mx)[8], int64_t (&vox)[8]) {
 #pragma unroll
   for (int i = 0; i < 8; ++i) { am[i] = 0; mx[i] = 0.f; }
@@ -352,8 +367,7 @@ __device__ __forceinline__ void window_argmax(const T* __restrict__ x, const Poo
   for (int k = 0; k < 8; ++k)
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const int c = c0 + i;
-      const float pre = bn_pre(xf[k][i], __ldg(mi + c), __ldg(mi + g.C + c), __ldg(af + c), __ldg(af + g.C + c));
+      const float pre = bn_pre(xf[k][i], P.m[i], P.is[i], P.w[i], P.b[i]);
       const float y = round_to<T>(pre > 0.f ? pre : 0.f);
       if (k == 0 || y > mx[i] || isnan(y)) {   // PyTorch's max_pool3d rule
         mx[i] = y;
@@ -368,20 +382,25 @@ __global__ void __launch_bounds__(128) pool_fwd_kernel(const T* __restrict__ x, 
                                                        PoolGeo g) {
   const int nv = g.C / 8;
   const int64_t total = g.pvox * nv;
+  BnPar8 P;
+  int pc0 = -1;  // channel group whose parameters P holds (fixed when blockDim % nv == 0)
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t pv = i / nv;
     const int c0 = (int)(i - pv * nv) * 8;
+    if (c0 != pc0) {
+      load_par8(P, mi, af, g.C, c0);
+      pc0 = c0;
+    }
     float xf[8][8], mx[8];
     int am[8];
     int64_t vox[8];
-    window_argmax<T>(x, g, pv, c0, mi, af, xf, am, mx, vox);
+    window_argmax<T>(x, g, pv, c0, P, xf, am, mx, vox);
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
       float f[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const int c = c0 + j;
-        const float pre = bn_pre(xf[k][j], __ldg(mi + c), __ldg(mi + g.C + c), __ldg(af + c), __ldg(af + g.C + c));
+        const float pre = bn_pre(xf[k][j], P.m[j], P.is[j], P.w[j], P.b[j]);
         f[j] = pre > 0.f ? pre : 0.f;
       }
       Vec8<T> o;
@@ -397,7 +416,7 @@ __global__ void __launch_bounds__(128) pool_fwd_kernel(const T* __restrict__ x, 
 // g per voxel k and channel j of the window.
 template <typename T>
 __device__ __forceinline__ void window_grad(const T* __restrict__ gy, const T* __restrict__ gp, const PoolGeo& g,
-                                            int64_t i, int c0, const float* mi, const float* af,
+                                            int64_t i, int c0, const BnPar8& P,
                                             const float (&xf)[8][8], const int (&am)[8], const int64_t (&vox)[8],
                                             float (&gf)[8][8]) {
   Vec8<T> pb;
@@ -411,8 +430,7 @@ __device__ __forceinline__ void window_grad(const T* __restrict__ gy, const T* _
     b.to_f(gf[k]);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      const int c = c0 + j;
-      const float pre = bn_pre(xf[k][j], __ldg(mi + c), __ldg(mi + g.C + c), __ldg(af + c), __ldg(af + g.C + c));
+      const float pre = bn_pre(xf[k][j], P.m[j], P.is[j], P.w[j], P.b[j]);
       float v = gf[k][j] + (am[j] == k ? gpf[j] : 0.f);
       gf[k][j] = pre > 0.f ? v : 0.f;
     }
@@ -430,6 +448,8 @@ __global__ void __launch_bounds__(128) pool_sums_kernel(const T* __restrict__ x,
   const int lane = threadIdx.x % nv, row = threadIdx.x / nv;
   const int R = blockDim.x / nv;
   const int c0 = lane * 8;
+  BnPar8 P;
+  load_par8(P, mi, af, g.C, c0);
   float s1[8], s2[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) { s1[j] = 0.f; s2[j] = 0.f; }
@@ -439,14 +459,14 @@ __global__ void __launch_bounds__(128) pool_sums_kernel(const T* __restrict__ x,
       float xf[8][8], mx[8], gf[8][8];
       int am[8];
       int64_t vox[8];
-      window_argmax<T>(x, g, pv, c0, mi, af, xf, am, mx, vox);
-      window_grad<T>(gy, gp, g, pv * nv + lane, c0, mi, af, xf, am, vox, gf);
+      window_argmax<T>(x, g, pv, c0, P, xf, am, mx, vox);
+      window_grad<T>(gy, gp, g, pv * nv + lane, c0, P, xf, am, vox, gf);
 #pragma unroll
       for (int k = 0; k < 8; ++k)
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           s1[j] += gf[k][j];
-          s2[j] = fmaf(gf[k][j], xf[k][j] - __ldg(mi + c0 + j), s2[j]);
+          s2[j] = fmaf(gf[k][j], xf[k][j] - P.m[j], s2[j]);
         }
     }
 #pragma unroll
@@ -470,23 +490,32 @@ __global__ void __launch_bounds__(128) pool_dx_kernel(const T* __restrict__ x, c
                                                       const float* __restrict__ coef, PoolGeo g) {
   const int nv = g.C / 8;
   const int64_t total = g.pvox * nv;
+  BnPar8 P;
+  float q0[8], q1[8], q2[8];
+  int pc0 = -1;  // channel group whose parameters are held (fixed when blockDim % nv == 0)
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t pv = i / nv;
     const int c0 = (int)(i - pv * nv) * 8;
+    if (c0 != pc0) {
+      load_par8(P, mi, af, g.C, c0);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        q0[j] = __ldg(coef + c0 + j);
+        q1[j] = __ldg(coef + g.C + c0 + j);
+        q2[j] = __ldg(coef + 2 * g.C + c0 + j);
+      }
+      pc0 = c0;
+    }
     float xf[8][8], mx[8], gf[8][8];
     int am[8];
     int64_t vox[8];
-    window_argmax<T>(x, g, pv, c0, mi, af, xf, am, mx, vox);
-    window_grad<T>(gy, gp, g, i, c0, mi, af, xf, am, vox, gf);
+    window_argmax<T>(x, g, pv, c0, P, xf, am, mx, vox);
+    window_grad<T>(gy, gp, g, i, c0, P, xf, am, vox, gf);
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
       float f[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int c = c0 + j;
-        f[j] = (gf[k][j] - __ldg(coef + c) - (xf[k][j] - __ldg(mi + c)) * __ldg(coef + g.C + c)) *
-               __ldg(coef + 2 * g.C + c);
-      }
+      for (int j = 0; j < 8; ++j) f[j] = (gf[k][j] - q0[j] - (xf[k][j] - P.m[j]) * q1[j]) * q2[j];
       Vec8<T> o;
       o.from_f(f);
       *reinterpret_cast<uint4*>(dx + vox[k] * g.C + c0) = o.raw;
@@ -515,6 +544,8 @@ static int grid_for(int64_t nvec) {
 // Threads per block of the element-wise kernels: a multiple of C/8 (the 16-byte
 // vectors of one voxel), so each thread keeps the same 8 channels.
 static int vec_threads(int C) { return (256 / (C / 8)) * (C / 8); }
+// Pool kernels (128 threads): likewise a multiple of C/8 when C/8 <= 128.
+static int pool_threads(int C) { return C / 8 <= 128 ? (128 / (C / 8)) * (C / 8) : 128; }
 
 static bool ok_args(const void* p, int64_t vox, int C, int dtype) {
   return p && vox >= 0 && C > 0 && C % 8 == 0 && C <= 2048 && (dtype == R4C_BF16 || dtype == R4C_F16) &&
@@ -665,11 +696,11 @@ int r4c_bn_relu_pool_fwd(const void* x, void* y, int y_pitch, void* p, const flo
   const int64_t total = g.pvox * (C / 8);
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((total + 127) / 128, 148 * 8));
   if (dtype == R4C_BF16)
-    pool_fwd_kernel<__nv_bfloat16><<<grid, 128, 0, s>>>(static_cast<const __nv_bfloat16*>(x),
+    pool_fwd_kernel<__nv_bfloat16><<<grid, pool_threads(g.C), 0, s>>>(static_cast<const __nv_bfloat16*>(x),
                                                         static_cast<__nv_bfloat16*>(y), static_cast<__nv_bfloat16*>(p),
                                                         mean_invstd, affine, g);
   else
-    pool_fwd_kernel<__half><<<grid, 128, 0, s>>>(static_cast<const __half*>(x), static_cast<__half*>(y),
+    pool_fwd_kernel<__half><<<grid, pool_threads(g.C), 0, s>>>(static_cast<const __half*>(x), static_cast<__half*>(y),
                                                  static_cast<__half*>(p), mean_invstd, affine, g);
   r4c::note_launches(1);
   return cudaGetLastError() == cudaSuccess ? R4C_OK : R4C_ERR_CUDA;
@@ -729,11 +760,11 @@ int r4c_bn_relu_pool_bwd_dx(const void* gy, int gy_pitch, const void* gp, const 
     const int64_t total = g.pvox * (C / 8);
     const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((total + 127) / 128, 148 * 8));
     if (dtype == R4C_BF16)
-      pool_dx_kernel<__nv_bfloat16><<<grid, 128, 0, s>>>(
+      pool_dx_kernel<__nv_bfloat16><<<grid, pool_threads(g.C), 0, s>>>(
           static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(gy),
           static_cast<const __nv_bfloat16*>(gp), static_cast<__nv_bfloat16*>(dx), mean_invstd, affine, coef, g);
     else
-      pool_dx_kernel<__half><<<grid, 128, 0, s>>>(static_cast<const __half*>(x), static_cast<const __half*>(gy),
+      pool_dx_kernel<__half><<<grid, pool_threads(g.C), 0, s>>>(static_cast<const __half*>(x), static_cast<const __half*>(gy),
                                                   static_cast<const __half*>(gp), static_cast<__half*>(dx), mean_invstd,
                                                   affine, coef, g);
     r4c::note_launches(1);

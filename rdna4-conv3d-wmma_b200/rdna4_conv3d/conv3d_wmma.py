@@ -764,7 +764,8 @@ class ConvTranspose3dWmma(nn.ConvTranspose3d):
         )
         if direct:
             xa, weight, bias = _autocast_args(x, self.weight, self.bias)
-            direct = xa.dtype in _HALF and buf.dtype == xa.dtype
+            direct = (xa.dtype in _HALF and buf.dtype == xa.dtype and _native.plan_kernel(
+                _tdesc(xa.shape, self.out_channels, xa.dtype), _native.LEG_TFWD) == _native.KERNEL_TC)
         if not direct:
             from .bn_relu import skip_cat
             return skip_cat(self(x), buf, lead)

@@ -176,3 +176,25 @@ def test_up_conv_writes_into_concat_buffer(cuda_ready, cin, cout, pitch, amp, mo
     for a, b in zip(*outs):
         assert torch.equal(a, b)
     assert torch.equal(outs[0][0][:, cout:], skip)          # the skip channels are untouched
+
+
+def test_up_conv_into_buffer_without_native_plan(cuda_ready, monkeypatch):
+    """A transpose conv the tcgen05 planner does not take (here 128 -> 64 at
+    4 x 16 x 32 x 32) falls back to the up-conv-then-copy path, same result."""
+    import sys
+    from rdna4_conv3d import ConvTranspose3dWmma
+    from rdna4_conv3d.bn_relu import skip_cat
+    cw = sys.modules["rdna4_conv3d.conv3d_wmma"]
+    calls = []
+    orig = cw.UpConcatFn.apply
+    monkeypatch.setattr(cw.UpConcatFn, "apply", lambda *a: calls.append(1) or orig(*a))
+    torch.manual_seed(0)
+    up = ConvTranspose3dWmma(128, 64, 2, stride=2).cuda()
+    cl = torch.channels_last_3d
+    x = torch.randn(4, 128, 16, 32, 32, device="cuda").to(torch.bfloat16).contiguous(memory_format=cl)
+    buf = torch.randn(4, 128, 32, 64, 64, device="cuda").to(torch.bfloat16).contiguous(memory_format=cl)
+    with torch.no_grad():
+        a = up.forward_into(x, buf.clone(), 64)
+        b = skip_cat(up(x), buf.clone(), 64)
+    assert calls == []
+    assert torch.equal(a, b)

@@ -795,30 +795,31 @@ bool make_plan(int mode, int n, int d, int h, int w, int cin, int cout, TPlan* o
   p.nyb = (h + p.R - 1) / p.R;
   p.tiles = (long long)n * d * p.nyb * p.nwt;
   // forward: stage the output through two [blocks][positions][2*Cout] tiles
-  // stored by TMA when the task's columns are whole (a, b) blocks
-  // (R4C_TCONV_STG=0 keeps per-thread stores)
-  p.stg_blk = 0;
-  {
-    const char* ev = getenv("R4C_TCONV_STG");
-    if (mode == 0 && p.ncol % (2 * cout) == 0 && (8 * cout) % p.ncol == 0 && 2 * cout <= 256 &&
-        !(ev && ev[0] == '0'))
-      p.stg_blk = (p.R * p.wt * 2 * cout * 2 + 127) / 128 * 128;
-  }
-  const int stg_total = p.stg_blk ? 2 * (p.ncol / (2 * cout)) * p.stg_blk : 0;
-  // stages of up to 4 boxes (64 KB) balanced over the tile: the largest
-  // that leaves three stages (else two) beside the resident weights
-  const int avail = kSmemMax - kHeader - (p.b_bytes + 1023) / 1024 * 1024 - stg_total;
+  // stored by TMA when the task's columns are whole (a, b) blocks and the
+  // staging leaves room for two load stages (R4C_TCONV_STG=0 keeps
+  // per-thread stores)
+  const char* ev = getenv("R4C_TCONV_STG");
+  const bool stg_ok = mode == 0 && p.ncol % (2 * cout) == 0 && (8 * cout) % p.ncol == 0 &&
+                      2 * cout <= 256 && !(ev && ev[0] == '0');
+  int stg_total = 0;
   p.nstages = 0;
-  for (int need = 3; need >= 2 && p.nstages == 0; --need) {
-    for (int bp = std::min(4, p.nbox); bp >= 1; --bp) {
-      const int spt = (p.nbox + bp - 1) / bp;
-      const int bpst = (p.nbox + spt - 1) / spt;
-      const int ns = std::min(kMaxStages, avail / (bpst * kBoxBytes));
-      if (ns >= need) {
-        p.spt = spt;
-        p.bpst = bpst;
-        p.nstages = ns;
-        break;
+  for (int stg = stg_ok ? 1 : 0; stg >= 0 && p.nstages == 0; --stg) {
+    p.stg_blk = stg ? (p.R * p.wt * 2 * cout * 2 + 127) / 128 * 128 : 0;
+    stg_total = p.stg_blk ? 2 * (p.ncol / (2 * cout)) * p.stg_blk : 0;
+    // stages of up to 4 boxes (64 KB) balanced over the tile: the largest
+    // that leaves three stages (else two) beside the resident weights
+    const int avail = kSmemMax - kHeader - (p.b_bytes + 1023) / 1024 * 1024 - stg_total;
+    for (int need = 3; need >= 2 && p.nstages == 0; --need) {
+      for (int bp = std::min(4, p.nbox); bp >= 1; --bp) {
+        const int spt = (p.nbox + bp - 1) / bp;
+        const int bpst = (p.nbox + spt - 1) / spt;
+        const int ns = std::min(kMaxStages, avail / (bpst * kBoxBytes));
+        if (ns >= need) {
+          p.spt = spt;
+          p.bpst = bpst;
+          p.nstages = ns;
+          break;
+        }
       }
     }
   }

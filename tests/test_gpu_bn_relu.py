@@ -178,9 +178,15 @@ def test_up_conv_writes_into_concat_buffer(cuda_ready, cin, cout, pitch, amp, mo
     assert torch.equal(outs[0][0][:, cout:], skip)          # the skip channels are untouched
 
 
-def test_up_conv_into_buffer_without_native_plan(cuda_ready, monkeypatch):
-    """A transpose conv the tcgen05 planner does not take (here 128 -> 64 at
-    4 x 16 x 32 x 32) falls back to the up-conv-then-copy path, same result."""
+
+@pytest.mark.parametrize("cin,cout,shape,direct", [
+    (128, 64, (4, 16, 32, 32), True),    # tcgen05 plan with per-thread stores
+    (832, 16, (1, 2, 4, 4), False),      # 13 K boxes: no tcgen05 plan
+], ids=["128x64", "832x16"])
+def test_up_conv_into_buffer_plans(cuda_ready, monkeypatch, cin, cout, shape, direct):
+    """The up-conv writes into the buffer when the transpose conv has a
+    tcgen05 plan and falls back to up-conv-then-copy otherwise; either way
+    the result equals the copy path."""
     import sys
     from rdna4_conv3d import ConvTranspose3dWmma
     from rdna4_conv3d.bn_relu import skip_cat
@@ -189,12 +195,13 @@ def test_up_conv_into_buffer_without_native_plan(cuda_ready, monkeypatch):
     orig = cw.UpConcatFn.apply
     monkeypatch.setattr(cw.UpConcatFn, "apply", lambda *a: calls.append(1) or orig(*a))
     torch.manual_seed(0)
-    up = ConvTranspose3dWmma(128, 64, 2, stride=2).cuda()
+    up = ConvTranspose3dWmma(cin, cout, 2, stride=2).cuda()
     cl = torch.channels_last_3d
-    x = torch.randn(4, 128, 16, 32, 32, device="cuda").to(torch.bfloat16).contiguous(memory_format=cl)
-    buf = torch.randn(4, 128, 32, 64, 64, device="cuda").to(torch.bfloat16).contiguous(memory_format=cl)
+    n, d, h, w = shape
+    x = torch.randn(n, cin, d, h, w, device="cuda").to(torch.bfloat16).contiguous(memory_format=cl)
+    buf = torch.randn(n, 2 * cout, 2 * d, 2 * h, 2 * w, device="cuda").to(torch.bfloat16).contiguous(memory_format=cl)
     with torch.no_grad():
-        a = up.forward_into(x, buf.clone(), 64)
-        b = skip_cat(up(x), buf.clone(), 64)
-    assert calls == []
+        a = up.forward_into(x, buf.clone(), cout)
+        b = skip_cat(up(x), buf.clone(), cout)
+    assert calls == ([1] if direct else [])
     assert torch.equal(a, b)

@@ -78,6 +78,9 @@ TCONV_CASES = [
     (2, 48, 24, 2, 5, 64),
     (1, 192, 96, 3, 8, 16),
     (1, 96, 48, 2, 4, 32),
+    # 2 tasks of N = 256: the output staging would leave one load stage, so
+    # per-thread stores
+    (1, 128, 64, 2, 4, 32),
     (1, 24, 40, 2, 3, 7),
     # last M tile of 8 channels: db from the dW kernel's ones row there
     (1, 136, 16, 2, 3, 8),

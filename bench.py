@@ -768,6 +768,11 @@ def main():
         reducer = GradAllReducer()
 
     step_flops = sum(len(legs) * L.flops for L in layers)
+    # the clocks sampler starts before the warm-up, so the GPU does not sit
+    # idle (and drop its clocks) between the warm-up and the timed steps
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
     for _ in range(args.warmup):
         run_step(layers, reducer, legs=legs)
     torch.cuda.synchronize()
@@ -778,11 +783,8 @@ def main():
     evs = [[[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in layers]
            for _ in range(args.steps)]
     leg_ms = [[0.0, 0.0, 0.0] for _ in layers]
-    sampler = ClockSampler(local)
     barrier(world)
     torch.cuda.synchronize()
-    sampler.start()
-    time.sleep(0.3)
     n_launch0 = _native.launch_count()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record()

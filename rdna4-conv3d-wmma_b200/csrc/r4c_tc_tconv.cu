@@ -1140,11 +1140,14 @@ int launch_dw(int n, int d, int h, int w, int cin, int cout, const void* x, cons
   a.ones_mt = (cin - 1) / 128;
   const int cin_last = cin - 128 * a.ones_mt;
   a.ones = (db != nullptr && cin_last <= 64) ? 1 : 0;
-  const char* fe = getenv("R4C_TCONV_DBFILL");
-  // Opt-in: at 96->48 the db kernel path measured 82 us for the dW leg, this
-  // fill path 91 us (the MMA warp's stores + proxy fence stall each stage).
-  a.ones_fill = (db != nullptr && cin_last > 64 && cin_last <= 120 && cin_last % 8 == 0 && fe && fe[0] == '1')
-                    ? 1 : 0;
+  // Opt-in (R4C_TCONV_DBFILL=1, read once): at 96->48 the db kernel path
+  // measured 82 us for the dW leg, this fill path 91 us (the MMA warp's
+  // stores + proxy fence stall each stage).
+  static const bool fill_on = [] {
+    const char* fe = getenv("R4C_TCONV_DBFILL");
+    return fe && fe[0] == '1';
+  }();
+  a.ones_fill = (db != nullptr && cin_last > 64 && cin_last <= 120 && cin_last % 8 == 0 && fill_on) ? 1 : 0;
   a.ones_row = a.ones_fill ? cin_last : 64;
   a.one_bits = dtype == R4C_BF16 ? 0x3F80u : 0x3C00u;
   static bool done[64] = {false};

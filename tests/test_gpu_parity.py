@@ -220,20 +220,34 @@ def test_tconv_legs_match_oracle(cuda_ready, case, dtype, force, monkeypatch):
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16], ids=["bf16", "fp16"])
 @pytest.mark.parametrize("case", [(1, 104, 16, 2, 2, 8), (1, 96, 48, 2, 4, 32)], ids=["104x16", "96x48"])
-def test_tconv_dw_db_fill_opt_in(cuda_ready, case, dtype, monkeypatch):
+def test_tconv_dw_db_fill_opt_in(cuda_ready, case, dtype, tmp_path):
     """R4C_TCONV_DBFILL=1: db from a 1 written into the zero fill of a last
-    M tile of 72-120 channels, checked against the same oracle as the default."""
+    M tile of 72-120 channels, checked against the same oracle as the default.
+    The library reads the switch once per process, so the GPU leg runs in a
+    child process started with it set."""
+    import subprocess
+    import sys
     n, cin, cout, d, h, w = case
-    cw = _cw()
-    monkeypatch.setenv("R4C_TCONV_DBFILL", "1")
     g = torch.Generator().manual_seed(1)
     x = torch.randn(n, cin, d, h, w, generator=g).to(dtype)
     wt = (torch.randn(cin, cout, 2, 2, 2, generator=g) / cin ** 0.5).to(dtype)
     go = torch.randn(n, cout, 2 * d, 2 * h, 2 * w, generator=g).to(dtype)
-    dw, db = cw.transpose_k2s2_dw(x.cuda(), wt.shape, go.cuda(), True)
+    torch.save({"x": x, "wshape": tuple(wt.shape), "go": go}, tmp_path / "in.pt")
+    pkg = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "rdna4-conv3d-wmma_b200")
+    code = (
+        "import sys, torch; sys.path.insert(0, %r)\n"
+        "import rdna4_conv3d\n"
+        "cw = sys.modules['rdna4_conv3d.conv3d_wmma']\n"
+        "t = torch.load(%r)\n"
+        "dw, db = cw.transpose_k2s2_dw(t['x'].cuda(), t['wshape'], t['go'].cuda(), True)\n"
+        "torch.save({'dw': dw.cpu(), 'db': db.cpu()}, %r)\n"
+    ) % (pkg, str(tmp_path / "in.pt"), str(tmp_path / "out.pt"))
+    env = dict(os.environ, R4C_TCONV_DBFILL="1")
+    subprocess.run([sys.executable, "-c", code], env=env, check=True, timeout=600)
+    out = torch.load(tmp_path / "out.pt")
     _, dwr = O.torch_tconv_grads(x, wt, go)
-    assert O.norm_rel(dw.cpu(), dwr) <= 1e-4
-    assert O.norm_rel(db.cpu(), go.float().sum(dim=(0, 2, 3, 4))) <= 1e-4
+    assert O.norm_rel(out["dw"], dwr) <= 1e-4
+    assert O.norm_rel(out["db"], go.float().sum(dim=(0, 2, 3, 4))) <= 1e-4
 
 
 GOLDEN =sorted(glob.glob(os.path.join(GOLDEN_DIR, "*.npz")))

@@ -297,6 +297,15 @@ int r4c_bn_relu_bwd_dx(const void* dy, const void* x, void* dx, const float* mea
  * then r4c_bn_relu_pool_bwd_dx, workspace r4c_bn_pool_workspace_size().
  * Statistics come from r4c_bn_stats / r4c_bn_finalize over x as above.
  */
+/*
+ * Dense NDHWC copy of a channel slice: dst[v][0..C) = src[v * src_pitch +
+ * 0..C) for vox voxels (src points at the slice's first channel). The
+ * up-conv backward's dY is such a slice of the decoder concatenation's
+ * gradient (torch.cat in the reference's UNet, benches/unet_e2e.py:38).
+ * C and src_pitch multiples of 8, 16-bit dtypes, 16-byte aligned pointers.
+ */
+int r4c_channel_slice_copy(const void* src, int src_pitch, void* dst, int64_t vox, int C, int dtype,
+                           r4c_stream_t stream);
 int r4c_bn_relu_pool_fwd(const void* x, void* y, int y_pitch, void* p, const float* mean_invstd, const float* affine,
                          int n, int d, int h, int w, int C, int dtype, r4c_stream_t stream);
 size_t r4c_bn_pool_workspace_size(int n, int d, int h, int w, int C);

@@ -306,43 +306,63 @@ __global__ void __launch_bounds__(256) dx_kernel(const T* __restrict__ dy, const
 
 // ---------------------------------------------------------------------------
 // BatchNorm + ReLU + MaxPool3d(2), NDHWC, even extents. One thread per
-// (pooled voxel, 8-channel vector): it normalises the 2x2x2 window, writes
+// (pooled voxel, 4-channel group): it normalises the 2x2x2 window, writes
 // the eight outputs y (with a channel pitch, so y can be a channel slice of a
 // wider buffer: the decoder's concatenation) and their maximum p. Backward
 // recomputes the window's outputs from x, takes the argmax the way PyTorch's
 // max_pool3d does (scan in (d, h, w) order, first maximum; a NaN wins), and
 // routes dP there: g = [pre > 0] * (dY + [argmax] * dP).
+// Four channels (8-byte vectors) per thread rather than eight: the backward
+// holds the window's x and dY as raw vectors plus the parameters, and at
+// eight channels that took ~250 registers (two blocks per SM, issue-bound);
+// at four the kernels fit in 128 registers, four blocks per SM.
 // ---------------------------------------------------------------------------
 struct PoolGeo {
   int n, d, h, w, C;
   int ypitch;          // channels between consecutive voxels of y / dY
-  int64_t pvox;        // pooled voxels n * d/2 * h/2 * w/2
+  int64_t pvox;        // pooled voxels n * d/2 * h/2 * w/2 (< 2^32: a pooled voxel is >= 128 bytes of x)
 };
 
-__device__ __forceinline__ int64_t window_voxel(const PoolGeo& g, int64_t pv, int k) {
-  const int pw = g.w >> 1, ph = g.h >> 1, pd = g.d >> 1;
-  int64_t t = pv;
-  const int px = (int)(t % pw); t /= pw;
-  const int py = (int)(t % ph); t /= ph;
-  const int pz = (int)(t % pd);
-  const int nb = (int)(t / pd);
-  const int a = k >> 2, b = (k >> 1) & 1, c = k & 1;
-  return (((int64_t)nb * g.d + 2 * pz + a) * g.h + 2 * py + b) * g.w + 2 * px + c;
+template <typename T>
+struct Vec4 {
+  uint2 raw;
+  __device__ __forceinline__ void to_f(float* f) const {
+    const T* p = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) f[i] = Elem<T>::to_f(p[i]);
+  }
+  __device__ __forceinline__ void from_f(const float* f) {
+    T* p = reinterpret_cast<T*>(&raw);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) p[i] = Elem<T>::from_f(f[i]);
+  }
+};
+
+// Voxel index of the (0, 0, 0) corner of pooled voxel pv's window, and the
+// offset of window voxel k = (a, b, c) from it (32-bit decomposition of pv).
+__device__ __forceinline__ int64_t window_base(const PoolGeo& g, uint32_t pv) {
+  const uint32_t pw = (uint32_t)g.w >> 1, ph = (uint32_t)g.h >> 1, pd = (uint32_t)g.d >> 1;
+  uint32_t t = pv;
+  const uint32_t px = t % pw; t /= pw;
+  const uint32_t py = t % ph; t /= ph;
+  const uint32_t pz = t % pd;
+  const uint32_t nb = t / pd;
+  return (((int64_t)nb * g.d + 2 * pz) * g.h + 2 * py) * g.w + 2 * px;
+}
+__device__ __forceinline__ int64_t window_off(const PoolGeo& g, int k) {
+  return (int64_t)(k >> 2) * g.h * g.w + ((k >> 1) & 1) * g.w + (k & 1);
 }
 
 template <typename T>
 __device__ __forceinline__ float round_to(float v) { return Elem<T>::to_f(Elem<T>::from_f(v)); }
 
-// Window pass shared by the three kernels: loads x for the 8 voxels and
-// returns, per channel, the argmax voxel of the rounded outputs.
-// The normalisation parameters of the 8 channels c0..c0+7, loaded once per
-// thread instead of per element.
-struct BnPar8 {
-  float m[8], is[8], w[8], b[8];
+// The normalisation parameters of the 4 channels c0..c0+3.
+struct BnPar4 {
+  float m[4], is[4], w[4], b[4];
 };
-__device__ __forceinline__ void load_par8(BnPar8& P, const float* mi, const float* af, int C, int c0) {
+__device__ __forceinline__ void load_par4(BnPar4& P, const float* mi, const float* af, int C, int c0) {
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
+  for (int j = 0; j < 4; ++j) {
     P.m[j] = __ldg(mi + c0 + j);
     P.is[j] = __ldg(mi + C + c0 + j);
     P.w[j] = __ldg(af + c0 + j);
@@ -350,127 +370,140 @@ __device__ __forceinline__ void load_par8(BnPar8& P, const float* mi, const floa
   }
 }
 
+// 8 window voxels x 4 channels of a pitched NDHWC tensor, as raw vectors.
 template <typename T>
-__device__ __forceinline__ void window_argmax(const T* __restrict__ x, const PoolGeo& g, int64_t pv, int c0,
-                                              const BnPar8& P, float (&xf)[8][8], int (&am)[8],
-                                              float (&mx)[8], int64_t (&vox)[8]) {
+__device__ __forceinline__ void window_load(const T* __restrict__ src, const PoolGeo& g, int64_t base, int pitch,
+                                            int c0, uint2 (&r)[8]) {
 #pragma unroll
-  for (int i = 0; i < 8; ++i) { am[i] = 0; mx[i] = 0.f; }
+  for (int k = 0; k < 8; ++k) r[k] = *reinterpret_cast<const uint2*>(src + (base + window_off(g, k)) * pitch + c0);
+}
+
+// Per channel j the maximum of the window's rounded outputs (mx) and its
+// voxel (3 bits at 3j of the result), the way PyTorch's max_pool3d scans:
+// (d, h, w) order, first maximum, a NaN wins.
+template <typename T>
+__device__ __forceinline__ uint32_t window_argmax(const uint2 (&xr)[8], const BnPar4& P, float (&mx)[4]) {
+  uint32_t am = 0u;
 #pragma unroll
   for (int k = 0; k < 8; ++k) {
-    vox[k] = window_voxel(g, pv, k);
-    Vec8<T> a;
-    a.raw = *reinterpret_cast<const uint4*>(x + vox[k] * g.C + c0);
-    a.to_f(xf[k]);
-  }
+    Vec4<T> a;
+    a.raw = xr[k];
+    float xf[4];
+    a.to_f(xf);
 #pragma unroll
-  for (int k = 0; k < 8; ++k)
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float pre = bn_pre(xf[k][i], P.m[i], P.is[i], P.w[i], P.b[i]);
+    for (int i = 0; i < 4; ++i) {
+      const float pre = bn_pre(xf[i], P.m[i], P.is[i], P.w[i], P.b[i]);
       const float y = round_to<T>(pre > 0.f ? pre : 0.f);
-      if (k == 0 || y > mx[i] || isnan(y)) {   // PyTorch's max_pool3d rule
+      if (k == 0 || y > mx[i] || isnan(y)) {
         mx[i] = y;
-        am[i] = k;
+        am = (am & ~(7u << (3 * i))) | ((uint32_t)k << (3 * i));
       }
     }
+  }
+  return am;
+}
+
+// g = [pre > 0] * (dY + [argmax] * dP) of window voxel k; xf = x there.
+template <typename T>
+__device__ __forceinline__ void window_grad_k(int k, const uint2& xr, const uint2& gyr, const float (&gpf)[4],
+                                              uint32_t am, const BnPar4& P, float (&xf)[4], float (&gf)[4]) {
+  Vec4<T> a, b;
+  a.raw = xr;
+  b.raw = gyr;
+  a.to_f(xf);
+  b.to_f(gf);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float pre = bn_pre(xf[j], P.m[j], P.is[j], P.w[j], P.b[j]);
+    const float v = gf[j] + (((am >> (3 * j)) & 7u) == (uint32_t)k ? gpf[j] : 0.f);
+    gf[j] = pre > 0.f ? v : 0.f;
+  }
 }
 
 template <typename T>
-__global__ void __launch_bounds__(128) pool_fwd_kernel(const T* __restrict__ x, T* __restrict__ y, T* __restrict__ p,
-                                                       const float* __restrict__ mi, const float* __restrict__ af,
-                                                       PoolGeo g) {
-  const int nv = g.C / 8;
-  const int64_t total = g.pvox * nv;
-  BnPar8 P;
+__global__ void __launch_bounds__(128, 4) pool_fwd_kernel(const T* __restrict__ x, T* __restrict__ y,
+                                                          T* __restrict__ p, const float* __restrict__ mi,
+                                                          const float* __restrict__ af, PoolGeo g) {
+  const uint32_t nv = (uint32_t)g.C / 4;
+  const uint64_t total = (uint64_t)g.pvox * nv;
+  BnPar4 P;
   int pc0 = -1;  // channel group whose parameters P holds (fixed when blockDim % nv == 0)
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t pv = i / nv;
-    const int c0 = (int)(i - pv * nv) * 8;
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
+    const uint32_t pv = (uint32_t)i / nv;  // i < total < 2^32
+    const int c0 = (int)((uint32_t)i - pv * nv) * 4;
     if (c0 != pc0) {
-      load_par8(P, mi, af, g.C, c0);
+      load_par4(P, mi, af, g.C, c0);
       pc0 = c0;
     }
-    float xf[8][8], mx[8];
-    int am[8];
-    int64_t vox[8];
-    window_argmax<T>(x, g, pv, c0, P, xf, am, mx, vox);
+    const int64_t base = window_base(g, pv);
+    uint2 xr[8];
+    window_load<T>(x, g, base, g.C, c0, xr);
+    float mx[4];
+    window_argmax<T>(xr, P, mx);
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
-      float f[8];
+      Vec4<T> a;
+      a.raw = xr[k];
+      float f[4];
+      a.to_f(f);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float pre = bn_pre(xf[k][j], P.m[j], P.is[j], P.w[j], P.b[j]);
+      for (int j = 0; j < 4; ++j) {
+        const float pre = bn_pre(f[j], P.m[j], P.is[j], P.w[j], P.b[j]);
         f[j] = pre > 0.f ? pre : 0.f;
       }
-      Vec8<T> o;
+      Vec4<T> o;
       o.from_f(f);
-      *reinterpret_cast<uint4*>(y + vox[k] * g.ypitch + c0) = o.raw;
+      *reinterpret_cast<uint2*>(y + (base + window_off(g, k)) * g.ypitch + c0) = o.raw;
     }
-    Vec8<T> o;
+    Vec4<T> o;
     o.from_f(mx);
-    reinterpret_cast<uint4*>(p)[i] = o.raw;
+    reinterpret_cast<uint2*>(p)[i] = o.raw;
   }
 }
 
-// g per voxel k and channel j of the window.
+// part[b] = (sum g, sum g*(x - mean)) over the block's pooled voxels; a
+// block is R rows of C/4 lanes (R = 1 and several groups per lane when
+// C/4 > blockDim).
 template <typename T>
-__device__ __forceinline__ void window_grad(const T* __restrict__ gy, const T* __restrict__ gp, const PoolGeo& g,
-                                            int64_t i, int c0, const BnPar8& P,
-                                            const float (&xf)[8][8], const int (&am)[8], const int64_t (&vox)[8],
-                                            float (&gf)[8][8]) {
-  Vec8<T> pb;
-  pb.raw = reinterpret_cast<const uint4*>(gp)[i];
-  float gpf[8];
-  pb.to_f(gpf);
-#pragma unroll
-  for (int k = 0; k < 8; ++k) {
-    Vec8<T> b;
-    b.raw = *reinterpret_cast<const uint4*>(gy + vox[k] * g.ypitch + c0);
-    b.to_f(gf[k]);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float pre = bn_pre(xf[k][j], P.m[j], P.is[j], P.w[j], P.b[j]);
-      float v = gf[k][j] + (am[j] == k ? gpf[j] : 0.f);
-      gf[k][j] = pre > 0.f ? v : 0.f;
-    }
-  }
-}
-
-// part[b] = (sum g, sum g*(x - mean)) over the block's pooled voxels.
-template <typename T>
-__global__ void __launch_bounds__(128) pool_sums_kernel(const T* __restrict__ x, const T* __restrict__ gy,
+__global__ void __launch_bounds__(512) pool_sums_kernel(const T* __restrict__ x, const T* __restrict__ gy,
                                                         const T* __restrict__ gp, const float* __restrict__ mi,
                                                         const float* __restrict__ af, PoolGeo g, int64_t chunk,
                                                         float* __restrict__ part) {
   extern __shared__ float red[];  // [R][2*C]
-  const int nv = g.C / 8;
+  const int nv = g.C / 4;
   const int lane = threadIdx.x % nv, row = threadIdx.x / nv;
   const int R = blockDim.x / nv;
-  const int c0 = lane * 8;
-  BnPar8 P;
-  load_par8(P, mi, af, g.C, c0);
-  float s1[8], s2[8];
+  const int c0 = lane * 4;
+  BnPar4 P;
+  load_par4(P, mi, af, g.C, c0);
+  float s1[4], s2[4];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) { s1[j] = 0.f; s2[j] = 0.f; }
+  for (int j = 0; j < 4; ++j) { s1[j] = 0.f; s2[j] = 0.f; }
   const int64_t v0 = (int64_t)blockIdx.x * chunk, v1 = min(v0 + chunk, g.pvox);
   if (row < R) {
     for (int64_t pv = v0 + row; pv < v1; pv += R) {
-      float xf[8][8], mx[8], gf[8][8];
-      int am[8];
-      int64_t vox[8];
-      window_argmax<T>(x, g, pv, c0, P, xf, am, mx, vox);
-      window_grad<T>(gy, gp, g, pv * nv + lane, c0, P, xf, am, vox, gf);
+      const int64_t base = window_base(g, (uint32_t)pv);
+      uint2 xr[8], gyr[8];
+      window_load<T>(x, g, base, g.C, c0, xr);
+      window_load<T>(gy, g, base, g.ypitch, c0, gyr);
+      Vec4<T> pb;
+      pb.raw = reinterpret_cast<const uint2*>(gp)[pv * nv + lane];
+      float gpf[4], mx[4];
+      pb.to_f(gpf);
+      const uint32_t am = window_argmax<T>(xr, P, mx);
 #pragma unroll
-      for (int k = 0; k < 8; ++k)
+      for (int k = 0; k < 8; ++k) {
+        float xf[4], gf[4];
+        window_grad_k<T>(k, xr[k], gyr[k], gpf, am, P, xf, gf);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          s1[j] += gf[k][j];
-          s2[j] = fmaf(gf[k][j], xf[k][j] - P.m[j], s2[j]);
+        for (int j = 0; j < 4; ++j) {
+          s1[j] += gf[j];
+          s2[j] = fmaf(gf[j], xf[j] - P.m[j], s2[j]);
         }
+      }
     }
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
+    for (int j = 0; j < 4; ++j) {
       red[row * 2 * g.C + c0 + j] = s1[j];
       red[row * 2 * g.C + g.C + c0 + j] = s2[j];
     }
@@ -484,41 +517,46 @@ __global__ void __launch_bounds__(128) pool_sums_kernel(const T* __restrict__ x,
 }
 
 template <typename T>
-__global__ void __launch_bounds__(128) pool_dx_kernel(const T* __restrict__ x, const T* __restrict__ gy,
-                                                      const T* __restrict__ gp, T* __restrict__ dx,
-                                                      const float* __restrict__ mi, const float* __restrict__ af,
-                                                      const float* __restrict__ coef, PoolGeo g) {
-  const int nv = g.C / 8;
-  const int64_t total = g.pvox * nv;
-  BnPar8 P;
-  float q0[8], q1[8], q2[8];
+__global__ void __launch_bounds__(128, 3) pool_dx_kernel(const T* __restrict__ x, const T* __restrict__ gy,
+                                                         const T* __restrict__ gp, T* __restrict__ dx,
+                                                         const float* __restrict__ mi, const float* __restrict__ af,
+                                                         const float* __restrict__ coef, PoolGeo g) {
+  const uint32_t nv = (uint32_t)g.C / 4;
+  const uint64_t total = (uint64_t)g.pvox * nv;
+  BnPar4 P;
+  float q0[4], q1[4], q2[4];
   int pc0 = -1;  // channel group whose parameters are held (fixed when blockDim % nv == 0)
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t pv = i / nv;
-    const int c0 = (int)(i - pv * nv) * 8;
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
+    const uint32_t pv = (uint32_t)i / nv;  // i < total < 2^32
+    const int c0 = (int)((uint32_t)i - pv * nv) * 4;
     if (c0 != pc0) {
-      load_par8(P, mi, af, g.C, c0);
+      load_par4(P, mi, af, g.C, c0);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
+      for (int j = 0; j < 4; ++j) {
         q0[j] = __ldg(coef + c0 + j);
         q1[j] = __ldg(coef + g.C + c0 + j);
         q2[j] = __ldg(coef + 2 * g.C + c0 + j);
       }
       pc0 = c0;
     }
-    float xf[8][8], mx[8], gf[8][8];
-    int am[8];
-    int64_t vox[8];
-    window_argmax<T>(x, g, pv, c0, P, xf, am, mx, vox);
-    window_grad<T>(gy, gp, g, i, c0, P, xf, am, vox, gf);
+    const int64_t base = window_base(g, pv);
+    uint2 xr[8], gyr[8];
+    window_load<T>(x, g, base, g.C, c0, xr);
+    window_load<T>(gy, g, base, g.ypitch, c0, gyr);
+    Vec4<T> pb;
+    pb.raw = reinterpret_cast<const uint2*>(gp)[i];
+    float gpf[4], mx[4];
+    pb.to_f(gpf);
+    const uint32_t am = window_argmax<T>(xr, P, mx);
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
-      float f[8];
+      float xf[4], gf[4], f[4];
+      window_grad_k<T>(k, xr[k], gyr[k], gpf, am, P, xf, gf);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) f[j] = (gf[k][j] - q0[j] - (xf[k][j] - P.m[j]) * q1[j]) * q2[j];
-      Vec8<T> o;
+      for (int j = 0; j < 4; ++j) f[j] = (gf[j] - q0[j] - (xf[j] - P.m[j]) * q1[j]) * q2[j];
+      Vec4<T> o;
       o.from_f(f);
-      *reinterpret_cast<uint4*>(dx + vox[k] * g.C + c0) = o.raw;
+      *reinterpret_cast<uint2*>(dx + (base + window_off(g, k)) * g.C + c0) = o.raw;
     }
   }
 }
@@ -544,12 +582,41 @@ static int grid_for(int64_t nvec) {
 // Threads per block of the element-wise kernels: a multiple of C/8 (the 16-byte
 // vectors of one voxel), so each thread keeps the same 8 channels.
 static int vec_threads(int C) { return (256 / (C / 8)) * (C / 8); }
-// Pool kernels (128 threads): likewise a multiple of C/8 when C/8 <= 128.
-static int pool_threads(int C) { return C / 8 <= 128 ? (128 / (C / 8)) * (C / 8) : 128; }
+// Pool kernels (128 threads, 4 channels each): likewise a multiple of C/4
+// when C/4 <= 128.
+static int pool_threads(int C) { return C / 4 <= 128 ? (128 / (C / 4)) * (C / 4) : 128; }
 
 static bool ok_args(const void* p, int64_t vox, int C, int dtype) {
   return p && vox >= 0 && C > 0 && C % 8 == 0 && C <= 2048 && (dtype == R4C_BF16 || dtype == R4C_F16) &&
          (reinterpret_cast<uintptr_t>(p) & 15) == 0;
+}
+
+// Dense copy of a channel slice: dst[v][0..C) = src[v * pitch + 0..C), in
+// 16-byte vectors (nvec = C/8 per voxel, pitch16 = pitch/8). A slice of a
+// wider NDHWC buffer read this way touches only its own bytes; PyTorch's
+// strided copy of the same view runs a scalar element loop (~1.8 TB/s at
+// UNet sizes). Four independent vectors per thread and step keep enough
+// loads in flight.
+template <typename I>
+__global__ void __launch_bounds__(256) slice_copy_kernel(const uint4* __restrict__ src, int64_t pitch16,
+                                                         uint4* __restrict__ dst, I nvec, I total) {
+  const I stride = (I)gridDim.x * blockDim.x;
+  for (I i = (I)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += 4 * stride) {
+    uint4 v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const I e = i + u * stride;
+      if (e < total) {
+        const I vx = e / nvec;
+        v[u] = src[(int64_t)vx * pitch16 + (e - vx * nvec)];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const I e = i + u * stride;
+      if (e < total) dst[e] = v[u];
+    }
+  }
 }
 
 }  // namespace bn
@@ -685,6 +752,27 @@ static PoolGeo pool_geo(int n, int d, int h, int w, int C, int pitch) {
   return g;
 }
 
+int r4c_channel_slice_copy(const void* src, int src_pitch, void* dst, int64_t vox, int C, int dtype,
+                           r4c_stream_t stream) {
+  if (!src || !dst || vox < 0 || C <= 0 || C % 8 || src_pitch < C || src_pitch % 8 ||
+      (dtype != R4C_BF16 && dtype != R4C_F16) || (reinterpret_cast<uintptr_t>(src) & 15) ||
+      (reinterpret_cast<uintptr_t>(dst) & 15))
+    return R4C_ERR_INVALID;
+  const int64_t nvec = C / 8;
+  const int64_t total = vox * nvec;
+  if (total == 0) return R4C_OK;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((total + 1023) / 1024, 148 * 8));
+  if (total < (int64_t)0xFFFFFFFF - 4ll * grid * 256)
+    slice_copy_kernel<uint32_t><<<grid, 256, 0, s>>>(static_cast<const uint4*>(src), src_pitch / 8,
+                                                     static_cast<uint4*>(dst), (uint32_t)nvec, (uint32_t)total);
+  else
+    slice_copy_kernel<int64_t><<<grid, 256, 0, s>>>(static_cast<const uint4*>(src), src_pitch / 8,
+                                                    static_cast<uint4*>(dst), nvec, total);
+  r4c::note_launches(1);
+  return cudaGetLastError() == cudaSuccess ? R4C_OK : R4C_ERR_CUDA;
+}
+
 int r4c_bn_relu_pool_fwd(const void* x, void* y, int y_pitch, void* p, const float* mean_invstd, const float* affine,
                          int n, int d, int h, int w, int C, int dtype, r4c_stream_t stream) {
   if (!pool_args(x, n, d, h, w, C, C, dtype) || !pool_args(y, n, d, h, w, C, y_pitch, dtype) ||
@@ -693,7 +781,7 @@ int r4c_bn_relu_pool_fwd(const void* x, void* y, int y_pitch, void* p, const flo
   const PoolGeo g = pool_geo(n, d, h, w, C, y_pitch);
   if (g.pvox == 0) return R4C_OK;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  const int64_t total = g.pvox * (C / 8);
+  const int64_t total = g.pvox * (C / 4);
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((total + 127) / 128, 148 * 8));
   if (dtype == R4C_BF16)
     pool_fwd_kernel<__nv_bfloat16><<<grid, pool_threads(g.C), 0, s>>>(static_cast<const __nv_bfloat16*>(x),
@@ -724,8 +812,8 @@ int r4c_bn_relu_pool_bwd_sums(const void* gy, int gy_pitch, const void* gp, cons
   const Split sp = split_for(g.pvox, 8);   // a pooled voxel is 8 voxels of work
   if (!ws || ws_bytes < r4c_bn_pool_workspace_size(n, d, h, w, C)) return R4C_ERR_WORKSPACE;
   float* part = static_cast<float*>(ws);
-  const int R = std::max(1, 128 / (C / 8));
-  const int threads = R * (C / 8);
+  const int R = std::max(1, 128 / (C / 4));
+  const int threads = R * (C / 4);  // <= 512: C <= 2048
   const size_t smem = (size_t)R * 2 * C * sizeof(float);
   if (smem > 48 * 1024) return R4C_ERR_UNSUPPORTED;
   if (dtype == R4C_BF16)
@@ -757,7 +845,7 @@ int r4c_bn_relu_pool_bwd_dx(const void* gy, int gy_pitch, const void* gp, const 
   bwd_finalize_kernel<<<(C + 127) / 128, 128, 0, s>>>(sums, mean_invstd, affine, C, count, dgamma, dbeta, coef);
   r4c::note_launches(1);
   if (dx && g.pvox > 0) {
-    const int64_t total = g.pvox * (C / 8);
+    const int64_t total = g.pvox * (C / 4);
     const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((total + 127) / 128, 148 * 8));
     if (dtype == R4C_BF16)
       pool_dx_kernel<__nv_bfloat16><<<grid, pool_threads(g.C), 0, s>>>(

@@ -88,6 +88,7 @@ def _bind(lib) -> None:
         "r4c_bn_relu_fwd": ([P, P, P, P, i64, i, i, i, P], i),
         "r4c_bn_relu_bwd_sums": ([P, P, P, P, i64, i, i, i, P, P, sz, P], i),
         "r4c_bn_relu_bwd_dx": ([P, P, P, P, P, P, dbl, i64, i, i, i, P, P, P, P], i),
+        "r4c_channel_slice_copy": ([P, i, P, i64, i, i, P], i),
         "r4c_bn_relu_pool_fwd": ([P, P, i, P, P, P, i, i, i, i, i, i, P], i),
         "r4c_bn_pool_workspace_size": ([i, i, i, i, i], sz),
         "r4c_bn_relu_pool_bwd_sums": ([P, i, P, P, P, P, i, i, i, i, i, i, P, P, sz, P], i),
@@ -448,6 +449,28 @@ def bn_relu_backward(dy_cl: torch.Tensor, x_cl: torch.Tensor, mean_invstd, affin
                                   _ptr(coef), _stream(dev))
         _check(st, "r4c_bn_relu_bwd_dx")
     return dx, dg, db
+
+
+def channel_slice_dense(t: torch.Tensor) -> Optional[torch.Tensor]:
+    """A dense channels_last_3d copy of ``t`` when ``t`` is a channel slice of
+    a wider NDHWC tensor (voxel stride = pitch >= C, channel stride 1), made
+    by the library's slice copy; None when ``t`` is not such a slice or the
+    copy's alignment rules do not hold."""
+    if t.dim() != 5 or not t.is_cuda or t.dtype not in (torch.bfloat16, torch.float16):
+        return None
+    n, C, d, h, w = (int(v) for v in t.shape)
+    sn, sc, sd, sh, sw = t.stride()
+    pitch = sw
+    if (sc != 1 or C % 8 or pitch % 8 or pitch < C or sh != pitch * w or sd != pitch * w * h
+            or (n > 1 and sn != pitch * w * h * d) or t.data_ptr() % 16):
+        return None
+    dev = t.device
+    out = _ndhwc_empty(n, C, d, h, w, dev, t.dtype)
+    with torch.cuda.device(dev):
+        st = lib().r4c_channel_slice_copy(_ptr(t), pitch, _ptr(out), n * d * h * w, C, dtype_code(t.dtype),
+                                          _stream(dev))
+    _check(st, "r4c_channel_slice_copy")
+    return out
 
 
 def bn_relu_pool_forward(x_cl: torch.Tensor, mean_invstd, affine, lead: int):

@@ -677,7 +677,12 @@ def _tconv_backward(ctx, grad_out):
     x_c = x if x.dtype in _HALF else x.to(torch.float16)
     go = grad_out.to(x_c.dtype) if grad_out.dtype != x_c.dtype else grad_out
     # one dense NDHWC copy shared by both legs when dY arrives as a view
-    # (e.g. the channel slice of a concatenation's gradient)
+    # (e.g. the channel slice of a concatenation's gradient: the library's
+    # slice copy, else PyTorch's)
+    if not go.is_contiguous(memory_format=torch.channels_last_3d):
+        dense = _native.channel_slice_dense(go)
+        if dense is not None:
+            go = dense
     go = _as_ndhwc(go)
     want_db = ctx.has_bias and need_b
     dw = db = None

@@ -91,9 +91,18 @@ def test_bn_relu_eval_and_fallbacks(cuda_ready):
     assert _native.launch_count() == n0
 
 
-@pytest.mark.parametrize("quantised", [False, True], ids=["random", "ties"])
-@pytest.mark.parametrize("shape,lead", [((2, 24, 8, 16, 16), 24), ((1, 48, 4, 8, 8), 48), ((2, 8, 6, 4, 10), 0),
-                                        ((4, 24, 64, 128, 128), 24)], ids=["24", "48", "lead0", "full"])
+_POOL_SHAPES = [((2, 24, 8, 16, 16), 24), ((1, 48, 4, 8, 8), 48), ((2, 8, 6, 4, 10), 0), ((4, 24, 64, 128, 128), 24)]
+
+
+# ties: quantised inputs. The wide case (C/4 = 132 > 128 threads: a thread's
+# channel group changes between steps) runs on random inputs only: with 32
+# voxels per channel its quantised batch mean lands exactly on input values
+# (27 of the 528 channels),
+# and whether BatchNorm's output there is 0 or a rounding residue (which
+# decides ReLU's gradient) depends on how each implementation sums the mean.
+@pytest.mark.parametrize("shape,lead,quantised",
+                         [(s, l, q) for s, l in _POOL_SHAPES for q in (False, True)] + [((1, 528, 2, 4, 4), 8, False)],
+                         ids=[f"{i}-{q}" for i in ("24", "48", "lead0", "full") for q in ("random", "ties")] + ["wide-random"])
 def test_bn_relu_pool_and_skip_buffer(cuda_ready, shape, lead, quantised):
     """forward_pool (BN + ReLU + MaxPool3d(2), skip written after `lead`
     channels of the concatenation buffer) and skip_cat against stock
@@ -205,3 +214,36 @@ def test_up_conv_into_buffer_plans(cuda_ready, monkeypatch, cin, cout, shape, di
         b = skip_cat(up(x), buf.clone(), cout)
     assert calls == ([1] if direct else [])
     assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16], ids=["bf16", "fp16"])
+@pytest.mark.parametrize("shape,lead,pitch", [
+    ((4, 24, 8, 16, 16), 0, 48),     # the up-conv part of a UNet concatenation
+    ((4, 24, 8, 16, 16), 24, 48),    # the skip part
+    ((1, 8, 3, 5, 7), 16, 32),       # odd extents, one vector per voxel
+    ((2, 96, 2, 4, 6), 96, 192),
+], ids=["lead", "skip", "odd", "wide"])
+def test_channel_slice_copy(cuda_ready, shape, lead, pitch, dtype):
+    """r4c_channel_slice_copy: a channel slice of an NDHWC buffer copied dense,
+    bit-identical to PyTorch's copy of the same view."""
+    from rdna4_conv3d import _native
+    n, C, d, h, w = shape
+    torch.manual_seed(0)
+    buf = torch.randn(n, pitch, d, h, w, device="cuda").to(dtype).contiguous(memory_format=torch.channels_last_3d)
+    view = buf[:, lead:lead + C]
+    out = _native.channel_slice_dense(view)
+    assert out is not None and out.is_contiguous(memory_format=torch.channels_last_3d)
+    assert torch.equal(out, view.contiguous(memory_format=torch.channels_last_3d))
+
+
+def test_channel_slice_copy_declines_other_views(cuda_ready):
+    """Views that are not a channel slice of an NDHWC buffer (NCDHW, a
+    channel count that is not a multiple of 8, fp32) are left to PyTorch."""
+    from rdna4_conv3d import _native
+    cl = torch.channels_last_3d
+    a = torch.randn(2, 16, 4, 4, 4, device="cuda", dtype=torch.bfloat16)
+    assert _native.channel_slice_dense(a[:, :8]) is None
+    b = torch.randn(2, 16, 4, 4, 4, device="cuda", dtype=torch.bfloat16).contiguous(memory_format=cl)
+    assert _native.channel_slice_dense(b[:, :12]) is None
+    c = torch.randn(2, 16, 4, 4, 4, device="cuda").contiguous(memory_format=cl)
+    assert _native.channel_slice_dense(c[:, :8]) is None

@@ -420,10 +420,16 @@ __device__ __forceinline__ void window_grad_k(int k, const uint2& xr, const uint
   }
 }
 
+// zlead > 0: the zlead channels before y's of each voxel (the lead part of
+// the concatenation buffer that y is a slice of) are written with zeros in
+// the same pass, so that every line of the buffer is written whole. A
+// slice written alone leaves partial 32-byte sectors, and on this HBM a
+// partial sector costs a read-modify-write: at the UNet's level 0 the
+// pitched forward measured 222 us against 97 us for the same bytes dense.
 template <typename T>
 __global__ void __launch_bounds__(128, 4) pool_fwd_kernel(const T* __restrict__ x, T* __restrict__ y,
                                                           T* __restrict__ p, const float* __restrict__ mi,
-                                                          const float* __restrict__ af, PoolGeo g) {
+                                                          const float* __restrict__ af, PoolGeo g, int zlead) {
   const uint32_t nv = (uint32_t)g.C / 4;
   const uint64_t total = (uint64_t)g.pvox * nv;
   BnPar4 P;
@@ -453,7 +459,9 @@ __global__ void __launch_bounds__(128, 4) pool_fwd_kernel(const T* __restrict__ 
       }
       Vec4<T> o;
       o.from_f(f);
-      *reinterpret_cast<uint2*>(y + (base + window_off(g, k)) * g.ypitch + c0) = o.raw;
+      T* yv = y + (base + window_off(g, k)) * g.ypitch;
+      for (int c = c0; c < zlead; c += g.C) *reinterpret_cast<uint2*>(yv - zlead + c) = make_uint2(0u, 0u);
+      *reinterpret_cast<uint2*>(yv + c0) = o.raw;
     }
     Vec4<T> o;
     o.from_f(mx);
@@ -773,11 +781,8 @@ int r4c_channel_slice_copy(const void* src, int src_pitch, void* dst, int64_t vo
   return cudaGetLastError() == cudaSuccess ? R4C_OK : R4C_ERR_CUDA;
 }
 
-int r4c_bn_relu_pool_fwd(const void* x, void* y, int y_pitch, void* p, const float* mean_invstd, const float* affine,
-                         int n, int d, int h, int w, int C, int dtype, r4c_stream_t stream) {
-  if (!pool_args(x, n, d, h, w, C, C, dtype) || !pool_args(y, n, d, h, w, C, y_pitch, dtype) ||
-      !pool_args(p, n, d, h, w, C, C, dtype) || !mean_invstd || !affine)
-    return R4C_ERR_INVALID;
+static int pool_fwd_launch(const void* x, void* y, int y_pitch, int zlead, void* p, const float* mean_invstd,
+                           const float* affine, int n, int d, int h, int w, int C, int dtype, r4c_stream_t stream) {
   const PoolGeo g = pool_geo(n, d, h, w, C, y_pitch);
   if (g.pvox == 0) return R4C_OK;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
@@ -786,12 +791,30 @@ int r4c_bn_relu_pool_fwd(const void* x, void* y, int y_pitch, void* p, const flo
   if (dtype == R4C_BF16)
     pool_fwd_kernel<__nv_bfloat16><<<grid, pool_threads(g.C), 0, s>>>(static_cast<const __nv_bfloat16*>(x),
                                                         static_cast<__nv_bfloat16*>(y), static_cast<__nv_bfloat16*>(p),
-                                                        mean_invstd, affine, g);
+                                                        mean_invstd, affine, g, zlead);
   else
     pool_fwd_kernel<__half><<<grid, pool_threads(g.C), 0, s>>>(static_cast<const __half*>(x), static_cast<__half*>(y),
-                                                 static_cast<__half*>(p), mean_invstd, affine, g);
+                                                 static_cast<__half*>(p), mean_invstd, affine, g, zlead);
   r4c::note_launches(1);
   return cudaGetLastError() == cudaSuccess ? R4C_OK : R4C_ERR_CUDA;
+}
+
+int r4c_bn_relu_pool_fwd(const void* x, void* y, int y_pitch, void* p, const float* mean_invstd, const float* affine,
+                         int n, int d, int h, int w, int C, int dtype, r4c_stream_t stream) {
+  if (!pool_args(x, n, d, h, w, C, C, dtype) || !pool_args(y, n, d, h, w, C, y_pitch, dtype) ||
+      !pool_args(p, n, d, h, w, C, C, dtype) || !mean_invstd || !affine)
+    return R4C_ERR_INVALID;
+  return pool_fwd_launch(x, y, y_pitch, 0, p, mean_invstd, affine, n, d, h, w, C, dtype, stream);
+}
+
+int r4c_bn_relu_pool_fwd_cat(const void* x, void* buf, int lead, void* p, const float* mean_invstd,
+                             const float* affine, int n, int d, int h, int w, int C, int dtype, r4c_stream_t stream) {
+  if (lead < 0 || lead % 8 || !buf || (reinterpret_cast<uintptr_t>(buf) & 15)) return R4C_ERR_INVALID;
+  void* y = static_cast<uint8_t*>(buf) + (size_t)lead * 2;
+  if (!pool_args(x, n, d, h, w, C, C, dtype) || !pool_args(y, n, d, h, w, C, lead + C, dtype) ||
+      !pool_args(p, n, d, h, w, C, C, dtype) || !mean_invstd || !affine)
+    return R4C_ERR_INVALID;
+  return pool_fwd_launch(x, y, lead + C, lead, p, mean_invstd, affine, n, d, h, w, C, dtype, stream);
 }
 
 size_t r4c_bn_pool_workspace_size(int n, int d, int h, int w, int C) {

@@ -90,6 +90,7 @@ def _bind(lib) -> None:
         "r4c_bn_relu_bwd_dx": ([P, P, P, P, P, P, dbl, i64, i, i, i, P, P, P, P], i),
         "r4c_channel_slice_copy": ([P, i, P, i64, i, i, P], i),
         "r4c_bn_relu_pool_fwd": ([P, P, i, P, P, P, i, i, i, i, i, i, P], i),
+        "r4c_bn_relu_pool_fwd_cat": ([P, P, i, P, P, P, i, i, i, i, i, i, P], i),
         "r4c_bn_pool_workspace_size": ([i, i, i, i, i], sz),
         "r4c_bn_relu_pool_bwd_sums": ([P, i, P, P, P, P, i, i, i, i, i, i, P, P, sz, P], i),
         "r4c_bn_relu_pool_bwd_dx": ([P, i, P, P, P, P, P, P, dbl, i, i, i, i, i, i, P, P, P, P], i),
@@ -475,16 +476,22 @@ def channel_slice_dense(t: torch.Tensor) -> Optional[torch.Tensor]:
 
 def bn_relu_pool_forward(x_cl: torch.Tensor, mean_invstd, affine, lead: int):
     """(buf, p): buf is a new NDHWC tensor of lead + C channels whose channels
-    [lead, lead + C) hold relu(bn(x)) (the rest left for the caller), p the
-    2x2x2 max-pool of those channels."""
+    [lead, lead + C) hold relu(bn(x)) (the first lead channels zero when lead
+    is a multiple of 8, else unwritten: the caller's), p the 2x2x2 max-pool
+    of those channels."""
     dev = _require_cuda(x_cl)
     n, C, d, h, w = (int(v) for v in x_cl.shape)
     buf = _ndhwc_empty(n, lead + C, d, h, w, dev, x_cl.dtype)
     p = _ndhwc_empty(n, C, d // 2, h // 2, w // 2, dev, x_cl.dtype)
-    yptr = ctypes.c_void_p(buf.data_ptr() + lead * buf.element_size())
     with torch.cuda.device(dev):
-        st = lib().r4c_bn_relu_pool_fwd(_ptr(x_cl), yptr, lead + C, _ptr(p), _ptr(mean_invstd), _ptr(affine),
-                                        n, d, h, w, C, dtype_code(x_cl.dtype), _stream(dev))
+        if lead % 8 == 0:
+            # whole voxels in one pass (channels [0, lead) zero until the up-conv writes them)
+            st = lib().r4c_bn_relu_pool_fwd_cat(_ptr(x_cl), _ptr(buf), lead, _ptr(p), _ptr(mean_invstd),
+                                                _ptr(affine), n, d, h, w, C, dtype_code(x_cl.dtype), _stream(dev))
+        else:
+            yptr = ctypes.c_void_p(buf.data_ptr() + lead * buf.element_size())
+            st = lib().r4c_bn_relu_pool_fwd(_ptr(x_cl), yptr, lead + C, _ptr(p), _ptr(mean_invstd), _ptr(affine),
+                                            n, d, h, w, C, dtype_code(x_cl.dtype), _stream(dev))
     _check(st, "r4c_bn_relu_pool_fwd")
     return buf, p
 

@@ -313,14 +313,20 @@ int r4c_bn_relu_pool_fwd(const void* x, void* y, int y_pitch, void* p, const flo
  * [0, lead) zeros (the caller's up-conv output overwrites them), so that
  * every line of buf is written whole in one pass: writing only the slice
  * leaves partial sectors, which HBM3e merges by read-modify-write (2.3x the
- * time at the UNet's level 0). lead a multiple of 8. */
-int r4c_bn_relu_pool_fwd_cat(const void* x, void* buf, int lead, void* p, const float* mean_invstd,
+ * time at the UNet's level 0). lead a multiple of 8. argmax (nullable):
+ * n*(d/2)*(h/2)*(w/2)*(C/4) uint16, per (pooled voxel, 4-channel group) the
+ * window position of each channel's maximum in 3-bit fields; the backward
+ * entries take it instead of recomputing it from x. */
+int r4c_bn_relu_pool_fwd_cat(const void* x, void* buf, int lead, void* p, void* argmax, const float* mean_invstd,
                              const float* affine, int n, int d, int h, int w, int C, int dtype, r4c_stream_t stream);
 size_t r4c_bn_pool_workspace_size(int n, int d, int h, int w, int C);
-int r4c_bn_relu_pool_bwd_sums(const void* gy, int gy_pitch, const void* gp, const void* x, const float* mean_invstd,
+/* argmax (nullable): as written by r4c_bn_relu_pool_fwd_cat for the same x
+ * and statistics; null recomputes it from x. */
+int r4c_bn_relu_pool_bwd_sums(const void* gy, int gy_pitch, const void* gp, const void* argmax, const void* x,
+                              const float* mean_invstd,
                               const float* affine, int n, int d, int h, int w, int C, int dtype, float* sums, void* ws,
                               size_t ws_bytes, r4c_stream_t stream);
-int r4c_bn_relu_pool_bwd_dx(const void* gy, int gy_pitch, const void* gp, const void* x, void* dx,
+int r4c_bn_relu_pool_bwd_dx(const void* gy, int gy_pitch, const void* gp, const void* argmax, const void* x, void* dx,
                             const float* mean_invstd, const float* affine, const float* sums, double count, int n,
                             int d, int h, int w, int C, int dtype, float* dgamma, float* dbeta, float* coef,
                             r4c_stream_t stream);

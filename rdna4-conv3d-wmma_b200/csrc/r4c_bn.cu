@@ -429,7 +429,8 @@ __device__ __forceinline__ void window_grad_k(int k, const uint2& xr, const uint
 template <typename T>
 __global__ void __launch_bounds__(128, 4) pool_fwd_kernel(const T* __restrict__ x, T* __restrict__ y,
                                                           T* __restrict__ p, const float* __restrict__ mi,
-                                                          const float* __restrict__ af, PoolGeo g, int zlead) {
+                                                          const float* __restrict__ af, PoolGeo g, int zlead,
+                                                          uint16_t* __restrict__ amo) {
   const uint32_t nv = (uint32_t)g.C / 4;
   const uint64_t total = (uint64_t)g.pvox * nv;
   BnPar4 P;
@@ -445,7 +446,8 @@ __global__ void __launch_bounds__(128, 4) pool_fwd_kernel(const T* __restrict__ 
     uint2 xr[8];
     window_load<T>(x, g, base, g.C, c0, xr);
     float mx[4];
-    window_argmax<T>(xr, P, mx);
+    const uint32_t am = window_argmax<T>(xr, P, mx);
+    if (amo) amo[i] = (uint16_t)am;
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
       Vec4<T> a;
@@ -476,7 +478,7 @@ template <typename T>
 __global__ void __launch_bounds__(512) pool_sums_kernel(const T* __restrict__ x, const T* __restrict__ gy,
                                                         const T* __restrict__ gp, const float* __restrict__ mi,
                                                         const float* __restrict__ af, PoolGeo g, int64_t chunk,
-                                                        float* __restrict__ part) {
+                                                        const uint16_t* __restrict__ ami, float* __restrict__ part) {
   extern __shared__ float red[];  // [R][2*C]
   const int nv = g.C / 4;
   const int lane = threadIdx.x % nv, row = threadIdx.x / nv;
@@ -498,7 +500,7 @@ __global__ void __launch_bounds__(512) pool_sums_kernel(const T* __restrict__ x,
       pb.raw = reinterpret_cast<const uint2*>(gp)[pv * nv + lane];
       float gpf[4], mx[4];
       pb.to_f(gpf);
-      const uint32_t am = window_argmax<T>(xr, P, mx);
+      const uint32_t am = ami ? (uint32_t)ami[pv * nv + lane] : window_argmax<T>(xr, P, mx);
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
         float xf[4], gf[4];
@@ -528,7 +530,8 @@ template <typename T>
 __global__ void __launch_bounds__(128, 3) pool_dx_kernel(const T* __restrict__ x, const T* __restrict__ gy,
                                                          const T* __restrict__ gp, T* __restrict__ dx,
                                                          const float* __restrict__ mi, const float* __restrict__ af,
-                                                         const float* __restrict__ coef, PoolGeo g) {
+                                                         const float* __restrict__ coef, PoolGeo g,
+                                                         const uint16_t* __restrict__ ami) {
   const uint32_t nv = (uint32_t)g.C / 4;
   const uint64_t total = (uint64_t)g.pvox * nv;
   BnPar4 P;
@@ -555,7 +558,7 @@ __global__ void __launch_bounds__(128, 3) pool_dx_kernel(const T* __restrict__ x
     pb.raw = reinterpret_cast<const uint2*>(gp)[i];
     float gpf[4], mx[4];
     pb.to_f(gpf);
-    const uint32_t am = window_argmax<T>(xr, P, mx);
+    const uint32_t am = ami ? (uint32_t)ami[i] : window_argmax<T>(xr, P, mx);
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
       float xf[4], gf[4], f[4];
@@ -781,8 +784,9 @@ int r4c_channel_slice_copy(const void* src, int src_pitch, void* dst, int64_t vo
   return cudaGetLastError() == cudaSuccess ? R4C_OK : R4C_ERR_CUDA;
 }
 
-static int pool_fwd_launch(const void* x, void* y, int y_pitch, int zlead, void* p, const float* mean_invstd,
-                           const float* affine, int n, int d, int h, int w, int C, int dtype, r4c_stream_t stream) {
+static int pool_fwd_launch(const void* x, void* y, int y_pitch, int zlead, void* p, void* argmax,
+                           const float* mean_invstd, const float* affine, int n, int d, int h, int w, int C,
+                           int dtype, r4c_stream_t stream) {
   const PoolGeo g = pool_geo(n, d, h, w, C, y_pitch);
   if (g.pvox == 0) return R4C_OK;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
@@ -791,10 +795,12 @@ static int pool_fwd_launch(const void* x, void* y, int y_pitch, int zlead, void*
   if (dtype == R4C_BF16)
     pool_fwd_kernel<__nv_bfloat16><<<grid, pool_threads(g.C), 0, s>>>(static_cast<const __nv_bfloat16*>(x),
                                                         static_cast<__nv_bfloat16*>(y), static_cast<__nv_bfloat16*>(p),
-                                                        mean_invstd, affine, g, zlead);
+                                                        mean_invstd, affine, g, zlead,
+                                                        static_cast<uint16_t*>(argmax));
   else
     pool_fwd_kernel<__half><<<grid, pool_threads(g.C), 0, s>>>(static_cast<const __half*>(x), static_cast<__half*>(y),
-                                                 static_cast<__half*>(p), mean_invstd, affine, g, zlead);
+                                                 static_cast<__half*>(p), mean_invstd, affine, g, zlead,
+                                                 static_cast<uint16_t*>(argmax));
   r4c::note_launches(1);
   return cudaGetLastError() == cudaSuccess ? R4C_OK : R4C_ERR_CUDA;
 }
@@ -804,17 +810,18 @@ int r4c_bn_relu_pool_fwd(const void* x, void* y, int y_pitch, void* p, const flo
   if (!pool_args(x, n, d, h, w, C, C, dtype) || !pool_args(y, n, d, h, w, C, y_pitch, dtype) ||
       !pool_args(p, n, d, h, w, C, C, dtype) || !mean_invstd || !affine)
     return R4C_ERR_INVALID;
-  return pool_fwd_launch(x, y, y_pitch, 0, p, mean_invstd, affine, n, d, h, w, C, dtype, stream);
+  return pool_fwd_launch(x, y, y_pitch, 0, p, nullptr, mean_invstd, affine, n, d, h, w, C, dtype, stream);
 }
 
-int r4c_bn_relu_pool_fwd_cat(const void* x, void* buf, int lead, void* p, const float* mean_invstd,
+int r4c_bn_relu_pool_fwd_cat(const void* x, void* buf, int lead, void* p, void* argmax, const float* mean_invstd,
                              const float* affine, int n, int d, int h, int w, int C, int dtype, r4c_stream_t stream) {
+  if (argmax && (reinterpret_cast<uintptr_t>(argmax) & 1)) return R4C_ERR_INVALID;
   if (lead < 0 || lead % 8 || !buf || (reinterpret_cast<uintptr_t>(buf) & 15)) return R4C_ERR_INVALID;
   void* y = static_cast<uint8_t*>(buf) + (size_t)lead * 2;
   if (!pool_args(x, n, d, h, w, C, C, dtype) || !pool_args(y, n, d, h, w, C, lead + C, dtype) ||
       !pool_args(p, n, d, h, w, C, C, dtype) || !mean_invstd || !affine)
     return R4C_ERR_INVALID;
-  return pool_fwd_launch(x, y, lead + C, lead, p, mean_invstd, affine, n, d, h, w, C, dtype, stream);
+  return pool_fwd_launch(x, y, lead + C, lead, p, argmax, mean_invstd, affine, n, d, h, w, C, dtype, stream);
 }
 
 size_t r4c_bn_pool_workspace_size(int n, int d, int h, int w, int C) {
@@ -823,9 +830,10 @@ size_t r4c_bn_pool_workspace_size(int n, int d, int h, int w, int C) {
   return r4c::align_up((size_t)s.S * 2 * C * sizeof(float), 256);
 }
 
-int r4c_bn_relu_pool_bwd_sums(const void* gy, int gy_pitch, const void* gp, const void* x, const float* mean_invstd,
-                              const float* affine, int n, int d, int h, int w, int C, int dtype, float* sums, void* ws,
-                              size_t ws_bytes, r4c_stream_t stream) {
+int r4c_bn_relu_pool_bwd_sums(const void* gy, int gy_pitch, const void* gp, const void* argmax, const void* x,
+                              const float* mean_invstd, const float* affine, int n, int d, int h, int w, int C,
+                              int dtype, float* sums, void* ws, size_t ws_bytes, r4c_stream_t stream) {
+  if (argmax && (reinterpret_cast<uintptr_t>(argmax) & 1)) return R4C_ERR_INVALID;
   if (!pool_args(x, n, d, h, w, C, C, dtype) || !pool_args(gy, n, d, h, w, C, gy_pitch, dtype) ||
       !pool_args(gp, n, d, h, w, C, C, dtype) || !mean_invstd || !affine || !sums)
     return R4C_ERR_INVALID;
@@ -842,11 +850,12 @@ int r4c_bn_relu_pool_bwd_sums(const void* gy, int gy_pitch, const void* gp, cons
   if (dtype == R4C_BF16)
     pool_sums_kernel<__nv_bfloat16><<<sp.S, threads, smem, s>>>(
         static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(gy),
-        static_cast<const __nv_bfloat16*>(gp), mean_invstd, affine, g, sp.chunk, part);
+        static_cast<const __nv_bfloat16*>(gp), mean_invstd, affine, g, sp.chunk,
+        static_cast<const uint16_t*>(argmax), part);
   else
     pool_sums_kernel<__half><<<sp.S, threads, smem, s>>>(static_cast<const __half*>(x), static_cast<const __half*>(gy),
                                                          static_cast<const __half*>(gp), mean_invstd, affine, g,
-                                                         sp.chunk, part);
+                                                         sp.chunk, static_cast<const uint16_t*>(argmax), part);
   if (dtype == R4C_BF16)
     sum_parts_kernel<__nv_bfloat16><<<(2 * C + 7) / 8, 256, 0, s>>>(part, sp.S, C, sums, 0, nullptr, nullptr);
   else
@@ -855,10 +864,11 @@ int r4c_bn_relu_pool_bwd_sums(const void* gy, int gy_pitch, const void* gp, cons
   return cudaGetLastError() == cudaSuccess ? R4C_OK : R4C_ERR_CUDA;
 }
 
-int r4c_bn_relu_pool_bwd_dx(const void* gy, int gy_pitch, const void* gp, const void* x, void* dx,
+int r4c_bn_relu_pool_bwd_dx(const void* gy, int gy_pitch, const void* gp, const void* argmax, const void* x, void* dx,
                             const float* mean_invstd, const float* affine, const float* sums, double count, int n,
                             int d, int h, int w, int C, int dtype, float* dgamma, float* dbeta, float* coef,
                             r4c_stream_t stream) {
+  if (argmax && (reinterpret_cast<uintptr_t>(argmax) & 1)) return R4C_ERR_INVALID;
   if (!pool_args(x, n, d, h, w, C, C, dtype) || !pool_args(gy, n, d, h, w, C, gy_pitch, dtype) ||
       !pool_args(gp, n, d, h, w, C, C, dtype) || !mean_invstd || !affine || !sums || !coef || count <= 0.0)
     return R4C_ERR_INVALID;
@@ -873,11 +883,12 @@ int r4c_bn_relu_pool_bwd_dx(const void* gy, int gy_pitch, const void* gp, const 
     if (dtype == R4C_BF16)
       pool_dx_kernel<__nv_bfloat16><<<grid, pool_threads(g.C), 0, s>>>(
           static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(gy),
-          static_cast<const __nv_bfloat16*>(gp), static_cast<__nv_bfloat16*>(dx), mean_invstd, affine, coef, g);
+          static_cast<const __nv_bfloat16*>(gp), static_cast<__nv_bfloat16*>(dx), mean_invstd, affine, coef, g,
+          static_cast<const uint16_t*>(argmax));
     else
       pool_dx_kernel<__half><<<grid, pool_threads(g.C), 0, s>>>(static_cast<const __half*>(x), static_cast<const __half*>(gy),
                                                   static_cast<const __half*>(gp), static_cast<__half*>(dx), mean_invstd,
-                                                  affine, coef, g);
+                                                  affine, coef, g, static_cast<const uint16_t*>(argmax));
     r4c::note_launches(1);
   }
   return cudaGetLastError() == cudaSuccess ? R4C_OK : R4C_ERR_CUDA;

@@ -90,10 +90,10 @@ def _bind(lib) -> None:
         "r4c_bn_relu_bwd_dx": ([P, P, P, P, P, P, dbl, i64, i, i, i, P, P, P, P], i),
         "r4c_channel_slice_copy": ([P, i, P, i64, i, i, P], i),
         "r4c_bn_relu_pool_fwd": ([P, P, i, P, P, P, i, i, i, i, i, i, P], i),
-        "r4c_bn_relu_pool_fwd_cat": ([P, P, i, P, P, P, i, i, i, i, i, i, P], i),
+        "r4c_bn_relu_pool_fwd_cat": ([P, P, i, P, P, P, P, i, i, i, i, i, i, P], i),
         "r4c_bn_pool_workspace_size": ([i, i, i, i, i], sz),
-        "r4c_bn_relu_pool_bwd_sums": ([P, i, P, P, P, P, i, i, i, i, i, i, P, P, sz, P], i),
-        "r4c_bn_relu_pool_bwd_dx": ([P, i, P, P, P, P, P, P, dbl, i, i, i, i, i, i, P, P, P, P], i),
+        "r4c_bn_relu_pool_bwd_sums": ([P, i, P, P, P, P, P, i, i, i, i, i, i, P, P, sz, P], i),
+        "r4c_bn_relu_pool_bwd_dx": ([P, i, P, P, P, P, P, P, P, dbl, i, i, i, i, i, i, P, P, P, P], i),
         "r4c_ce_workspace_size": ([i64], sz),
         "r4c_ce_fwd": ([P, P, i64, i, i, i64, P, P, sz, P], i),
         "r4c_ce_bwd": ([P, P, i64, i, i, i64, P, P, P, P], i),
@@ -475,31 +475,34 @@ def channel_slice_dense(t: torch.Tensor) -> Optional[torch.Tensor]:
 
 
 def bn_relu_pool_forward(x_cl: torch.Tensor, mean_invstd, affine, lead: int):
-    """(buf, p): buf is a new NDHWC tensor of lead + C channels whose channels
-    [lead, lead + C) hold relu(bn(x)) (the first lead channels zero when lead
-    is a multiple of 8, else unwritten: the caller's), p the 2x2x2 max-pool
-    of those channels."""
+    """(buf, p, argmax): buf is a new NDHWC tensor of lead + C channels whose
+    channels [lead, lead + C) hold relu(bn(x)) (the first lead channels zero
+    when lead is a multiple of 8, else unwritten: the caller's), p the 2x2x2
+    max-pool of those channels, argmax the windows' argmax for the backward
+    (int16 storage of the uint16 fields; None when lead is not a multiple of 8)."""
     dev = _require_cuda(x_cl)
     n, C, d, h, w = (int(v) for v in x_cl.shape)
     buf = _ndhwc_empty(n, lead + C, d, h, w, dev, x_cl.dtype)
     p = _ndhwc_empty(n, C, d // 2, h // 2, w // 2, dev, x_cl.dtype)
+    am = None
     with torch.cuda.device(dev):
         if lead % 8 == 0:
             # whole voxels in one pass (channels [0, lead) zero until the up-conv writes them)
-            st = lib().r4c_bn_relu_pool_fwd_cat(_ptr(x_cl), _ptr(buf), lead, _ptr(p), _ptr(mean_invstd),
+            am = torch.empty(n * (d // 2) * (h // 2) * (w // 2) * (C // 4), dtype=torch.int16, device=dev)
+            st = lib().r4c_bn_relu_pool_fwd_cat(_ptr(x_cl), _ptr(buf), lead, _ptr(p), _ptr(am), _ptr(mean_invstd),
                                                 _ptr(affine), n, d, h, w, C, dtype_code(x_cl.dtype), _stream(dev))
         else:
             yptr = ctypes.c_void_p(buf.data_ptr() + lead * buf.element_size())
             st = lib().r4c_bn_relu_pool_fwd(_ptr(x_cl), yptr, lead + C, _ptr(p), _ptr(mean_invstd), _ptr(affine),
                                             n, d, h, w, C, dtype_code(x_cl.dtype), _stream(dev))
     _check(st, "r4c_bn_relu_pool_fwd")
-    return buf, p
+    return buf, p, am
 
 
 def bn_relu_pool_backward(gbuf_cl: torch.Tensor, lead: int, gp_cl: torch.Tensor, x_cl: torch.Tensor, mean_invstd,
-                          affine, count: float, need_dx: bool = True, sums_hook=None):
+                          affine, count: float, need_dx: bool = True, sums_hook=None, argmax=None):
     """(dx or None, dgamma, dbeta) from dY = channels [lead, lead + C) of gbuf
-    and dP = gp."""
+    and dP = gp; argmax: the forward's (None: recomputed from x)."""
     dev = _require_cuda(gbuf_cl, gp_cl, x_cl)
     n, C, d, h, w = (int(v) for v in x_cl.shape)
     L = lib()
@@ -514,12 +517,14 @@ def bn_relu_pool_backward(gbuf_cl: torch.Tensor, lead: int, gp_cl: torch.Tensor,
     pitch = int(gbuf_cl.shape[1])
     gyptr = ctypes.c_void_p(gbuf_cl.data_ptr() + lead * gbuf_cl.element_size())
     with torch.cuda.device(dev):
-        st = L.r4c_bn_relu_pool_bwd_sums(gyptr, pitch, _ptr(gp_cl), _ptr(x_cl), _ptr(mean_invstd), _ptr(affine),
+        st = L.r4c_bn_relu_pool_bwd_sums(gyptr, pitch, _ptr(gp_cl), _ptr(argmax), _ptr(x_cl), _ptr(mean_invstd),
+                                         _ptr(affine),
                                          n, d, h, w, C, dt, _ptr(sums), _ptr(ws), ws.numel(), _stream(dev))
         _check(st, "r4c_bn_relu_pool_bwd_sums")
         if sums_hook is not None:
             sums_hook(sums, None)
-        st = L.r4c_bn_relu_pool_bwd_dx(gyptr, pitch, _ptr(gp_cl), _ptr(x_cl), _ptr(dx), _ptr(mean_invstd),
+        st = L.r4c_bn_relu_pool_bwd_dx(gyptr, pitch, _ptr(gp_cl), _ptr(argmax), _ptr(x_cl), _ptr(dx),
+                                       _ptr(mean_invstd),
                                        _ptr(affine), _ptr(sums), float(count), n, d, h, w, C, dt, _ptr(dg), _ptr(db),
                                        _ptr(coef), _stream(dev))
         _check(st, "r4c_bn_relu_pool_bwd_dx")

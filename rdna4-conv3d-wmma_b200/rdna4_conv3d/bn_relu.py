@@ -61,8 +61,8 @@ class BNReLUPoolFn(torch.autograd.Function):
         beta = None if bias is None else bias.detach().float().contiguous()
         _, mi, af, count = _native.bn_relu_forward(x, gamma, beta, running_mean, running_var, momentum, eps, True,
                                                    sums_hook, pivot, apply=False)
-        buf, p = _native.bn_relu_pool_forward(x, mi, af, lead)
-        ctx.save_for_backward(x, mi, af)
+        buf, p, am = _native.bn_relu_pool_forward(x, mi, af, lead)
+        ctx.save_for_backward(x, mi, af, am)
         ctx.count, ctx.lead, ctx.sums_hook = count, lead, sums_hook
         ctx.wdtype = None if weight is None else weight.dtype
         ctx.bdtype = None if bias is None else bias.dtype
@@ -70,7 +70,7 @@ class BNReLUPoolFn(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, gbuf, gp):
-        x, mi, af = ctx.saved_tensors
+        x, mi, af, am = ctx.saved_tensors
         cl = torch.channels_last_3d
         if gbuf is None:
             gbuf = torch.zeros((x.shape[0], ctx.lead + x.shape[1]) + tuple(x.shape[2:]), dtype=x.dtype,
@@ -81,7 +81,7 @@ class BNReLUPoolFn(torch.autograd.Function):
         gbuf = gbuf.to(x.dtype).contiguous(memory_format=cl)
         gp = gp.to(x.dtype).contiguous(memory_format=cl)
         dx, dg, db = _native.bn_relu_pool_backward(gbuf, ctx.lead, gp, x, mi, af, ctx.count, ctx.needs_input_grad[0],
-                                                   ctx.sums_hook)
+                                                   ctx.sums_hook, argmax=am)
         dg = dg.to(ctx.wdtype) if ctx.wdtype is not None and ctx.needs_input_grad[1] else None
         db = db.to(ctx.bdtype) if ctx.bdtype is not None and ctx.needs_input_grad[2] else None
         return dx, dg, db, None, None, None, None, None, None, None

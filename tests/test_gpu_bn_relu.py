@@ -247,3 +247,31 @@ def test_channel_slice_copy_declines_other_views(cuda_ready):
     assert _native.channel_slice_dense(b[:, :12]) is None
     c = torch.randn(2, 16, 4, 4, 4, device="cuda").contiguous(memory_format=cl)
     assert _native.channel_slice_dense(c[:, :8]) is None
+
+
+@pytest.mark.parametrize("quantised", [False, True], ids=["random", "ties"])
+def test_pool_backward_with_forward_argmax(cuda_ready, quantised):
+    """The pool backward fed the forward's argmax gives bit-identical dx,
+    dgamma, dbeta to the backward that recomputes the argmax from x."""
+    from rdna4_conv3d import _native
+    cl = torch.channels_last_3d
+    n, C, d, h, w, lead = 2, 24, 8, 12, 16, 24
+    g = torch.Generator().manual_seed(7)
+    x = torch.randn(n, C, d, h, w, generator=g) * 2.0 + 0.3
+    if quantised:
+        x = torch.round(x * 2) / 2
+    x = x.to(torch.bfloat16).cuda().contiguous(memory_format=cl)
+    mi = torch.stack([x.float().mean(dim=(0, 2, 3, 4)), 1.0 / (x.float().var(dim=(0, 2, 3, 4)) + 1e-5).sqrt()])
+    af = torch.stack([torch.rand(C, generator=g) + 0.5, torch.randn(C, generator=g) * 0.1]).cuda()
+    mi, af = mi.contiguous(), af.contiguous()
+    buf, p, am = _native.bn_relu_pool_forward(x, mi, af, lead)
+    assert am is not None
+    gbuf = torch.randn(n, lead + C, d, h, w, generator=g).to(torch.bfloat16).cuda().contiguous(memory_format=cl)
+    gp = torch.randn(n, C, d // 2, h // 2, w // 2, generator=g).to(torch.bfloat16).cuda().contiguous(memory_format=cl)
+    cnt = float(n * d * h * w)
+    a = _native.bn_relu_pool_backward(gbuf, lead, gp, x, mi, af, cnt, True, None, argmax=am)
+    b = _native.bn_relu_pool_backward(gbuf, lead, gp, x, mi, af, cnt, True, None, argmax=None)
+    for u, v in zip(a, b):
+        assert torch.equal(u, v)
+    # channels [0, lead) of the buffer are zero until an up-conv writes them
+    assert torch.count_nonzero(buf[:, :lead]) == 0

@@ -177,12 +177,24 @@ template <typename T>
 __global__ void sum_parts_kernel(const float* __restrict__ part, int S, int C, float* __restrict__ sums, int pivots,
                                  const float* __restrict__ pivot, const T* __restrict__ x) {
   // one warp per output: lane l sums partials l, l+32, ... in order, then a
-  // fixed butterfly over the lanes (same result on every run)
+  // fixed butterfly over the lanes (same result on every run). Four loads
+  // are issued before their adds (the adds keep their order): one load at a
+  // time left each of these small launches waiting on ~19 L2 round trips.
   const int o = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   if (o < 2 * C) {
     double a = 0.0;
-    for (int s = lane; s < S; s += 32) a += part[(int64_t)s * 2 * C + o];
+    const int64_t st = 2 * (int64_t)C;
+    int s = lane;
+    for (; s + 96 < S; s += 128) {
+      const float v0 = part[(int64_t)s * st + o], v1 = part[(int64_t)(s + 32) * st + o];
+      const float v2 = part[(int64_t)(s + 64) * st + o], v3 = part[(int64_t)(s + 96) * st + o];
+      a += v0;
+      a += v1;
+      a += v2;
+      a += v3;
+    }
+    for (; s < S; s += 32) a += part[(int64_t)s * st + o];
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) a += __shfl_xor_sync(0xffffffffu, a, off);
     if (lane == 0) sums[o] = (float)a;

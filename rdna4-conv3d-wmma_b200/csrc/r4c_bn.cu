@@ -2,7 +2,7 @@
 //
 // The reference's model blocks are Conv3d -> BatchNorm3d -> ReLU
 // (benches/unet_e2e.py:13-20 of the reference), and its design notes put
-// BatchNorm at ~11 ms of its step (docs/DESIGN.md:66). Stock PyTorch runs BN
+// BatchNorm at ~11 ms of its step (the reference's docs/DESIGN.md:66). Stock PyTorch runs BN
 // and ReLU as separate kernels: statistics, normalise, ReLU forward; ReLU
 // backward, BN reduction, BN dX — about 13 full passes over the activation.
 // Here the pair takes 5 + 3:

@@ -2,7 +2,7 @@
 
 The reference's UNet blocks are Conv3d -> BatchNorm3d -> ReLU on the vendor
 library (benches/unet_e2e.py:13-20 of the reference), BatchNorm costing about
-11 ms of its step (docs/DESIGN.md:66). ``BatchNormReLU3d`` is an
+11 ms of its step (the reference's docs/DESIGN.md:66). ``BatchNormReLU3d`` is an
 ``nn.BatchNorm3d`` (same parameters, buffers and state_dict) whose training
 forward, on a CUDA NDHWC bf16/fp16 activation with a multiple of 8 channels,
 runs the library's r4c_bn_* kernels: one statistics pass, a per-channel
